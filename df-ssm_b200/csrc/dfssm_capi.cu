@@ -1,0 +1,686 @@
+// C ABI of the DF-SSM B200 decode engine: .dfssm loading, device arena, state,
+// step execution (CUDA graph of per-op kernels, or the persistent step kernel) and the
+// stand-alone reference-op replacements.  See include/dfssm.h for the contract.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "engine.h"
+#include "kernels.cuh"
+
+using namespace dfssm;
+
+thread_local std::string g_err;
+
+int dfssm_fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+namespace {
+
+#define CU(call)                                                                              \
+  do {                                                                                        \
+    cudaError_t _e = (call);                                                                  \
+    if (_e != cudaSuccess)                                                                    \
+      return dfssm_fail(DFSSM_ERR_CUDA, "%s failed: %s (%d) at %s:%d", #call, cudaGetErrorString(_e), \
+                  (int)_e, __FILE__, __LINE__);                                               \
+  } while (0)
+
+#define CHECK_LAUNCH() CU(cudaGetLastError())
+
+constexpr size_t kHeader = 64;
+constexpr int kRank = DFSSM_RANK;
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Layout {  // offsets inside the .dfssm image
+  size_t emb, emb_s, layer0, layer_bytes, norm_f, total;
+  size_t proj_bytes(int n, int k) const {
+    return (size_t)n * (k / 32) * 4 + n * 2 + (size_t)n * kRank + n * 2 + (size_t)kRank * k + kRank * 2;
+  }
+};
+
+}  // namespace
+
+
+namespace {
+
+int effective_mode(const dfssm_engine* e) {
+  if (e->mode != 0) return e->mode;
+  return 1;
+}
+
+// ------------------------------------------------------------------ kernel launches
+
+int launch_prep(dfssm_engine* e, const __half* in, int K, const float* w, int quant, const ProjW* p,
+                cudaStream_t s) {
+  const size_t sm = (size_t)K * sizeof(__half);
+  act_prep_kernel<<<e->batch, kPrepThreads, sm, s>>>(in, K, w, quant, e->xn, e->q, e->xs, e->qsum,
+                                                     p ? p->lB : nullptr, p ? p->lBs : nullptr, e->t);
+  CHECK_LAUNCH();
+  return DFSSM_OK;
+}
+
+int gemv_grid(const dfssm_engine* e, int N) {
+  const int rows_per_cta = 2 * (kGemvThreads / 32);
+  int g = (N + rows_per_cta - 1) / rows_per_cta;
+  return g < 1 ? 1 : g;
+}
+
+template <int MODE>
+int launch_gemv(dfssm_engine* e, const ProjW& p, int B, const int8_t* q, const int* qsum, const __half* xs,
+                const __half* t, void* out, int ld_out, float* conv_state, const LayerW* L, cudaStream_t s) {
+  const size_t sm = (size_t)kGemvBT * p.K;
+  proj_gemv_kernel<MODE><<<gemv_grid(e, p.N), kGemvThreads, sm, s>>>(
+      p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out), ld_out, conv_state, L ? L->conv_w : nullptr,
+      L ? L->conv_b : nullptr, e->d.d_inner, e->d.d_xbc);
+  CHECK_LAUNCH();
+  return DFSSM_OK;
+}
+
+int enqueue_layer(dfssm_engine* e, int l, cudaStream_t s) {
+  const dfssm_dims& d = e->d;
+  const LayerW& L = e->layers[l];
+  const int B = e->batch;
+  int rc;
+  if ((rc = launch_prep(e, e->x, d.d_model, L.ln_w, 1, &L.in, s))) return rc;
+  if ((rc = launch_gemv<0>(e, L.in, B, e->q, e->qsum, e->xs, e->t, e->proj, d.n_in,
+                           e->conv + (size_t)l * e->conv_layer, &L, s)))
+    return rc;
+  ssm_gate_kernel<<<dim3(d.nheads, B), kSsmThreads, 0, s>>>(
+      e->proj + d.d_inner, d.n_in, e->proj + d.d_inner + d.d_xbc, d.n_in, e->proj, d.n_in, d.d_inner,
+      d.d_state, d.nheads, L.dt_bias, L.A_log, L.Dp, e->ssm + (size_t)l * e->ssm_layer, e->gated, d.d_inner);
+  CHECK_LAUNCH();
+  if ((rc = launch_prep(e, e->gated, d.d_inner, L.norm_w, 1, &L.out, s))) return rc;
+  if ((rc = launch_gemv<1>(e, L.out, B, e->q, e->qsum, e->xs, e->t, e->x, d.d_model, nullptr, nullptr, s)))
+    return rc;
+  return DFSSM_OK;
+}
+
+int enqueue_head(dfssm_engine* e, cudaStream_t s) {
+  const dfssm_dims& d = e->d;
+  int rc;
+  if ((rc = launch_prep(e, e->x, d.d_model, e->norm_f, 0, nullptr, s))) return rc;
+  const size_t sm = (size_t)kHeadBT * d.d_model * sizeof(float);
+  lm_head_kernel<<<e->sm_count * 4, kHeadThreads, sm, s>>>(e->Eq, e->Es, d.vocab, d.d_model, e->xn, e->batch,
+                                                           e->logits, e->best);
+  CHECK_LAUNCH();
+  finalize_kernel<<<(e->batch + 127) / 128, 128, 0, s>>>(e->best, e->batch, e->tokens);
+  CHECK_LAUNCH();
+  return DFSSM_OK;
+}
+
+int enqueue_step_ops(dfssm_engine* e, cudaStream_t s) {
+  const dfssm_dims& d = e->d;
+  embed_kernel<<<e->batch, 256, 0, s>>>(e->tokens, e->Eq, e->Es, d.d_model, d.vocab, e->x);
+  CHECK_LAUNCH();
+  int rc;
+  for (int l = 0; l < d.n_layer; ++l)
+    if ((rc = enqueue_layer(e, l, s))) return rc;
+  return enqueue_head(e, s);
+}
+
+int enqueue_step(dfssm_engine* e, int mode, cudaStream_t s) {
+  if (mode == 3) return launch_persistent_step(e, s);
+  return enqueue_step_ops(e, s);
+}
+
+int ensure_graph(dfssm_engine* e, int mode) {
+  if (e->gexec && e->graph_batch == e->batch && e->graph_mode == mode) return DFSSM_OK;
+  if (e->gexec) {
+    cudaGraphExecDestroy(e->gexec);
+    e->gexec = nullptr;
+  }
+  cudaGraph_t g = nullptr;
+  CU(cudaStreamBeginCapture(e->s, cudaStreamCaptureModeThreadLocal));
+  int rc = enqueue_step(e, mode, e->s);
+  cudaError_t ce = cudaStreamEndCapture(e->s, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (ce != cudaSuccess) return dfssm_fail(DFSSM_ERR_CUDA, "graph capture failed: %s", cudaGetErrorString(ce));
+  ce = cudaGraphInstantiate(&e->gexec, g, 0);
+  cudaGraphDestroy(g);
+  if (ce != cudaSuccess) return dfssm_fail(DFSSM_ERR_CUDA, "graph instantiate failed: %s", cudaGetErrorString(ce));
+  e->graph_batch = e->batch;
+  e->graph_mode = mode;
+  return DFSSM_OK;
+}
+
+// ------------------------------------------------------------------ loading
+
+int parse_dims(const unsigned char* img, size_t n, dfssm_dims* d, int* emb_kind) {
+  if (n < kHeader) return dfssm_fail(DFSSM_ERR_FORMAT, "image shorter than the 64-byte header (%zu bytes)", n);
+  if (memcmp(img, "DFSSM001", 8) != 0) return dfssm_fail(DFSSM_ERR_FORMAT, "bad magic (expected DFSSM001)");
+  uint32_t h[9];
+  memcpy(h, img + 8, sizeof(h));
+  d->n_layer = (int)h[0];
+  d->d_model = (int)h[1];
+  d->d_inner = (int)h[2];
+  d->d_state = (int)h[3];
+  d->nheads = (int)h[4];
+  d->headdim = (int)h[5];
+  d->ngroups = (int)h[6];
+  d->vocab = (int)h[7];
+  *emb_kind = img[8 + 36];
+  if (d->n_layer <= 0 || d->n_layer > 4096 || d->d_model <= 0 || d->d_inner <= 0 || d->vocab <= 0 ||
+      d->nheads <= 0 || d->d_model > (1 << 16) || d->d_inner > (1 << 16) || d->vocab > (1 << 24))
+    return dfssm_fail(DFSSM_ERR_FORMAT, "implausible header dims");
+  if ((int64_t)d->nheads * d->headdim != d->d_inner)
+    return dfssm_fail(DFSSM_ERR_FORMAT, "nheads*headdim (%d*%d) != d_inner (%d)", d->nheads, d->headdim, d->d_inner);
+  if (d->ngroups != 1) return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "ngroups=%d (only 1 supported)", d->ngroups);
+  if (d->headdim != DFSSM_HEADDIM || d->d_state != DFSSM_DSTATE)
+    return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "headdim=%d d_state=%d (kernels are built for 64/128)", d->headdim,
+                d->d_state);
+  if (d->d_model % 128 || d->d_inner % 128)
+    return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "d_model and d_inner must be multiples of 128");
+  if (*emb_kind != 0 && *emb_kind != 1) return dfssm_fail(DFSSM_ERR_FORMAT, "unknown embedding kind %d", *emb_kind);
+  d->d_xbc = d->d_inner + 2 * d->ngroups * d->d_state;
+  d->n_in = 2 * d->d_inner + 2 * d->ngroups * d->d_state + d->nheads;
+  return DFSSM_OK;
+}
+
+// Device arena: per layer, each array starts on a 256-byte boundary.
+struct ArenaPlan {
+  struct P {
+    size_t bits, scale, lA, lAs, lB, lBs;
+  };
+  struct Lyr {
+    P in, out;
+    size_t conv_w, conv_b, A_log, Dp, dt_bias, norm_w, ln_w;
+  };
+  std::vector<Lyr> L;
+  size_t Eq, Es, norm_f, total;
+};
+
+ArenaPlan plan_arena(const dfssm_dims& d) {
+  ArenaPlan a;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  auto proj = [&](int n, int k) {
+    ArenaPlan::P p;
+    p.bits = take((size_t)n * (k / 32) * 4);
+    p.scale = take((size_t)n * 2);
+    p.lA = take((size_t)n * kRank);
+    p.lAs = take((size_t)n * 2);
+    p.lB = take((size_t)kRank * k);
+    p.lBs = take(kRank * 2);
+    return p;
+  };
+  for (int l = 0; l < d.n_layer; ++l) {
+    ArenaPlan::Lyr y;
+    y.in = proj(d.n_in, d.d_model);
+    y.out = proj(d.d_model, d.d_inner);
+    y.conv_w = take((size_t)d.d_xbc * 4 * 2);
+    y.conv_b = take((size_t)d.d_xbc * 2);
+    y.A_log = take((size_t)d.nheads * 4);
+    y.Dp = take((size_t)d.nheads * 4);
+    y.dt_bias = take((size_t)d.nheads * 4);
+    y.norm_w = take((size_t)d.d_inner * 4);
+    y.ln_w = take((size_t)d.d_model * 4);
+    a.L.push_back(y);
+  }
+  a.norm_f = take((size_t)d.d_model * 4);
+  a.Es = take((size_t)d.vocab * 4);
+  a.Eq = take((size_t)d.vocab * d.d_model);
+  a.total = off;
+  return a;
+}
+
+int build_engine(const unsigned char* img, size_t n, int device, int max_batch, dfssm_engine** out) {
+  if (!out) return dfssm_fail(DFSSM_ERR_ARG, "out is NULL");
+  *out = nullptr;
+  if (!img) return dfssm_fail(DFSSM_ERR_ARG, "image is NULL");
+  if (max_batch < 1 || max_batch > 4096) return dfssm_fail(DFSSM_ERR_ARG, "max_batch=%d out of range", max_batch);
+  dfssm_dims d;
+  int emb_kind = 0;
+  int rc = parse_dims(img, n, &d, &emb_kind);
+  if (rc) return rc;
+  const size_t emb_bytes = emb_kind == 0 ? (size_t)d.vocab * d.d_model * 2 : (size_t)d.vocab * d.d_model + (size_t)d.vocab * 2;
+  Layout lay;
+  const size_t per_layer = lay.proj_bytes(d.n_in, d.d_model) + lay.proj_bytes(d.d_model, d.d_inner) +
+                           (size_t)d.d_xbc * 4 * 2 + (size_t)d.d_xbc * 2 + 3 * (size_t)d.nheads * 4 +
+                           (size_t)d.d_inner * 4 + (size_t)d.d_model * 4;
+  const size_t need = kHeader + emb_bytes + (size_t)d.n_layer * per_layer + (size_t)d.d_model * 4;
+  if (n != need) return dfssm_fail(DFSSM_ERR_FORMAT, "image is %zu bytes, header implies %zu", n, need);
+
+  ArenaPlan ap = plan_arena(d);
+  std::vector<char> host(ap.total, 0);
+  size_t src = kHeader;
+  auto copy = [&](size_t dst, size_t bytes) {
+    memcpy(host.data() + dst, img + src, bytes);
+    src += bytes;
+  };
+  // embedding: int8 rows + fp32 per-row scale
+  {
+    int8_t* Eq = reinterpret_cast<int8_t*>(host.data() + ap.Eq);
+    float* Es = reinterpret_cast<float*>(host.data() + ap.Es);
+    if (emb_kind == 1) {
+      memcpy(Eq, img + src, (size_t)d.vocab * d.d_model);
+      src += (size_t)d.vocab * d.d_model;
+      const __half* hs = reinterpret_cast<const __half*>(img + src);
+      for (int v = 0; v < d.vocab; ++v) Es[v] = __half2float(hs[v]);
+      src += (size_t)d.vocab * 2;
+    } else {
+      // fp16 embedding: per-row symmetric int8 quantisation, scale = absmax / 127.
+      const __half* E = reinterpret_cast<const __half*>(img + src);
+      for (int v = 0; v < d.vocab; ++v) {
+        const __half* row = E + (size_t)v * d.d_model;
+        float amax = 0.f;
+        for (int k = 0; k < d.d_model; ++k) amax = fmaxf(amax, fabsf(__half2float(row[k])));
+        const float s = amax > 0.f ? amax / 127.0f : 1.0f;
+        Es[v] = s;
+        for (int k = 0; k < d.d_model; ++k) {
+          float qv = nearbyintf(__half2float(row[k]) / s);
+          qv = fminf(127.f, fmaxf(-127.f, qv));
+          Eq[(size_t)v * d.d_model + k] = (int8_t)qv;
+        }
+      }
+      src += (size_t)d.vocab * d.d_model * 2;
+    }
+  }
+  for (int l = 0; l < d.n_layer; ++l) {
+    const ArenaPlan::Lyr& y = ap.L[l];
+    const ArenaPlan::P* ps[2] = {&y.in, &y.out};
+    const int ns[2] = {d.n_in, d.d_model}, ks[2] = {d.d_model, d.d_inner};
+    for (int j = 0; j < 2; ++j) {
+      copy(ps[j]->bits, (size_t)ns[j] * (ks[j] / 32) * 4);
+      copy(ps[j]->scale, (size_t)ns[j] * 2);
+      copy(ps[j]->lA, (size_t)ns[j] * kRank);
+      copy(ps[j]->lAs, (size_t)ns[j] * 2);
+      copy(ps[j]->lB, (size_t)kRank * ks[j]);
+      copy(ps[j]->lBs, kRank * 2);
+    }
+    copy(y.conv_w, (size_t)d.d_xbc * 4 * 2);
+    copy(y.conv_b, (size_t)d.d_xbc * 2);
+    copy(y.A_log, (size_t)d.nheads * 4);
+    copy(y.Dp, (size_t)d.nheads * 4);
+    copy(y.dt_bias, (size_t)d.nheads * 4);
+    copy(y.norm_w, (size_t)d.d_inner * 4);
+    copy(y.ln_w, (size_t)d.d_model * 4);
+  }
+  copy(ap.norm_f, (size_t)d.d_model * 4);
+  if (src != n) return dfssm_fail(DFSSM_ERR_FORMAT, "internal: parsed %zu of %zu bytes", src, n);
+
+  dfssm_engine* e = new dfssm_engine();
+  e->device = device;
+  e->d = d;
+  e->emb_kind = emb_kind;
+  e->max_batch = max_batch;
+  e->batch = max_batch;
+  auto cleanup = [&](int code) {
+    dfssm_destroy(e);
+    return code;
+  };
+  cudaError_t ce = cudaSetDevice(device);
+  if (ce != cudaSuccess) return cleanup(dfssm_fail(DFSSM_ERR_CUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(ce)));
+  cudaDeviceGetAttribute(&e->sm_count, cudaDevAttrMultiProcessorCount, device);
+  if (cudaMalloc(&e->arena, ap.total) != cudaSuccess)
+    return cleanup(dfssm_fail(DFSSM_ERR_OOM, "cudaMalloc(%zu) for weights failed", ap.total));
+  e->arena_bytes = ap.total;
+  ce = cudaMemcpy(e->arena, host.data(), ap.total, cudaMemcpyHostToDevice);
+  if (ce != cudaSuccess) return cleanup(dfssm_fail(DFSSM_ERR_CUDA, "weight upload: %s", cudaGetErrorString(ce)));
+  char* A = e->arena;
+  for (int l = 0; l < d.n_layer; ++l) {
+    const ArenaPlan::Lyr& y = ap.L[l];
+    LayerW L;
+    auto mk = [&](const ArenaPlan::P& p, int nrows, int k) {
+      ProjW w;
+      w.bits = reinterpret_cast<const uint32_t*>(A + p.bits);
+      w.scale = reinterpret_cast<const __half*>(A + p.scale);
+      w.lA = reinterpret_cast<const int8_t*>(A + p.lA);
+      w.lAs = reinterpret_cast<const __half*>(A + p.lAs);
+      w.lB = reinterpret_cast<const int8_t*>(A + p.lB);
+      w.lBs = reinterpret_cast<const __half*>(A + p.lBs);
+      w.N = nrows;
+      w.K = k;
+      return w;
+    };
+    L.in = mk(y.in, d.n_in, d.d_model);
+    L.out = mk(y.out, d.d_model, d.d_inner);
+    L.conv_w = reinterpret_cast<const __half*>(A + y.conv_w);
+    L.conv_b = reinterpret_cast<const __half*>(A + y.conv_b);
+    L.A_log = reinterpret_cast<const float*>(A + y.A_log);
+    L.Dp = reinterpret_cast<const float*>(A + y.Dp);
+    L.dt_bias = reinterpret_cast<const float*>(A + y.dt_bias);
+    L.norm_w = reinterpret_cast<const float*>(A + y.norm_w);
+    L.ln_w = reinterpret_cast<const float*>(A + y.ln_w);
+    e->layers.push_back(L);
+  }
+  e->Eq = reinterpret_cast<const int8_t*>(A + ap.Eq);
+  e->Es = reinterpret_cast<const float*>(A + ap.Es);
+  e->norm_f = reinterpret_cast<const float*>(A + ap.norm_f);
+
+  // state + activations
+  const int B = max_batch;
+  const int kmax = d.d_inner > d.d_model ? d.d_inner : d.d_model;
+  e->ssm_layer = (size_t)B * d.nheads * DFSSM_HEADDIM * DFSSM_DSTATE;
+  e->conv_layer = (size_t)B * 3 * d.d_xbc;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  const size_t o_ssm = take(e->ssm_layer * d.n_layer * 4);
+  const size_t o_conv = take(e->conv_layer * d.n_layer * 4);
+  const size_t o_x = take((size_t)B * d.d_model * 2);
+  const size_t o_xn = take((size_t)B * kmax * 2);
+  const size_t o_q = take((size_t)B * kmax);
+  const size_t o_xs = take((size_t)B * 2);
+  const size_t o_qsum = take((size_t)B * 4);
+  const size_t o_t = take((size_t)B * kRank * 2);
+  const size_t o_proj = take((size_t)B * d.n_in * 2);
+  const size_t o_gated = take((size_t)B * d.d_inner * 2);
+  const size_t o_logits = take((size_t)B * d.vocab * 4);
+  const size_t o_best = take((size_t)B * 8);
+  const size_t o_tok = take((size_t)B * 4);
+  const size_t o_sync = take(4096);
+  const size_t o_layers = take(sizeof(LayerW) * d.n_layer);
+  if (cudaMalloc(&e->work, off) != cudaSuccess)
+    return cleanup(dfssm_fail(DFSSM_ERR_OOM, "cudaMalloc(%zu) for state/activations failed", off));
+  e->work_bytes = off;
+  char* W = e->work;
+  e->ssm = reinterpret_cast<float*>(W + o_ssm);
+  e->conv = reinterpret_cast<float*>(W + o_conv);
+  e->x = reinterpret_cast<__half*>(W + o_x);
+  e->xn = reinterpret_cast<__half*>(W + o_xn);
+  e->q = reinterpret_cast<int8_t*>(W + o_q);
+  e->xs = reinterpret_cast<__half*>(W + o_xs);
+  e->qsum = reinterpret_cast<int*>(W + o_qsum);
+  e->t = reinterpret_cast<__half*>(W + o_t);
+  e->proj = reinterpret_cast<__half*>(W + o_proj);
+  e->gated = reinterpret_cast<__half*>(W + o_gated);
+  e->logits = reinterpret_cast<float*>(W + o_logits);
+  e->best = reinterpret_cast<unsigned long long*>(W + o_best);
+  e->tokens = reinterpret_cast<int*>(W + o_tok);
+  e->sync = reinterpret_cast<unsigned int*>(W + o_sync);
+  e->d_layers = reinterpret_cast<LayerW*>(W + o_layers);
+  ce = cudaMemset(e->work, 0, off);
+  if (ce != cudaSuccess) return cleanup(dfssm_fail(DFSSM_ERR_CUDA, "state clear: %s", cudaGetErrorString(ce)));
+  ce = cudaMemcpy(e->d_layers, e->layers.data(), sizeof(LayerW) * d.n_layer, cudaMemcpyHostToDevice);
+  if (ce != cudaSuccess) return cleanup(dfssm_fail(DFSSM_ERR_CUDA, "layer table upload: %s", cudaGetErrorString(ce)));
+  if (cudaStreamCreateWithFlags(&e->s, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&e->ev_in, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&e->ev_out, cudaEventDisableTiming) != cudaSuccess)
+    return cleanup(dfssm_fail(DFSSM_ERR_CUDA, "stream/event creation failed"));
+  // kernels that need more than 48 KB of dynamic shared memory
+  const int gemv_smem = kGemvBT * kmax;
+  const int head_smem = kHeadBT * d.d_model * 4;
+  if (cudaFuncSetAttribute(proj_gemv_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemv_smem) != cudaSuccess ||
+      cudaFuncSetAttribute(proj_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, gemv_smem) != cudaSuccess ||
+      cudaFuncSetAttribute(lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, head_smem) != cudaSuccess)
+    return cleanup(dfssm_fail(DFSSM_ERR_CUDA, "cudaFuncSetAttribute failed: %s", cudaGetErrorString(cudaGetLastError())));
+  rc = persistent_init(e);
+  if (rc) return cleanup(rc);
+  *out = e;
+  return DFSSM_OK;
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+
+extern "C" {
+
+const char* dfssm_version(void) { return "dfssm-b200 0.1 (sm_100a)"; }
+const char* dfssm_last_error(void) { return g_err.c_str(); }
+
+int dfssm_create_from_memory(const void* image, size_t image_bytes, int device, int max_batch, dfssm_engine** out) {
+  return build_engine(static_cast<const unsigned char*>(image), image_bytes, device, max_batch, out);
+}
+
+int dfssm_create_from_file(const char* path, int device, int max_batch, dfssm_engine** out) {
+  if (!path) return dfssm_fail(DFSSM_ERR_ARG, "path is NULL");
+  FILE* f = fopen(path, "rb");
+  if (!f) return dfssm_fail(DFSSM_ERR_ARG, "cannot open %s", path);
+  std::vector<unsigned char> buf;
+  fseek(f, 0, SEEK_END);
+  long n = ftell(f);
+  fseek(f, 0, SEEK_SET);
+  if (n < 0) {
+    fclose(f);
+    return dfssm_fail(DFSSM_ERR_ARG, "cannot size %s", path);
+  }
+  buf.resize((size_t)n);
+  size_t got = n ? fread(buf.data(), 1, (size_t)n, f) : 0;
+  fclose(f);
+  if (got != (size_t)n) return dfssm_fail(DFSSM_ERR_FORMAT, "short read of %s", path);
+  return build_engine(buf.data(), buf.size(), device, max_batch, out);
+}
+
+void dfssm_destroy(dfssm_engine* e) {
+  if (!e) return;
+  cudaSetDevice(e->device);
+  if (e->gexec) cudaGraphExecDestroy(e->gexec);
+  if (e->s) cudaStreamSynchronize(e->s);
+  if (e->ev_in) cudaEventDestroy(e->ev_in);
+  if (e->ev_out) cudaEventDestroy(e->ev_out);
+  if (e->s) cudaStreamDestroy(e->s);
+  if (e->arena) cudaFree(e->arena);
+  if (e->work) cudaFree(e->work);
+  delete e;
+}
+
+int dfssm_get_dims(const dfssm_engine* e, dfssm_dims* out) {
+  if (!e || !out) return dfssm_fail(DFSSM_ERR_ARG, "NULL argument");
+  *out = e->d;
+  return DFSSM_OK;
+}
+
+int dfssm_set_batch(dfssm_engine* e, int batch) {
+  if (!e) return dfssm_fail(DFSSM_ERR_ARG, "NULL engine");
+  if (batch < 1 || batch > e->max_batch)
+    return dfssm_fail(DFSSM_ERR_ARG, "batch=%d outside [1, max_batch=%d]", batch, e->max_batch);
+  e->batch = batch;
+  return DFSSM_OK;
+}
+
+int dfssm_set_mode(dfssm_engine* e, int mode) {
+  if (!e) return dfssm_fail(DFSSM_ERR_ARG, "NULL engine");
+  if (mode < 0 || mode > 3) return dfssm_fail(DFSSM_ERR_ARG, "mode=%d unknown", mode);
+  if (mode == 3 && !persistent_supported(e))
+    return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "persistent step kernel not available for these dims/batch");
+  e->mode = mode;
+  return DFSSM_OK;
+}
+
+int dfssm_get_mode(const dfssm_engine* e, int* mode) {
+  if (!e || !mode) return dfssm_fail(DFSSM_ERR_ARG, "NULL argument");
+  *mode = effective_mode(e);
+  return DFSSM_OK;
+}
+
+int dfssm_reset(dfssm_engine* e, void* stream) {
+  if (!e) return dfssm_fail(DFSSM_ERR_ARG, "NULL engine");
+  CU(cudaSetDevice(e->device));
+  cudaStream_t us = static_cast<cudaStream_t>(stream);
+  CU(cudaMemsetAsync(e->ssm, 0, e->ssm_layer * e->d.n_layer * 4, us));
+  CU(cudaMemsetAsync(e->conv, 0, e->conv_layer * e->d.n_layer * 4, us));
+  CU(cudaMemsetAsync(e->best, 0, (size_t)e->max_batch * 8, us));
+  return DFSSM_OK;
+}
+
+int dfssm_step(dfssm_engine* e, const int32_t* tokens_dev, float* logits_dev, int32_t* next_tokens_dev,
+               void* stream) {
+  if (!e) return dfssm_fail(DFSSM_ERR_ARG, "NULL engine");
+  CU(cudaSetDevice(e->device));
+  cudaStream_t us = static_cast<cudaStream_t>(stream);
+  const int mode = effective_mode(e);
+  if (mode == 3 && !persistent_supported(e))
+    return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "persistent step kernel not available for batch %d", e->batch);
+  CU(cudaEventRecord(e->ev_in, us));
+  CU(cudaStreamWaitEvent(e->s, e->ev_in, 0));
+  if (tokens_dev)
+    CU(cudaMemcpyAsync(e->tokens, tokens_dev, (size_t)e->batch * 4, cudaMemcpyDeviceToDevice, e->s));
+  int rc;
+  if (mode == 2) {
+    if ((rc = enqueue_step(e, 1, e->s))) return rc;
+  } else {
+    if ((rc = ensure_graph(e, mode))) return rc;
+    CU(cudaGraphLaunch(e->gexec, e->s));
+  }
+  if (logits_dev)
+    CU(cudaMemcpyAsync(logits_dev, e->logits, (size_t)e->batch * e->d.vocab * 4, cudaMemcpyDeviceToDevice, e->s));
+  if (next_tokens_dev)
+    CU(cudaMemcpyAsync(next_tokens_dev, e->tokens, (size_t)e->batch * 4, cudaMemcpyDeviceToDevice, e->s));
+  CU(cudaEventRecord(e->ev_out, e->s));
+  CU(cudaStreamWaitEvent(us, e->ev_out, 0));
+  return DFSSM_OK;
+}
+
+int dfssm_step_host(dfssm_engine* e, const int32_t* tokens_host, float* logits_host, int32_t* next_tokens_host,
+                    void* stream) {
+  if (!e) return dfssm_fail(DFSSM_ERR_ARG, "NULL engine");
+  CU(cudaSetDevice(e->device));
+  cudaStream_t us = static_cast<cudaStream_t>(stream);
+  if (tokens_host) CU(cudaMemcpyAsync(e->tokens, tokens_host, (size_t)e->batch * 4, cudaMemcpyHostToDevice, us));
+  int rc = dfssm_step(e, nullptr, nullptr, nullptr, stream);
+  if (rc) return rc;
+  if (logits_host)
+    CU(cudaMemcpyAsync(logits_host, e->logits, (size_t)e->batch * e->d.vocab * 4, cudaMemcpyDeviceToHost, us));
+  if (next_tokens_host)
+    CU(cudaMemcpyAsync(next_tokens_host, e->tokens, (size_t)e->batch * 4, cudaMemcpyDeviceToHost, us));
+  CU(cudaStreamSynchronize(us));
+  return DFSSM_OK;
+}
+
+int dfssm_check_finite(dfssm_engine* e, void* stream) {
+  if (!e) return dfssm_fail(DFSSM_ERR_ARG, "NULL engine");
+  CU(cudaSetDevice(e->device));
+  std::vector<float> h((size_t)e->batch * e->d.vocab);
+  CU(cudaMemcpyAsync(h.data(), e->logits, h.size() * 4, cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream)));
+  CU(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  for (size_t i = 0; i < h.size(); ++i)
+    if (!std::isfinite(h[i])) return dfssm_fail(DFSSM_ERR_NUMERIC, "non-finite logit at flat index %zu", i);
+  return DFSSM_OK;
+}
+
+int dfssm_state_ptrs(dfssm_engine* e, int layer, float** ssm, float** conv) {
+  if (!e || !ssm || !conv) return dfssm_fail(DFSSM_ERR_ARG, "NULL argument");
+  if (layer < 0 || layer >= e->d.n_layer) return dfssm_fail(DFSSM_ERR_ARG, "layer %d out of range", layer);
+  *ssm = e->ssm + (size_t)layer * e->ssm_layer;
+  *conv = e->conv + (size_t)layer * e->conv_layer;
+  return DFSSM_OK;
+}
+
+int dfssm_get_buffer(dfssm_engine* e, const char* name, void** ptr, size_t* bytes) {
+  if (!e || !name || !ptr || !bytes) return dfssm_fail(DFSSM_ERR_ARG, "NULL argument");
+  const dfssm_dims& d = e->d;
+  const size_t B = e->max_batch;
+  if (!strcmp(name, "x")) { *ptr = e->x; *bytes = B * d.d_model * 2; }
+  else if (!strcmp(name, "proj")) { *ptr = e->proj; *bytes = B * d.n_in * 2; }
+  else if (!strcmp(name, "gated")) { *ptr = e->gated; *bytes = B * d.d_inner * 2; }
+  else if (!strcmp(name, "logits")) { *ptr = e->logits; *bytes = B * d.vocab * 4; }
+  else if (!strcmp(name, "tokens")) { *ptr = e->tokens; *bytes = B * 4; }
+  else return dfssm_fail(DFSSM_ERR_ARG, "unknown buffer '%s'", name);
+  return DFSSM_OK;
+}
+
+int dfssm_layer_step(dfssm_engine* e, int layer, void* stream) {
+  if (!e) return dfssm_fail(DFSSM_ERR_ARG, "NULL engine");
+  if (layer < 0 || layer >= e->d.n_layer) return dfssm_fail(DFSSM_ERR_ARG, "layer %d out of range", layer);
+  CU(cudaSetDevice(e->device));
+  return enqueue_layer(e, layer, static_cast<cudaStream_t>(stream));
+}
+
+size_t dfssm_scaffold_gemm_workspace(int M, int K) {
+  if (M <= 0 || K <= 0) return 0;
+  return align256((size_t)M * K) + align256((size_t)M * 4) + align256((size_t)M * 2) + align256((size_t)M * kRank * 2);
+}
+
+int dfssm_scaffold_gemm(const uint32_t* packed, const int8_t* q, int M, int N, int K, int32_t* acc, void* workspace,
+                        void* stream) {
+  if (!packed || !q || !acc || !workspace) return dfssm_fail(DFSSM_ERR_ARG, "NULL argument");
+  if (M < 1 || N < 1 || K < 128 || K % 128 || K > 65536) return dfssm_fail(DFSSM_ERR_ARG, "bad sizes M=%d N=%d K=%d", M, N, K);
+  if (((uintptr_t)packed | (uintptr_t)workspace) & 15) return dfssm_fail(DFSSM_ERR_ARG, "packed/workspace must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  int8_t* qp = reinterpret_cast<int8_t*>(ws);
+  int* qsum = reinterpret_cast<int*>(ws + align256((size_t)M * K));
+  permute_q_kernel<<<M, kPrepThreads, 0, s>>>(q, K, qp, qsum);
+  CHECK_LAUNCH();
+  ProjW p{};
+  p.bits = packed;
+  p.N = N;
+  p.K = K;
+  const size_t sm = (size_t)kGemvBT * K;
+  if (sm > 48 * 1024) CU(cudaFuncSetAttribute(proj_gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  const int rows_per_cta = 2 * (kGemvThreads / 32);
+  proj_gemv_kernel<2><<<(N + rows_per_cta - 1) / rows_per_cta, kGemvThreads, sm, s>>>(
+      p, qp, qsum, nullptr, nullptr, M, reinterpret_cast<__half*>(acc), N, nullptr, nullptr, nullptr, 0, 0);
+  CHECK_LAUNCH();
+  return DFSSM_OK;
+}
+
+int dfssm_conv_step(float* conv_state, void* xbc_f16, int ld_xbc, const void* conv_w_f16, const void* conv_b_f16,
+                    int batch, int d_xbc, void* stream) {
+  if (!conv_state || !xbc_f16 || !conv_w_f16 || !conv_b_f16) return dfssm_fail(DFSSM_ERR_ARG, "NULL argument");
+  if (batch < 1 || d_xbc < 1 || ld_xbc < d_xbc) return dfssm_fail(DFSSM_ERR_ARG, "bad sizes");
+  conv_step_kernel<<<dim3((d_xbc + 255) / 256, batch), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      conv_state, static_cast<__half*>(xbc_f16), ld_xbc, static_cast<const __half*>(conv_w_f16),
+      static_cast<const __half*>(conv_b_f16), d_xbc);
+  CHECK_LAUNCH();
+  return DFSSM_OK;
+}
+
+int dfssm_ssm_step(const void* xbc_f16, int ld_xbc, const void* dt_f16, int ld_dt, const float* dt_bias,
+                   const float* A_log, const float* D, float* h_state, void* y_f16, int ld_y, int batch, int nheads,
+                   int headdim, int d_state, void* stream) {
+  if (!xbc_f16 || !dt_f16 || !dt_bias || !A_log || !D || !h_state || !y_f16) return dfssm_fail(DFSSM_ERR_ARG, "NULL argument");
+  if (headdim != DFSSM_HEADDIM || d_state != DFSSM_DSTATE)
+    return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "headdim=%d d_state=%d (built for 64/128)", headdim, d_state);
+  if (batch < 1 || nheads < 1) return dfssm_fail(DFSSM_ERR_ARG, "bad sizes");
+  if ((uintptr_t)h_state & 15) return dfssm_fail(DFSSM_ERR_ARG, "h_state must be 16-byte aligned");
+  const int d_inner = nheads * headdim;
+  ssm_gate_kernel<<<dim3(nheads, batch), kSsmThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(xbc_f16), ld_xbc, static_cast<const __half*>(dt_f16), ld_dt, nullptr, 0, d_inner,
+      d_state, nheads, dt_bias, A_log, D, h_state, static_cast<__half*>(y_f16), ld_y);
+  CHECK_LAUNCH();
+  return DFSSM_OK;
+}
+
+size_t dfssm_lm_head_workspace(int batch) { return batch > 0 ? align256((size_t)batch * 8) : 0; }
+
+int dfssm_lm_head_argmax(const int8_t* E_q, const float* E_s, int vocab, int d, const void* x_f16, int batch,
+                         float* logits, int32_t* next, void* workspace, void* stream) {
+  if (!E_q || !E_s || !x_f16 || !next || !workspace) return dfssm_fail(DFSSM_ERR_ARG, "NULL argument");
+  if (vocab < 1 || batch < 1 || d < 16 || d % 16) return dfssm_fail(DFSSM_ERR_ARG, "bad sizes");
+  if ((uintptr_t)E_q & 15 || (d % 16)) return dfssm_fail(DFSSM_ERR_ARG, "E_q rows must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  unsigned long long* best = static_cast<unsigned long long*>(workspace);
+  CU(cudaMemsetAsync(best, 0, (size_t)batch * 8, s));
+  float* lg = logits;
+  if (!lg) return dfssm_fail(DFSSM_ERR_ARG, "logits output is required by this build");
+  const size_t sm = (size_t)kHeadBT * d * sizeof(float);
+  if (sm > 48 * 1024) CU(cudaFuncSetAttribute(lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  int sms = 148;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  lm_head_kernel<<<sms * 4, kHeadThreads, sm, s>>>(E_q, E_s, vocab, d, static_cast<const __half*>(x_f16), batch, lg,
+                                                    best);
+  CHECK_LAUNCH();
+  finalize_kernel<<<(batch + 127) / 128, 128, 0, s>>>(best, batch, reinterpret_cast<int*>(next));
+  CHECK_LAUNCH();
+  return DFSSM_OK;
+}
+
+}  // extern "C"

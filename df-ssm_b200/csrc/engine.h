@@ -1,0 +1,51 @@
+// Internal engine definition shared by the C-ABI and the persistent step kernel.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/dfssm.h"
+#include "types.cuh"
+
+struct dfssm_engine {
+  int device = 0;
+  dfssm_dims d{};
+  int emb_kind = 0;
+  int max_batch = 0, batch = 0;
+  int mode = 0;  // requested mode (0 = auto)
+  // device memory
+  char* arena = nullptr;
+  size_t arena_bytes = 0;
+  char* work = nullptr;
+  size_t work_bytes = 0;
+  std::vector<dfssm::LayerW> layers;
+  dfssm::LayerW* d_layers = nullptr;  // device copy for the persistent kernel
+  const int8_t* Eq = nullptr;
+  const float* Es = nullptr;
+  const float* norm_f = nullptr;
+  float* ssm = nullptr;
+  float* conv = nullptr;
+  size_t ssm_layer = 0, conv_layer = 0;  // elements per layer (max_batch rows)
+  __half *x = nullptr, *xn = nullptr, *xs = nullptr, *t = nullptr, *proj = nullptr, *gated = nullptr;
+  int8_t* q = nullptr;
+  int* qsum = nullptr;
+  float* logits = nullptr;
+  unsigned long long* best = nullptr;
+  int* tokens = nullptr;
+  unsigned int* sync = nullptr;  // persistent-kernel barrier words
+  // execution
+  cudaStream_t s = nullptr;
+  cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+  cudaGraphExec_t gexec = nullptr;
+  int graph_batch = -1, graph_mode = -1;
+  int sm_count = 148;
+};
+
+// Sets the thread's last-error message and returns `code`.
+int dfssm_fail(int code, const char* fmt, ...);
+
+// Persistent whole-step kernel (persistent.cu).
+int persistent_init(dfssm_engine* e);
+bool persistent_supported(const dfssm_engine* e);
+int launch_persistent_step(dfssm_engine* e, cudaStream_t s);

@@ -1,0 +1,444 @@
+// Per-op decode kernels for sm_100a (any batch size).
+//
+// One decode step of one layer is, in launch order:
+//   act_prep   (in)  RMSNorm(x)·ln_w -> fp16, per-row int8 quantisation, LoRA t = x·B^T
+//   proj_gemv  (in)  packed 1-bit scaffold GEMV + dequant + LoRA + conv1d/SiLU epilogue
+//   ssm_gate         dt softplus, exp(A·dt), state update, C·h + D·x, y·silu(z)
+//   act_prep   (out) RMSNorm(gated)·norm_w, quantisation, LoRA t
+//   proj_gemv  (out) scaffold GEMV + dequant + LoRA + residual add into x
+// and once per step: embed (token -> x), act_prep (final norm), lm_head (int8 GEMV with
+// a fused fp16-rounded argmax), finalize (winning token id).
+//
+// Every rounding point follows the reference GPU path
+// (inference/gpu/df_ssm_inference.py:141-210, inference/gpu/df_ssm_kernels.cu:27-103).
+#pragma once
+#include "types.cuh"
+
+namespace dfssm {
+
+constexpr int kPrepThreads = 256;
+constexpr int kGemvThreads = 256;
+constexpr int kGemvBT = 16;      // batch rows per GEMV pass (one per lane of a half-warp)
+constexpr int kSsmThreads = 256;
+constexpr int kHeadThreads = 256;
+constexpr int kHeadBT = 8;
+
+// ---------------------------------------------------------------------------------------
+// act_prep: one CTA per batch row.
+//   xn = fp16((x * rsqrt(mean(x^2) + 1e-5)) * w)          df_ssm_inference.py:141-145
+//   s  = fp16(max(amax|xn|, fp16(1e-4)) * (1/127))          df_ssm_inference.py:150
+//   q  = clamp(rne(fp16(xn / s)), -128, 127)                df_ssm_inference.py:151
+//   t_r = fp16(sum_k xn_k * fp16(lB[r][k] * lBs[r]))        df_ssm_inference.py:92-97,173
+// q is written in the permuted layout of qperm_index(); qsum = sum_k q_k.
+// With quant == 0 only xn is produced (final norm before the LM head).
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kPrepThreads)
+act_prep_kernel(const __half* __restrict__ in, int K, const float* __restrict__ w, int quant,
+                __half* __restrict__ xn_out, int8_t* __restrict__ q_out, __half* __restrict__ xs_out,
+                int* __restrict__ qsum_out, const int8_t* __restrict__ lB, const __half* __restrict__ lBs,
+                __half* __restrict__ t_out) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __half* sxn = reinterpret_cast<__half*>(smem);
+  __shared__ float red[kPrepThreads / 32];
+  __shared__ int ired[kPrepThreads / 32];
+  const int b = blockIdx.x;
+  const __half* xr = in + (size_t)b * K;
+
+  float ss = 0.f;
+  for (int k = threadIdx.x; k < K; k += kPrepThreads) {
+    float v = h2f(xr[k]);
+    ss = __fadd_rn(ss, __fmul_rn(v, v));
+  }
+  ss = block_sum<kPrepThreads / 32>(ss, red);
+  const float var = __fmul_rn(ss, 1.0f / (float)K);
+  const float r = rsqrtf(__fadd_rn(var, 1e-5f));
+
+  float amax = 0.f;
+  for (int k = threadIdx.x; k < K; k += kPrepThreads) {
+    __half xn = f2h(__fmul_rn(__fmul_rn(h2f(xr[k]), r), w[k]));
+    sxn[k] = xn;
+    amax = fmaxf(amax, fabsf(h2f(xn)));
+    if (!quant) xn_out[(size_t)b * K + k] = xn;
+  }
+  if (!quant) return;
+  amax = block_max<kPrepThreads / 32>(amax, red);
+  const __half s16 = f2h(__fmul_rn(fmaxf(amax, qscale_floor()), 1.0f / 127.0f));
+  const float s = h2f(s16);
+
+  int qs = 0;
+  int8_t* qrow = q_out + (size_t)b * K;
+  for (int k = threadIdx.x; k < K; k += kPrepThreads) {
+    float t = round_h(h2f(sxn[k]) / s);
+    int q = (int)rintf(t);
+    q = max(-128, min(127, q));
+    qrow[qperm_index(k)] = (int8_t)q;
+    qs += q;
+  }
+  qs = block_isum<kPrepThreads / 32>(qs, ired);
+  if (threadIdx.x == 0) {
+    xs_out[b] = s16;
+    qsum_out[b] = qs;
+  }
+  // LoRA down-projection: warp w handles ranks 2w and 2w+1.
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const int rk = wid * 2 + rr;
+    const float bs = h2f(lBs[rk]);
+    const int8_t* brow = lB + (size_t)rk * K;
+    float acc = 0.f;
+    for (int k = lane; k < K; k += 32) acc = fmaf(h2f(sxn[k]), round_h((float)brow[k] * bs), acc);
+    acc = warp_sum(acc);
+    if (lane == 0) t_out[b * DFSSM_RANK + rk] = f2h(acc);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// proj_gemv: packed 1-bit scaffold projection.
+// Each half-warp owns one output row at a time; lane l16 streams 128-bit chunks
+// c = l16, l16+16, ... of the row, expands the 128 sign bits into 32 0/1-byte masks
+// ((word >> i) & 0x01010101) and dot-products them with the permuted int8 activations
+// (dp4a).  sum_k s_k q_k = 2 * sum_{bit=1} q_k - sum_k q_k with s = +-1, so the int32
+// result equals torch._int_mm on the unpacked +-1 weights bit for bit
+// (df_ssm_inference.py:157).  The 16 per-batch partial sums of a half-warp are combined
+// by a reduce-scatter so that lane l16 ends up with batch row l16 and runs its epilogue:
+//   base = fp16(fp16(fp16(acc) * xs) * w_scale)                df_ssm_inference.py:158
+//   v    = fp16(base + sum_r t_r * fp16(lA[n][r] * lAs[n]))    df_ssm_inference.py:173,204
+// MODE 0 (in_proj): rows in [d_inner, d_inner + d_xbc) also run the conv1d shift
+// register + SiLU (df_ssm_kernels.cu:27-47) with fp32 state [B][3][d_xbc].
+// MODE 1 (out_proj): x = fp16(x + v)                           df_ssm_inference.py:207
+// MODE 2: raw int32 accumulators (stand-alone scaffold GEMM), `out` is int32 [B][ld_out].
+// ---------------------------------------------------------------------------------------
+template <int MODE>
+__global__ void __launch_bounds__(kGemvThreads)
+proj_gemv_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ qsum,
+                 const __half* __restrict__ xs, const __half* __restrict__ t, int B,
+                 __half* __restrict__ out, int ld_out,
+                 float* __restrict__ conv_state, const __half* __restrict__ conv_w,
+                 const __half* __restrict__ conv_b, int d_inner, int d_xbc) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  int8_t* sq = reinterpret_cast<int8_t*>(smem);  // [kGemvBT][K]
+  const int K = p.K, N = p.N;
+  const int C = K >> 7;  // 128-bit chunks per row
+  const int lane = threadIdx.x & 31, l16 = lane & 15, half = lane >> 4;
+  const int warp_g = blockIdx.x * (kGemvThreads / 32) + (threadIdx.x >> 5);
+  const int warp_stride = gridDim.x * (kGemvThreads / 32);
+
+  for (int bt0 = 0; bt0 < B; bt0 += kGemvBT) {
+    const int nb = min(kGemvBT, B - bt0);
+    __syncthreads();
+    {
+      const uint4* src = reinterpret_cast<const uint4*>(q + (size_t)bt0 * K);
+      uint4* dst = reinterpret_cast<uint4*>(sq);
+      const int n16 = nb * K / 16;
+      for (int i = threadIdx.x; i < n16; i += kGemvThreads) dst[i] = src[i];
+    }
+    __syncthreads();
+    for (int rp = warp_g; rp * 2 < N; rp += warp_stride) {
+      const int row = rp * 2 + half;
+      const bool valid = row < N;
+      int acc[kGemvBT];
+#pragma unroll
+      for (int b = 0; b < kGemvBT; ++b) acc[b] = 0;
+      if (valid) {
+        const uint4* wrow = reinterpret_cast<const uint4*>(p.bits + (size_t)row * (K >> 5));
+        for (int c = l16; c < C; c += 16) {
+          const uint4 wv = ldg_stream(wrow + c);
+          unsigned m[32];
+          const unsigned ws[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) m[j * 8 + i] = (ws[j] >> i) & 0x01010101u;
+#pragma unroll
+          for (int b = 0; b < kGemvBT; ++b) {
+            if (b < nb) {
+              const int4* qv = reinterpret_cast<const int4*>(sq + b * K + c * 128);
+              int a = acc[b];
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                const int4 qq = qv[u];
+                a = dp4a_us(m[4 * u + 0], qq.x, a);
+                a = dp4a_us(m[4 * u + 1], qq.y, a);
+                a = dp4a_us(m[4 * u + 2], qq.z, a);
+                a = dp4a_us(m[4 * u + 3], qq.w, a);
+              }
+              acc[b] = a;
+            }
+          }
+        }
+      }
+      // reduce-scatter across the 16 lanes of each half-warp: lane l16 <- batch row l16
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const bool up = l16 & 8;
+        const int send = up ? acc[j] : acc[j + 8];
+        const int keep = up ? acc[j + 8] : acc[j];
+        acc[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const bool up = l16 & 4;
+        const int send = up ? acc[j] : acc[j + 4];
+        const int keep = up ? acc[j + 4] : acc[j];
+        acc[j] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const bool up = l16 & 2;
+        const int send = up ? acc[j] : acc[j + 2];
+        const int keep = up ? acc[j + 2] : acc[j];
+        acc[j] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+      }
+      {
+        const bool up = l16 & 1;
+        const int send = up ? acc[0] : acc[1];
+        const int keep = up ? acc[1] : acc[0];
+        acc[0] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+      }
+      const int b = bt0 + l16;
+      if (!valid || l16 >= nb) continue;
+      const int dot = 2 * acc[0] - qsum[b];
+      if (MODE == 2) {
+        reinterpret_cast<int*>(out)[(size_t)b * ld_out + row] = dot;
+        continue;
+      }
+      const float base = round_h(round_h(round_h((float)dot) * h2f(xs[b])) * h2f(p.scale[row]));
+      // LoRA up-projection
+      const float as = h2f(p.lAs[row]);
+      const int4 arow = *reinterpret_cast<const int4*>(p.lA + (size_t)row * DFSSM_RANK);
+      const int av[4] = {arow.x, arow.y, arow.z, arow.w};
+      const __half* tb = t + b * DFSSM_RANK;
+      float la = 0.f;
+#pragma unroll
+      for (int r = 0; r < DFSSM_RANK; ++r) {
+        const int a8 = (int)(int8_t)((av[r >> 2] >> (8 * (r & 3))) & 0xff);
+        la = fmaf(h2f(tb[r]), round_h((float)a8 * as), la);
+      }
+      const float v = round_h(base + la);
+      if (MODE == 0) {
+        float res = v;
+        const int ch = row - d_inner;
+        if (ch >= 0 && ch < d_xbc) {
+          float* cs = conv_state + (size_t)b * 3 * d_xbc;
+          const float s0 = cs[ch], s1 = cs[d_xbc + ch], s2 = cs[2 * d_xbc + ch];
+          cs[ch] = s1;
+          cs[d_xbc + ch] = s2;
+          cs[2 * d_xbc + ch] = v;
+          const __half* cw = conv_w + ch * DFSSM_DCONV;
+          const float o = s0 * h2f(cw[0]) + s1 * h2f(cw[1]) + s2 * h2f(cw[2]) + v * h2f(cw[3]) + h2f(conv_b[ch]);
+          const float sig = 1.0f / (1.0f + expf(-o));
+          res = o * sig;
+        }
+        out[(size_t)b * ld_out + row] = f2h(res);
+      } else {
+        __half* xo = out + (size_t)b * ld_out + row;
+        *xo = f2h(h2f(*xo) + v);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// ssm_gate: one CTA per (head, batch row); 64 x 128 fp32 state updated in place.
+//   dt = softplus(dt_raw + dt_bias); Abar = exp(dt * -exp(A_log))   df_ssm_kernels.cu:77-79
+//   h  = Abar * h + (x * dt) * B_n;  y = sum_n C_n h + D x           df_ssm_kernels.cu:80-101
+//   gated = fp16(fp16(y) * fp16(z * fp16(sigmoid(z))))               df_ssm_inference.py:194-195
+// Warp w owns rows p = 8w..8w+7, lane owns n = 4*lane..4*lane+3 (512 B coalesced per row).
+// With zin == nullptr the ungated y is written instead (the reference ssm_step output).
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kSsmThreads)
+ssm_gate_kernel(const __half* __restrict__ xbc, int ld_xbc, const __half* __restrict__ dtr, int ld_dt,
+                const __half* __restrict__ zin, int ld_z, int d_inner, int d_state, int nheads,
+                const float* __restrict__ dt_bias, const float* __restrict__ A_log,
+                const float* __restrict__ Dp, float* __restrict__ hstate, __half* __restrict__ out, int ld_out) {
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const __half* xc = xbc + (size_t)b * ld_xbc;     // conv'd x   [d_inner]
+  const __half* Bc = xc + d_inner;                 // conv'd B   [d_state]
+  const __half* Cc = xc + d_inner + d_state;       // conv'd C   [d_state]
+  float dtv = h2f(dtr[(size_t)b * ld_dt + h]) + dt_bias[h];
+  dtv = log1pf(expf(dtv));
+  const float Abar = expf(dtv * (-expf(A_log[h])));
+  const float Dh = Dp[h];
+
+  const int n0 = lane * 4;
+  float Bn[4], Cn[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    Bn[i] = h2f(Bc[n0 + i]);
+    Cn[i] = h2f(Cc[n0 + i]);
+  }
+  float* hs = hstate + ((size_t)b * nheads + h) * (DFSSM_HEADDIM * DFSSM_DSTATE);
+  float4 hv[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) hv[r] = __ldcs(reinterpret_cast<const float4*>(hs + (wid * 8 + r) * DFSSM_DSTATE + n0));
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const int pp = wid * 8 + r;
+    const float xv = h2f(xc[h * DFSSM_HEADDIM + pp]);
+    const float X = xv * dtv;
+    float4 o;
+    o.x = Abar * hv[r].x + X * Bn[0];
+    o.y = Abar * hv[r].y + X * Bn[1];
+    o.z = Abar * hv[r].z + X * Bn[2];
+    o.w = Abar * hv[r].w + X * Bn[3];
+    __stcs(reinterpret_cast<float4*>(hs + pp * DFSSM_DSTATE + n0), o);
+    float part = Cn[0] * o.x + Cn[1] * o.y + Cn[2] * o.z + Cn[3] * o.w;
+    part = warp_sum(part);
+    if (lane == r) {
+      const float y = part + xv * Dh;
+      __half o16 = f2h(y);
+      if (zin != nullptr) {
+        const float z = h2f(zin[(size_t)b * ld_z + h * DFSSM_HEADDIM + pp]);
+        const float sig = round_h(1.0f / (1.0f + expf(-z)));
+        const float silu = round_h(z * sig);
+        o16 = f2h(h2f(o16) * silu);
+      }
+      out[(size_t)b * ld_out + h * DFSSM_HEADDIM + pp] = o16;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// embed: x[b] = fp16(E_q[tok] * E_s[tok])  (the fp16 row the reference gathers,
+// df_ssm_inference.py:220, for an int8 embedding with per-row scale).
+// ---------------------------------------------------------------------------------------
+__global__ void embed_kernel(const int* __restrict__ tokens, const int8_t* __restrict__ Eq,
+                             const float* __restrict__ Es, int d_model, int vocab, __half* __restrict__ x) {
+  const int b = blockIdx.x;
+  int tok = tokens[b];
+  tok = min(max(tok, 0), vocab - 1);
+  const float s = Es[tok];
+  const int8_t* er = Eq + (size_t)tok * d_model;
+  for (int k = threadIdx.x; k < d_model; k += blockDim.x) x[(size_t)b * d_model + k] = f2h((float)er[k] * s);
+}
+
+// ---------------------------------------------------------------------------------------
+// lm_head: logits[b][v] = E_s[v] * sum_k E_q[v][k] * xn[b][k] (fp32), plus an argmax over
+// the fp16-rounded logits with first-index tie-breaking, as the reference's fp16 GEMM +
+// argmax (df_ssm_inference.py:224,236).  One warp per vocabulary row; per-CTA best keys are
+// merged with atomicMax into best[b] (reset by finalize_kernel).
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kHeadThreads)
+lm_head_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, int vocab, int d,
+               const __half* __restrict__ xn, int B, float* __restrict__ logits,
+               unsigned long long* __restrict__ best) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* sx = reinterpret_cast<float*>(smem);  // [kHeadBT][d]
+  __shared__ unsigned long long sbest[kHeadThreads / 32][kHeadBT];
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int C = d >> 4;  // 16-byte chunks per row
+  for (int bt0 = 0; bt0 < B; bt0 += kHeadBT) {
+    const int nb = min(kHeadBT, B - bt0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nb * d; i += kHeadThreads) sx[i] = h2f(xn[(size_t)bt0 * d + i]);
+    __syncthreads();
+    unsigned long long mybest[kHeadBT];
+#pragma unroll
+    for (int b = 0; b < kHeadBT; ++b) mybest[b] = 0ull;
+    for (int v = blockIdx.x * (kHeadThreads / 32) + wid; v < vocab; v += gridDim.x * (kHeadThreads / 32)) {
+      float acc[kHeadBT];
+#pragma unroll
+      for (int b = 0; b < kHeadBT; ++b) acc[b] = 0.f;
+      const uint4* er = reinterpret_cast<const uint4*>(Eq + (size_t)v * d);
+      for (int c = lane; c < C; c += 32) {
+        const uint4 ev = ldg_stream(er + c);
+        float e[16];
+        const unsigned w4[4] = {ev.x, ev.y, ev.z, ev.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) e[j * 4 + i] = (float)(int8_t)((w4[j] >> (8 * i)) & 0xff);
+#pragma unroll
+        for (int b = 0; b < kHeadBT; ++b) {
+          if (b < nb) {
+            const float4* xv = reinterpret_cast<const float4*>(sx + b * d + c * 16);
+            float a = acc[b];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float4 xx = xv[u];
+              a = fmaf(e[4 * u + 0], xx.x, a);
+              a = fmaf(e[4 * u + 1], xx.y, a);
+              a = fmaf(e[4 * u + 2], xx.z, a);
+              a = fmaf(e[4 * u + 3], xx.w, a);
+            }
+            acc[b] = a;
+          }
+        }
+      }
+      const float sv = Es[v];
+#pragma unroll
+      for (int b = 0; b < kHeadBT; ++b) {
+        if (b < nb) {
+          const float s = warp_sum(acc[b]);
+          const float lg = s * sv;
+          if (lane == 0) {
+            logits[(size_t)(bt0 + b) * vocab + v] = lg;
+            const unsigned long long key = argmax_key(f2h(lg), (uint32_t)v);
+            mybest[b] = key > mybest[b] ? key : mybest[b];
+          }
+        }
+      }
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int b = 0; b < kHeadBT; ++b) sbest[wid][b] = mybest[b];
+    }
+    __syncthreads();
+    if (threadIdx.x < nb) {
+      unsigned long long k = 0ull;
+      for (int w = 0; w < kHeadThreads / 32; ++w) k = sbest[w][threadIdx.x] > k ? sbest[w][threadIdx.x] : k;
+      atomicMax(best + bt0 + threadIdx.x, k);
+    }
+  }
+}
+
+__global__ void finalize_kernel(unsigned long long* __restrict__ best, int B, int* __restrict__ tokens) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < B) {
+    tokens[b] = (int)argmax_key_index(best[b]);
+    best[b] = 0ull;
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// permute_q: row-major int8 activations -> permuted layout + row sums (stand-alone GEMM).
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kPrepThreads)
+permute_q_kernel(const int8_t* __restrict__ q, int K, int8_t* __restrict__ qp, int* __restrict__ qsum) {
+  __shared__ int ired[kPrepThreads / 32];
+  const int b = blockIdx.x;
+  int s = 0;
+  for (int k = threadIdx.x; k < K; k += kPrepThreads) {
+    const int8_t v = q[(size_t)b * K + k];
+    qp[(size_t)b * K + qperm_index(k)] = v;
+    s += v;
+  }
+  s = block_isum<kPrepThreads / 32>(s, ired);
+  if (threadIdx.x == 0) qsum[b] = s;
+}
+
+// ---------------------------------------------------------------------------------------
+// conv_step: stand-alone conv1d shift register + SiLU (df_ssm_kernels.cu:27-47), fp32
+// tap-major state [B][3][d_xbc], xbc fp16 in place.
+// ---------------------------------------------------------------------------------------
+__global__ void conv_step_kernel(float* __restrict__ conv_state, __half* __restrict__ xbc, int ld_xbc,
+                                 const __half* __restrict__ conv_w, const __half* __restrict__ conv_b, int d_xbc) {
+  const int b = blockIdx.y;
+  const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+  if (ch >= d_xbc) return;
+  float* cs = conv_state + (size_t)b * 3 * d_xbc;
+  __half* xr = xbc + (size_t)b * ld_xbc;
+  const float s0 = cs[ch], s1 = cs[d_xbc + ch], s2 = cs[2 * d_xbc + ch];
+  const float v = h2f(xr[ch]);
+  cs[ch] = s1;
+  cs[d_xbc + ch] = s2;
+  cs[2 * d_xbc + ch] = v;
+  const __half* cw = conv_w + ch * DFSSM_DCONV;
+  const float o = s0 * h2f(cw[0]) + s1 * h2f(cw[1]) + s2 * h2f(cw[2]) + v * h2f(cw[3]) + h2f(conv_b[ch]);
+  const float sig = 1.0f / (1.0f + expf(-o));
+  xr[ch] = f2h(o * sig);
+}
+
+}  // namespace dfssm

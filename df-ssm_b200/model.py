@@ -1,0 +1,199 @@
+"""DFSSMModel — drop-in for the reference GPU decode driver.
+
+Mirrors class DFSSMModel of inference/gpu/df_ssm_inference.py:47-243 (constructor
+`DFSSMModel(path, device="cuda", batch_size=1)`, `forward(token_ids) -> logits`,
+`generate(n_tokens=128)`, `reset_state()`, attributes `h_states`, `conv_states`) and
+its CLI (`model --batch_size B --n_tokens N`, :246-252).  All compute runs in
+libdfssm.so (sm_100a kernels behind a C ABI); PyTorch only supplies device memory,
+the current stream and tensor views.
+
+Documented differences from the reference driver:
+  * dims come from the .dfssm header; norms are read as fp32 (the exporter's dtype);
+  * SSM/conv state is fp32 (the reference keeps fp16); `conv_states[l]` is the
+    reference's [B, D_XBC, 3] layout as a strided view of the tap-major buffer;
+  * `forward` returns fp32 logits (scale * int8-dot of the int8 tied embedding) and the
+    greedy argmax is taken on their fp16 rounding, as the reference's fp16 logits;
+  * `generate(n_tokens, prompt=None)` resets the state once and feeds the prompt token by
+    token (token 0 when no prompt is given) instead of advancing the state twice on a
+    warm-up token (df_ssm_inference.py:228-231); the greedy loop stays on the device.
+"""
+from __future__ import annotations
+
+import ctypes
+import time
+from typing import Optional, Sequence, Union
+
+import numpy as np
+
+from . import _lib
+from . import dfssm_format as fmt
+
+
+class _DevArray:
+    """Minimal __cuda_array_interface__ view of engine-owned device memory."""
+
+    def __init__(self, ptr: int, shape, typestr: str, strides=None):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 2, "strides": strides}
+
+
+class DFSSMModel:
+    MODES = {"auto": 0, "graph": 1, "eager": 2, "persistent": 3}
+
+    def __init__(self, path: Union[str, bytes, fmt.Weights], device="cuda", batch_size: int = 1,
+                 max_batch: Optional[int] = None, mode: str = "auto", emb_kind: int = fmt.EMB_INT8):
+        import torch
+        self.torch = torch
+        self.lib = _lib.load()
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("DFSSMModel runs on CUDA devices only (there is no CPU fallback)")
+        dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        self.device = torch.device("cuda", dev_index)
+        torch.cuda.set_device(dev_index)
+        self.batch_size = batch_size
+        self.max_batch = max(batch_size, max_batch or batch_size)
+        h = ctypes.c_void_p()
+        if isinstance(path, fmt.Weights):
+            path = fmt.to_bytes(path, emb_kind)
+        if isinstance(path, (bytes, bytearray, memoryview)):
+            buf = bytes(path)
+            _lib.check(self.lib.dfssm_create_from_memory(buf, len(buf), dev_index, self.max_batch, ctypes.byref(h)))
+        else:
+            _lib.check(self.lib.dfssm_create_from_file(str(path).encode(), dev_index, self.max_batch, ctypes.byref(h)))
+        self._h = h
+        dims = _lib.Dims()
+        _lib.check(self.lib.dfssm_get_dims(self._h, ctypes.byref(dims)))
+        self.dims = dims
+        self.vocab = dims.vocab
+        _lib.check(self.lib.dfssm_set_batch(self._h, batch_size))
+        self.set_mode(mode)
+        self.logits = torch.empty(self.max_batch, dims.vocab, dtype=torch.float32, device=self.device)
+        self._tok_in = torch.zeros(self.max_batch, dtype=torch.int32, device=self.device)
+        self._tok_out = torch.zeros(self.max_batch, dtype=torch.int32, device=self.device)
+        self.h_states, self.conv_states = [], []
+        B = self.max_batch
+        for l in range(dims.n_layer):
+            sp, cp = ctypes.c_void_p(), ctypes.c_void_p()
+            _lib.check(self.lib.dfssm_state_ptrs(self._h, l, ctypes.byref(sp), ctypes.byref(cp)))
+            self.h_states.append(torch.as_tensor(
+                _DevArray(sp.value, (B, dims.nheads, dims.headdim, dims.d_state), "<f4"), device=self.device))
+            conv = torch.as_tensor(_DevArray(cp.value, (B, 3, dims.d_xbc), "<f4"), device=self.device)
+            self.conv_states.append(conv.permute(0, 2, 1))  # [B, D_XBC, 3] view
+
+    # ------------------------------------------------------------------ lifecycle
+    def close(self):
+        if getattr(self, "_h", None):
+            self.lib.dfssm_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _stream(self):
+        return ctypes.c_void_p(self.torch.cuda.current_stream(self.device).cuda_stream)
+
+    def set_mode(self, mode: str):
+        _lib.check(self.lib.dfssm_set_mode(self._h, self.MODES[mode]))
+        m = ctypes.c_int()
+        _lib.check(self.lib.dfssm_get_mode(self._h, ctypes.byref(m)))
+        self.mode = {v: k for k, v in self.MODES.items()}[m.value]
+
+    def set_batch(self, batch_size: int):
+        _lib.check(self.lib.dfssm_set_batch(self._h, batch_size))
+        self.batch_size = batch_size
+
+    def reset_state(self):
+        _lib.check(self.lib.dfssm_reset(self._h, self._stream()))
+
+    # ------------------------------------------------------------------ decode
+    def step(self, token_ids=None, logits: bool = True):
+        """One decode step.  token_ids: [B] ints (host or device) or None to continue from the
+        previous step's greedy tokens.  Returns the greedy next tokens (int32 [B], device)."""
+        torch = self.torch
+        B = self.batch_size
+        tin = None
+        if token_ids is not None:
+            t = torch.as_tensor(token_ids).reshape(-1)
+            if t.numel() != B:
+                raise ValueError(f"expected {B} token ids, got {t.numel()}")
+            self._tok_in[:B].copy_(t.to(torch.int32), non_blocking=True)
+            tin = ctypes.c_void_p(self._tok_in.data_ptr())
+        lg = ctypes.c_void_p(self.logits.data_ptr()) if logits else None
+        _lib.check(self.lib.dfssm_step(self._h, tin, lg, ctypes.c_void_p(self._tok_out.data_ptr()), self._stream()))
+        return self._tok_out[:B]
+
+    def forward(self, token_ids):
+        """Reference-compatible forward: logits [B, vocab] (fp32) for token_ids [B]."""
+        self.step(token_ids, logits=True)
+        return self.logits[:self.batch_size]
+
+    __call__ = forward
+
+    def prefill(self, prompt) -> "object":
+        """Feed prompt tokens [B, T] one at a time; returns the greedy token after the prompt."""
+        prompt = self.torch.as_tensor(prompt)
+        if prompt.dim() == 1:
+            prompt = prompt.reshape(self.batch_size, -1)
+        nxt = None
+        for t in range(prompt.shape[1]):
+            nxt = self.step(prompt[:, t], logits=False)
+        return nxt
+
+    def generate(self, n_tokens: int = 128, prompt=None, verbose: bool = True, logits: bool = False):
+        """Greedy decode: reset, consume `prompt` ([B, T]; token 0 if None), then n_tokens steps.
+        Returns int32 tokens [B, n_tokens] (host numpy)."""
+        torch = self.torch
+        B = self.batch_size
+        self.reset_state()
+        if prompt is None:
+            prompt = torch.zeros(B, 1, dtype=torch.int64)
+        self.prefill(prompt)
+        out = torch.empty(n_tokens, B, dtype=torch.int32, device=self.device)
+        torch.cuda.synchronize(self.device)
+        start = time.perf_counter()
+        stream = self._stream()
+        lg = ctypes.c_void_p(self.logits.data_ptr()) if logits else None
+        for s in range(n_tokens):
+            # tokens_dev = NULL: the step consumes the previous step's greedy token on device
+            _lib.check(self.lib.dfssm_step(self._h, None, lg, ctypes.c_void_p(out[s].data_ptr()), stream))
+        torch.cuda.synchronize(self.device)
+        elapsed = time.perf_counter() - start
+        total = n_tokens * B
+        if verbose:
+            print(f"batch={B}  {n_tokens} steps  {total} total tokens")
+            print(f"  {elapsed * 1000:.1f} ms  ({total / elapsed:.0f} tok/s total, "
+                  f"{elapsed / n_tokens * 1e6:.0f} us/step, {total / elapsed / B:.0f} tok/s/seq)")
+        self.last_elapsed = elapsed
+        return out.t().contiguous().cpu().numpy()
+
+    # ------------------------------------------------------------------ tools
+    def buffer(self, name: str, dtype, shape):
+        p, n = ctypes.c_void_p(), ctypes.c_size_t()
+        _lib.check(self.lib.dfssm_get_buffer(self._h, name.encode(), ctypes.byref(p), ctypes.byref(n)))
+        ts = {self.torch.float16: "<f2", self.torch.float32: "<f4", self.torch.int32: "<i4"}[dtype]
+        return self.torch.as_tensor(_DevArray(p.value, shape, ts), device=self.device)
+
+    def layer_step(self, layer: int):
+        _lib.check(self.lib.dfssm_layer_step(self._h, layer, self._stream()))
+
+    def check_finite(self):
+        _lib.check(self.lib.dfssm_check_finite(self._h, self._stream()))
+
+
+def main(argv: Optional[Sequence[str]] = None):
+    import argparse
+    p = argparse.ArgumentParser(description="DF-SSM B200 greedy decode (drop-in for df_ssm_inference.py)")
+    p.add_argument("model")
+    p.add_argument("--batch_size", type=int, default=1)
+    p.add_argument("--n_tokens", type=int, default=128)
+    p.add_argument("--mode", default="auto", choices=list(DFSSMModel.MODES))
+    a = p.parse_args(argv)
+    DFSSMModel(a.model, batch_size=a.batch_size, mode=a.mode).generate(n_tokens=a.n_tokens)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,140 @@
+/*
+ * dfssm.h — C ABI of the B200 (sm_100a) DF-SSM per-token decode engine (libdfssm.so).
+ *
+ * Plain C: pointers, sizes and int status codes only.  Streams are passed as `void*`
+ * holding a cudaStream_t (NULL = the legacy default stream).  Device pointers are
+ * CUDA device addresses on the engine's device.  Every call returns DFSSM_OK (0) or a
+ * dfssm_status code; dfssm_last_error() gives a message for the calling thread.
+ *
+ * Reference interfaces replaced (cs-cmyk/df-ssm):
+ *   engine lifecycle   inference/gpu/df_ssm_inference.py:47-139  DFSSMModel.__init__/_load/_alloc_state/reset_state
+ *   decode step        inference/gpu/df_ssm_inference.py:160-224  _run_layers + graph replay + LM head (forward)
+ *   conv step          inference/gpu/df_ssm_kernels.cu:109-125     conv_step (pybind)
+ *   SSM step           inference/gpu/df_ssm_kernels.cu:127-151     ssm_step (pybind)
+ *   scaffold matmul    inference/gpu/df_ssm_inference.py:154-158  _scaffold_matmul (torch._int_mm)
+ *   LM head + argmax   inference/gpu/df_ssm_inference.py:224,236  norm_out @ embedding.T, argmax
+ */
+#ifndef DFSSM_H
+#define DFSSM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum dfssm_status {
+  DFSSM_OK = 0,
+  DFSSM_ERR_ARG = 1,         /* bad argument (null pointer, size out of range, ...) */
+  DFSSM_ERR_FORMAT = 2,      /* malformed or truncated .dfssm image */
+  DFSSM_ERR_UNSUPPORTED = 3, /* dims this build has no kernel for */
+  DFSSM_ERR_CUDA = 4,        /* a CUDA runtime call failed (message has the cudaError_t) */
+  DFSSM_ERR_OOM = 5,         /* device allocation failed */
+  DFSSM_ERR_STATE = 6,       /* call not valid in the engine's current state */
+  DFSSM_ERR_NUMERIC = 7      /* non-finite logits detected (dfssm_check_finite) */
+} dfssm_status;
+
+/* Model dimensions, all read from the .dfssm header (export_dfssm.py:106-119). */
+typedef struct dfssm_dims {
+  int32_t n_layer, d_model, d_inner, d_state, nheads, headdim, ngroups, vocab;
+  int32_t d_xbc; /* d_inner + 2 * ngroups * d_state */
+  int32_t n_in;  /* in_proj rows: 2 * d_inner + 2 * ngroups * d_state + nheads */
+} dfssm_dims;
+
+typedef struct dfssm_engine dfssm_engine;
+
+/* Library version string. */
+const char* dfssm_version(void);
+/* Message of the last failed call on this thread ("" if none). */
+const char* dfssm_last_error(void);
+
+/* Create an engine from a .dfssm image in host memory (exporter byte map,
+ * export_dfssm.py:104-193; fp16 or int8 tied embedding).  Uploads all weights to
+ * `device` and allocates fp32 state for `max_batch` sequences.
+ * Replaces DFSSMModel.__init__ / _load / _alloc_state (df_ssm_inference.py:48-135). */
+int dfssm_create_from_memory(const void* image, size_t image_bytes, int device, int max_batch,
+                             dfssm_engine** out);
+/* Same, reading the image from a file path. */
+int dfssm_create_from_file(const char* path, int device, int max_batch, dfssm_engine** out);
+void dfssm_destroy(dfssm_engine* e);
+
+int dfssm_get_dims(const dfssm_engine* e, dfssm_dims* out);
+/* Number of sequences decoded by dfssm_step (1..max_batch).  Drops the captured graph. */
+int dfssm_set_batch(dfssm_engine* e, int batch);
+/* Step execution mode: 0 = automatic, 1 = per-op kernels replayed from a CUDA graph,
+ * 2 = per-op kernels launched eagerly, 3 = persistent whole-step kernel (batch <= 8). */
+int dfssm_set_mode(dfssm_engine* e, int mode);
+int dfssm_get_mode(const dfssm_engine* e, int* mode);
+
+/* Zero all SSM and conv state (DFSSMModel.reset_state, df_ssm_inference.py:137-139). */
+int dfssm_reset(dfssm_engine* e, void* stream);
+
+/* One decode step for the current batch: embeds tokens_dev[b] (int32 [batch], or the
+ * engine's own next-token buffer when NULL, i.e. greedy continuation), runs all layers,
+ * the final norm, the LM head and the greedy argmax.  Optional outputs: logits_dev
+ * (fp32 [batch][vocab]; fp32 scale*int8-dot logits) and next_tokens_dev (int32 [batch]).
+ * Stream-ordered; no host synchronisation and no allocation.
+ * Replaces DFSSMModel.forward + argmax (df_ssm_inference.py:219-224,236). */
+int dfssm_step(dfssm_engine* e, const int32_t* tokens_dev, float* logits_dev,
+               int32_t* next_tokens_dev, void* stream);
+/* Same with host buffers: copies tokens in and next tokens / logits out (pinned or
+ * pageable host memory) around the step, and synchronises the stream. */
+int dfssm_step_host(dfssm_engine* e, const int32_t* tokens_host, float* logits_host,
+                    int32_t* next_tokens_host, void* stream);
+/* Returns DFSSM_ERR_NUMERIC when any logit of the last step is NaN/inf (synchronises). */
+int dfssm_check_finite(dfssm_engine* e, void* stream);
+
+/* Device pointers to layer `layer`'s state: ssm fp32 [max_batch][nheads][headdim][d_state]
+ * and conv fp32 [max_batch][3][d_xbc] (tap-major: tap 0 is the oldest input).
+ * The reference keeps these as per-layer lists h_states / conv_states
+ * (df_ssm_inference.py:112-121, fp16, conv layout [B][D_XBC][3]). */
+int dfssm_state_ptrs(dfssm_engine* e, int layer, float** ssm, float** conv);
+
+/* Named internal device buffers for tests and tools: "x" (fp16 [B][d_model] residual),
+ * "proj" (fp16 [B][n_in]: z | conv'd xBC | raw dt), "gated" (fp16 [B][d_inner]),
+ * "logits" (fp32 [B][vocab]), "tokens" (int32 [B]). */
+int dfssm_get_buffer(dfssm_engine* e, const char* name, void** ptr, size_t* bytes);
+/* Run layer `layer` alone on the engine's "x" buffer (eager kernels). */
+int dfssm_layer_step(dfssm_engine* e, int layer, void* stream);
+
+/* ---- stand-alone ops (reference operator replacements) ---- */
+
+/* Scratch bytes dfssm_scaffold_gemm needs for M activation rows of length K. */
+size_t dfssm_scaffold_gemm_workspace(int M, int K);
+/* acc[m][n] = sum_k q[m][k] * s[n][k], s = +-1 from packed sign bits [N][K/32]
+ * (bit b of word j <-> column 32j+b, 1 -> +1), q int8 row-major [M][K], acc int32 [M][N].
+ * Bit-exact with torch._int_mm(q, unpack(W).T) (df_ssm_inference.py:23-29,157).
+ * K % 128 == 0.  `workspace` is device memory of dfssm_scaffold_gemm_workspace(M, K) bytes. */
+int dfssm_scaffold_gemm(const uint32_t* packed, const int8_t* q, int M, int N, int K,
+                        int32_t* acc, void* workspace, void* stream);
+
+/* Conv1d shift-register step (df_ssm_kernels.cu:27-47, conv_step): for each channel,
+ * out = s0*w0 + s1*w1 + s2*w2 + x*w3 + b, state <- (s1, s2, x), xbc <- fp16(SiLU(out)).
+ * conv_state fp32 [B][3][d_xbc] (tap-major), xbc fp16 [B][ld_xbc] in place,
+ * conv_w fp16 [d_xbc][4], conv_b fp16 [d_xbc]. */
+int dfssm_conv_step(float* conv_state, void* xbc_f16, int ld_xbc, const void* conv_w_f16,
+                    const void* conv_b_f16, int batch, int d_xbc, void* stream);
+
+/* Mamba-2 state update (df_ssm_kernels.cu:53-103, ssm_step), fp32 state:
+ * xbc fp16 [B][ld_xbc] holds conv'd x [d_inner] | B [d_state] | C [d_state];
+ * dt fp16 [B][ld_dt] raw (before softplus); h fp32 [B][nheads][64][128] in place;
+ * y fp16 [B][ld_y] = C.h + D*x.  headdim must be 64 and d_state 128. */
+int dfssm_ssm_step(const void* xbc_f16, int ld_xbc, const void* dt_f16, int ld_dt,
+                   const float* dt_bias, const float* A_log, const float* D, float* h_state,
+                   void* y_f16, int ld_y, int batch, int nheads, int headdim, int d_state,
+                   void* stream);
+
+/* Scratch bytes dfssm_lm_head_argmax needs for `batch` rows. */
+size_t dfssm_lm_head_workspace(int batch);
+/* logits[b][v] = E_s[v] * sum_k E_q[v][k] * x[b][k] (fp32) and next[b] = argmax_v of the
+ * fp16-rounded logits, first index on ties (df_ssm_inference.py:224,236 with an int8
+ * embedding E_q int8 [vocab][d] and scale E_s fp32 [vocab]; x fp16 [batch][d]).
+ * logits may be NULL.  d % 16 == 0. */
+int dfssm_lm_head_argmax(const int8_t* E_q, const float* E_s, int vocab, int d, const void* x_f16,
+                         int batch, float* logits, int32_t* next, void* workspace, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DFSSM_H */

@@ -1,0 +1,155 @@
+"""GPU parity of the whole decode engine (C ABI + DFSSMModel) against the CPU oracle and the
+reference golden vectors.  Tolerances as in test_oracle_golden.py (max-abs 2e-2 / rel 1e-2 of
+the logit scale per step, identical greedy tokens, state rel 2e-3)."""
+import os
+
+import numpy as np
+import pytest
+
+import dfssm_oracle as O
+from helpers import model, oracle_layer_parts, weights
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _close(got, ref, frac_exact=0.9, rel=1e-2):
+    got = np.asarray(got, np.float32)
+    ref = np.asarray(ref, np.float32)
+    scale = float(np.abs(ref).max()) + 1e-6
+    assert np.abs(got - ref).max() <= rel * scale, (np.abs(got - ref).max(), scale)
+    assert (got == ref).mean() >= frac_exact, (got == ref).mean()
+
+
+@pytest.mark.parametrize("B", [1, 3, 17])
+def test_single_layer_matches_oracle(B):
+    w = weights("tiny", 1, seed=2)
+    d = w.dims
+    m = model(w, B)
+    m.reset_state()
+    rng = np.random.default_rng(B)
+    # non-zero incoming state so that every term of the update is exercised
+    h0 = (rng.standard_normal((B, d.nheads, 64, 128)) * 0.1).astype(np.float32)
+    c0 = rng.standard_normal((B, d.d_xbc, 3)).astype(np.float16).astype(np.float32)
+    m.h_states[0][:B].copy_(torch.from_numpy(h0))
+    m.conv_states[0][:B].copy_(torch.from_numpy(c0))
+    x = w.embedding_f16()[rng.integers(0, d.vocab, B)]
+    xb = m.buffer("x", torch.float16, (m.max_batch, d.d_model))
+    xb[:B].copy_(torch.from_numpy(x))
+    m.layer_step(0)
+    torch.cuda.synchronize()
+    hs, cs = h0.copy(), c0.copy()
+    ref = oracle_layer_parts(w, 0, x, cs, hs)
+    proj = m.buffer("proj", torch.float16, (m.max_batch, d.n_in))[:B].cpu().numpy()
+    _close(proj[:, :d.d_inner], ref["z"])
+    _close(proj[:, d.d_inner:d.d_inner + d.d_xbc], ref["xbc"])
+    _close(proj[:, d.d_inner + d.d_xbc:], ref["dt"])
+    _close(m.buffer("gated", torch.float16, (m.max_batch, d.d_inner))[:B].cpu().numpy(), ref["gated"], 0.85)
+    _close(xb[:B].cpu().numpy(), ref["x"], 0.85)
+    np.testing.assert_allclose(m.h_states[0][:B].cpu().numpy(), hs, rtol=2e-3, atol=2e-4)
+    np.testing.assert_allclose(m.conv_states[0][:B].cpu().numpy(), cs, rtol=1e-2, atol=1e-2)
+
+
+def _run_engine(m, prompts, steps, teacher=None):
+    B = prompts.shape[0]
+    m.reset_state()
+    tok = None
+    for t in range(prompts.shape[1]):
+        tok = m.step(torch.from_numpy(prompts[:, t]), logits=False)
+    toks, logs = [], []
+    for s in range(steps):
+        toks.append(tok.cpu().numpy().copy())
+        inp = tok if teacher is None else torch.from_numpy(teacher[s])
+        tok = m.step(inp, logits=True)
+        logs.append(m.logits[:B].cpu().numpy().copy())
+    return np.stack(toks), np.stack(logs)
+
+
+def _check_logits(got, ref):
+    for s in range(got.shape[0]):
+        scale = np.abs(ref[s]).max(axis=-1, keepdims=True)
+        assert np.all(np.abs(got[s] - ref[s]) <= 2e-2 + 1e-2 * scale), (s, np.abs(got[s] - ref[s]).max())
+
+
+@pytest.mark.parametrize("B", [1, 3])
+def test_tiny_model_matches_oracle(B):
+    w = weights("tiny", 2, seed=0)
+    prompts = np.random.default_rng(9).integers(0, w.dims.vocab, (B, 4))
+    orc = O.OracleModel(w, B, state_dtype="f32", emb="int8")
+    otoks, ologs = orc.generate(prompts, 16)
+    m = model(w, B)
+    toks, logs = _run_engine(m, prompts, 16, teacher=otoks)
+    _check_logits(logs, np.stack([l.astype(np.float32) for l in ologs]))
+    # free-running greedy decode must give the oracle's tokens
+    ftoks, _ = _run_engine(m, prompts, 16)
+    np.testing.assert_array_equal(ftoks, otoks)
+    for l in range(2):
+        h = m.h_states[l][:B].cpu().numpy()
+        assert np.abs(h - orc.h[l]).max() / np.abs(orc.h[l]).max() <= 2e-3
+
+
+@pytest.mark.parametrize("variant", ["f32state", "f16state"])
+def test_cfg0_matches_reference_golden(variant):
+    """Config 0 (2-layer 1.3B width, batch 1) against the reference driver's own outputs."""
+    g = np.load(os.path.join(GOLDEN, "golden_cfg0.npz"))
+    w = weights("1.3b", 2, seed=0)
+    m = model(w, 1)
+    gt = g[f"{variant}_tokens"]
+    toks, logs = _run_engine(m, g["prompts"], gt.shape[0], teacher=gt)
+    idx = g[f"{variant}_top_idx"]
+    ref = g[f"{variant}_top_val"].astype(np.float32)
+    mine = np.take_along_axis(logs, idx, -1)
+    _check_logits(mine, ref)
+    np.testing.assert_array_equal(toks, gt)
+    if variant == "f32state":
+        for l in range(2):
+            h = m.h_states[l][:1, :2].cpu().numpy()
+            rh = g[f"f32state_h{l}"]
+            assert np.abs(h - rh).max() / np.abs(rh).max() <= 5e-3
+
+
+def test_graph_and_eager_are_bitwise_equal():
+    w = weights("tiny", 2, seed=4)
+    prompts = np.random.default_rng(1).integers(0, w.dims.vocab, (2, 3))
+    res = []
+    for mode in ("graph", "eager"):
+        m = model(w, 2, mode=mode)
+        res.append(_run_engine(m, prompts, 6))
+    np.testing.assert_array_equal(res[0][0], res[1][0])
+    np.testing.assert_array_equal(res[0][1], res[1][1])
+
+
+def test_batch_rows_are_independent():
+    w = weights("tiny", 2, seed=5)
+    prompts = np.random.default_rng(2).integers(0, w.dims.vocab, (3, 4))
+    m = model(w, 3)
+    toks3, logs3 = _run_engine(m, prompts, 5)
+    m1 = model(w, 1)
+    for b in range(3):
+        toks1, logs1 = _run_engine(m1, prompts[b:b + 1], 5)
+        np.testing.assert_array_equal(toks1[:, 0], toks3[:, b])
+        np.testing.assert_array_equal(logs1[:, 0], logs3[:, b])
+
+
+def test_generate_is_repeatable_and_finite():
+    w = weights("tiny", 2, seed=6)
+    m = model(w, 2)
+    p = np.random.default_rng(3).integers(0, w.dims.vocab, (2, 5))
+    a = m.generate(12, prompt=p, verbose=False)
+    b = m.generate(12, prompt=p, verbose=False)
+    np.testing.assert_array_equal(a, b)
+    m.check_finite()
+    assert a.shape == (2, 12)
+
+
+def test_cfg1_48_layers_matches_oracle():
+    """Config 1 shape (48 layers, 1.3B), batch 1: a short teacher-forced run against the oracle."""
+    w = weights("1.3b", 48, seed=0)
+    prompts = np.random.default_rng(0).integers(0, w.dims.vocab, (1, 3))
+    orc = O.OracleModel(w, 1, state_dtype="f32", emb="int8", cache_signs=False)
+    otoks, ologs = orc.generate(prompts, 3)
+    m = model(w, 1)
+    toks, logs = _run_engine(m, prompts, 3, teacher=otoks)
+    _check_logits(logs, np.stack([l.astype(np.float32) for l in ologs]))
+    np.testing.assert_array_equal(toks, otoks)
