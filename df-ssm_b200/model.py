@@ -126,6 +126,16 @@ class DFSSMModel:
         _lib.check(self.lib.dfssm_step(self._h, tin, lg, ctypes.c_void_p(self._tok_out.data_ptr()), self._stream()))
         return self._tok_out[:B]
 
+    def step_host(self, tokens_host, next_host, logits_host=None):
+        """One step through host buffers (numpy int32 [B], ideally pinned): copies the tokens in,
+        runs the step, copies the next greedy tokens (and optionally fp32 logits) out and
+        synchronises the stream (dfssm_step_host)."""
+        _lib.check(self.lib.dfssm_step_host(
+            self._h, ctypes.c_void_p(tokens_host.ctypes.data) if tokens_host is not None else None,
+            ctypes.c_void_p(logits_host.ctypes.data) if logits_host is not None else None,
+            ctypes.c_void_p(next_host.ctypes.data), self._stream()))
+        return next_host
+
     def forward(self, token_ids):
         """Reference-compatible forward: logits [B, vocab] (fp32) for token_ids [B]."""
         self.step(token_ids, logits=True)

@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 
 import dfssm_oracle as O
-from helpers import model, oracle_layer_parts, weights
+from helpers import f16_ulp, model, oracle_layer_parts, weights
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -143,13 +143,34 @@ def test_generate_is_repeatable_and_finite():
     assert a.shape == (2, 12)
 
 
-def test_cfg1_48_layers_matches_oracle():
-    """Config 1 shape (48 layers, 1.3B), batch 1: a short teacher-forced run against the oracle."""
+def test_cfg1_48_layers_layerwise_match_oracle():
+    """Config 1 shape (48 layers, 1.3B), batch 1, layer by layer (teacher-forced per layer).
+
+    The synthetic 48-layer model is chaotic under the reference's fp16/int8 numerics: one
+    fp16 ulp in one input element changes the residual stream by ~4% after a few layers
+    (tests/test_sensitivity.py), so end-to-end logits of two correct implementations that
+    differ only in fp32 summation order cannot agree at depth 48.  Every layer is therefore
+    checked on the engine's own input for that layer and the engine's incoming state, over
+    two consecutive tokens."""
     w = weights("1.3b", 48, seed=0)
-    prompts = np.random.default_rng(0).integers(0, w.dims.vocab, (1, 3))
-    orc = O.OracleModel(w, 1, state_dtype="f32", emb="int8", cache_signs=False)
-    otoks, ologs = orc.generate(prompts, 3)
+    d = w.dims
     m = model(w, 1)
-    toks, logs = _run_engine(m, prompts, 3, teacher=otoks)
-    _check_logits(logs, np.stack([l.astype(np.float32) for l in ologs]))
-    np.testing.assert_array_equal(toks, otoks)
+    m.reset_state()
+    xb = m.buffer("x", torch.float16, (1, d.d_model))
+    E16 = w.embedding_f16()
+    exact = []
+    for tok in (11, 4242):
+        xb.copy_(torch.from_numpy(E16[[tok]]))
+        for l in range(d.n_layer):
+            x_in = xb.cpu().numpy()
+            hs = m.h_states[l][:1].cpu().numpy().copy()
+            cs = m.conv_states[l][:1].cpu().numpy().copy()
+            m.layer_step(l)
+            torch.cuda.synchronize()
+            ref = oracle_layer_parts(w, l, x_in, cs, hs)
+            got, want = xb.cpu().numpy().astype(np.float32), ref["x"].astype(np.float32)
+            # an int8 quantisation flip moves a whole out_proj row by ~1 fp16 ulp of x
+            assert np.abs(got - want).max() <= 2 * f16_ulp(np.abs(want).max()), (tok, l)
+            exact.append((got == want).mean())
+            np.testing.assert_allclose(m.h_states[l][:1].cpu().numpy(), hs, rtol=2e-3, atol=2e-3 * np.abs(hs).max())
+    assert np.mean(exact) >= 0.8, np.mean(exact)
