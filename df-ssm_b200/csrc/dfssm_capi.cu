@@ -474,6 +474,7 @@ void dfssm_destroy(dfssm_engine* e) {
   if (e->ev_in) cudaEventDestroy(e->ev_in);
   if (e->ev_out) cudaEventDestroy(e->ev_out);
   if (e->s) cudaStreamDestroy(e->s);
+  persistent_destroy(e);
   if (e->arena) cudaFree(e->arena);
   if (e->work) cudaFree(e->work);
   delete e;
@@ -515,6 +516,7 @@ int dfssm_reset(dfssm_engine* e, void* stream) {
   CU(cudaMemsetAsync(e->ssm, 0, e->ssm_layer * e->d.n_layer * 4, us));
   CU(cudaMemsetAsync(e->conv, 0, e->conv_layer * e->d.n_layer * 4, us));
   CU(cudaMemsetAsync(e->best, 0, (size_t)e->max_batch * 8, us));
+  CU(cudaMemsetAsync(e->sync, 0, 16, us));
   return DFSSM_OK;
 }
 
@@ -533,6 +535,8 @@ int dfssm_step(dfssm_engine* e, const int32_t* tokens_dev, float* logits_dev, in
   int rc;
   if (mode == 2) {
     if ((rc = enqueue_step(e, 1, e->s))) return rc;
+  } else if (mode == 3) {
+    if ((rc = launch_persistent_step(e, e->s))) return rc;
   } else {
     if ((rc = ensure_graph(e, mode))) return rc;
     CU(cudaGraphLaunch(e->gexec, e->s));
@@ -568,6 +572,10 @@ int dfssm_check_finite(dfssm_engine* e, void* stream) {
   std::vector<float> h((size_t)e->batch * e->d.vocab);
   CU(cudaMemcpyAsync(h.data(), e->logits, h.size() * 4, cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream)));
   CU(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  unsigned sync_err = 0;
+  CU(cudaMemcpy(&sync_err, e->sync + 3, 4, cudaMemcpyDeviceToHost));
+  if (sync_err)
+    return dfssm_fail(DFSSM_ERR_STATE, "persistent step kernel recorded a timed-out wait (code %u)", sync_err);
   for (size_t i = 0; i < h.size(); ++i)
     if (!std::isfinite(h[i])) return dfssm_fail(DFSSM_ERR_NUMERIC, "non-finite logit at flat index %zu", i);
   return DFSSM_OK;
@@ -598,6 +606,8 @@ int dfssm_layer_step(dfssm_engine* e, int layer, void* stream) {
   if (!e) return dfssm_fail(DFSSM_ERR_ARG, "NULL engine");
   if (layer < 0 || layer >= e->d.n_layer) return dfssm_fail(DFSSM_ERR_ARG, "layer %d out of range", layer);
   CU(cudaSetDevice(e->device));
+  if (effective_mode(e) == 3)
+    return launch_persistent_layers(e, layer, layer + 1, 1, 0, static_cast<cudaStream_t>(stream));
   return enqueue_layer(e, layer, static_cast<cudaStream_t>(stream));
 }
 

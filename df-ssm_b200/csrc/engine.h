@@ -40,6 +40,7 @@ struct dfssm_engine {
   cudaGraphExec_t gexec = nullptr;
   int graph_batch = -1, graph_mode = -1;
   int sm_count = 148;
+  void* persist = nullptr;  // persistent-kernel launch state (persistent.cu)
 };
 
 // Sets the thread's last-error message and returns `code`.
@@ -47,5 +48,7 @@ int dfssm_fail(int code, const char* fmt, ...);
 
 // Persistent whole-step kernel (persistent.cu).
 int persistent_init(dfssm_engine* e);
+void persistent_destroy(dfssm_engine* e);
 bool persistent_supported(const dfssm_engine* e);
 int launch_persistent_step(dfssm_engine* e, cudaStream_t s);
+int launch_persistent_layers(dfssm_engine* e, int l0, int l1, int from_x, int do_head, cudaStream_t s);

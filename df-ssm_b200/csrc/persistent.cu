@@ -1,8 +1,976 @@
-// Persistent whole-step decode kernel (small batch): not yet built in this revision.
+// Persistent whole-step decode kernel for small batches (B <= 2): one cooperative launch per
+// greedy decode step runs the embedding gather, every layer, the final norm, the LM head and
+// the argmax.  One CTA per SM, 512 threads.
+//
+// Per layer there are two grid-wide barriers:
+//   alpha: every CTA rebuilds RMSNorm(x) -> int8 q and the in_proj LoRA down-projection t.
+//          "head" CTAs own half a head (32 channels p of head h): their z/x/dt in_proj rows,
+//          conv1d of their x channels, and their 32x128 slice of the fp32 SSM state.
+//          "BC" CTAs own 8-row groups of the B/C in_proj rows and their conv1d channels and
+//          publish conv'd B/C through global memory + a counter; head CTAs wait on that
+//          counter, then run the state update, C.h + D.x and the SiLU(z) gate.
+//   beta:  every CTA owns 8-row groups of out_proj: gate-RMSNorm of the full gated vector,
+//          quantisation, LoRA, the 1-bit GEMV and the residual add into x.
+// Weights and state of upcoming layers stream into a shared-memory ring with cp.async.bulk
+// (TMA bulk copies completing on mbarriers) while earlier layers compute, so the HBM stream
+// is off the barrier-to-barrier critical path.  Every wait is bounded: a timeout sets an error
+// word (reported by dfssm_check_finite) and makes every later wait return at once, so a
+// failed step ends quickly instead of hanging.
+//
+// Arithmetic follows the per-op kernels (kernels.cuh) and the reference rounding points,
+// except the LoRA down-projection, computed as fp16(s_r * sum_k xn_k * q_rk) instead of
+// fp16(sum_k xn_k * fp16(q_rk * s_r)) (difference below the fp16 rounding of t).
+#include <cuda_runtime.h>
+
+#include <vector>
+
 #include "engine.h"
 
-int persistent_init(dfssm_engine*) { return DFSSM_OK; }
-bool persistent_supported(const dfssm_engine*) { return false; }
-int launch_persistent_step(dfssm_engine*, cudaStream_t) {
-  return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "persistent step kernel not built");
+using namespace dfssm;
+
+namespace {
+
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+constexpr unsigned kSpinLimit = 1u << 22;
+
+struct CtaPlan {
+  int role;       // 0 = head item, 1 = B/C rows, 2 = no in_proj rows
+  int h, p0, np;  // head item
+  int bc0, nbc;   // B/C rows [bc0, bc0 + nbc) within [0, 2*d_state)
+  int o0, no;     // out_proj rows
+  int v0, nv;     // LM head rows
+};
+
+struct Layout {  // byte offsets inside one ring stage (identical for every CTA)
+  int in_bits, in_scale, in_lA, in_lAs, conv_w, conv_b, out_bits, out_scale, out_lA, out_lAs, state, cstate;
+  int stage_bytes;
+};
+
+struct PParams {
+  const LayerW* layers;
+  const CtaPlan* plans;
+  Layout lay;
+  int n_layer, d_model, d_inner, d_state, d_xbc, n_in, nheads, vocab;
+  const int8_t* Eq;
+  const float* Es;
+  const float* norm_f;
+  float* ssm;
+  float* conv;
+  long long ssm_layer, conv_layer;  // elements per layer
+  __half* x_g;      // [B][d_model]
+  __half* bc_g;     // [B][2*d_state]
+  __half* gated_g;  // [B][d_inner]
+  float* logits;    // [B][vocab]
+  unsigned long long* best;
+  int* tokens;
+  unsigned* sync;  // [0] barrier count, [1] exit count, [2] B/C count, [3] error
+  int l0, l1;      // layers run by this launch
+  int from_x;      // 1: layer l0 starts from x_g instead of the token embedding
+  int do_head;     // 1: final norm + LM head + argmax after layer l1-1
+  int n_bc;        // number of B/C CTAs
+  int ns;          // ring stages
+  int ring_off;    // byte offset of the ring in dynamic smem
+};
+
+// ------------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Wait (thread 0 spins, the block follows) until *cnt >= target; bounded.  Once any wait has
+// timed out (error word != 0) every later wait returns at once.
+__device__ __forceinline__ void wait_counter(unsigned* cnt, unsigned target, unsigned* err, unsigned code) {
+  if (threadIdx.x == 0) {
+    unsigned it = 0;
+    while (ld_acquire(cnt) < target) {
+      if ((++it & 1023u) == 0 && ld_acquire(err) != 0) break;
+      if (it > kSpinLimit) {
+        atomicOr(err, code);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ void grid_barrier(const PParams& P, unsigned& nbar) {
+  __syncthreads();
+  ++nbar;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    red_release_add(P.sync, 1u);
+  }
+  wait_counter(P.sync, nbar * gridDim.x, P.sync + 3, 1u);
+}
+
+// Wait for the ring slot of `layer` to hold its data (bounded).
+__device__ __forceinline__ void wait_stage(const PParams& P, uint64_t* bars, int layer) {
+  const int slot = (layer - P.l0) % P.ns;
+  const unsigned parity = (unsigned)(((layer - P.l0) / P.ns) & 1);
+  if (threadIdx.x == 0) {
+    unsigned it = 0;
+    while (!mbar_try_wait(bars + slot, parity)) {
+      if ((++it & 1023u) == 0 && ld_acquire(P.sync + 3) != 0) break;
+      if (it > kSpinLimit) {
+        atomicOr(P.sync + 3, 2u);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// Issue the bulk copies that fill the ring slot of `layer` with this CTA's slice of it.
+// Lane i of warp 0 issues copy i of the table below (all 16-byte aligned, sizes multiples of 16).
+template <int B>
+__device__ void issue_stage(const PParams& P, const CtaPlan& pl, int layer, unsigned char* ring, uint64_t* bars) {
+  if (layer >= P.l1 || threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  const int slot = (layer - P.l0) % P.ns;
+  unsigned char* st = ring + (size_t)slot * P.lay.stage_bytes;
+  uint64_t* bar = bars + slot;
+  const LayerW& L = P.layers[layer];
+  const Layout& Y = P.lay;
+  const int RB = P.d_model / 8, RBO = P.d_inner / 8;
+  const void* src = nullptr;
+  int dst = 0;
+  unsigned bytes = 0;
+  unsigned total = 0;
+  for (int i = 0; i < 32; ++i) {
+    const void* s_ = nullptr;
+    int d_ = 0;
+    unsigned n_ = 0;
+    const char* inb = reinterpret_cast<const char*>(L.in.bits);
+    if (pl.role == 0) {
+      const int c0 = pl.h * DFSSM_HEADDIM + pl.p0, np = pl.np;
+      switch (i) {
+        case 0: s_ = inb + (size_t)c0 * RB; d_ = Y.in_bits; n_ = np * RB; break;
+        case 1: s_ = inb + (size_t)(P.d_inner + c0) * RB; d_ = Y.in_bits + np * RB; n_ = np * RB; break;
+        case 2: s_ = inb + (size_t)(P.d_inner + P.d_xbc + pl.h) * RB; d_ = Y.in_bits + 2 * np * RB; n_ = RB; break;
+        case 3: s_ = L.in.scale + c0; d_ = Y.in_scale; n_ = np * 2; break;
+        case 4: s_ = L.in.scale + P.d_inner + c0; d_ = Y.in_scale + np * 2; n_ = np * 2; break;
+        case 5: s_ = L.in.lA + (size_t)c0 * 16; d_ = Y.in_lA; n_ = np * 16; break;
+        case 6: s_ = L.in.lA + (size_t)(P.d_inner + c0) * 16; d_ = Y.in_lA + np * 16; n_ = np * 16; break;
+        case 7: s_ = L.in.lAs + c0; d_ = Y.in_lAs; n_ = np * 2; break;
+        case 8: s_ = L.in.lAs + P.d_inner + c0; d_ = Y.in_lAs + np * 2; n_ = np * 2; break;
+        case 9: s_ = L.conv_w + (size_t)c0 * 4; d_ = Y.conv_w; n_ = np * 8; break;
+        case 10: s_ = L.conv_b + c0; d_ = Y.conv_b; n_ = np * 2; break;
+        default: break;
+      }
+      const int j = i - 15;
+      if (j >= 0 && j < B) {
+        s_ = P.ssm + (long long)layer * P.ssm_layer +
+             ((long long)(j * P.nheads + pl.h) * DFSSM_HEADDIM + pl.p0) * DFSSM_DSTATE;
+        d_ = Y.state + j * np * DFSSM_DSTATE * 4;
+        n_ = np * DFSSM_DSTATE * 4;
+      }
+      const int k = i - 15 - B;
+      if (k >= 0 && k < 3 * B) {
+        s_ = P.conv + (long long)layer * P.conv_layer + (long long)k * P.d_xbc + c0;
+        d_ = Y.cstate + k * np * 4;
+        n_ = np * 4;
+      }
+    } else if (pl.role == 1) {
+      const int r0 = 2 * P.d_inner + pl.bc0, c0 = P.d_inner + pl.bc0, nb = pl.nbc;
+      switch (i) {
+        case 0: s_ = inb + (size_t)r0 * RB; d_ = Y.in_bits; n_ = nb * RB; break;
+        case 3: s_ = L.in.scale + r0; d_ = Y.in_scale; n_ = nb * 2; break;
+        case 5: s_ = L.in.lA + (size_t)r0 * 16; d_ = Y.in_lA; n_ = nb * 16; break;
+        case 7: s_ = L.in.lAs + r0; d_ = Y.in_lAs; n_ = nb * 2; break;
+        case 9: s_ = L.conv_w + (size_t)c0 * 4; d_ = Y.conv_w; n_ = nb * 8; break;
+        case 10: s_ = L.conv_b + c0; d_ = Y.conv_b; n_ = nb * 2; break;
+        default: break;
+      }
+      const int k = i - 15 - B;
+      if (k >= 0 && k < 3 * B) {
+        s_ = P.conv + (long long)layer * P.conv_layer + (long long)k * P.d_xbc + c0;
+        d_ = Y.cstate + k * nb * 4;
+        n_ = nb * 4;
+      }
+    }
+    if (pl.no > 0) {
+      const char* ob = reinterpret_cast<const char*>(L.out.bits);
+      switch (i) {
+        case 11: s_ = ob + (size_t)pl.o0 * RBO; d_ = Y.out_bits; n_ = pl.no * RBO; break;
+        case 12: s_ = L.out.scale + pl.o0; d_ = Y.out_scale; n_ = pl.no * 2; break;
+        case 13: s_ = L.out.lA + (size_t)pl.o0 * 16; d_ = Y.out_lA; n_ = pl.no * 16; break;
+        case 14: s_ = L.out.lAs + pl.o0; d_ = Y.out_lAs; n_ = pl.no * 2; break;
+        default: break;
+      }
+    }
+    total += n_;
+    if (i == lane) {
+      src = s_;
+      dst = d_;
+      bytes = n_;
+    }
+  }
+  if (lane == 0) {
+    fence_proxy_async();
+    mbar_expect_tx(bar, total);
+  }
+  __syncwarp();
+  if (bytes) bulk_g2s(st + dst, src, bytes, bar);
+}
+
+// ------------------------------------------------------------------ block reductions (512 threads)
+template <int N>
+__device__ __forceinline__ void block_sum_n(float (&v)[N], float* red) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = warp_sum(v[i]);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0)
+#pragma unroll
+    for (int i = 0; i < N; ++i) red[w * N + i] = v[i];
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < kWarps; ++j) s += red[j * N + i];
+    v[i] = s;
+  }
+}
+template <int N>
+__device__ __forceinline__ void block_max_n(float (&v)[N], float* red) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = warp_max(v[i]);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0)
+#pragma unroll
+    for (int i = 0; i < N; ++i) red[w * N + i] = v[i];
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    float s = red[i];
+#pragma unroll
+    for (int j = 1; j < kWarps; ++j) s = fmaxf(s, red[j * N + i]);
+    v[i] = s;
+  }
+}
+
+template <int KPT>
+struct RankBytes;  // KPT int8 LoRA-B values of one rank for this thread's columns
+template <> struct RankBytes<1> { using T = uint8_t; };
+template <> struct RankBytes<2> { using T = uint16_t; };
+template <> struct RankBytes<4> { using T = uint32_t; };
+template <> struct RankBytes<8> { using T = unsigned long long; };
+
+template <int KPT>
+__device__ __forceinline__ void load_lora_b(const int8_t* lB, int K, typename RankBytes<KPT>::T (&out)[DFSSM_RANK]) {
+  using T = typename RankBytes<KPT>::T;
+  const int k0 = threadIdx.x * KPT;
+#pragma unroll
+  for (int r = 0; r < DFSSM_RANK; ++r) out[r] = __ldg(reinterpret_cast<const T*>(lB + (size_t)r * K + k0));
+}
+
+template <int KPT>
+__device__ __forceinline__ int byte_of(typename RankBytes<KPT>::T v, int j) {
+  return (int)(int8_t)((unsigned long long)v >> (8 * j));
+}
+
+// RMSNorm + per-row int8 quantisation + LoRA down-projection of this thread's KPT columns of
+// B activation rows.  vals[b][j]: fp16-exact inputs of columns k0 + j.  Writes q (permuted) to
+// sq[b][*] and xs/qsum/t to smem; returns after a __syncthreads.
+template <int B, int KPT>
+__device__ void prep_rows(float (&vals)[B][KPT], const float (&w)[KPT], int K,
+                          const typename RankBytes<KPT>::T (&lb)[DFSSM_RANK], const float* lbs, int8_t* sq, int Kq,
+                          float* s_xs, int* s_qsum, float* s_t, float* red) {
+  const int k0 = threadIdx.x * KPT;
+  float ss[B];
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    float a = 0.f;
+#pragma unroll
+    for (int j = 0; j < KPT; ++j) a = __fadd_rn(a, __fmul_rn(vals[b][j], vals[b][j]));
+    ss[b] = a;
+  }
+  block_sum_n<B>(ss, red);
+  float am[B];
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    const float r = rsqrtf(__fadd_rn(__fmul_rn(ss[b], 1.0f / (float)K), 1e-5f));
+    float a = 0.f;
+#pragma unroll
+    for (int j = 0; j < KPT; ++j) {
+      const float xn = round_h(__fmul_rn(__fmul_rn(vals[b][j], r), w[j]));
+      vals[b][j] = xn;
+      a = fmaxf(a, fabsf(xn));
+    }
+    am[b] = a;
+  }
+  block_max_n<B>(am, red);
+  float all[B * DFSSM_RANK + B];  // LoRA partials t[b][r] = sum_j xn_j * q_rj, then the q sums
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    const float s = round_h(__fmul_rn(fmaxf(am[b], qscale_floor()), 1.0f / 127.0f));
+    int qsum = 0;
+#pragma unroll
+    for (int j = 0; j < KPT; ++j) {
+      int q = (int)rintf(round_h(vals[b][j] / s));
+      q = max(-128, min(127, q));
+      sq[b * Kq + qperm_index(k0 + j)] = (int8_t)q;
+      qsum += q;
+    }
+    all[B * DFSSM_RANK + b] = (float)qsum;
+    if (threadIdx.x == 0) s_xs[b] = s;
+#pragma unroll
+    for (int r = 0; r < DFSSM_RANK; ++r) {
+      float a = 0.f;
+#pragma unroll
+      for (int j = 0; j < KPT; ++j) a = fmaf(vals[b][j], (float)byte_of<KPT>(lb[r], j), a);
+      all[b * DFSSM_RANK + r] = a;
+    }
+  }
+  block_sum_n<B * DFSSM_RANK + B>(all, red);
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < B * DFSSM_RANK; ++i) s_t[i] = round_h(all[i] * lbs[i % DFSSM_RANK]);
+#pragma unroll
+    for (int b = 0; b < B; ++b) s_qsum[b] = (int)all[B * DFSSM_RANK + b];
+  }
+  __syncthreads();
+}
+
+// 1-bit GEMV of one row held in shared memory for B activation rows: returns the int32
+// sum_k s_k q_k for every b in all 16 lanes of the half-warp.
+template <int B>
+__device__ __forceinline__ void row_dot(const unsigned char* bits, int K, const int8_t* sq, int Kq, int l16,
+                                        const int* s_qsum, int (&dot)[B]) {
+  int acc[B];
+#pragma unroll
+  for (int b = 0; b < B; ++b) acc[b] = 0;
+  const int C = K >> 7;
+  for (int c = l16; c < C; c += 16) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(bits + c * 16);
+    const unsigned ws[4] = {wv.x, wv.y, wv.z, wv.w};
+    unsigned m[32];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m[j * 8 + i] = (ws[j] >> i) & 0x01010101u;
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const int4* qv = reinterpret_cast<const int4*>(sq + b * Kq + c * 128);
+      int a = acc[b];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int4 qq = qv[u];
+        a = dp4a_us(m[4 * u + 0], qq.x, a);
+        a = dp4a_us(m[4 * u + 1], qq.y, a);
+        a = dp4a_us(m[4 * u + 2], qq.z, a);
+        a = dp4a_us(m[4 * u + 3], qq.w, a);
+      }
+      acc[b] = a;
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    int a = acc[b];
+    a += __shfl_xor_sync(0xffffffffu, a, 8);
+    a += __shfl_xor_sync(0xffffffffu, a, 4);
+    a += __shfl_xor_sync(0xffffffffu, a, 2);
+    a += __shfl_xor_sync(0xffffffffu, a, 1);
+    dot[b] = 2 * a - s_qsum[b];
+  }
+}
+
+// dequant + LoRA up-projection of one output row (reference rounding points)
+__device__ __forceinline__ float proj_out(int dot, float xs, float wscale, const int8_t* lA, float las,
+                                          const float* t) {
+  const float base = round_h(round_h(round_h((float)dot) * xs) * wscale);
+  float la = 0.f;
+#pragma unroll
+  for (int r = 0; r < DFSSM_RANK; ++r) la = fmaf(t[r], round_h((float)lA[r] * las), la);
+  return round_h(base + la);
+}
+
+__device__ __forceinline__ float conv_silu(float s0, float s1, float s2, float v, const __half* cw, float cb) {
+  const float o = s0 * h2f(cw[0]) + s1 * h2f(cw[1]) + s2 * h2f(cw[2]) + v * h2f(cw[3]) + cb;
+  const float sig = 1.0f / (1.0f + expf(-o));
+  return o * sig;
+}
+
+template <int B, int KI, int KO>
+__global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int d_model = P.d_model, d_inner = P.d_inner;
+  // working smem (carve-up mirrored by build_plan)
+  __half* s_x = reinterpret_cast<__half*>(smem);                   // [B][d_model]
+  int8_t* s_q = reinterpret_cast<int8_t*>(smem + B * d_model * 2);  // [B][d_inner]
+  float* s_misc = reinterpret_cast<float*>(smem + B * d_model * 2 + B * d_inner);
+  float* red = s_misc;                              // [kWarps * (B*16+B)]
+  float* s_t = red + kWarps * (B * 16 + B);         // [B*16]
+  float* s_xs = s_t + B * 16;                       // [B]
+  int* s_qsum = reinterpret_cast<int*>(s_xs + B);   // [B]
+  float* s_lbs = reinterpret_cast<float*>(s_qsum + B);  // [16]
+  float* s_z = s_lbs + 16;                          // [B][64]
+  float* s_xc = s_z + B * 64;                       // [B][64]
+  float* s_dt = s_xc + B * 64;                      // [B]
+  float* s_bc = s_dt + B;                           // [B][2*d_state] (fp32)
+  float* s_hp = s_bc + B * 2 * DFSSM_DSTATE;        // [4] dt_bias, A_log, D, dt-row scale
+  float* s_dtla = s_hp + 4;                         // [17] dt-row LoRA A (16) + its scale
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.ring_off - 8 * 8);
+  unsigned char* ring = smem + P.ring_off;
+
+  const CtaPlan pl = P.plans[blockIdx.x];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, l16 = lane & 15, hw = tid >> 4;
+  unsigned nbar = 0;
+
+  if (tid == 0) {
+    for (int i = 0; i < P.ns; ++i) mbar_init(bars + i, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  for (int l = 0; l < P.ns - 1; ++l) issue_stage<B>(P, pl, P.l0 + l, ring, bars);
+
+  // embedding gather (every CTA needs the full x of the first layer)
+  for (int i = tid; i < B * d_model && !P.from_x; i += kThreads) {
+    const int b = i / d_model, k = i - b * d_model;
+    int tok = P.tokens[b];
+    tok = min(max(tok, 0), P.vocab - 1);
+    s_x[i] = f2h((float)P.Eq[(size_t)tok * d_model + k] * P.Es[tok]);
+  }
+  __syncthreads();
+
+  for (int layer = P.l0; layer < P.l1; ++layer) {
+    const LayerW& L = P.layers[layer];
+    issue_stage<B>(P, pl, layer + P.ns - 1, ring, bars);
+    unsigned char* st = ring + (size_t)((layer - P.l0) % P.ns) * P.lay.stage_bytes;
+    // ---------------- alpha: per-thread weights are loaded before waiting for x
+    float w_in[KI];
+    typename RankBytes<KI>::T lb_in[DFSSM_RANK];
+    {
+      const int k0 = tid * KI;
+#pragma unroll
+      for (int j = 0; j < KI; ++j) w_in[j] = __ldg(L.ln_w + k0 + j);
+      load_lora_b<KI>(L.in.lB, d_model, lb_in);
+      if (tid < 16) s_lbs[tid] = h2f(L.in.lBs[tid]);
+      if (pl.role == 0 && tid == 32) {
+        s_hp[0] = L.dt_bias[pl.h];
+        s_hp[1] = L.A_log[pl.h];
+        s_hp[2] = L.Dp[pl.h];
+        const int dtrow = d_inner + P.d_xbc + pl.h;
+        s_hp[3] = h2f(L.in.scale[dtrow]);
+        for (int r = 0; r < 16; ++r) s_dtla[r] = (float)L.in.lA[(size_t)dtrow * 16 + r];
+        s_dtla[16] = h2f(L.in.lAs[dtrow]);
+      }
+    }
+    if (layer > P.l0) grid_barrier(P, nbar);  // x of the previous layer complete
+    if (layer > P.l0 || P.from_x) {
+      for (int i = tid; i < B * d_model / 8; i += kThreads)
+        reinterpret_cast<uint4*>(s_x)[i] = __ldcg(reinterpret_cast<const uint4*>(P.x_g) + i);
+      __syncthreads();
+    }
+    {
+      float vals[B][KI];
+#pragma unroll
+      for (int b = 0; b < B; ++b)
+#pragma unroll
+        for (int j = 0; j < KI; ++j) vals[b][j] = h2f(s_x[b * d_model + tid * KI + j]);
+      prep_rows<B, KI>(vals, w_in, d_model, lb_in, s_lbs, s_q, d_inner, s_xs, s_qsum, s_t, red);
+    }
+    wait_stage(P, bars, layer);
+    const int RB = d_model / 8;
+    if (pl.role == 0) {
+      const int np = pl.np, nrows = 2 * np + 1;
+      const __half* sc = reinterpret_cast<const __half*>(st + P.lay.in_scale);
+      const int8_t* la = reinterpret_cast<const int8_t*>(st + P.lay.in_lA);
+      const __half* las = reinterpret_cast<const __half*>(st + P.lay.in_lAs);
+      const __half* cw = reinterpret_cast<const __half*>(st + P.lay.conv_w);
+      const __half* cb = reinterpret_cast<const __half*>(st + P.lay.conv_b);
+      const float* cst = reinterpret_cast<const float*>(st + P.lay.cstate);
+      for (int i = hw; i < ((nrows + 1) & ~1); i += 2 * kWarps) {
+        const int row = i < nrows ? i : nrows - 1;
+        int dot[B];
+        row_dot<B>(st + P.lay.in_bits + (size_t)row * RB, d_model, s_q, d_inner, l16, s_qsum, dot);
+        if (i < nrows && l16 < B) {
+          const int b = l16;
+          float v;
+          if (row < 2 * np) {
+            v = proj_out(dot[b], s_xs[b], h2f(sc[row]), la + row * 16, h2f(las[row]), s_t + b * 16);
+          } else {
+            int8_t a2[16];
+            for (int r = 0; r < 16; ++r) a2[r] = (int8_t)s_dtla[r];
+            v = proj_out(dot[b], s_xs[b], s_hp[3], a2, s_dtla[16], s_t + b * 16);
+          }
+          if (row < np) {
+            s_z[b * 64 + row] = v;
+          } else if (row < 2 * np) {
+            const int j = row - np, ch = pl.h * DFSSM_HEADDIM + pl.p0 + j;
+            const float s0 = cst[(b * 3 + 0) * np + j], s1 = cst[(b * 3 + 1) * np + j],
+                        s2 = cst[(b * 3 + 2) * np + j];
+            float* gcs = P.conv + (long long)layer * P.conv_layer + (long long)b * 3 * P.d_xbc + ch;
+            gcs[0] = s1;
+            gcs[P.d_xbc] = s2;
+            gcs[2 * P.d_xbc] = v;
+            s_xc[b * 64 + j] = round_h(conv_silu(s0, s1, s2, v, cw + j * 4, h2f(cb[j])));
+          } else {
+            s_dt[b] = v;
+          }
+        }
+      }
+      __syncthreads();
+      // wait for every B/C CTA of this layer, then fetch conv'd B and C
+      wait_counter(P.sync + 2, (unsigned)(layer - P.l0 + 1) * P.n_bc, P.sync + 3, 4u);
+      for (int i = tid; i < B * 2 * DFSSM_DSTATE; i += kThreads) s_bc[i] = h2f(__ldcg(P.bc_g + i));
+      __syncthreads();
+      // SSM state update + gate; warp w owns rows p = w*RPW.., lane owns n = 4*lane..
+      const int RPW = np / kWarps;
+      const float* sst = reinterpret_cast<const float*>(st + P.lay.state);
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        float dtv = s_dt[b] + s_hp[0];
+        dtv = log1pf(expf(dtv));
+        const float Abar = expf(dtv * (-expf(s_hp[1])));
+        const float Dh = s_hp[2];
+        const float* bb = s_bc + b * 256 + lane * 4;
+        const float4 Bn = make_float4(bb[0], bb[1], bb[2], bb[3]);
+        const float4 Cn = make_float4(bb[128], bb[129], bb[130], bb[131]);
+        for (int rr = 0; rr < RPW; ++rr) {
+          const int p = wid * RPW + rr;
+          const float4 hv = *reinterpret_cast<const float4*>(sst + ((size_t)b * np + p) * DFSSM_DSTATE + lane * 4);
+          const float xv = s_xc[b * 64 + p];
+          const float X = xv * dtv;
+          float4 o;
+          o.x = Abar * hv.x + X * Bn.x;
+          o.y = Abar * hv.y + X * Bn.y;
+          o.z = Abar * hv.z + X * Bn.z;
+          o.w = Abar * hv.w + X * Bn.w;
+          float* gh = P.ssm + (long long)layer * P.ssm_layer +
+                      ((long long)(b * P.nheads + pl.h) * DFSSM_HEADDIM + pl.p0 + p) * DFSSM_DSTATE + lane * 4;
+          __stcs(reinterpret_cast<float4*>(gh), o);
+          float part = Cn.x * o.x + Cn.y * o.y + Cn.z * o.z + Cn.w * o.w;
+          part = warp_sum(part);
+          if (lane == 0) {
+            const float y = part + xv * Dh;
+            const float z = s_z[b * 64 + p];
+            const float sig = round_h(1.0f / (1.0f + expf(-z)));
+            const float silu = round_h(z * sig);
+            P.gated_g[(size_t)b * d_inner + pl.h * DFSSM_HEADDIM + pl.p0 + p] = f2h(round_h(y) * silu);
+          }
+        }
+      }
+    } else if (pl.role == 1) {
+      const int nb = pl.nbc;
+      const __half* sc = reinterpret_cast<const __half*>(st + P.lay.in_scale);
+      const int8_t* la = reinterpret_cast<const int8_t*>(st + P.lay.in_lA);
+      const __half* las = reinterpret_cast<const __half*>(st + P.lay.in_lAs);
+      const __half* cw = reinterpret_cast<const __half*>(st + P.lay.conv_w);
+      const __half* cb = reinterpret_cast<const __half*>(st + P.lay.conv_b);
+      const float* cst = reinterpret_cast<const float*>(st + P.lay.cstate);
+      for (int i = hw; i < ((nb + 1) & ~1); i += 2 * kWarps) {
+        const int row = i < nb ? i : nb - 1;
+        int dot[B];
+        row_dot<B>(st + P.lay.in_bits + (size_t)row * RB, d_model, s_q, d_inner, l16, s_qsum, dot);
+        if (i < nb && l16 < B) {
+          const int b = l16;
+          const float v = proj_out(dot[b], s_xs[b], h2f(sc[row]), la + row * 16, h2f(las[row]), s_t + b * 16);
+          const int ch = d_inner + pl.bc0 + row;
+          const float s0 = cst[(b * 3 + 0) * nb + row], s1 = cst[(b * 3 + 1) * nb + row],
+                      s2 = cst[(b * 3 + 2) * nb + row];
+          float* gcs = P.conv + (long long)layer * P.conv_layer + (long long)b * 3 * P.d_xbc + ch;
+          gcs[0] = s1;
+          gcs[P.d_xbc] = s2;
+          gcs[2 * P.d_xbc] = v;
+          P.bc_g[b * 256 + pl.bc0 + row] = f2h(conv_silu(s0, s1, s2, v, cw + row * 4, h2f(cb[row])));
+        }
+      }
+      __syncthreads();
+      if (tid == 0) {
+        __threadfence();
+        red_release_add(P.sync + 2, 1u);
+      }
+    }
+    // ---------------- beta: out_proj rows
+    float w_out[KO];
+    typename RankBytes<KO>::T lb_out[DFSSM_RANK];
+    {
+      const int k0 = tid * KO;
+#pragma unroll
+      for (int j = 0; j < KO; ++j) w_out[j] = __ldg(L.norm_w + k0 + j);
+      load_lora_b<KO>(L.out.lB, d_inner, lb_out);
+    }
+    grid_barrier(P, nbar);  // gated complete
+    if (tid < 16) s_lbs[tid] = h2f(L.out.lBs[tid]);
+    {
+      float vals[B][KO];
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const __half* g = P.gated_g + (size_t)b * d_inner + tid * KO;
+#pragma unroll
+        for (int j = 0; j < KO; ++j) vals[b][j] = h2f(__ldcg(g + j));
+      }
+      __syncthreads();
+      prep_rows<B, KO>(vals, w_out, d_inner, lb_out, s_lbs, s_q, d_inner, s_xs, s_qsum, s_t, red);
+    }
+    if (pl.no > 0) {
+      const int RBO = d_inner / 8;
+      const __half* sc = reinterpret_cast<const __half*>(st + P.lay.out_scale);
+      const int8_t* la = reinterpret_cast<const int8_t*>(st + P.lay.out_lA);
+      const __half* las = reinterpret_cast<const __half*>(st + P.lay.out_lAs);
+      for (int i = hw; i < ((pl.no + 1) & ~1); i += 2 * kWarps) {
+        const int row = i < pl.no ? i : pl.no - 1;
+        int dot[B];
+        row_dot<B>(st + P.lay.out_bits + (size_t)row * RBO, d_inner, s_q, d_inner, l16, s_qsum, dot);
+        if (i < pl.no && l16 < B) {
+          const int b = l16;
+          const float v = proj_out(dot[b], s_xs[b], h2f(sc[row]), la + row * 16, h2f(las[row]), s_t + b * 16);
+          const int o = pl.o0 + row;
+          P.x_g[(size_t)b * d_model + o] = f2h(h2f(s_x[b * d_model + o]) + v);
+        }
+      }
+    }
+    __syncthreads();
+  }
+
+  // ---------------- final norm + LM head + argmax
+  if (P.do_head) {
+    grid_barrier(P, nbar);
+    for (int i = tid; i < B * d_model / 8; i += kThreads)
+      reinterpret_cast<uint4*>(s_x)[i] = __ldcg(reinterpret_cast<const uint4*>(P.x_g) + i);
+    __syncthreads();
+    float* s_no = reinterpret_cast<float*>(ring);  // [B][d_model] fp32 normalised x (ring is idle now)
+    {
+      float vals[B][KI];
+      float ss[B];
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        float a = 0.f;
+#pragma unroll
+        for (int j = 0; j < KI; ++j) {
+          vals[b][j] = h2f(s_x[b * d_model + tid * KI + j]);
+          a = __fadd_rn(a, __fmul_rn(vals[b][j], vals[b][j]));
+        }
+        ss[b] = a;
+      }
+      block_sum_n<B>(ss, red);
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const float r = rsqrtf(__fadd_rn(__fmul_rn(ss[b], 1.0f / (float)d_model), 1e-5f));
+#pragma unroll
+        for (int j = 0; j < KI; ++j) {
+          const int k = tid * KI + j;
+          s_no[b * d_model + k] = round_h(__fmul_rn(__fmul_rn(vals[b][j], r), P.norm_f[k]));
+        }
+      }
+    }
+    __syncthreads();
+    unsigned long long mybest[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) mybest[b] = 0ull;
+    const int C = d_model >> 4;
+    for (int v = pl.v0 + wid; v < pl.v0 + pl.nv; v += kWarps) {
+      float acc[B];
+#pragma unroll
+      for (int b = 0; b < B; ++b) acc[b] = 0.f;
+      const uint4* er = reinterpret_cast<const uint4*>(P.Eq + (size_t)v * d_model);
+      for (int c = lane; c < C; c += 32) {
+        const uint4 ev = ldg_stream(er + c);
+        const unsigned w4[4] = {ev.x, ev.y, ev.z, ev.w};
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+          const float4* xv = reinterpret_cast<const float4*>(s_no + b * d_model + c * 16);
+          float a = acc[b];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float4 xx = xv[u];
+            a = fmaf((float)(int8_t)(w4[u] & 0xff), xx.x, a);
+            a = fmaf((float)(int8_t)((w4[u] >> 8) & 0xff), xx.y, a);
+            a = fmaf((float)(int8_t)((w4[u] >> 16) & 0xff), xx.z, a);
+            a = fmaf((float)(int8_t)(w4[u] >> 24), xx.w, a);
+          }
+          acc[b] = a;
+        }
+      }
+      const float sv = P.Es[v];
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const float lg = warp_sum(acc[b]) * sv;
+        if (lane == 0) {
+          P.logits[(size_t)b * P.vocab + v] = lg;
+          const unsigned long long key = argmax_key(f2h(lg), (uint32_t)v);
+          mybest[b] = key > mybest[b] ? key : mybest[b];
+        }
+      }
+    }
+    unsigned long long* sb = reinterpret_cast<unsigned long long*>(red);
+    __syncthreads();
+    if (lane == 0)
+#pragma unroll
+      for (int b = 0; b < B; ++b) sb[wid * B + b] = mybest[b];
+    __syncthreads();
+    if (tid < B) {
+      unsigned long long k = 0ull;
+      for (int w = 0; w < kWarps; ++w) k = sb[w * B + tid] > k ? sb[w * B + tid] : k;
+      atomicMax(P.best + tid, k);
+    }
+  }  // do_head
+  __syncthreads();
+  // drain: no bulk copy into this CTA's ring may still be in flight when it exits (only
+  // possible after a timed-out wait); bounded, ignores the error word
+  if (tid == 0) {
+    const int nl = P.l1 - P.l0;
+    for (int s = 0; s < P.ns && s < nl; ++s) {
+      const int last = s + ((nl - 1 - s) / P.ns) * P.ns;
+      unsigned it = 0;
+      while (!mbar_try_wait(bars + s, (unsigned)((last / P.ns) & 1)) && ++it < kSpinLimit) {
+      }
+    }
+  }
+  // exit protocol: the last CTA out publishes the tokens and resets the sync words
+  if (tid == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(P.sync + 1, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence();
+      for (int b = 0; b < B && P.do_head; ++b) {
+        const unsigned long long k = atomicExch(P.best + b, 0ull);
+        P.tokens[b] = (int)argmax_key_index(k);
+      }
+      P.sync[0] = 0;
+      P.sync[2] = 0;
+      __threadfence();
+      P.sync[1] = 0;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+struct PersistentState {
+  int ready = 0;
+  void* fn = nullptr;
+  PParams params{};
+  CtaPlan* d_plans = nullptr;
+  int smem = 0;
+  int grid = 0;
+};
+
+struct PersistentSet {
+  PersistentState st[3];  // indexed by batch size 1, 2
+};
+
+template <int B, int KI, int KO>
+void* kernel_ptr() {
+  return reinterpret_cast<void*>(persistent_step_kernel<B, KI, KO>);
+}
+
+void* pick_kernel(int B, int KI, int KO) {
+#define DFSSM_PK(b, ki, ko) \
+  if (B == b && KI == ki && KO == ko) return kernel_ptr<b, ki, ko>();
+  DFSSM_PK(1, 4, 8)
+  DFSSM_PK(2, 4, 8)
+  DFSSM_PK(1, 1, 2)
+  DFSSM_PK(2, 1, 2)
+#undef DFSSM_PK
+  return nullptr;
+}
+
+PersistentSet* set_of(const dfssm_engine* e) { return static_cast<PersistentSet*>(e->persist); }
+
+// Per-CTA work plans and the ring-stage layout for batch B.  Returns 0 if the dims or the
+// batch are not supported by the persistent kernel.
+int build_plan(const dfssm_engine* e, int B, int grid, std::vector<CtaPlan>& plans, Layout& lay, int& ns,
+               int& smem_total, int& n_bc) {
+  const dfssm_dims& d = e->d;
+  if (d.d_model % 512 || d.d_inner % 512) return 0;
+  const int KI = d.d_model / 512, KO = d.d_inner / 512;
+  if (!pick_kernel(B, KI, KO)) return 0;
+  const int S = 2, np = DFSSM_HEADDIM / S;
+  const int n_items = d.nheads * S;
+  n_bc = grid - n_items;
+  const int bc_groups = 2 * d.d_state / 8;
+  if (n_bc < 1) return 0;
+  if (n_bc > bc_groups) n_bc = bc_groups;
+  plans.assign(grid, CtaPlan{});
+  const int og = d.d_model / 8;  // out rows in 8-row groups
+  int max_no = 0, max_nbc = 0;
+  for (int c = 0; c < grid; ++c) {
+    CtaPlan& p = plans[c];
+    const int g0 = (int)((long long)og * c / grid), g1 = (int)((long long)og * (c + 1) / grid);
+    p.o0 = g0 * 8;
+    p.no = (g1 - g0) * 8;
+    max_no = p.no > max_no ? p.no : max_no;
+    const long long v0 = (long long)d.vocab * c / grid, v1 = (long long)d.vocab * (c + 1) / grid;
+    p.v0 = (int)v0;
+    p.nv = (int)(v1 - v0);
+    if (c < n_items) {
+      p.role = 0;
+      p.h = c / S;
+      p.p0 = (c % S) * np;
+      p.np = np;
+    } else if (c < n_items + n_bc) {
+      const int j = c - n_items;
+      const int b0 = bc_groups * j / n_bc, b1 = bc_groups * (j + 1) / n_bc;
+      p.role = 1;
+      p.bc0 = b0 * 8;
+      p.nbc = (b1 - b0) * 8;
+      max_nbc = p.nbc > max_nbc ? p.nbc : max_nbc;
+    } else {
+      p.role = 2;
+    }
+  }
+  const int RB = d.d_model / 8, RBO = d.d_inner / 8;
+  const int rows_in = (2 * np + 1) > max_nbc ? (2 * np + 1) : max_nbc;
+  const int ch = np > max_nbc ? np : max_nbc;
+  auto a16 = [](int x) { return (x + 15) & ~15; };
+  int off = 0;
+  lay.in_bits = off; off += a16(rows_in * RB);
+  lay.in_scale = off; off += a16(2 * ch * 2);
+  lay.in_lA = off; off += a16(2 * ch * 16);
+  lay.in_lAs = off; off += a16(2 * ch * 2);
+  lay.conv_w = off; off += a16(ch * 8);
+  lay.conv_b = off; off += a16(ch * 2);
+  lay.out_bits = off; off += a16(max_no * RBO);
+  lay.out_scale = off; off += a16(max_no * 2);
+  lay.out_lA = off; off += a16(max_no * 16);
+  lay.out_lAs = off; off += a16(max_no * 2);
+  lay.state = off; off += a16(B * np * DFSSM_DSTATE * 4);
+  lay.cstate = off; off += a16(B * 3 * ch * 4);
+  lay.stage_bytes = (off + 127) & ~127;
+  const int misc_floats = kWarps * (B * 16 + B) + B * 16 + B + B + 16 + B * 64 * 2 + B + B * 256 + 4 + 17;
+  int work = B * d.d_model * 2 + B * d.d_inner + misc_floats * 4;
+  work = (work + 127) & ~127;
+  const int ring_off = work + 128;  // 8 mbarriers live just below the ring
+  int max_smem = 0;
+  cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, e->device);
+  ns = (max_smem - ring_off) / lay.stage_bytes;
+  if (ns > 6) ns = 6;
+  if (ns < 2) return 0;
+  if (ns * lay.stage_bytes < B * d.d_model * 4) return 0;  // the head phase reuses the ring
+  smem_total = ring_off + ns * lay.stage_bytes;
+  return 1;
+}
+
+}  // namespace
+
+void persistent_destroy(dfssm_engine* e) {
+  PersistentSet* ps = set_of(e);
+  if (!ps) return;
+  for (auto& s : ps->st)
+    if (s.d_plans) cudaFree(s.d_plans);
+  delete ps;
+  e->persist = nullptr;
+}
+
+int persistent_init(dfssm_engine* e) {
+  if (!e->persist) e->persist = new PersistentSet();
+  for (int B = 1; B <= 2; ++B) {
+    PersistentState& ps = set_of(e)->st[B];
+    ps.ready = 0;
+    if (B > e->max_batch) continue;
+    std::vector<CtaPlan> plans;
+    Layout lay;
+    int ns = 0, smem = 0, n_bc = 0;
+    const int grid = e->sm_count;
+    if (!build_plan(e, B, grid, plans, lay, ns, smem, n_bc)) continue;
+    const dfssm_dims& d = e->d;
+    void* fn = pick_kernel(B, d.d_model / 512, d.d_inner / 512);
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+      cudaGetLastError();
+      continue;
+    }
+    int nblk = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nblk, fn, kThreads, smem) != cudaSuccess || nblk < 1) {
+      cudaGetLastError();
+      continue;
+    }
+    if (cudaMalloc(&ps.d_plans, sizeof(CtaPlan) * grid) != cudaSuccess) return dfssm_fail(DFSSM_ERR_OOM, "plan alloc");
+    if (cudaMemcpy(ps.d_plans, plans.data(), sizeof(CtaPlan) * grid, cudaMemcpyHostToDevice) != cudaSuccess)
+      return dfssm_fail(DFSSM_ERR_CUDA, "plan upload");
+    PParams& P = ps.params;
+    P.layers = e->d_layers;
+    P.plans = ps.d_plans;
+    P.lay = lay;
+    P.n_layer = d.n_layer;
+    P.d_model = d.d_model;
+    P.d_inner = d.d_inner;
+    P.d_state = d.d_state;
+    P.d_xbc = d.d_xbc;
+    P.n_in = d.n_in;
+    P.nheads = d.nheads;
+    P.vocab = d.vocab;
+    P.Eq = e->Eq;
+    P.Es = e->Es;
+    P.norm_f = e->norm_f;
+    P.ssm = e->ssm;
+    P.conv = e->conv;
+    P.ssm_layer = (long long)e->ssm_layer;
+    P.conv_layer = (long long)e->conv_layer;
+    P.x_g = e->x;
+    P.bc_g = e->proj;  // [B][256] fp16 scratch (the per-op path's proj buffer)
+    P.gated_g = e->gated;
+    P.logits = e->logits;
+    P.best = e->best;
+    P.tokens = e->tokens;
+    P.sync = e->sync;
+    P.l0 = 0;
+    P.l1 = d.n_layer;
+    P.from_x = 0;
+    P.do_head = 1;
+    P.n_bc = n_bc;
+    P.ns = ns;
+    P.ring_off = smem - ns * lay.stage_bytes;
+    ps.fn = fn;
+    ps.smem = smem;
+    ps.grid = grid;
+    ps.ready = 1;
+  }
+  return DFSSM_OK;
+}
+
+bool persistent_supported(const dfssm_engine* e) {
+  return e->persist && e->batch >= 1 && e->batch <= 2 && set_of(e)->st[e->batch].ready;
+}
+
+int launch_persistent_layers(dfssm_engine* e, int l0, int l1, int from_x, int do_head, cudaStream_t s) {
+  if (!persistent_supported(e)) return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "persistent kernel unavailable");
+  if (l0 < 0 || l1 > e->d.n_layer || l0 >= l1) return dfssm_fail(DFSSM_ERR_ARG, "bad layer range [%d, %d)", l0, l1);
+  PersistentState& ps = set_of(e)->st[e->batch];
+  PParams P = ps.params;
+  P.l0 = l0;
+  P.l1 = l1;
+  P.from_x = from_x;
+  P.do_head = do_head;
+  void* args[] = {&P};
+  cudaError_t ce = cudaLaunchCooperativeKernel(ps.fn, dim3(ps.grid), dim3(kThreads), args, (size_t)ps.smem, s);
+  if (ce != cudaSuccess) return dfssm_fail(DFSSM_ERR_CUDA, "cooperative launch failed: %s", cudaGetErrorString(ce));
+  return DFSSM_OK;
+}
+
+int launch_persistent_step(dfssm_engine* e, cudaStream_t s) {
+  return launch_persistent_layers(e, 0, e->d.n_layer, 0, 1, s);
 }

@@ -23,8 +23,9 @@ from .dfssm_format import D_CONV, LORA_RANK, Dims, Layer, Proj, Weights
 SHAPES = {
     "1.3b": dict(d_model=2048, d_inner=4096, d_state=128, nheads=64, headdim=64, ngroups=1, vocab=50280),
     "2.7b": dict(d_model=2560, d_inner=5120, d_state=128, nheads=80, headdim=64, ngroups=1, vocab=50280),
-    # small shape for fast tests (same head geometry as the real ones)
+    # small shapes for fast tests (same head geometry as the real ones)
     "tiny": dict(d_model=256, d_inner=512, d_state=128, nheads=8, headdim=64, ngroups=1, vocab=512),
+    "small": dict(d_model=512, d_inner=1024, d_state=128, nheads=16, headdim=64, ngroups=1, vocab=1000),
 }
 
 

@@ -63,7 +63,7 @@ int dfssm_get_dims(const dfssm_engine* e, dfssm_dims* out);
 /* Number of sequences decoded by dfssm_step (1..max_batch).  Drops the captured graph. */
 int dfssm_set_batch(dfssm_engine* e, int batch);
 /* Step execution mode: 0 = automatic, 1 = per-op kernels replayed from a CUDA graph,
- * 2 = per-op kernels launched eagerly, 3 = persistent whole-step kernel (batch <= 8). */
+ * 2 = per-op kernels launched eagerly, 3 = persistent whole-step kernel (batch <= 2, d_model and d_inner multiples of 512). */
 int dfssm_set_mode(dfssm_engine* e, int mode);
 int dfssm_get_mode(const dfssm_engine* e, int* mode);
 
@@ -95,7 +95,8 @@ int dfssm_state_ptrs(dfssm_engine* e, int layer, float** ssm, float** conv);
  * "proj" (fp16 [B][n_in]: z | conv'd xBC | raw dt), "gated" (fp16 [B][d_inner]),
  * "logits" (fp32 [B][vocab]), "tokens" (int32 [B]). */
 int dfssm_get_buffer(dfssm_engine* e, const char* name, void** ptr, size_t* bytes);
-/* Run layer `layer` alone on the engine's "x" buffer (eager kernels). */
+/* Run layer `layer` alone on the engine's "x" buffer with the kernels of the current mode
+ * (per-op kernels, or the persistent kernel over the single layer when mode 3 is selected). */
 int dfssm_layer_step(dfssm_engine* e, int layer, void* stream);
 
 /* ---- stand-alone ops (reference operator replacements) ---- */

@@ -22,11 +22,12 @@ def _close(got, ref, frac_exact=0.9, rel=1e-2):
     assert (got == ref).mean() >= frac_exact, (got == ref).mean()
 
 
-@pytest.mark.parametrize("B", [1, 3, 17])
-def test_single_layer_matches_oracle(B):
-    w = weights("tiny", 1, seed=2)
+@pytest.mark.parametrize("B,mode,shape", [(1, "graph", "tiny"), (3, "graph", "tiny"), (17, "graph", "tiny"),
+                                          (1, "persistent", "small"), (2, "persistent", "small")])
+def test_single_layer_matches_oracle(B, mode, shape):
+    w = weights(shape, 1, seed=2)
     d = w.dims
-    m = model(w, B)
+    m = model(w, B, mode=mode)
     m.reset_state()
     rng = np.random.default_rng(B)
     # non-zero incoming state so that every term of the update is exercised
@@ -72,13 +73,14 @@ def _check_logits(got, ref):
         assert np.all(np.abs(got[s] - ref[s]) <= 2e-2 + 1e-2 * scale), (s, np.abs(got[s] - ref[s]).max())
 
 
-@pytest.mark.parametrize("B", [1, 3])
-def test_tiny_model_matches_oracle(B):
-    w = weights("tiny", 2, seed=0)
+@pytest.mark.parametrize("B,mode,shape", [(1, "graph", "tiny"), (3, "graph", "tiny"),
+                                          (1, "persistent", "small"), (2, "persistent", "small")])
+def test_tiny_model_matches_oracle(B, mode, shape):
+    w = weights(shape, 2, seed=0)
     prompts = np.random.default_rng(9).integers(0, w.dims.vocab, (B, 4))
     orc = O.OracleModel(w, B, state_dtype="f32", emb="int8")
     otoks, ologs = orc.generate(prompts, 16)
-    m = model(w, B)
+    m = model(w, B, mode=mode)
     toks, logs = _run_engine(m, prompts, 16, teacher=otoks)
     _check_logits(logs, np.stack([l.astype(np.float32) for l in ologs]))
     # free-running greedy decode must give the oracle's tokens
@@ -89,12 +91,13 @@ def test_tiny_model_matches_oracle(B):
         assert np.abs(h - orc.h[l]).max() / np.abs(orc.h[l]).max() <= 2e-3
 
 
+@pytest.mark.parametrize("mode", ["graph", "persistent"])
 @pytest.mark.parametrize("variant", ["f32state", "f16state"])
-def test_cfg0_matches_reference_golden(variant):
+def test_cfg0_matches_reference_golden(variant, mode):
     """Config 0 (2-layer 1.3B width, batch 1) against the reference driver's own outputs."""
     g = np.load(os.path.join(GOLDEN, "golden_cfg0.npz"))
     w = weights("1.3b", 2, seed=0)
-    m = model(w, 1)
+    m = model(w, 1, mode=mode)
     gt = g[f"{variant}_tokens"]
     toks, logs = _run_engine(m, g["prompts"], gt.shape[0], teacher=gt)
     idx = g[f"{variant}_top_idx"]
@@ -143,7 +146,8 @@ def test_generate_is_repeatable_and_finite():
     assert a.shape == (2, 12)
 
 
-def test_cfg1_48_layers_layerwise_match_oracle():
+@pytest.mark.parametrize("mode", ["graph", "persistent"])
+def test_cfg1_48_layers_layerwise_match_oracle(mode):
     """Config 1 shape (48 layers, 1.3B), batch 1, layer by layer (teacher-forced per layer).
 
     The synthetic 48-layer model is chaotic under the reference's fp16/int8 numerics: one
@@ -154,7 +158,7 @@ def test_cfg1_48_layers_layerwise_match_oracle():
     two consecutive tokens."""
     w = weights("1.3b", 48, seed=0)
     d = w.dims
-    m = model(w, 1)
+    m = model(w, 1, mode=mode)
     m.reset_state()
     xb = m.buffer("x", torch.float16, (1, d.d_model))
     E16 = w.embedding_f16()
@@ -174,3 +178,25 @@ def test_cfg1_48_layers_layerwise_match_oracle():
             exact.append((got == want).mean())
             np.testing.assert_allclose(m.h_states[l][:1].cpu().numpy(), hs, rtol=2e-3, atol=2e-3 * np.abs(hs).max())
     assert np.mean(exact) >= 0.8, np.mean(exact)
+
+
+@pytest.mark.parametrize("B", [1, 2])
+def test_persistent_is_deterministic_and_reports_no_timeouts(B):
+    w = weights("1.3b", 4, seed=7)
+    p = np.random.default_rng(5).integers(0, w.dims.vocab, (B, 4))
+    m = model(w, B, mode="persistent")
+    assert m.mode == "persistent"
+    a = m.generate(10, prompt=p, verbose=False, logits=True)
+    la = m.logits[:B].cpu().numpy().copy()
+    b = m.generate(10, prompt=p, verbose=False, logits=True)
+    np.testing.assert_array_equal(a, b)
+    np.testing.assert_array_equal(la, m.logits[:B].cpu().numpy())
+    m.check_finite()  # also fails if any bounded wait in the kernel timed out
+
+
+def test_persistent_matches_graph_tokens_on_1p3b_two_layers():
+    w = weights("1.3b", 2, seed=3)
+    p = np.random.default_rng(8).integers(0, w.dims.vocab, (2, 4))
+    a = model(w, 2, mode="persistent").generate(12, prompt=p, verbose=False)
+    b = model(w, 2, mode="graph").generate(12, prompt=p, verbose=False)
+    np.testing.assert_array_equal(a, b)
