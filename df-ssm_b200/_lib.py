@@ -34,6 +34,8 @@ SIGNATURES = {
     "dfssm_state_ptrs": (c_int, [c_void_p, c_int, POINTER(c_void_p), POINTER(c_void_p)]),
     "dfssm_get_buffer": (c_int, [c_void_p, c_char_p, POINTER(c_void_p), POINTER(c_size_t)]),
     "dfssm_layer_step": (c_int, [c_void_p, c_int, c_void_p]),
+    "dfssm_trace_entries": (c_size_t, [c_void_p]),
+    "dfssm_trace_step": (c_int, [c_void_p, c_void_p, c_void_p]),
     "dfssm_scaffold_gemm_workspace": (c_size_t, [c_int, c_int]),
     "dfssm_scaffold_gemm": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "dfssm_conv_step": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p]),

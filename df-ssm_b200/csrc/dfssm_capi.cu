@@ -611,6 +611,14 @@ int dfssm_layer_step(dfssm_engine* e, int layer, void* stream) {
   return enqueue_layer(e, layer, static_cast<cudaStream_t>(stream));
 }
 
+size_t dfssm_trace_entries(const dfssm_engine* e) { return e ? persistent_trace_entries(e) : 0; }
+
+int dfssm_trace_step(dfssm_engine* e, unsigned long long* trace_dev, void* stream) {
+  if (!e || !trace_dev) return dfssm_fail(DFSSM_ERR_ARG, "NULL argument");
+  CU(cudaSetDevice(e->device));
+  return launch_persistent_traced(e, trace_dev, static_cast<cudaStream_t>(stream));
+}
+
 size_t dfssm_scaffold_gemm_workspace(int M, int K) {
   if (M <= 0 || K <= 0) return 0;
   return align256((size_t)M * K) + align256((size_t)M * 4) + align256((size_t)M * 2) + align256((size_t)M * kRank * 2);

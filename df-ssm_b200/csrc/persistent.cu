@@ -17,9 +17,8 @@
 // word (reported by dfssm_check_finite) and makes every later wait return at once, so a
 // failed step ends quickly instead of hanging.
 //
-// Arithmetic follows the per-op kernels (kernels.cuh) and the reference rounding points,
-// except the LoRA down-projection, computed as fp16(s_r * sum_k xn_k * q_rk) instead of
-// fp16(sum_k xn_k * fp16(q_rk * s_r)) (difference below the fp16 rounding of t).
+// Arithmetic follows the per-op kernels (kernels.cuh) and the reference rounding points;
+// only fp32 summation orders differ.
 #include <cuda_runtime.h>
 
 #include <vector>
@@ -71,7 +70,17 @@ struct PParams {
   int n_bc;        // number of B/C CTAs
   int ns;          // ring stages
   int ring_off;    // byte offset of the ring in dynamic smem
+  unsigned long long* trace;  // optional: per-CTA globaltimer stamps (kTraceStride entries per CTA)
 };
+
+constexpr int kTracePerLayer = 8;
+__device__ __forceinline__ void stamp(const PParams& P, int idx) {
+  if (P.trace && threadIdx.x == 0) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    P.trace[(size_t)blockIdx.x * (4 + kTracePerLayer * P.n_layer) + idx] = t;
+  }
+}
 
 // ------------------------------------------------------------------ PTX helpers
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -159,8 +168,8 @@ __device__ void issue_stage(const PParams& P, const CtaPlan& pl, int layer, unsi
   const int slot = (layer - P.l0) % P.ns;
   unsigned char* st = ring + (size_t)slot * P.lay.stage_bytes;
   uint64_t* bar = bars + slot;
-  const LayerW& L = P.layers[layer];
-  const Layout& Y = P.lay;
+  const LayerW L = P.layers[layer];  // by value: one load of the pointer table, not one per use
+  const Layout Y = P.lay;
   const int RB = P.d_model / 8, RBO = P.d_inner / 8;
   const void* src = nullptr;
   int dst = 0;
@@ -244,6 +253,9 @@ __device__ void issue_stage(const PParams& P, const CtaPlan& pl, int layer, unsi
 }
 
 // ------------------------------------------------------------------ block reductions (512 threads)
+// Block-wide sum / max of N values per thread with a fixed combination order.  Warp partials
+// go to red[w*N + i]; thread i < N combines column i into red[kWarps*N + i]; every thread then
+// reads the N totals.  `red` holds (kWarps + 1) * N floats.
 template <int N>
 __device__ __forceinline__ void block_sum_n(float (&v)[N], float* red) {
 #pragma unroll
@@ -254,13 +266,15 @@ __device__ __forceinline__ void block_sum_n(float (&v)[N], float* red) {
 #pragma unroll
     for (int i = 0; i < N; ++i) red[w * N + i] = v[i];
   __syncthreads();
-#pragma unroll
-  for (int i = 0; i < N; ++i) {
+  if (threadIdx.x < N) {
     float s = 0.f;
 #pragma unroll
-    for (int j = 0; j < kWarps; ++j) s += red[j * N + i];
-    v[i] = s;
+    for (int j = 0; j < kWarps; ++j) s += red[j * N + threadIdx.x];
+    red[kWarps * N + threadIdx.x] = s;
   }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = red[kWarps * N + i];
 }
 template <int N>
 __device__ __forceinline__ void block_max_n(float (&v)[N], float* red) {
@@ -272,13 +286,33 @@ __device__ __forceinline__ void block_max_n(float (&v)[N], float* red) {
 #pragma unroll
     for (int i = 0; i < N; ++i) red[w * N + i] = v[i];
   __syncthreads();
+  if (threadIdx.x < N) {
+    float s = red[threadIdx.x];
 #pragma unroll
-  for (int i = 0; i < N; ++i) {
-    float s = red[i];
-#pragma unroll
-    for (int j = 1; j < kWarps; ++j) s = fmaxf(s, red[j * N + i]);
-    v[i] = s;
+    for (int j = 1; j < kWarps; ++j) s = fmaxf(s, red[j * N + threadIdx.x]);
+    red[kWarps * N + threadIdx.x] = s;
   }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = red[kWarps * N + i];
+}
+
+// Like block_sum_n but only threads i < N receive total i (returned), for the LoRA partials.
+template <int N>
+__device__ __forceinline__ float block_sum_scatter(float (&v)[N], float* red) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = warp_sum(v[i]);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0)
+#pragma unroll
+    for (int i = 0; i < N; ++i) red[w * N + i] = v[i];
+  __syncthreads();
+  float s = 0.f;
+  if (threadIdx.x < N)
+#pragma unroll
+    for (int j = 0; j < kWarps; ++j) s += red[j * N + threadIdx.x];
+  return s;
 }
 
 template <int KPT>
@@ -350,17 +384,13 @@ __device__ void prep_rows(float (&vals)[B][KPT], const float (&w)[KPT], int K,
     for (int r = 0; r < DFSSM_RANK; ++r) {
       float a = 0.f;
 #pragma unroll
-      for (int j = 0; j < KPT; ++j) a = fmaf(vals[b][j], (float)byte_of<KPT>(lb[r], j), a);
+      for (int j = 0; j < KPT; ++j) a = fmaf(vals[b][j], round_h((float)byte_of<KPT>(lb[r], j) * lbs[r]), a);
       all[b * DFSSM_RANK + r] = a;
     }
   }
-  block_sum_n<B * DFSSM_RANK + B>(all, red);
-  if (threadIdx.x == 0) {
-#pragma unroll
-    for (int i = 0; i < B * DFSSM_RANK; ++i) s_t[i] = round_h(all[i] * lbs[i % DFSSM_RANK]);
-#pragma unroll
-    for (int b = 0; b < B; ++b) s_qsum[b] = (int)all[B * DFSSM_RANK + b];
-  }
+  const float tot = block_sum_scatter<B * DFSSM_RANK + B>(all, red);
+  if (threadIdx.x < B * DFSSM_RANK) s_t[threadIdx.x] = round_h(tot);
+  else if (threadIdx.x < B * DFSSM_RANK + B) s_qsum[threadIdx.x - B * DFSSM_RANK] = (int)tot;
   __syncthreads();
 }
 
@@ -431,8 +461,8 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
   __half* s_x = reinterpret_cast<__half*>(smem);                   // [B][d_model]
   int8_t* s_q = reinterpret_cast<int8_t*>(smem + B * d_model * 2);  // [B][d_inner]
   float* s_misc = reinterpret_cast<float*>(smem + B * d_model * 2 + B * d_inner);
-  float* red = s_misc;                              // [kWarps * (B*16+B)]
-  float* s_t = red + kWarps * (B * 16 + B);         // [B*16]
+  float* red = s_misc;                              // [(kWarps + 1) * (B*16+B)]
+  float* s_t = red + (kWarps + 1) * (B * 16 + B);   // [B*16]
   float* s_xs = s_t + B * 16;                       // [B]
   int* s_qsum = reinterpret_cast<int*>(s_xs + B);   // [B]
   float* s_lbs = reinterpret_cast<float*>(s_qsum + B);  // [16]
@@ -454,6 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  stamp(P, 0);
   for (int l = 0; l < P.ns - 1; ++l) issue_stage<B>(P, pl, P.l0 + l, ring, bars);
 
   // embedding gather (every CTA needs the full x of the first layer)
@@ -488,7 +519,10 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         s_dtla[16] = h2f(L.in.lAs[dtrow]);
       }
     }
+    const int tb = 2 + kTracePerLayer * layer;
+    stamp(P, tb + 0);
     if (layer > P.l0) grid_barrier(P, nbar);  // x of the previous layer complete
+    stamp(P, tb + 1);
     if (layer > P.l0 || P.from_x) {
       for (int i = tid; i < B * d_model / 8; i += kThreads)
         reinterpret_cast<uint4*>(s_x)[i] = __ldcg(reinterpret_cast<const uint4*>(P.x_g) + i);
@@ -502,7 +536,9 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         for (int j = 0; j < KI; ++j) vals[b][j] = h2f(s_x[b * d_model + tid * KI + j]);
       prep_rows<B, KI>(vals, w_in, d_model, lb_in, s_lbs, s_q, d_inner, s_xs, s_qsum, s_t, red);
     }
+    stamp(P, tb + 2);
     wait_stage(P, bars, layer);
+    stamp(P, tb + 3);
     const int RB = d_model / 8;
     if (pl.role == 0) {
       const int np = pl.np, nrows = 2 * np + 1;
@@ -543,8 +579,10 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         }
       }
       __syncthreads();
+      stamp(P, tb + 4);
       // wait for every B/C CTA of this layer, then fetch conv'd B and C
       wait_counter(P.sync + 2, (unsigned)(layer - P.l0 + 1) * P.n_bc, P.sync + 3, 4u);
+      stamp(P, tb + 5);
       for (int i = tid; i < B * 2 * DFSSM_DSTATE; i += kThreads) s_bc[i] = h2f(__ldcg(P.bc_g + i));
       __syncthreads();
       // SSM state update + gate; warp w owns rows p = w*RPW.., lane owns n = 4*lane..
@@ -623,7 +661,9 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
       for (int j = 0; j < KO; ++j) w_out[j] = __ldg(L.norm_w + k0 + j);
       load_lora_b<KO>(L.out.lB, d_inner, lb_out);
     }
+    stamp(P, tb + 6);
     grid_barrier(P, nbar);  // gated complete
+    stamp(P, tb + 7);
     if (tid < 16) s_lbs[tid] = h2f(L.out.lBs[tid]);
     {
       float vals[B][KO];
@@ -657,8 +697,10 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
   }
 
   // ---------------- final norm + LM head + argmax
+  stamp(P, 2 + kTracePerLayer * P.n_layer);
   if (P.do_head) {
     grid_barrier(P, nbar);
+    stamp(P, 3 + kTracePerLayer * P.n_layer);
     for (int i = tid; i < B * d_model / 8; i += kThreads)
       reinterpret_cast<uint4*>(s_x)[i] = __ldcg(reinterpret_cast<const uint4*>(P.x_g) + i);
     __syncthreads();
@@ -691,38 +733,59 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
     unsigned long long mybest[B];
 #pragma unroll
     for (int b = 0; b < B; ++b) mybest[b] = 0ull;
+    // Each warp takes 2 rows per iteration; with d_model = 512*KI a row is 32*KI 16-byte chunks,
+    // KI per lane, and all 2*KI loads are issued before any arithmetic.
+    constexpr int CPL = KI;
     const int C = d_model >> 4;
-    for (int v = pl.v0 + wid; v < pl.v0 + pl.nv; v += kWarps) {
-      float acc[B];
+    const int vend = pl.v0 + pl.nv;
+    for (int v = pl.v0 + 2 * wid; v < vend; v += 2 * kWarps) {
+      uint4 ev[2][CPL];
 #pragma unroll
-      for (int b = 0; b < B; ++b) acc[b] = 0.f;
-      const uint4* er = reinterpret_cast<const uint4*>(P.Eq + (size_t)v * d_model);
-      for (int c = lane; c < C; c += 32) {
-        const uint4 ev = ldg_stream(er + c);
-        const unsigned w4[4] = {ev.x, ev.y, ev.z, ev.w};
+      for (int r = 0; r < 2; ++r) {
+        const int vr = v + r < vend ? v + r : v;
+        const uint4* er = reinterpret_cast<const uint4*>(P.Eq + (size_t)vr * d_model);
 #pragma unroll
-        for (int b = 0; b < B; ++b) {
-          const float4* xv = reinterpret_cast<const float4*>(s_no + b * d_model + c * 16);
-          float a = acc[b];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float4 xx = xv[u];
-            a = fmaf((float)(int8_t)(w4[u] & 0xff), xx.x, a);
-            a = fmaf((float)(int8_t)((w4[u] >> 8) & 0xff), xx.y, a);
-            a = fmaf((float)(int8_t)((w4[u] >> 16) & 0xff), xx.z, a);
-            a = fmaf((float)(int8_t)(w4[u] >> 24), xx.w, a);
-          }
-          acc[b] = a;
+        for (int u = 0; u < CPL; ++u) {
+          const int c = lane + 32 * u;
+          ev[r][u] = c < C ? ldg_stream(er + c) : make_uint4(0, 0, 0, 0);
         }
       }
-      const float sv = P.Es[v];
 #pragma unroll
-      for (int b = 0; b < B; ++b) {
-        const float lg = warp_sum(acc[b]) * sv;
-        if (lane == 0) {
-          P.logits[(size_t)b * P.vocab + v] = lg;
-          const unsigned long long key = argmax_key(f2h(lg), (uint32_t)v);
-          mybest[b] = key > mybest[b] ? key : mybest[b];
+      for (int r = 0; r < 2; ++r) {
+        float acc[B];
+#pragma unroll
+        for (int b = 0; b < B; ++b) acc[b] = 0.f;
+#pragma unroll
+        for (int u = 0; u < CPL; ++u) {
+          const int c = lane + 32 * u;
+          if (c >= C) continue;
+          const unsigned w4[4] = {ev[r][u].x, ev[r][u].y, ev[r][u].z, ev[r][u].w};
+#pragma unroll
+          for (int b = 0; b < B; ++b) {
+            const float4* xv = reinterpret_cast<const float4*>(s_no + b * d_model + c * 16);
+            float a = acc[b];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float4 xx = xv[q];
+              a = fmaf((float)(int8_t)(w4[q] & 0xff), xx.x, a);
+              a = fmaf((float)(int8_t)((w4[q] >> 8) & 0xff), xx.y, a);
+              a = fmaf((float)(int8_t)((w4[q] >> 16) & 0xff), xx.z, a);
+              a = fmaf((float)(int8_t)(w4[q] >> 24), xx.w, a);
+            }
+            acc[b] = a;
+          }
+        }
+        const int vr = v + r;
+        if (vr >= vend) break;
+        const float sv = P.Es[vr];
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+          const float lg = warp_sum(acc[b]) * sv;
+          if (lane == 0) {
+            P.logits[(size_t)b * P.vocab + vr] = lg;
+            const unsigned long long key = argmax_key(f2h(lg), (uint32_t)vr);
+            mybest[b] = key > mybest[b] ? key : mybest[b];
+          }
         }
       }
     }
@@ -738,6 +801,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
       atomicMax(P.best + tid, k);
     }
   }  // do_head
+  stamp(P, 1);
   __syncthreads();
   // drain: no bulk copy into this CTA's ring may still be in flight when it exits (only
   // possible after a timed-out wait); bounded, ignores the error word
@@ -861,7 +925,7 @@ int build_plan(const dfssm_engine* e, int B, int grid, std::vector<CtaPlan>& pla
   lay.state = off; off += a16(B * np * DFSSM_DSTATE * 4);
   lay.cstate = off; off += a16(B * 3 * ch * 4);
   lay.stage_bytes = (off + 127) & ~127;
-  const int misc_floats = kWarps * (B * 16 + B) + B * 16 + B + B + 16 + B * 64 * 2 + B + B * 256 + 4 + 17;
+  const int misc_floats = (kWarps + 1) * (B * 16 + B) + B * 16 + B + B + 16 + B * 64 * 2 + B + B * 256 + 4 + 17;
   int work = B * d.d_model * 2 + B * d.d_inner + misc_floats * 4;
   work = (work + 127) & ~127;
   const int ring_off = work + 128;  // 8 mbarriers live just below the ring
@@ -944,6 +1008,7 @@ int persistent_init(dfssm_engine* e) {
     P.n_bc = n_bc;
     P.ns = ns;
     P.ring_off = smem - ns * lay.stage_bytes;
+    P.trace = nullptr;
     ps.fn = fn;
     ps.smem = smem;
     ps.grid = grid;
@@ -973,4 +1038,19 @@ int launch_persistent_layers(dfssm_engine* e, int l0, int l1, int from_x, int do
 
 int launch_persistent_step(dfssm_engine* e, cudaStream_t s) {
   return launch_persistent_layers(e, 0, e->d.n_layer, 0, 1, s);
+}
+
+size_t persistent_trace_entries(const dfssm_engine* e) {
+  return (size_t)e->sm_count * (4 + kTracePerLayer * e->d.n_layer);
+}
+
+int launch_persistent_traced(dfssm_engine* e, unsigned long long* trace_dev, cudaStream_t s) {
+  if (!persistent_supported(e)) return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "persistent kernel unavailable");
+  PersistentState& ps = set_of(e)->st[e->batch];
+  PParams P = ps.params;
+  P.trace = trace_dev;
+  void* args[] = {&P};
+  cudaError_t ce = cudaLaunchCooperativeKernel(ps.fn, dim3(ps.grid), dim3(kThreads), args, (size_t)ps.smem, s);
+  if (ce != cudaSuccess) return dfssm_fail(DFSSM_ERR_CUDA, "cooperative launch failed: %s", cudaGetErrorString(ce));
+  return DFSSM_OK;
 }

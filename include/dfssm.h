@@ -99,6 +99,15 @@ int dfssm_get_buffer(dfssm_engine* e, const char* name, void** ptr, size_t* byte
  * (per-op kernels, or the persistent kernel over the single layer when mode 3 is selected). */
 int dfssm_layer_step(dfssm_engine* e, int layer, void* stream);
 
+/* Diagnostics (no counterpart in the reference, which has no profiler hooks): number of
+ * uint64 entries of a persistent-step trace, and one persistent decode step (mode 3 batch)
+ * that records %globaltimer stamps at its phase boundaries into trace_dev
+ * [sm_count][4 + 8 * n_layer]: [0] start, [1] end, [2 + 8l + k] layer l phase k
+ * (0 alpha entry, 1 after the x barrier, 2 after norm/quant, 3 after the weight ring wait,
+ *  4 after the in_proj GEMV, 5 after the B/C wait, 6 before the gated barrier, 7 after it). */
+size_t dfssm_trace_entries(const dfssm_engine* e);
+int dfssm_trace_step(dfssm_engine* e, unsigned long long* trace_dev, void* stream);
+
 /* ---- stand-alone ops (reference operator replacements) ---- */
 
 /* Scratch bytes dfssm_scaffold_gemm needs for M activation rows of length K. */
