@@ -17,7 +17,26 @@ __device__ __forceinline__ float qscale_floor() { return __half2float(__ushort_a
 
 __device__ __forceinline__ float h2f(__half h) { return __half2float(h); }
 __device__ __forceinline__ __half f2h(float f) { return __float2half_rn(f); }
-__device__ __forceinline__ float round_h(float f) { return __half2float(__float2half_rn(f)); }
+// Round an fp32 value to the nearest fp16 value (ties to even), returned as fp32, using two
+// exact-rounding fp32 additions instead of the F2H/H2F conversion pair (which issue on the
+// low-throughput conversion pipe): adding M = 1.5 * 2^(E+13), E the value's binary exponent
+// clamped to fp16's subnormal floor 2^-14, leaves the sum with fp16's spacing 2^(E-10) as its
+// last fp32 bit, so fp32's own round-to-nearest-even performs the fp16 rounding.  Results with
+// magnitude above 65504 are fp16 overflow and become +-inf, as __float2half_rn does.
+__device__ __forceinline__ float round_h(float v) {
+  unsigned e = (__float_as_uint(v) >> 23) & 0xffu;
+  e = e < 113u ? 113u : (e > 160u ? 160u : e);
+  const float M = __uint_as_float(((e + 13u) << 23) | 0x400000u);
+  const float r = copysignf(__fsub_rn(__fadd_rn(v, M), M), v);  // keeps -0 for tiny negatives
+  return fabsf(r) > 65504.f ? copysignf(__int_as_float(0x7f800000), v) : r;
+}
+// Round to the nearest integer, ties to even (|v| < 2^22): same trick with M = 1.5 * 2^23.
+__device__ __forceinline__ float rint_alu(float v) { return __fsub_rn(__fadd_rn(v, 12582912.0f), 12582912.0f); }
+// Signed byte j of w as fp32 without I2F: w ^ 0x80808080 biases the bytes to 0..255, a byte
+// permute places byte j in the mantissa of 2^23, and one exact subtraction removes 2^23 + 128.
+__device__ __forceinline__ float i8_to_f(unsigned w_biased, int j) {
+  return __fsub_rn(__uint_as_float(__byte_perm(w_biased, 0x4B000000u, 0x7540u | (unsigned)j)), 8388736.0f);
+}
 
 template <typename T>
 __device__ __forceinline__ T warp_sum(T v) {

@@ -68,7 +68,7 @@ int launch_prep(dfssm_engine* e, const __half* in, int K, const float* w, int qu
                 cudaStream_t s) {
   const size_t sm = (size_t)K * sizeof(__half);
   act_prep_kernel<<<e->batch, kPrepThreads, sm, s>>>(in, K, w, quant, e->xn, e->q, e->xs, e->qsum,
-                                                     p ? p->lB : nullptr, p ? p->lBs : nullptr, e->t);
+                                                     p ? p->B16 : nullptr, e->t);
   CHECK_LAUNCH();
   return DFSSM_OK;
 }
@@ -196,7 +196,7 @@ int parse_dims(const unsigned char* img, size_t n, dfssm_dims* d, int* emb_kind)
 // Device arena: per layer, each array starts on a 256-byte boundary.
 struct ArenaPlan {
   struct P {
-    size_t bits, scale, lA, lAs, lB, lBs;
+    size_t bits, scale, A16, B16;
   };
   struct Lyr {
     P in, out;
@@ -218,10 +218,8 @@ ArenaPlan plan_arena(const dfssm_dims& d) {
     ArenaPlan::P p;
     p.bits = take((size_t)n * (k / 32) * 4);
     p.scale = take((size_t)n * 2);
-    p.lA = take((size_t)n * kRank);
-    p.lAs = take((size_t)n * 2);
-    p.lB = take((size_t)kRank * k);
-    p.lBs = take(kRank * 2);
+    p.A16 = take((size_t)n * kRank * 2);
+    p.B16 = take((size_t)kRank * k * 2);
     return p;
   };
   for (int l = 0; l < d.n_layer; ++l) {
@@ -303,10 +301,23 @@ int build_engine(const unsigned char* img, size_t n, int device, int max_batch, 
     for (int j = 0; j < 2; ++j) {
       copy(ps[j]->bits, (size_t)ns[j] * (ks[j] / 32) * 4);
       copy(ps[j]->scale, (size_t)ns[j] * 2);
-      copy(ps[j]->lA, (size_t)ns[j] * kRank);
-      copy(ps[j]->lAs, (size_t)ns[j] * 2);
-      copy(ps[j]->lB, (size_t)kRank * ks[j]);
-      copy(ps[j]->lBs, kRank * 2);
+      // LoRA: int8 + fp16 scale on disk, dequantised to fp16 here exactly as the reference loader
+      // does ((q.float() * s.float()).half(), df_ssm_inference.py:78-83,92-97)
+      {
+        const int8_t* Aq = reinterpret_cast<const int8_t*>(img + src);
+        const __half* As = reinterpret_cast<const __half*>(img + src + (size_t)ns[j] * kRank);
+        __half* A16 = reinterpret_cast<__half*>(host.data() + ps[j]->A16);
+        for (size_t r = 0; r < (size_t)ns[j]; ++r)
+          for (int c = 0; c < kRank; ++c) A16[r * kRank + c] = __float2half_rn((float)Aq[r * kRank + c] * __half2float(As[r]));
+        src += (size_t)ns[j] * kRank + (size_t)ns[j] * 2;
+        const int8_t* Bq = reinterpret_cast<const int8_t*>(img + src);
+        const __half* Bs = reinterpret_cast<const __half*>(img + src + (size_t)kRank * ks[j]);
+        __half* B16 = reinterpret_cast<__half*>(host.data() + ps[j]->B16);
+        for (int r = 0; r < kRank; ++r)
+          for (size_t c = 0; c < (size_t)ks[j]; ++c)
+            B16[r * (size_t)ks[j] + c] = __float2half_rn((float)Bq[r * (size_t)ks[j] + c] * __half2float(Bs[r]));
+        src += (size_t)kRank * ks[j] + kRank * 2;
+      }
     }
     copy(y.conv_w, (size_t)d.d_xbc * 4 * 2);
     copy(y.conv_b, (size_t)d.d_xbc * 2);
@@ -345,10 +356,8 @@ int build_engine(const unsigned char* img, size_t n, int device, int max_batch, 
       ProjW w;
       w.bits = reinterpret_cast<const uint32_t*>(A + p.bits);
       w.scale = reinterpret_cast<const __half*>(A + p.scale);
-      w.lA = reinterpret_cast<const int8_t*>(A + p.lA);
-      w.lAs = reinterpret_cast<const __half*>(A + p.lAs);
-      w.lB = reinterpret_cast<const int8_t*>(A + p.lB);
-      w.lBs = reinterpret_cast<const __half*>(A + p.lBs);
+      w.A16 = reinterpret_cast<const __half*>(A + p.A16);
+      w.B16 = reinterpret_cast<const __half*>(A + p.B16);
       w.N = nrows;
       w.K = k;
       return w;

@@ -28,14 +28,14 @@ constexpr int kHeadBT = 8;
 //   xn = fp16((x * rsqrt(mean(x^2) + 1e-5)) * w)          df_ssm_inference.py:141-145
 //   s  = fp16(max(amax|xn|, fp16(1e-4)) * (1/127))          df_ssm_inference.py:150
 //   q  = clamp(rne(fp16(xn / s)), -128, 127)                df_ssm_inference.py:151
-//   t_r = fp16(sum_k xn_k * fp16(lB[r][k] * lBs[r]))        df_ssm_inference.py:92-97,173
+//   t_r = fp16(sum_k xn_k * B16[r][k])                      df_ssm_inference.py:92-97,173
 // q is written in the permuted layout of qperm_index(); qsum = sum_k q_k.
 // With quant == 0 only xn is produced (final norm before the LM head).
 // ---------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kPrepThreads)
 act_prep_kernel(const __half* __restrict__ in, int K, const float* __restrict__ w, int quant,
                 __half* __restrict__ xn_out, int8_t* __restrict__ q_out, __half* __restrict__ xs_out,
-                int* __restrict__ qsum_out, const int8_t* __restrict__ lB, const __half* __restrict__ lBs,
+                int* __restrict__ qsum_out, const __half* __restrict__ B16,
                 __half* __restrict__ t_out) {
   extern __shared__ __align__(16) unsigned char smem[];
   __half* sxn = reinterpret_cast<__half*>(smem);
@@ -69,7 +69,7 @@ act_prep_kernel(const __half* __restrict__ in, int K, const float* __restrict__ 
   int8_t* qrow = q_out + (size_t)b * K;
   for (int k = threadIdx.x; k < K; k += kPrepThreads) {
     float t = round_h(h2f(sxn[k]) / s);
-    int q = (int)rintf(t);
+    int q = (int)rint_alu(t);
     q = max(-128, min(127, q));
     qrow[qperm_index(k)] = (int8_t)q;
     qs += q;
@@ -84,10 +84,9 @@ act_prep_kernel(const __half* __restrict__ in, int K, const float* __restrict__ 
 #pragma unroll
   for (int rr = 0; rr < 2; ++rr) {
     const int rk = wid * 2 + rr;
-    const float bs = h2f(lBs[rk]);
-    const int8_t* brow = lB + (size_t)rk * K;
+    const __half* brow = B16 + (size_t)rk * K;
     float acc = 0.f;
-    for (int k = lane; k < K; k += 32) acc = fmaf(h2f(sxn[k]), round_h((float)brow[k] * bs), acc);
+    for (int k = lane; k < K; k += 32) acc = fmaf(h2f(sxn[k]), h2f(brow[k]), acc);
     acc = warp_sum(acc);
     if (lane == 0) t_out[b * DFSSM_RANK + rk] = f2h(acc);
   }
@@ -103,7 +102,7 @@ act_prep_kernel(const __half* __restrict__ in, int K, const float* __restrict__ 
 // (df_ssm_inference.py:157).  The 16 per-batch partial sums of a half-warp are combined
 // by a reduce-scatter so that lane l16 ends up with batch row l16 and runs its epilogue:
 //   base = fp16(fp16(fp16(acc) * xs) * w_scale)                df_ssm_inference.py:158
-//   v    = fp16(base + sum_r t_r * fp16(lA[n][r] * lAs[n]))    df_ssm_inference.py:173,204
+//   v    = fp16(base + sum_r t_r * A16[n][r])                  df_ssm_inference.py:173,204
 // MODE 0 (in_proj): rows in [d_inner, d_inner + d_xbc) also run the conv1d shift
 // register + SiLU (df_ssm_kernels.cu:27-47) with fp32 state [B][3][d_xbc].
 // MODE 1 (out_proj): x = fp16(x + v)                           df_ssm_inference.py:207
@@ -205,16 +204,11 @@ proj_gemv_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ 
       }
       const float base = round_h(round_h(round_h((float)dot) * h2f(xs[b])) * h2f(p.scale[row]));
       // LoRA up-projection
-      const float as = h2f(p.lAs[row]);
-      const int4 arow = *reinterpret_cast<const int4*>(p.lA + (size_t)row * DFSSM_RANK);
-      const int av[4] = {arow.x, arow.y, arow.z, arow.w};
+      const __half* arow = p.A16 + (size_t)row * DFSSM_RANK;
       const __half* tb = t + b * DFSSM_RANK;
       float la = 0.f;
 #pragma unroll
-      for (int r = 0; r < DFSSM_RANK; ++r) {
-        const int a8 = (int)(int8_t)((av[r >> 2] >> (8 * (r & 3))) & 0xff);
-        la = fmaf(h2f(tb[r]), round_h((float)a8 * as), la);
-      }
+      for (int r = 0; r < DFSSM_RANK; ++r) la = fmaf(h2f(tb[r]), h2f(arow[r]), la);
       const float v = round_h(base + la);
       if (MODE == 0) {
         float res = v;
@@ -345,11 +339,11 @@ lm_head_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, int 
       for (int c = lane; c < C; c += 32) {
         const uint4 ev = ldg_stream(er + c);
         float e[16];
-        const unsigned w4[4] = {ev.x, ev.y, ev.z, ev.w};
+        const unsigned w4[4] = {ev.x ^ 0x80808080u, ev.y ^ 0x80808080u, ev.z ^ 0x80808080u, ev.w ^ 0x80808080u};
 #pragma unroll
         for (int j = 0; j < 4; ++j)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) e[j * 4 + i] = (float)(int8_t)((w4[j] >> (8 * i)) & 0xff);
+          for (int i = 0; i < 4; ++i) e[j * 4 + i] = i8_to_f(w4[j], i);
 #pragma unroll
         for (int b = 0; b < kHeadBT; ++b) {
           if (b < nb) {

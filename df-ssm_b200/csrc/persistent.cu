@@ -39,6 +39,7 @@ struct CtaPlan {
   int bc0, nbc;   // B/C rows [bc0, bc0 + nbc) within [0, 2*d_state)
   int o0, no;     // out_proj rows
   int v0, nv;     // LM head rows
+  int tx;         // bytes of one ring stage (sum of this CTA's copies)
 };
 
 struct Layout {  // byte offsets inside one ring stage (identical for every CTA)
@@ -160,96 +161,82 @@ __device__ __forceinline__ void wait_stage(const PParams& P, uint64_t* bars, int
 }
 
 // Issue the bulk copies that fill the ring slot of `layer` with this CTA's slice of it.
-// Lane i of warp 0 issues copy i of the table below (all 16-byte aligned, sizes multiples of 16).
+// Lane i of warp 0 issues copy i of the table below (all 16-byte aligned, sizes multiples of
+// 16); the byte total of a stage is precomputed on the host (CtaPlan::tx).
 template <int B>
-__device__ void issue_stage(const PParams& P, const CtaPlan& pl, int layer, unsigned char* ring, uint64_t* bars) {
+__device__ __noinline__ void issue_stage(const PParams& P, const CtaPlan& pl, int layer, unsigned char* ring,
+                                         uint64_t* bars) {
   if (layer >= P.l1 || threadIdx.x >= 32) return;
-  const int lane = threadIdx.x;
+  const int i = threadIdx.x;
   const int slot = (layer - P.l0) % P.ns;
   unsigned char* st = ring + (size_t)slot * P.lay.stage_bytes;
   uint64_t* bar = bars + slot;
-  const LayerW L = P.layers[layer];  // by value: one load of the pointer table, not one per use
-  const Layout Y = P.lay;
+  const LayerW& L = P.layers[layer];
+  const Layout& Y = P.lay;
   const int RB = P.d_model / 8, RBO = P.d_inner / 8;
-  const void* src = nullptr;
-  int dst = 0;
-  unsigned bytes = 0;
-  unsigned total = 0;
-  for (int i = 0; i < 32; ++i) {
-    const void* s_ = nullptr;
-    int d_ = 0;
-    unsigned n_ = 0;
-    const char* inb = reinterpret_cast<const char*>(L.in.bits);
-    if (pl.role == 0) {
-      const int c0 = pl.h * DFSSM_HEADDIM + pl.p0, np = pl.np;
-      switch (i) {
-        case 0: s_ = inb + (size_t)c0 * RB; d_ = Y.in_bits; n_ = np * RB; break;
-        case 1: s_ = inb + (size_t)(P.d_inner + c0) * RB; d_ = Y.in_bits + np * RB; n_ = np * RB; break;
-        case 2: s_ = inb + (size_t)(P.d_inner + P.d_xbc + pl.h) * RB; d_ = Y.in_bits + 2 * np * RB; n_ = RB; break;
-        case 3: s_ = L.in.scale + c0; d_ = Y.in_scale; n_ = np * 2; break;
-        case 4: s_ = L.in.scale + P.d_inner + c0; d_ = Y.in_scale + np * 2; n_ = np * 2; break;
-        case 5: s_ = L.in.lA + (size_t)c0 * 16; d_ = Y.in_lA; n_ = np * 16; break;
-        case 6: s_ = L.in.lA + (size_t)(P.d_inner + c0) * 16; d_ = Y.in_lA + np * 16; n_ = np * 16; break;
-        case 7: s_ = L.in.lAs + c0; d_ = Y.in_lAs; n_ = np * 2; break;
-        case 8: s_ = L.in.lAs + P.d_inner + c0; d_ = Y.in_lAs + np * 2; n_ = np * 2; break;
-        case 9: s_ = L.conv_w + (size_t)c0 * 4; d_ = Y.conv_w; n_ = np * 8; break;
-        case 10: s_ = L.conv_b + c0; d_ = Y.conv_b; n_ = np * 2; break;
-        default: break;
-      }
-      const int j = i - 15;
-      if (j >= 0 && j < B) {
-        s_ = P.ssm + (long long)layer * P.ssm_layer +
-             ((long long)(j * P.nheads + pl.h) * DFSSM_HEADDIM + pl.p0) * DFSSM_DSTATE;
-        d_ = Y.state + j * np * DFSSM_DSTATE * 4;
-        n_ = np * DFSSM_DSTATE * 4;
-      }
-      const int k = i - 15 - B;
-      if (k >= 0 && k < 3 * B) {
-        s_ = P.conv + (long long)layer * P.conv_layer + (long long)k * P.d_xbc + c0;
-        d_ = Y.cstate + k * np * 4;
-        n_ = np * 4;
-      }
-    } else if (pl.role == 1) {
-      const int r0 = 2 * P.d_inner + pl.bc0, c0 = P.d_inner + pl.bc0, nb = pl.nbc;
-      switch (i) {
-        case 0: s_ = inb + (size_t)r0 * RB; d_ = Y.in_bits; n_ = nb * RB; break;
-        case 3: s_ = L.in.scale + r0; d_ = Y.in_scale; n_ = nb * 2; break;
-        case 5: s_ = L.in.lA + (size_t)r0 * 16; d_ = Y.in_lA; n_ = nb * 16; break;
-        case 7: s_ = L.in.lAs + r0; d_ = Y.in_lAs; n_ = nb * 2; break;
-        case 9: s_ = L.conv_w + (size_t)c0 * 4; d_ = Y.conv_w; n_ = nb * 8; break;
-        case 10: s_ = L.conv_b + c0; d_ = Y.conv_b; n_ = nb * 2; break;
-        default: break;
-      }
-      const int k = i - 15 - B;
-      if (k >= 0 && k < 3 * B) {
-        s_ = P.conv + (long long)layer * P.conv_layer + (long long)k * P.d_xbc + c0;
-        d_ = Y.cstate + k * nb * 4;
-        n_ = nb * 4;
-      }
+  const void* s_ = nullptr;
+  int d_ = 0;
+  unsigned n_ = 0;
+  const char* inb = reinterpret_cast<const char*>(L.in.bits);
+  if (pl.role == 0) {
+    const int c0 = pl.h * DFSSM_HEADDIM + pl.p0, np = pl.np;
+    switch (i) {
+      case 0: s_ = inb + (size_t)c0 * RB; d_ = Y.in_bits; n_ = np * RB; break;
+      case 1: s_ = inb + (size_t)(P.d_inner + c0) * RB; d_ = Y.in_bits + np * RB; n_ = np * RB; break;
+      case 2: s_ = inb + (size_t)(P.d_inner + P.d_xbc + pl.h) * RB; d_ = Y.in_bits + 2 * np * RB; n_ = RB; break;
+      case 3: s_ = L.in.scale + c0; d_ = Y.in_scale; n_ = np * 2; break;
+      case 4: s_ = L.in.scale + P.d_inner + c0; d_ = Y.in_scale + np * 2; n_ = np * 2; break;
+      case 5: s_ = L.in.A16 + (size_t)c0 * 16; d_ = Y.in_lA; n_ = np * 32; break;
+      case 6: s_ = L.in.A16 + (size_t)(P.d_inner + c0) * 16; d_ = Y.in_lA + np * 32; n_ = np * 32; break;
+      case 9: s_ = L.conv_w + (size_t)c0 * 4; d_ = Y.conv_w; n_ = np * 8; break;
+      case 10: s_ = L.conv_b + c0; d_ = Y.conv_b; n_ = np * 2; break;
+      default: break;
     }
-    if (pl.no > 0) {
-      const char* ob = reinterpret_cast<const char*>(L.out.bits);
-      switch (i) {
-        case 11: s_ = ob + (size_t)pl.o0 * RBO; d_ = Y.out_bits; n_ = pl.no * RBO; break;
-        case 12: s_ = L.out.scale + pl.o0; d_ = Y.out_scale; n_ = pl.no * 2; break;
-        case 13: s_ = L.out.lA + (size_t)pl.o0 * 16; d_ = Y.out_lA; n_ = pl.no * 16; break;
-        case 14: s_ = L.out.lAs + pl.o0; d_ = Y.out_lAs; n_ = pl.no * 2; break;
-        default: break;
-      }
+    const int j = i - 15;
+    if (j >= 0 && j < B) {
+      s_ = P.ssm + (long long)layer * P.ssm_layer +
+           ((long long)(j * P.nheads + pl.h) * DFSSM_HEADDIM + pl.p0) * DFSSM_DSTATE;
+      d_ = Y.state + j * np * DFSSM_DSTATE * 4;
+      n_ = np * DFSSM_DSTATE * 4;
     }
-    total += n_;
-    if (i == lane) {
-      src = s_;
-      dst = d_;
-      bytes = n_;
+    const int k = i - 15 - B;
+    if (k >= 0 && k < 3 * B) {
+      s_ = P.conv + (long long)layer * P.conv_layer + (long long)k * P.d_xbc + c0;
+      d_ = Y.cstate + k * np * 4;
+      n_ = np * 4;
+    }
+  } else if (pl.role == 1) {
+    const int r0 = 2 * P.d_inner + pl.bc0, c0 = P.d_inner + pl.bc0, nb = pl.nbc;
+    switch (i) {
+      case 0: s_ = inb + (size_t)r0 * RB; d_ = Y.in_bits; n_ = nb * RB; break;
+      case 3: s_ = L.in.scale + r0; d_ = Y.in_scale; n_ = nb * 2; break;
+      case 5: s_ = L.in.A16 + (size_t)r0 * 16; d_ = Y.in_lA; n_ = nb * 32; break;
+      case 9: s_ = L.conv_w + (size_t)c0 * 4; d_ = Y.conv_w; n_ = nb * 8; break;
+      case 10: s_ = L.conv_b + c0; d_ = Y.conv_b; n_ = nb * 2; break;
+      default: break;
+    }
+    const int k = i - 15 - B;
+    if (k >= 0 && k < 3 * B) {
+      s_ = P.conv + (long long)layer * P.conv_layer + (long long)k * P.d_xbc + c0;
+      d_ = Y.cstate + k * nb * 4;
+      n_ = nb * 4;
     }
   }
-  if (lane == 0) {
+  if (pl.no > 0) {
+    const char* ob = reinterpret_cast<const char*>(L.out.bits);
+    switch (i) {
+      case 11: s_ = ob + (size_t)pl.o0 * RBO; d_ = Y.out_bits; n_ = pl.no * RBO; break;
+      case 12: s_ = L.out.scale + pl.o0; d_ = Y.out_scale; n_ = pl.no * 2; break;
+      case 13: s_ = L.out.A16 + (size_t)pl.o0 * 16; d_ = Y.out_lA; n_ = pl.no * 32; break;
+      default: break;
+    }
+  }
+  if (i == 0) {
     fence_proxy_async();
-    mbar_expect_tx(bar, total);
+    mbar_expect_tx(bar, (unsigned)pl.tx);
   }
   __syncwarp();
-  if (bytes) bulk_g2s(st + dst, src, bytes, bar);
+  if (n_) bulk_g2s(st + d_, s_, n_, bar);
 }
 
 // ------------------------------------------------------------------ block reductions (512 threads)
@@ -316,23 +303,32 @@ __device__ __forceinline__ float block_sum_scatter(float (&v)[N], float* red) {
 }
 
 template <int KPT>
-struct RankBytes;  // KPT int8 LoRA-B values of one rank for this thread's columns
-template <> struct RankBytes<1> { using T = uint8_t; };
-template <> struct RankBytes<2> { using T = uint16_t; };
-template <> struct RankBytes<4> { using T = uint32_t; };
-template <> struct RankBytes<8> { using T = unsigned long long; };
+struct RankHalves;  // KPT fp16 LoRA-B values of one rank for this thread's columns
+template <> struct RankHalves<1> { using T = unsigned short; };
+template <> struct RankHalves<2> { using T = unsigned; };
+template <> struct RankHalves<4> { using T = uint2; };
+template <> struct RankHalves<8> { using T = uint4; };
 
 template <int KPT>
-__device__ __forceinline__ void load_lora_b(const int8_t* lB, int K, typename RankBytes<KPT>::T (&out)[DFSSM_RANK]) {
-  using T = typename RankBytes<KPT>::T;
+__device__ __forceinline__ void load_lora_b(const __half* B16, int K, typename RankHalves<KPT>::T (&out)[DFSSM_RANK]) {
+  using T = typename RankHalves<KPT>::T;
   const int k0 = threadIdx.x * KPT;
 #pragma unroll
-  for (int r = 0; r < DFSSM_RANK; ++r) out[r] = __ldg(reinterpret_cast<const T*>(lB + (size_t)r * K + k0));
+  for (int r = 0; r < DFSSM_RANK; ++r) out[r] = __ldg(reinterpret_cast<const T*>(B16 + (size_t)r * K + k0));
 }
 
 template <int KPT>
-__device__ __forceinline__ int byte_of(typename RankBytes<KPT>::T v, int j) {
-  return (int)(int8_t)((unsigned long long)v >> (8 * j));
+__device__ __forceinline__ float half_of(const typename RankHalves<KPT>::T& v, int j) {
+  const unsigned short* h = reinterpret_cast<const unsigned short*>(&v);
+  return __half2float(__ushort_as_half(h[j]));
+}
+
+// Shared-memory position of permuted activation byte p: 16-byte unit u of 128-byte chunk c is
+// stored at unit u ^ (c & 7), so the 8 lanes of a quarter-warp that read unit u of chunks
+// c..c+7 hit 8 different bank groups.
+__device__ __forceinline__ int qswz(int p) {
+  const int c = p >> 7;
+  return (p & ~127) | ((((p >> 4) & 7) ^ (c & 7)) << 4) | (p & 15);
 }
 
 // RMSNorm + per-row int8 quantisation + LoRA down-projection of this thread's KPT columns of
@@ -340,7 +336,7 @@ __device__ __forceinline__ int byte_of(typename RankBytes<KPT>::T v, int j) {
 // sq[b][*] and xs/qsum/t to smem; returns after a __syncthreads.
 template <int B, int KPT>
 __device__ void prep_rows(float (&vals)[B][KPT], const float (&w)[KPT], int K,
-                          const typename RankBytes<KPT>::T (&lb)[DFSSM_RANK], const float* lbs, int8_t* sq, int Kq,
+                          const typename RankHalves<KPT>::T (&lb)[DFSSM_RANK], int8_t* sq, int Kq,
                           float* s_xs, int* s_qsum, float* s_t, float* red) {
   const int k0 = threadIdx.x * KPT;
   float ss[B];
@@ -373,9 +369,9 @@ __device__ void prep_rows(float (&vals)[B][KPT], const float (&w)[KPT], int K,
     int qsum = 0;
 #pragma unroll
     for (int j = 0; j < KPT; ++j) {
-      int q = (int)rintf(round_h(vals[b][j] / s));
+      int q = (int)rint_alu(round_h(vals[b][j] / s));
       q = max(-128, min(127, q));
-      sq[b * Kq + qperm_index(k0 + j)] = (int8_t)q;
+      sq[b * Kq + qswz(qperm_index(k0 + j))] = (int8_t)q;
       qsum += q;
     }
     all[B * DFSSM_RANK + b] = (float)qsum;
@@ -384,7 +380,7 @@ __device__ void prep_rows(float (&vals)[B][KPT], const float (&w)[KPT], int K,
     for (int r = 0; r < DFSSM_RANK; ++r) {
       float a = 0.f;
 #pragma unroll
-      for (int j = 0; j < KPT; ++j) a = fmaf(vals[b][j], round_h((float)byte_of<KPT>(lb[r], j) * lbs[r]), a);
+      for (int j = 0; j < KPT; ++j) a = fmaf(vals[b][j], half_of<KPT>(lb[r], j), a);
       all[b * DFSSM_RANK + r] = a;
     }
   }
@@ -397,8 +393,14 @@ __device__ void prep_rows(float (&vals)[B][KPT], const float (&w)[KPT], int K,
 // 1-bit GEMV of one row held in shared memory for B activation rows: returns the int32
 // sum_k s_k q_k for every b in all 16 lanes of the half-warp.
 template <int B>
-__device__ __forceinline__ void row_dot(const unsigned char* bits, int K, const int8_t* sq, int Kq, int l16,
-                                        const int* s_qsum, int (&dot)[B]) {
+struct Dots {
+  int v[B];
+};
+
+template <int B>
+__device__ __noinline__ Dots<B> row_dot(const unsigned char* bits, int K, const int8_t* sq, int Kq, int l16,
+                                        const int* s_qsum) {
+  Dots<B> dot;
   int acc[B];
 #pragma unroll
   for (int b = 0; b < B; ++b) acc[b] = 0;
@@ -417,7 +419,7 @@ __device__ __forceinline__ void row_dot(const unsigned char* bits, int K, const 
       int a = acc[b];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const int4 qq = qv[u];
+        const int4 qq = qv[u ^ (c & 7)];  // swizzled: see qswz()
         a = dp4a_us(m[4 * u + 0], qq.x, a);
         a = dp4a_us(m[4 * u + 1], qq.y, a);
         a = dp4a_us(m[4 * u + 2], qq.z, a);
@@ -433,17 +435,17 @@ __device__ __forceinline__ void row_dot(const unsigned char* bits, int K, const 
     a += __shfl_xor_sync(0xffffffffu, a, 4);
     a += __shfl_xor_sync(0xffffffffu, a, 2);
     a += __shfl_xor_sync(0xffffffffu, a, 1);
-    dot[b] = 2 * a - s_qsum[b];
+    dot.v[b] = 2 * a - s_qsum[b];
   }
+  return dot;
 }
 
 // dequant + LoRA up-projection of one output row (reference rounding points)
-__device__ __forceinline__ float proj_out(int dot, float xs, float wscale, const int8_t* lA, float las,
-                                          const float* t) {
+__device__ __noinline__ float proj_out(int dot, float xs, float wscale, const __half* A16, const float* t) {
   const float base = round_h(round_h(round_h((float)dot) * xs) * wscale);
   float la = 0.f;
 #pragma unroll
-  for (int r = 0; r < DFSSM_RANK; ++r) la = fmaf(t[r], round_h((float)lA[r] * las), la);
+  for (int r = 0; r < DFSSM_RANK; ++r) la = fmaf(t[r], h2f(A16[r]), la);
   return round_h(base + la);
 }
 
@@ -471,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
   float* s_dt = s_xc + B * 64;                      // [B]
   float* s_bc = s_dt + B;                           // [B][2*d_state] (fp32)
   float* s_hp = s_bc + B * 2 * DFSSM_DSTATE;        // [4] dt_bias, A_log, D, dt-row scale
-  float* s_dtla = s_hp + 4;                         // [17] dt-row LoRA A (16) + its scale
+  float* s_dtla = s_hp + 4;                         // 16 fp16 dt-row LoRA-A values
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.ring_off - 8 * 8);
   unsigned char* ring = smem + P.ring_off;
 
@@ -502,21 +504,19 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
     unsigned char* st = ring + (size_t)((layer - P.l0) % P.ns) * P.lay.stage_bytes;
     // ---------------- alpha: per-thread weights are loaded before waiting for x
     float w_in[KI];
-    typename RankBytes<KI>::T lb_in[DFSSM_RANK];
+    typename RankHalves<KI>::T lb_in[DFSSM_RANK];
     {
       const int k0 = tid * KI;
 #pragma unroll
       for (int j = 0; j < KI; ++j) w_in[j] = __ldg(L.ln_w + k0 + j);
-      load_lora_b<KI>(L.in.lB, d_model, lb_in);
-      if (tid < 16) s_lbs[tid] = h2f(L.in.lBs[tid]);
+      load_lora_b<KI>(L.in.B16, d_model, lb_in);
       if (pl.role == 0 && tid == 32) {
         s_hp[0] = L.dt_bias[pl.h];
         s_hp[1] = L.A_log[pl.h];
         s_hp[2] = L.Dp[pl.h];
         const int dtrow = d_inner + P.d_xbc + pl.h;
         s_hp[3] = h2f(L.in.scale[dtrow]);
-        for (int r = 0; r < 16; ++r) s_dtla[r] = (float)L.in.lA[(size_t)dtrow * 16 + r];
-        s_dtla[16] = h2f(L.in.lAs[dtrow]);
+        for (int r = 0; r < 16; ++r) reinterpret_cast<__half*>(s_dtla)[r] = L.in.A16[(size_t)dtrow * 16 + r];
       }
     }
     const int tb = 2 + kTracePerLayer * layer;
@@ -534,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
       for (int b = 0; b < B; ++b)
 #pragma unroll
         for (int j = 0; j < KI; ++j) vals[b][j] = h2f(s_x[b * d_model + tid * KI + j]);
-      prep_rows<B, KI>(vals, w_in, d_model, lb_in, s_lbs, s_q, d_inner, s_xs, s_qsum, s_t, red);
+      prep_rows<B, KI>(vals, w_in, d_model, lb_in, s_q, d_inner, s_xs, s_qsum, s_t, red);
     }
     stamp(P, tb + 2);
     wait_stage(P, bars, layer);
@@ -543,24 +543,21 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
     if (pl.role == 0) {
       const int np = pl.np, nrows = 2 * np + 1;
       const __half* sc = reinterpret_cast<const __half*>(st + P.lay.in_scale);
-      const int8_t* la = reinterpret_cast<const int8_t*>(st + P.lay.in_lA);
-      const __half* las = reinterpret_cast<const __half*>(st + P.lay.in_lAs);
+      const __half* la = reinterpret_cast<const __half*>(st + P.lay.in_lA);
       const __half* cw = reinterpret_cast<const __half*>(st + P.lay.conv_w);
       const __half* cb = reinterpret_cast<const __half*>(st + P.lay.conv_b);
       const float* cst = reinterpret_cast<const float*>(st + P.lay.cstate);
       for (int i = hw; i < ((nrows + 1) & ~1); i += 2 * kWarps) {
         const int row = i < nrows ? i : nrows - 1;
-        int dot[B];
-        row_dot<B>(st + P.lay.in_bits + (size_t)row * RB, d_model, s_q, d_inner, l16, s_qsum, dot);
+        const Dots<B> dd = row_dot<B>(st + P.lay.in_bits + (size_t)row * RB, d_model, s_q, d_inner, l16, s_qsum);
+        const int* dot = dd.v;
         if (i < nrows && l16 < B) {
           const int b = l16;
           float v;
           if (row < 2 * np) {
-            v = proj_out(dot[b], s_xs[b], h2f(sc[row]), la + row * 16, h2f(las[row]), s_t + b * 16);
+            v = proj_out(dot[b], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
           } else {
-            int8_t a2[16];
-            for (int r = 0; r < 16; ++r) a2[r] = (int8_t)s_dtla[r];
-            v = proj_out(dot[b], s_xs[b], s_hp[3], a2, s_dtla[16], s_t + b * 16);
+            v = proj_out(dot[b], s_xs[b], s_hp[3], reinterpret_cast<const __half*>(s_dtla), s_t + b * 16);
           }
           if (row < np) {
             s_z[b * 64 + row] = v;
@@ -624,18 +621,17 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
     } else if (pl.role == 1) {
       const int nb = pl.nbc;
       const __half* sc = reinterpret_cast<const __half*>(st + P.lay.in_scale);
-      const int8_t* la = reinterpret_cast<const int8_t*>(st + P.lay.in_lA);
-      const __half* las = reinterpret_cast<const __half*>(st + P.lay.in_lAs);
+      const __half* la = reinterpret_cast<const __half*>(st + P.lay.in_lA);
       const __half* cw = reinterpret_cast<const __half*>(st + P.lay.conv_w);
       const __half* cb = reinterpret_cast<const __half*>(st + P.lay.conv_b);
       const float* cst = reinterpret_cast<const float*>(st + P.lay.cstate);
       for (int i = hw; i < ((nb + 1) & ~1); i += 2 * kWarps) {
         const int row = i < nb ? i : nb - 1;
-        int dot[B];
-        row_dot<B>(st + P.lay.in_bits + (size_t)row * RB, d_model, s_q, d_inner, l16, s_qsum, dot);
+        const Dots<B> dd = row_dot<B>(st + P.lay.in_bits + (size_t)row * RB, d_model, s_q, d_inner, l16, s_qsum);
+        const int* dot = dd.v;
         if (i < nb && l16 < B) {
           const int b = l16;
-          const float v = proj_out(dot[b], s_xs[b], h2f(sc[row]), la + row * 16, h2f(las[row]), s_t + b * 16);
+          const float v = proj_out(dot[b], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
           const int ch = d_inner + pl.bc0 + row;
           const float s0 = cst[(b * 3 + 0) * nb + row], s1 = cst[(b * 3 + 1) * nb + row],
                       s2 = cst[(b * 3 + 2) * nb + row];
@@ -654,17 +650,16 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
     }
     // ---------------- beta: out_proj rows
     float w_out[KO];
-    typename RankBytes<KO>::T lb_out[DFSSM_RANK];
+    typename RankHalves<KO>::T lb_out[DFSSM_RANK];
     {
       const int k0 = tid * KO;
 #pragma unroll
       for (int j = 0; j < KO; ++j) w_out[j] = __ldg(L.norm_w + k0 + j);
-      load_lora_b<KO>(L.out.lB, d_inner, lb_out);
+      load_lora_b<KO>(L.out.B16, d_inner, lb_out);
     }
     stamp(P, tb + 6);
     grid_barrier(P, nbar);  // gated complete
     stamp(P, tb + 7);
-    if (tid < 16) s_lbs[tid] = h2f(L.out.lBs[tid]);
     {
       float vals[B][KO];
 #pragma unroll
@@ -674,20 +669,19 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         for (int j = 0; j < KO; ++j) vals[b][j] = h2f(__ldcg(g + j));
       }
       __syncthreads();
-      prep_rows<B, KO>(vals, w_out, d_inner, lb_out, s_lbs, s_q, d_inner, s_xs, s_qsum, s_t, red);
+      prep_rows<B, KO>(vals, w_out, d_inner, lb_out, s_q, d_inner, s_xs, s_qsum, s_t, red);
     }
     if (pl.no > 0) {
       const int RBO = d_inner / 8;
       const __half* sc = reinterpret_cast<const __half*>(st + P.lay.out_scale);
-      const int8_t* la = reinterpret_cast<const int8_t*>(st + P.lay.out_lA);
-      const __half* las = reinterpret_cast<const __half*>(st + P.lay.out_lAs);
+      const __half* la = reinterpret_cast<const __half*>(st + P.lay.out_lA);
       for (int i = hw; i < ((pl.no + 1) & ~1); i += 2 * kWarps) {
         const int row = i < pl.no ? i : pl.no - 1;
-        int dot[B];
-        row_dot<B>(st + P.lay.out_bits + (size_t)row * RBO, d_inner, s_q, d_inner, l16, s_qsum, dot);
+        const Dots<B> dd = row_dot<B>(st + P.lay.out_bits + (size_t)row * RBO, d_inner, s_q, d_inner, l16, s_qsum);
+        const int* dot = dd.v;
         if (i < pl.no && l16 < B) {
           const int b = l16;
-          const float v = proj_out(dot[b], s_xs[b], h2f(sc[row]), la + row * 16, h2f(las[row]), s_t + b * 16);
+          const float v = proj_out(dot[b], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
           const int o = pl.o0 + row;
           P.x_g[(size_t)b * d_model + o] = f2h(h2f(s_x[b * d_model + o]) + v);
         }
@@ -759,7 +753,8 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         for (int u = 0; u < CPL; ++u) {
           const int c = lane + 32 * u;
           if (c >= C) continue;
-          const unsigned w4[4] = {ev[r][u].x, ev[r][u].y, ev[r][u].z, ev[r][u].w};
+          const unsigned w4[4] = {ev[r][u].x ^ 0x80808080u, ev[r][u].y ^ 0x80808080u, ev[r][u].z ^ 0x80808080u,
+                                  ev[r][u].w ^ 0x80808080u};
 #pragma unroll
           for (int b = 0; b < B; ++b) {
             const float4* xv = reinterpret_cast<const float4*>(s_no + b * d_model + c * 16);
@@ -767,10 +762,10 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const float4 xx = xv[q];
-              a = fmaf((float)(int8_t)(w4[q] & 0xff), xx.x, a);
-              a = fmaf((float)(int8_t)((w4[q] >> 8) & 0xff), xx.y, a);
-              a = fmaf((float)(int8_t)((w4[q] >> 16) & 0xff), xx.z, a);
-              a = fmaf((float)(int8_t)(w4[q] >> 24), xx.w, a);
+              a = fmaf(i8_to_f(w4[q], 0), xx.x, a);
+              a = fmaf(i8_to_f(w4[q], 1), xx.y, a);
+              a = fmaf(i8_to_f(w4[q], 2), xx.z, a);
+              a = fmaf(i8_to_f(w4[q], 3), xx.w, a);
             }
             acc[b] = a;
           }
@@ -908,24 +903,34 @@ int build_plan(const dfssm_engine* e, int B, int grid, std::vector<CtaPlan>& pla
     }
   }
   const int RB = d.d_model / 8, RBO = d.d_inner / 8;
+  for (CtaPlan& p : plans) {
+    long long tx = 0;
+    if (p.role == 0)
+      tx += (long long)(2 * p.np + 1) * RB + 2 * p.np * (2 + 32) + p.np * 8 + p.np * 2 +
+            (long long)B * p.np * DFSSM_DSTATE * 4 + 3LL * B * p.np * 4;
+    else if (p.role == 1)
+      tx += (long long)p.nbc * RB + p.nbc * (2 + 32) + p.nbc * 8 + p.nbc * 2 + 3LL * B * p.nbc * 4;
+    if (p.no > 0) tx += (long long)p.no * RBO + p.no * (2 + 32);
+    p.tx = (int)tx;
+  }
   const int rows_in = (2 * np + 1) > max_nbc ? (2 * np + 1) : max_nbc;
   const int ch = np > max_nbc ? np : max_nbc;
   auto a16 = [](int x) { return (x + 15) & ~15; };
   int off = 0;
   lay.in_bits = off; off += a16(rows_in * RB);
   lay.in_scale = off; off += a16(2 * ch * 2);
-  lay.in_lA = off; off += a16(2 * ch * 16);
-  lay.in_lAs = off; off += a16(2 * ch * 2);
+  lay.in_lA = off; off += a16(2 * ch * 32);  // fp16 LoRA A rows
+  lay.in_lAs = off;
   lay.conv_w = off; off += a16(ch * 8);
   lay.conv_b = off; off += a16(ch * 2);
   lay.out_bits = off; off += a16(max_no * RBO);
   lay.out_scale = off; off += a16(max_no * 2);
-  lay.out_lA = off; off += a16(max_no * 16);
-  lay.out_lAs = off; off += a16(max_no * 2);
+  lay.out_lA = off; off += a16(max_no * 32);
+  lay.out_lAs = off;
   lay.state = off; off += a16(B * np * DFSSM_DSTATE * 4);
   lay.cstate = off; off += a16(B * 3 * ch * 4);
   lay.stage_bytes = (off + 127) & ~127;
-  const int misc_floats = (kWarps + 1) * (B * 16 + B) + B * 16 + B + B + 16 + B * 64 * 2 + B + B * 256 + 4 + 17;
+  const int misc_floats = (kWarps + 1) * (B * 16 + B) + B * 16 + B + B + 16 + B * 64 * 2 + B + B * 256 + 4 + 17 + 4;
   int work = B * d.d_model * 2 + B * d.d_inner + misc_floats * 4;
   work = (work + 127) & ~127;
   const int ring_off = work + 128;  // 8 mbarriers live just below the ring

@@ -7,10 +7,8 @@ namespace dfssm {
 struct ProjW {
   const uint32_t* bits;  // [N][K/32] packed signs (bit b of word j <-> column 32j+b)
   const __half* scale;   // [N]
-  const int8_t* lA;      // [N][16]
-  const __half* lAs;     // [N]
-  const int8_t* lB;      // [16][K]
-  const __half* lBs;     // [16]
+  const __half* A16;     // [N][16] LoRA A dequantised at load: fp16(lora_A[n][r] * lora_A_scale[n])
+  const __half* B16;     // [16][K] LoRA B dequantised at load: fp16(lora_B[r][k] * lora_B_scale[r])
   int N, K;
 };
 

@@ -62,8 +62,8 @@ def test_conv_step(lib, B):
     dev = torch.device("cuda")
     ts = torch.from_numpy(np.ascontiguousarray(state.transpose(0, 2, 1))).to(dev)  # tap-major
     tx = torch.from_numpy(xbc).to(dev)
-    _lib.check(lib.dfssm_conv_step(ptr(ts), ptr(tx), D, ptr(torch.from_numpy(w).to(dev)),
-                                   ptr(torch.from_numpy(b).to(dev)), B, D, stream()))
+    tw, tb = torch.from_numpy(w).to(dev), torch.from_numpy(b).to(dev)  # keep alive across the launch
+    _lib.check(lib.dfssm_conv_step(ptr(ts), ptr(tx), D, ptr(tw), ptr(tb), B, D, stream()))
     torch.cuda.synchronize()
     st = state.copy()
     ref = O.conv_step(st, xbc, w, b)
