@@ -74,7 +74,7 @@ struct PParams {
   unsigned long long* trace;  // optional: per-CTA globaltimer stamps (kTraceStride entries per CTA)
 };
 
-constexpr int kTracePerLayer = 8;
+constexpr int kTracePerLayer = 12;
 __device__ __forceinline__ void stamp(const PParams& P, int idx) {
   if (P.trace && threadIdx.x == 0) {
     unsigned long long t;
@@ -528,6 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         reinterpret_cast<uint4*>(s_x)[i] = __ldcg(reinterpret_cast<const uint4*>(P.x_g) + i);
       __syncthreads();
     }
+    stamp(P, tb + 2);
     {
       float vals[B][KI];
 #pragma unroll
@@ -536,9 +537,9 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         for (int j = 0; j < KI; ++j) vals[b][j] = h2f(s_x[b * d_model + tid * KI + j]);
       prep_rows<B, KI>(vals, w_in, d_model, lb_in, s_q, d_inner, s_xs, s_qsum, s_t, red);
     }
-    stamp(P, tb + 2);
-    wait_stage(P, bars, layer);
     stamp(P, tb + 3);
+    wait_stage(P, bars, layer);
+    stamp(P, tb + 4);
     const int RB = d_model / 8;
     if (pl.role == 0) {
       const int np = pl.np, nrows = 2 * np + 1;
@@ -576,10 +577,10 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         }
       }
       __syncthreads();
-      stamp(P, tb + 4);
+      stamp(P, tb + 6);
       // wait for every B/C CTA of this layer, then fetch conv'd B and C
       wait_counter(P.sync + 2, (unsigned)(layer - P.l0 + 1) * P.n_bc, P.sync + 3, 4u);
-      stamp(P, tb + 5);
+      stamp(P, tb + 6);
       for (int i = tid; i < B * 2 * DFSSM_DSTATE; i += kThreads) s_bc[i] = h2f(__ldcg(P.bc_g + i));
       __syncthreads();
       // SSM state update + gate; warp w owns rows p = w*RPW.., lane owns n = 4*lane..
@@ -648,6 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         red_release_add(P.sync + 2, 1u);
       }
     }
+    stamp(P, tb + 7);
     // ---------------- beta: out_proj rows
     float w_out[KO];
     typename RankHalves<KO>::T lb_out[DFSSM_RANK];
@@ -657,9 +659,9 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
       for (int j = 0; j < KO; ++j) w_out[j] = __ldg(L.norm_w + k0 + j);
       load_lora_b<KO>(L.out.B16, d_inner, lb_out);
     }
-    stamp(P, tb + 6);
+    stamp(P, tb + 8);
     grid_barrier(P, nbar);  // gated complete
-    stamp(P, tb + 7);
+    stamp(P, tb + 9);
     {
       float vals[B][KO];
 #pragma unroll
@@ -671,6 +673,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
       __syncthreads();
       prep_rows<B, KO>(vals, w_out, d_inner, lb_out, s_q, d_inner, s_xs, s_qsum, s_t, red);
     }
+    stamp(P, tb + 10);
     if (pl.no > 0) {
       const int RBO = d_inner / 8;
       const __half* sc = reinterpret_cast<const __half*>(st + P.lay.out_scale);
@@ -688,6 +691,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
       }
     }
     __syncthreads();
+    stamp(P, tb + 11);
   }
 
   // ---------------- final norm + LM head + argmax
@@ -732,6 +736,14 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
     constexpr int CPL = KI;
     const int C = d_model >> 4;
     const int vend = pl.v0 + pl.nv;
+    // batch 1: this lane's KI*16 normalised activations stay in registers for all rows
+    float xr[B == 1 ? KI : 1][16];
+    if (B == 1) {
+#pragma unroll
+      for (int u = 0; u < (B == 1 ? KI : 1); ++u)
+#pragma unroll
+        for (int q = 0; q < 16; ++q) xr[u][q] = s_no[(lane + 32 * u) * 16 + q];
+    }
     for (int v = pl.v0 + 2 * wid; v < vend; v += 2 * kWarps) {
       uint4 ev[2][CPL];
 #pragma unroll
@@ -755,19 +767,31 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
           if (c >= C) continue;
           const unsigned w4[4] = {ev[r][u].x ^ 0x80808080u, ev[r][u].y ^ 0x80808080u, ev[r][u].z ^ 0x80808080u,
                                   ev[r][u].w ^ 0x80808080u};
-#pragma unroll
-          for (int b = 0; b < B; ++b) {
-            const float4* xv = reinterpret_cast<const float4*>(s_no + b * d_model + c * 16);
-            float a = acc[b];
+          if (B == 1) {
+            float a = acc[0];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              const float4 xx = xv[q];
-              a = fmaf(i8_to_f(w4[q], 0), xx.x, a);
-              a = fmaf(i8_to_f(w4[q], 1), xx.y, a);
-              a = fmaf(i8_to_f(w4[q], 2), xx.z, a);
-              a = fmaf(i8_to_f(w4[q], 3), xx.w, a);
+              a = fmaf(i8_to_f(w4[q], 0), xr[B == 1 ? u : 0][4 * q + 0], a);
+              a = fmaf(i8_to_f(w4[q], 1), xr[B == 1 ? u : 0][4 * q + 1], a);
+              a = fmaf(i8_to_f(w4[q], 2), xr[B == 1 ? u : 0][4 * q + 2], a);
+              a = fmaf(i8_to_f(w4[q], 3), xr[B == 1 ? u : 0][4 * q + 3], a);
             }
-            acc[b] = a;
+            acc[0] = a;
+          } else {
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+              const float4* xv = reinterpret_cast<const float4*>(s_no + b * d_model + c * 16);
+              float a = acc[b];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float4 xx = xv[q];
+                a = fmaf(i8_to_f(w4[q], 0), xx.x, a);
+                a = fmaf(i8_to_f(w4[q], 1), xx.y, a);
+                a = fmaf(i8_to_f(w4[q], 2), xx.z, a);
+                a = fmaf(i8_to_f(w4[q], 3), xx.w, a);
+              }
+              acc[b] = a;
+            }
           }
         }
         const int vr = v + r;

@@ -102,9 +102,11 @@ int dfssm_layer_step(dfssm_engine* e, int layer, void* stream);
 /* Diagnostics (no counterpart in the reference, which has no profiler hooks): number of
  * uint64 entries of a persistent-step trace, and one persistent decode step (mode 3 batch)
  * that records %globaltimer stamps at its phase boundaries into trace_dev
- * [sm_count][4 + 8 * n_layer]: [0] start, [1] end, [2 + 8l + k] layer l phase k
- * (0 alpha entry, 1 after the x barrier, 2 after norm/quant, 3 after the weight ring wait,
- *  4 after the in_proj GEMV, 5 after the B/C wait, 6 before the gated barrier, 7 after it). */
+ * [sm_count][4 + 12 * n_layer]: [0] start, [1] end, [2 + 12l + k] layer l point k
+ * (0 alpha entry, 1 after the x barrier, 2 after loading x, 3 after norm/quant/LoRA,
+ *  4 after the weight ring wait, 5 after the in_proj GEMV, 6 after the B/C wait, 7 after the
+ *  SSM, 8 before the gated barrier, 9 after it, 10 after the beta norm/quant/LoRA,
+ *  11 after the out_proj GEMV); [2 + 12 n_layer] head entry, [3 + 12 n_layer] after its barrier. */
 size_t dfssm_trace_entries(const dfssm_engine* e);
 int dfssm_trace_step(dfssm_engine* e, unsigned long long* trace_dev, void* stream);
 
