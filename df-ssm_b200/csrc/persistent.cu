@@ -71,6 +71,7 @@ struct PParams {
   int n_bc;        // number of B/C CTAs
   int ns;          // ring stages
   int ring_off;    // byte offset of the ring in dynamic smem
+  int tab_off;     // byte offset of the per-layer tables in dynamic smem
   unsigned long long* trace;  // optional: per-CTA globaltimer stamps (kTraceStride entries per CTA)
 };
 
@@ -165,13 +166,13 @@ __device__ __forceinline__ void wait_stage(const PParams& P, uint64_t* bars, int
 // 16); the byte total of a stage is precomputed on the host (CtaPlan::tx).
 template <int B>
 __device__ __noinline__ void issue_stage(const PParams& P, const CtaPlan& pl, int layer, unsigned char* ring,
-                                         uint64_t* bars) {
+                                         uint64_t* bars, const LayerW* layers) {
   if (layer >= P.l1 || threadIdx.x >= 32) return;
   const int i = threadIdx.x;
   const int slot = (layer - P.l0) % P.ns;
   unsigned char* st = ring + (size_t)slot * P.lay.stage_bytes;
   uint64_t* bar = bars + slot;
-  const LayerW& L = P.layers[layer];
+  const LayerW& L = layers[layer];
   const Layout& Y = P.lay;
   const int RB = P.d_model / 8, RBO = P.d_inner / 8;
   const void* s_ = nullptr;
@@ -474,6 +475,11 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
   float* s_bc = s_dt + B;                           // [B][2*d_state] (fp32)
   float* s_hp = s_bc + B * 2 * DFSSM_DSTATE;        // [4] dt_bias, A_log, D, dt-row scale
   float* s_dtla = s_hp + 4;                         // 16 fp16 dt-row LoRA-A values
+  // per-layer tables copied once at kernel start (no dependent global loads inside the loop):
+  // the layer pointer table, and this CTA's head scalars (dt_bias, A_log, D, dt-row scale,
+  // 16 fp16 dt-row LoRA-A values) for every layer
+  LayerW* s_layers = reinterpret_cast<LayerW*>(smem + P.tab_off);
+  float* s_hptab = reinterpret_cast<float*>(smem + P.tab_off + ((P.n_layer * (int)sizeof(LayerW) + 15) & ~15));  // [n_layer][12], 16-byte aligned
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.ring_off - 8 * 8);
   unsigned char* ring = smem + P.ring_off;
 
@@ -487,7 +493,27 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
   }
   __syncthreads();
   stamp(P, 0);
-  for (int l = 0; l < P.ns - 1; ++l) issue_stage<B>(P, pl, P.l0 + l, ring, bars);
+  {
+    const int nw = P.n_layer * (int)sizeof(LayerW) / 8;
+    for (int i = tid; i < nw; i += kThreads)
+      reinterpret_cast<unsigned long long*>(s_layers)[i] = reinterpret_cast<const unsigned long long*>(P.layers)[i];
+    if (pl.role == 0) {
+      for (int l = tid; l < P.n_layer; l += kThreads) {
+        const LayerW& G = P.layers[l];
+        const int dtrow = d_inner + P.d_xbc + pl.h;
+        float* e = s_hptab + l * 12;
+        e[0] = G.dt_bias[pl.h];
+        e[1] = G.A_log[pl.h];
+        e[2] = G.Dp[pl.h];
+        e[3] = h2f(G.in.scale[dtrow]);
+        const uint4* a16 = reinterpret_cast<const uint4*>(G.in.A16 + (size_t)dtrow * 16);
+        reinterpret_cast<uint4*>(e + 4)[0] = a16[0];
+        reinterpret_cast<uint4*>(e + 4)[1] = a16[1];
+      }
+    }
+  }
+  __syncthreads();
+  for (int l = 0; l < P.ns - 1; ++l) issue_stage<B>(P, pl, P.l0 + l, ring, bars, s_layers);
 
   // embedding gather (every CTA needs the full x of the first layer)
   for (int i = tid; i < B * d_model && !P.from_x; i += kThreads) {
@@ -499,8 +525,8 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
   __syncthreads();
 
   for (int layer = P.l0; layer < P.l1; ++layer) {
-    const LayerW& L = P.layers[layer];
-    issue_stage<B>(P, pl, layer + P.ns - 1, ring, bars);
+    const LayerW& L = s_layers[layer];
+    issue_stage<B>(P, pl, layer + P.ns - 1, ring, bars, s_layers);
     unsigned char* st = ring + (size_t)((layer - P.l0) % P.ns) * P.lay.stage_bytes;
     // ---------------- alpha: per-thread weights are loaded before waiting for x
     float w_in[KI];
@@ -510,14 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
 #pragma unroll
       for (int j = 0; j < KI; ++j) w_in[j] = __ldg(L.ln_w + k0 + j);
       load_lora_b<KI>(L.in.B16, d_model, lb_in);
-      if (pl.role == 0 && tid == 32) {
-        s_hp[0] = L.dt_bias[pl.h];
-        s_hp[1] = L.A_log[pl.h];
-        s_hp[2] = L.Dp[pl.h];
-        const int dtrow = d_inner + P.d_xbc + pl.h;
-        s_hp[3] = h2f(L.in.scale[dtrow]);
-        for (int r = 0; r < 16; ++r) reinterpret_cast<__half*>(s_dtla)[r] = L.in.A16[(size_t)dtrow * 16 + r];
-      }
+
     }
     const int tb = 2 + kTracePerLayer * layer;
     stamp(P, tb + 0);
@@ -558,7 +577,8 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
           if (row < 2 * np) {
             v = proj_out(dot[b], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
           } else {
-            v = proj_out(dot[b], s_xs[b], s_hp[3], reinterpret_cast<const __half*>(s_dtla), s_t + b * 16);
+            const float* hp = s_hptab + layer * 12;
+            v = proj_out(dot[b], s_xs[b], hp[3], reinterpret_cast<const __half*>(hp + 4), s_t + b * 16);
           }
           if (row < np) {
             s_z[b * 64 + row] = v;
@@ -587,11 +607,12 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
       const int RPW = np / kWarps;
       const float* sst = reinterpret_cast<const float*>(st + P.lay.state);
 #pragma unroll
+      const float* hp = s_hptab + layer * 12;
       for (int b = 0; b < B; ++b) {
-        float dtv = s_dt[b] + s_hp[0];
+        float dtv = s_dt[b] + hp[0];
         dtv = log1pf(expf(dtv));
-        const float Abar = expf(dtv * (-expf(s_hp[1])));
-        const float Dh = s_hp[2];
+        const float Abar = expf(dtv * (-expf(hp[1])));
+        const float Dh = hp[2];
         const float* bb = s_bc + b * 256 + lane * 4;
         const float4 Bn = make_float4(bb[0], bb[1], bb[2], bb[3]);
         const float4 Cn = make_float4(bb[128], bb[129], bb[130], bb[131]);
@@ -667,8 +688,15 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
 #pragma unroll
       for (int b = 0; b < B; ++b) {
         const __half* g = P.gated_g + (size_t)b * d_inner + tid * KO;
+        __half hv[KO];
+        if (KO == 8) {
+          *reinterpret_cast<uint4*>(hv) = __ldcg(reinterpret_cast<const uint4*>(g));
+        } else {
 #pragma unroll
-        for (int j = 0; j < KO; ++j) vals[b][j] = h2f(__ldcg(g + j));
+          for (int j = 0; j < KO; ++j) hv[j] = __ldcg(g + j);
+        }
+#pragma unroll
+        for (int j = 0; j < KO; ++j) vals[b][j] = h2f(hv[j]);
       }
       __syncthreads();
       prep_rows<B, KO>(vals, w_out, d_inner, lb_out, s_q, d_inner, s_xs, s_qsum, s_t, red);
@@ -887,7 +915,7 @@ PersistentSet* set_of(const dfssm_engine* e) { return static_cast<PersistentSet*
 // Per-CTA work plans and the ring-stage layout for batch B.  Returns 0 if the dims or the
 // batch are not supported by the persistent kernel.
 int build_plan(const dfssm_engine* e, int B, int grid, std::vector<CtaPlan>& plans, Layout& lay, int& ns,
-               int& smem_total, int& n_bc) {
+               int& smem_total, int& n_bc, int& tab_off) {
   const dfssm_dims& d = e->d;
   if (d.d_model % 512 || d.d_inner % 512) return 0;
   const int KI = d.d_model / 512, KO = d.d_inner / 512;
@@ -957,6 +985,9 @@ int build_plan(const dfssm_engine* e, int B, int grid, std::vector<CtaPlan>& pla
   const int misc_floats = (kWarps + 1) * (B * 16 + B) + B * 16 + B + B + 16 + B * 64 * 2 + B + B * 256 + 4 + 17 + 4;
   int work = B * d.d_model * 2 + B * d.d_inner + misc_floats * 4;
   work = (work + 127) & ~127;
+  tab_off = work;
+  work += ((d.n_layer * (int)sizeof(LayerW) + 15) & ~15) + d.n_layer * 12 * 4;
+  work = (work + 127) & ~127;
   const int ring_off = work + 128;  // 8 mbarriers live just below the ring
   int max_smem = 0;
   cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, e->device);
@@ -987,9 +1018,9 @@ int persistent_init(dfssm_engine* e) {
     if (B > e->max_batch) continue;
     std::vector<CtaPlan> plans;
     Layout lay;
-    int ns = 0, smem = 0, n_bc = 0;
+    int ns = 0, smem = 0, n_bc = 0, tab_off = 0;
     const int grid = e->sm_count;
-    if (!build_plan(e, B, grid, plans, lay, ns, smem, n_bc)) continue;
+    if (!build_plan(e, B, grid, plans, lay, ns, smem, n_bc, tab_off)) continue;
     const dfssm_dims& d = e->d;
     void* fn = pick_kernel(B, d.d_model / 512, d.d_inner / 512);
     if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
@@ -1038,6 +1069,7 @@ int persistent_init(dfssm_engine* e) {
     P.ns = ns;
     P.ring_off = smem - ns * lay.stage_bytes;
     P.trace = nullptr;
+    P.tab_off = tab_off;
     ps.fn = fn;
     ps.smem = smem;
     ps.grid = grid;
