@@ -57,9 +57,11 @@ struct Layout {  // offsets inside the .dfssm image
 
 namespace {
 
+// Automatic mode: the persistent whole-step kernel where it supports the batch and dims
+// (batch <= 2), else the per-op kernels replayed from a CUDA graph.
 int effective_mode(const dfssm_engine* e) {
   if (e->mode != 0) return e->mode;
-  return 1;
+  return persistent_supported(e) ? 3 : 1;
 }
 
 // ------------------------------------------------------------------ kernel launches

@@ -75,7 +75,7 @@ struct PParams {
   unsigned long long* trace;  // optional: per-CTA globaltimer stamps (kTraceStride entries per CTA)
 };
 
-constexpr int kTracePerLayer = 12;
+constexpr int kTracePerLayer = 14;
 __device__ __forceinline__ void stamp(const PParams& P, int idx) {
   if (P.trace && threadIdx.x == 0) {
     unsigned long long t;
@@ -165,7 +165,7 @@ __device__ __forceinline__ void wait_stage(const PParams& P, uint64_t* bars, int
 // Lane i of warp 0 issues copy i of the table below (all 16-byte aligned, sizes multiples of
 // 16); the byte total of a stage is precomputed on the host (CtaPlan::tx).
 template <int B>
-__device__ __noinline__ void issue_stage(const PParams& P, const CtaPlan& pl, int layer, unsigned char* ring,
+__device__ __forceinline__ void issue_stage(const PParams& P, const CtaPlan& pl, int layer, unsigned char* ring,
                                          uint64_t* bars, const LayerW* layers) {
   if (layer >= P.l1 || threadIdx.x >= 32) return;
   const int i = threadIdx.x;
@@ -232,10 +232,9 @@ __device__ __noinline__ void issue_stage(const PParams& P, const CtaPlan& pl, in
       default: break;
     }
   }
-  if (i == 0) {
-    fence_proxy_async();
-    mbar_expect_tx(bar, (unsigned)pl.tx);
-  }
+  // The slot's previous contents were read by this CTA's threads before a __syncthreads that
+  // precedes this call, which orders those reads before the bulk copies below.
+  if (i == 0) mbar_expect_tx(bar, (unsigned)pl.tx);
   __syncwarp();
   if (n_) bulk_g2s(st + d_, s_, n_, bar);
 }
@@ -399,7 +398,7 @@ struct Dots {
 };
 
 template <int B>
-__device__ __noinline__ Dots<B> row_dot(const unsigned char* bits, int K, const int8_t* sq, int Kq, int l16,
+__device__ __forceinline__ Dots<B> row_dot(const unsigned char* bits, int K, const int8_t* sq, int Kq, int l16,
                                         const int* s_qsum) {
   Dots<B> dot;
   int acc[B];
@@ -442,7 +441,7 @@ __device__ __noinline__ Dots<B> row_dot(const unsigned char* bits, int K, const 
 }
 
 // dequant + LoRA up-projection of one output row (reference rounding points)
-__device__ __noinline__ float proj_out(int dot, float xs, float wscale, const __half* A16, const float* t) {
+__device__ __forceinline__ float proj_out(int dot, float xs, float wscale, const __half* A16, const float* t) {
   const float base = round_h(round_h(round_h((float)dot) * xs) * wscale);
   float la = 0.f;
 #pragma unroll
@@ -526,7 +525,9 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
 
   for (int layer = P.l0; layer < P.l1; ++layer) {
     const LayerW& L = s_layers[layer];
+    stamp(P, 2 + kTracePerLayer * layer + 12);
     issue_stage<B>(P, pl, layer + P.ns - 1, ring, bars, s_layers);
+    stamp(P, 2 + kTracePerLayer * layer + 13);
     unsigned char* st = ring + (size_t)((layer - P.l0) % P.ns) * P.lay.stage_bytes;
     // ---------------- alpha: per-thread weights are loaded before waiting for x
     float w_in[KI];
@@ -597,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         }
       }
       __syncthreads();
-      stamp(P, tb + 6);
+      stamp(P, tb + 5);
       // wait for every B/C CTA of this layer, then fetch conv'd B and C
       wait_counter(P.sync + 2, (unsigned)(layer - P.l0 + 1) * P.n_bc, P.sync + 3, 4u);
       stamp(P, tb + 6);

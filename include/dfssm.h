@@ -62,7 +62,7 @@ void dfssm_destroy(dfssm_engine* e);
 int dfssm_get_dims(const dfssm_engine* e, dfssm_dims* out);
 /* Number of sequences decoded by dfssm_step (1..max_batch).  Drops the captured graph. */
 int dfssm_set_batch(dfssm_engine* e, int batch);
-/* Step execution mode: 0 = automatic, 1 = per-op kernels replayed from a CUDA graph,
+/* Step execution mode: 0 = automatic (3 where supported, else 1), 1 = per-op kernels replayed from a CUDA graph,
  * 2 = per-op kernels launched eagerly, 3 = persistent whole-step kernel (batch <= 2, d_model and d_inner multiples of 512). */
 int dfssm_set_mode(dfssm_engine* e, int mode);
 int dfssm_get_mode(const dfssm_engine* e, int* mode);
@@ -102,11 +102,12 @@ int dfssm_layer_step(dfssm_engine* e, int layer, void* stream);
 /* Diagnostics (no counterpart in the reference, which has no profiler hooks): number of
  * uint64 entries of a persistent-step trace, and one persistent decode step (mode 3 batch)
  * that records %globaltimer stamps at its phase boundaries into trace_dev
- * [sm_count][4 + 12 * n_layer]: [0] start, [1] end, [2 + 12l + k] layer l point k
+ * [sm_count][4 + 14 * n_layer]: [0] start, [1] end, [2 + 14l + k] layer l point k
  * (0 alpha entry, 1 after the x barrier, 2 after loading x, 3 after norm/quant/LoRA,
  *  4 after the weight ring wait, 5 after the in_proj GEMV, 6 after the B/C wait, 7 after the
  *  SSM, 8 before the gated barrier, 9 after it, 10 after the beta norm/quant/LoRA,
- *  11 after the out_proj GEMV); [2 + 12 n_layer] head entry, [3 + 12 n_layer] after its barrier. */
+ *  11 after the out_proj GEMV, 12 before and 13 after issuing the layer's weight prefetch);
+ * [2 + 14 n_layer] head entry, [3 + 14 n_layer] after its barrier. */
 size_t dfssm_trace_entries(const dfssm_engine* e);
 int dfssm_trace_step(dfssm_engine* e, unsigned long long* trace_dev, void* stream);
 
