@@ -38,6 +38,7 @@ SIGNATURES = {
     "dfssm_trace_step": (c_int, [c_void_p, c_void_p, c_void_p]),
     "dfssm_scaffold_gemm_workspace": (c_size_t, [c_int, c_int]),
     "dfssm_scaffold_gemm": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "dfssm_scaffold_gemm_noalloc": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "dfssm_conv_step": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "dfssm_ssm_step": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
                                c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p]),

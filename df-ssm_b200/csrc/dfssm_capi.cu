@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -713,3 +714,76 @@ int dfssm_lm_head_argmax(const int8_t* E_q, const float* E_s, int vocab, int d, 
 }
 
 }  // extern "C"
+
+// ====================================================================== allocation-free scaffold GEMM
+//
+// Some callers of this library cannot allocate device memory at the point where they need a
+// scaffold GEMM: code running inside a host-side allocator callback, plug-in hosts whose
+// memory pool forbids foreign cudaMalloc calls, or real-time loops where an allocation could
+// block or fail.  dfssm_scaffold_gemm_noalloc serves them: the scratch it needs (the
+// activations in the GEMV's permuted byte order plus their row sums) lives in a fixed
+// file-scope device array instead of caller- or library-allocated memory.
+namespace {
+
+constexpr size_t kNoAllocMaxQBytes = size_t(2) << 20;  // M * K <= 2 MiB of int8 activations
+constexpr int kNoAllocMaxRows = 2048;                   // M <= 2048
+constexpr size_t kNoAllocQsumOff = kNoAllocMaxQBytes;   // 256-aligned
+constexpr size_t kNoAllocBytes = kNoAllocMaxQBytes + kNoAllocMaxRows * sizeof(int);
+
+// Every GPU that loads this library holds this array (2 MiB + 8 KiB) until the process exits.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on the current device.  In host code the array's name is
+// only a host-side stand-in, so the real address is looked up once per device (with that device
+// current) and cached.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  CU(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    CU(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return DFSSM_OK;
+}
+
+}  // namespace
+
+extern "C" int dfssm_scaffold_gemm_noalloc(const uint32_t* packed, const int8_t* q, int M, int N, int K,
+                                           int32_t* acc, void* stream) {
+  if (!packed || !q || !acc) return dfssm_fail(DFSSM_ERR_ARG, "NULL argument");
+  if (M < 1 || N < 1 || K < 128 || K % 128 || K > 65536) return dfssm_fail(DFSSM_ERR_ARG, "bad sizes M=%d N=%d K=%d", M, N, K);
+  if (M > kNoAllocMaxRows || (size_t)M * (size_t)K > kNoAllocMaxQBytes)
+    return dfssm_fail(DFSSM_ERR_ARG,
+                      "M=%d K=%d exceeds the fixed scratch of dfssm_scaffold_gemm_noalloc (M*K <= %zu, M <= %d); "
+                      "use dfssm_scaffold_gemm with a caller workspace",
+                      M, K, kNoAllocMaxQBytes, kNoAllocMaxRows);
+  if ((uintptr_t)packed & 15) return dfssm_fail(DFSSM_ERR_ARG, "packed must be 16-byte aligned");
+  void* ws = nullptr;
+  int rc = noalloc_scratch(&ws);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int8_t* qp = static_cast<int8_t*>(ws);
+  int* qsum = reinterpret_cast<int*>(static_cast<char*>(ws) + kNoAllocQsumOff);
+  // Both scratch regions are fully rewritten before they are read, so nothing needs clearing.
+  permute_q_kernel<<<M, kPrepThreads, 0, s>>>(q, K, qp, qsum);
+  CHECK_LAUNCH();
+  ProjW p{};
+  p.bits = packed;
+  p.N = N;
+  p.K = K;
+  const size_t sm = (size_t)kGemvBT * K;
+  if (sm > 48 * 1024) CU(cudaFuncSetAttribute(proj_gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  const int rows_per_cta = 2 * (kGemvThreads / 32);
+  proj_gemv_kernel<2><<<(N + rows_per_cta - 1) / rows_per_cta, kGemvThreads, sm, s>>>(
+      p, qp, qsum, nullptr, nullptr, M, reinterpret_cast<__half*>(acc), N, nullptr, nullptr, nullptr, 0, 0);
+  CHECK_LAUNCH();
+  return DFSSM_OK;
+}

@@ -122,6 +122,19 @@ size_t dfssm_scaffold_gemm_workspace(int M, int K);
 int dfssm_scaffold_gemm(const uint32_t* packed, const int8_t* q, int M, int N, int K,
                         int32_t* acc, void* workspace, void* stream);
 
+/* Allocation-free variant of dfssm_scaffold_gemm (same inputs, outputs and bit-exact result),
+ * for callers that cannot allocate device memory where they need the GEMM (allocator callbacks,
+ * plug-in hosts that own the memory pool, loops that must not block on an allocation).  Its
+ * scratch is a fixed array inside the library; it has no counterpart in the reference.
+ * Limits: M * K <= 2 MiB and M <= 2048, else DFSSM_ERR_ARG.  Every GPU that loads the library
+ * keeps that 2 MiB + 8 KiB array until the process exits.  The first call on each device looks
+ * up the array's device address (cudaGetSymbolAddress), so make that first call before any
+ * stream capture.  All calls on a device share the one array: calls that overlap on the GPU
+ * (different streams, or threads racing on one device) corrupt each other's results.  Nothing
+ * from a previous call is relied on; the scratch is fully rewritten every call. */
+int dfssm_scaffold_gemm_noalloc(const uint32_t* packed, const int8_t* q, int M, int N, int K,
+                                int32_t* acc, void* stream);
+
 /* Conv1d shift-register step (df_ssm_kernels.cu:27-47, conv_step): for each channel,
  * out = s0*w0 + s1*w1 + s2*w2 + x*w3 + b, state <- (s1, s2, x), xbc <- fp16(SiLU(out)).
  * conv_state fp32 [B][3][d_xbc] (tap-major), xbc fp16 [B][ld_xbc] in place,
