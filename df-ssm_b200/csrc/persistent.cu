@@ -108,7 +108,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
 }
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -473,7 +472,6 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
   float* s_dt = s_xc + B * 64;                      // [B]
   float* s_bc = s_dt + B;                           // [B][2*d_state] (fp32)
   float* s_hp = s_bc + B * 2 * DFSSM_DSTATE;        // [4] dt_bias, A_log, D, dt-row scale
-  float* s_dtla = s_hp + 4;                         // 16 fp16 dt-row LoRA-A values
   // per-layer tables copied once at kernel start (no dependent global loads inside the loop):
   // the layer pointer table, and this CTA's head scalars (dt_bias, A_log, D, dt-row scale,
   // 16 fp16 dt-row LoRA-A values) for every layer
@@ -607,8 +605,8 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
       // SSM state update + gate; warp w owns rows p = w*RPW.., lane owns n = 4*lane..
       const int RPW = np / kWarps;
       const float* sst = reinterpret_cast<const float*>(st + P.lay.state);
-#pragma unroll
       const float* hp = s_hptab + layer * 12;
+#pragma unroll
       for (int b = 0; b < B; ++b) {
         float dtv = s_dt[b] + hp[0];
         dtv = log1pf(expf(dtv));
