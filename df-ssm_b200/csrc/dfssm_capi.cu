@@ -82,9 +82,44 @@ int gemv_grid(const dfssm_engine* e, int N) {
   return g < 1 ? 1 : g;
 }
 
+// Tensor-core projection for batches of 8 or more: RG row groups of 16 per CTA (2 for the wide
+// in_proj, 1 for out_proj so that enough CTAs exist), K split over the remaining warps.
+constexpr int kMmaMinBatch = 8;
+inline bool mma_ok(int K, int RG) {
+  const int KS = (kMmaThreads / 32) / RG;
+  return K % 128 == 0 && ((K / 32) % KS) == 0 && ((K / 32 / KS) % 4) == 0;
+}
+// Row groups per CTA for an N x K projection (0 = no tensor-core configuration fits).
+inline int mma_rg(int N, int K) {
+  const int pref = N >= 4096 ? 2 : 1, other = 3 - pref;
+  return mma_ok(K, pref) ? pref : (mma_ok(K, other) ? other : 0);
+}
+
+template <int MODE>
+int launch_mma(const ProjW& p, int B, const int8_t* q, const int* qsum, const __half* xs, const __half* t, void* out,
+               int ld_out, float* conv_state, const __half* conv_w, const __half* conv_b, int d_inner, int d_xbc,
+               cudaStream_t s) {
+  const int RG = mma_rg(p.N, p.K);
+  const size_t sm = proj_mma_smem(p.K, RG);
+  if (RG == 2) {
+    CU(cudaFuncSetAttribute(proj_mma_kernel<MODE, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    proj_mma_kernel<MODE, 2><<<(p.N + 31) / 32, kMmaThreads, sm, s>>>(p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out),
+                                                                     ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc);
+  } else {
+    CU(cudaFuncSetAttribute(proj_mma_kernel<MODE, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    proj_mma_kernel<MODE, 1><<<(p.N + 15) / 16, kMmaThreads, sm, s>>>(p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out),
+                                                                     ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc);
+  }
+  CHECK_LAUNCH();
+  return DFSSM_OK;
+}
+
 template <int MODE>
 int launch_gemv(dfssm_engine* e, const ProjW& p, int B, const int8_t* q, const int* qsum, const __half* xs,
                 const __half* t, void* out, int ld_out, float* conv_state, const LayerW* L, cudaStream_t s) {
+  if (B >= kMmaMinBatch && mma_rg(p.N, p.K))
+    return launch_mma<MODE>(p, B, q, qsum, xs, t, out, ld_out, conv_state, L ? L->conv_w : nullptr,
+                            L ? L->conv_b : nullptr, e->d.d_inner, e->d.d_xbc, s);
   const size_t sm = (size_t)kGemvBT * p.K;
   proj_gemv_kernel<MODE><<<gemv_grid(e, p.N), kGemvThreads, sm, s>>>(
       p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out), ld_out, conv_state, L ? L->conv_w : nullptr,
@@ -651,6 +686,8 @@ int dfssm_scaffold_gemm(const uint32_t* packed, const int8_t* q, int M, int N, i
   p.bits = packed;
   p.N = N;
   p.K = K;
+  if (M >= kMmaMinBatch && mma_rg(N, K))
+    return launch_mma<2>(p, M, qp, qsum, nullptr, nullptr, acc, N, nullptr, nullptr, nullptr, 0, 0, s);
   const size_t sm = (size_t)kGemvBT * K;
   if (sm > 48 * 1024) CU(cudaFuncSetAttribute(proj_gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
   const int rows_per_cta = 2 * (kGemvThreads / 32);

@@ -234,6 +234,139 @@ proj_gemv_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ 
 }
 
 // ---------------------------------------------------------------------------------------
+// proj_mma: the same projection as proj_gemv on int8 tensor cores, for batches of 8 or more.
+// mma.sync m16n8k32 (s8 x s8 -> s32) with the weights on the M side: a warp owns 16 output rows
+// and a slice of K, and the batch rows are the N side (NT tiles of 8).  The A fragment of row r
+// for 32 columns is built straight from the packed word w of those columns: register
+// (w >> j) & 0x01010101 holds the 0/1 signs of columns {j, 8+j, 16+j, 24+j}, which is exactly
+// the permuted activation int j of that word (qperm_index), so lane (g, c) uses j = c and c + 4.
+// sum_k s_k q_k = 2 * sum_{bit=1} q_k - sum_k q_k as in proj_gemv; the K slices of a CTA's warps
+// are added exactly in int32 through shared memory before the shared epilogue.
+// Activation rows sit in shared memory with a stride of K + 16 bytes (bank-conflict-free B loads).
+// ---------------------------------------------------------------------------------------
+constexpr int kMmaThreads = 256;
+constexpr int kMmaNT = 4;  // batch tiles of 8 per pass (32 rows)
+
+__device__ __forceinline__ void mma_s8(int (&d)[4], unsigned a0, unsigned a1, unsigned a2, unsigned a3, unsigned b0,
+                                       unsigned b1) {
+  asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+               : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <int MODE, int RG>
+__global__ void __launch_bounds__(kMmaThreads)
+proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ qsum,
+                const __half* __restrict__ xs, const __half* __restrict__ t, int B,
+                __half* __restrict__ out, int ld_out,
+                float* __restrict__ conv_state, const __half* __restrict__ conv_w,
+                const __half* __restrict__ conv_b, int d_inner, int d_xbc) {
+  constexpr int KS = (kMmaThreads / 32) / RG;  // K slices per CTA
+  constexpr int NB = 8 * kMmaNT;               // batch rows per pass
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int K = p.K, N = p.N, W = K >> 5;
+  const int SQ = K + 16;                                         // padded activation row stride
+  int8_t* sq = reinterpret_cast<int8_t*>(smem);                  // [NB][SQ]
+  int* red = reinterpret_cast<int*>(smem + NB * SQ);             // [KS][16*RG][NB]
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
+  const int rg = wid % RG, ks = wid / RG;
+  const int row0 = blockIdx.x * 16 * RG;
+  const int wr = row0 + rg * 16;                                 // this warp's first row
+  const int wpw = W / KS, kw0 = ks * wpw;                        // words per warp slice
+  const int ra = min(wr + g, N - 1), rb = min(wr + g + 8, N - 1);
+  const uint4* pa = reinterpret_cast<const uint4*>(p.bits + (size_t)ra * W);
+  const uint4* pb = reinterpret_cast<const uint4*>(p.bits + (size_t)rb * W);
+
+  for (int bt0 = 0; bt0 < B; bt0 += NB) {
+    const int nb = min(NB, B - bt0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < NB * (K / 16); i += kMmaThreads) {
+      const int b = i / (K / 16), u = i - b * (K / 16);
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (b < nb) v = *reinterpret_cast<const uint4*>(q + (size_t)(bt0 + b) * K + u * 16);
+      *reinterpret_cast<uint4*>(sq + b * SQ + u * 16) = v;
+    }
+    __syncthreads();
+    int acc[kMmaNT][4];
+#pragma unroll
+    for (int tt = 0; tt < kMmaNT; ++tt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[tt][i] = 0;
+    for (int kw = kw0; kw < kw0 + wpw; kw += 4) {
+      const uint4 va = ldg_stream(pa + (kw >> 2));
+      const uint4 vb = ldg_stream(pb + (kw >> 2));
+      const unsigned wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const unsigned a0 = (wa[j] >> c) & 0x01010101u, a2 = (wa[j] >> (c + 4)) & 0x01010101u;
+        const unsigned a1 = (wb[j] >> c) & 0x01010101u, a3 = (wb[j] >> (c + 4)) & 0x01010101u;
+#pragma unroll
+        for (int tt = 0; tt < kMmaNT; ++tt) {
+          const int8_t* qb = sq + (tt * 8 + g) * SQ + (kw + j) * 32;
+          const unsigned b0 = *reinterpret_cast<const unsigned*>(qb + c * 4);
+          const unsigned b1 = *reinterpret_cast<const unsigned*>(qb + (c + 4) * 4);
+          mma_s8(acc[tt], a0, a1, a2, a3, b0, b1);
+        }
+      }
+    }
+    // D fragment: acc[tt][0..1] -> row g, batch cols 2c, 2c+1 of tile tt; [2..3] -> row g+8
+#pragma unroll
+    for (int tt = 0; tt < kMmaNT; ++tt) {
+      int* r = red + (ks * 16 * RG + rg * 16) * NB + tt * 8 + 2 * c;
+      r[g * NB] = acc[tt][0];
+      r[g * NB + 1] = acc[tt][1];
+      r[(g + 8) * NB] = acc[tt][2];
+      r[(g + 8) * NB + 1] = acc[tt][3];
+    }
+    __syncthreads();
+    for (int o = threadIdx.x; o < 16 * RG * NB; o += kMmaThreads) {
+      const int lr = o / NB, bb = o - lr * NB;
+      const int row = row0 + lr, b = bt0 + bb;
+      if (row >= N || bb >= nb) continue;
+      int sacc = 0;
+#pragma unroll
+      for (int k2 = 0; k2 < KS; ++k2) sacc += red[(k2 * 16 * RG + lr) * NB + bb];
+      const int dot = 2 * sacc - qsum[b];
+      if (MODE == 2) {
+        reinterpret_cast<int*>(out)[(size_t)b * ld_out + row] = dot;
+        continue;
+      }
+      const float base = round_h(round_h(round_h((float)dot) * h2f(xs[b])) * h2f(p.scale[row]));
+      const __half* arow = p.A16 + (size_t)row * DFSSM_RANK;
+      const __half* tb = t + b * DFSSM_RANK;
+      float la = 0.f;
+#pragma unroll
+      for (int r = 0; r < DFSSM_RANK; ++r) la = fmaf(h2f(tb[r]), h2f(arow[r]), la);
+      const float v = round_h(base + la);
+      if (MODE == 0) {
+        float res = v;
+        const int ch = row - d_inner;
+        if (ch >= 0 && ch < d_xbc) {
+          float* cs = conv_state + (size_t)b * 3 * d_xbc;
+          const float s0 = cs[ch], s1 = cs[d_xbc + ch], s2 = cs[2 * d_xbc + ch];
+          cs[ch] = s1;
+          cs[d_xbc + ch] = s2;
+          cs[2 * d_xbc + ch] = v;
+          const __half* cw = conv_w + ch * DFSSM_DCONV;
+          const float o2 = s0 * h2f(cw[0]) + s1 * h2f(cw[1]) + s2 * h2f(cw[2]) + v * h2f(cw[3]) + h2f(conv_b[ch]);
+          const float sig = 1.0f / (1.0f + expf(-o2));
+          res = o2 * sig;
+        }
+        out[(size_t)b * ld_out + row] = f2h(res);
+      } else {
+        __half* xo = out + (size_t)b * ld_out + row;
+        *xo = f2h(h2f(*xo) + v);
+      }
+    }
+  }
+}
+
+inline size_t proj_mma_smem(int K, int RG) {
+  const int NB = 8 * kMmaNT, KS = (kMmaThreads / 32) / RG;
+  return (size_t)NB * (K + 16) + (size_t)KS * 16 * RG * NB * 4;
+}
+
+// ---------------------------------------------------------------------------------------
 // ssm_gate: one CTA per (head, batch row); 64 x 128 fp32 state updated in place.
 //   dt = softplus(dt_raw + dt_bias); Abar = exp(dt * -exp(A_log))   df_ssm_kernels.cu:77-79
 //   h  = Abar * h + (x * dt) * B_n;  y = sum_n C_n h + D x           df_ssm_kernels.cu:80-101

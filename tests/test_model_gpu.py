@@ -23,6 +23,7 @@ def _close(got, ref, frac_exact=0.9, rel=1e-2):
 
 
 @pytest.mark.parametrize("B,mode,shape", [(1, "graph", "tiny"), (3, "graph", "tiny"), (17, "graph", "tiny"),
+                                          (17, "graph", "small"), (40, "graph", "small"),
                                           (1, "persistent", "small"), (2, "persistent", "small")])
 def test_single_layer_matches_oracle(B, mode, shape):
     w = weights(shape, 1, seed=2)
@@ -74,7 +75,7 @@ def _check_logits(got, ref):
         assert np.all(np.abs(got[s] - ref[s]) <= 2e-2 + 1e-2 * scale), (s, np.abs(got[s] - ref[s]).max())
 
 
-@pytest.mark.parametrize("B,mode,shape", [(1, "graph", "tiny"), (3, "graph", "tiny"),
+@pytest.mark.parametrize("B,mode,shape", [(1, "graph", "tiny"), (3, "graph", "tiny"), (9, "graph", "small"),
                                           (1, "persistent", "small"), (2, "persistent", "small")])
 def test_tiny_model_matches_oracle(B, mode, shape):
     w = weights(shape, 2, seed=0)
