@@ -151,9 +151,16 @@ int enqueue_head(dfssm_engine* e, cudaStream_t s) {
   const dfssm_dims& d = e->d;
   int rc;
   if ((rc = launch_prep(e, e->x, d.d_model, e->norm_f, 0, nullptr, s))) return rc;
-  const size_t sm = (size_t)kHeadBT * d.d_model * sizeof(float);
-  lm_head_kernel<<<e->sm_count * 4, kHeadThreads, sm, s>>>(e->Eq, e->Es, d.vocab, d.d_model, e->xn, e->batch,
-                                                           e->logits, e->best);
+  if (e->batch >= kMmaMinBatch && d.d_model % 64 == 0) {
+    const size_t sm = lm_head_mma_smem(d.d_model);
+    CU(cudaFuncSetAttribute(lm_head_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    lm_head_mma_kernel<<<e->sm_count, kHeadMmaThreads, sm, s>>>(e->Eq, e->Es, d.vocab, d.d_model, e->xn, e->batch,
+                                                               e->logits, e->best);
+  } else {
+    const size_t sm = (size_t)kHeadBT * d.d_model * sizeof(float);
+    lm_head_kernel<<<e->sm_count * 4, kHeadThreads, sm, s>>>(e->Eq, e->Es, d.vocab, d.d_model, e->xn, e->batch,
+                                                             e->logits, e->best);
+  }
   CHECK_LAUNCH();
   finalize_kernel<<<(e->batch + 127) / 128, 128, 0, s>>>(e->best, e->batch, e->tokens);
   CHECK_LAUNCH();
@@ -742,8 +749,15 @@ int dfssm_lm_head_argmax(const int8_t* E_q, const float* E_s, int vocab, int d, 
   int dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  lm_head_kernel<<<sms * 4, kHeadThreads, sm, s>>>(E_q, E_s, vocab, d, static_cast<const __half*>(x_f16), batch, lg,
-                                                    best);
+  if (batch >= kMmaMinBatch && d % 64 == 0) {
+    const size_t sm2 = lm_head_mma_smem(d);
+    CU(cudaFuncSetAttribute(lm_head_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2));
+    lm_head_mma_kernel<<<sms, kHeadMmaThreads, sm2, s>>>(E_q, E_s, vocab, d, static_cast<const __half*>(x_f16), batch,
+                                                          lg, best);
+  } else {
+    lm_head_kernel<<<sms * 4, kHeadThreads, sm, s>>>(E_q, E_s, vocab, d, static_cast<const __half*>(x_f16), batch, lg,
+                                                      best);
+  }
   CHECK_LAUNCH();
   finalize_kernel<<<(batch + 127) / 128, 128, 0, s>>>(best, batch, reinterpret_cast<int*>(next));
   CHECK_LAUNCH();

@@ -86,7 +86,20 @@ act_prep_kernel(const __half* __restrict__ in, int K, const float* __restrict__ 
     const int rk = wid * 2 + rr;
     const __half* brow = B16 + (size_t)rk * K;
     float acc = 0.f;
-    for (int k = lane; k < K; k += 32) acc = fmaf(h2f(sxn[k]), h2f(brow[k]), acc);
+    if ((K & 255) == 0) {
+      // 8 contiguous columns per lane per step: one 16-byte load of B and of x_norm
+#pragma unroll 4
+      for (int k = lane * 8; k < K; k += 256) {
+        const uint4 bv = __ldg(reinterpret_cast<const uint4*>(brow + k));
+        const uint4 xv = *reinterpret_cast<const uint4*>(sxn + k);
+        const __half* bh = reinterpret_cast<const __half*>(&bv);
+        const __half* xh = reinterpret_cast<const __half*>(&xv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc = fmaf(h2f(xh[j]), h2f(bh[j]), acc);
+      }
+    } else {
+      for (int k = lane; k < K; k += 32) acc = fmaf(h2f(sxn[k]), h2f(brow[k]), acc);
+    }
     acc = warp_sum(acc);
     if (lane == 0) t_out[b * DFSSM_RANK + rk] = f2h(acc);
   }
@@ -520,6 +533,123 @@ lm_head_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, int 
     }
   }
 }
+
+// ---------------------------------------------------------------------------------------
+// lm_head_mma: the LM head on fp16 tensor cores for batches of 8 or more (mma.sync m16n8k16,
+// fp16 x fp16 -> fp32).  int8 embedding bytes become exact fp16 values with a byte permute that
+// places them in the mantissa of 1024 (0x64xx) and one half2 subtraction of 1152; the fp16
+// normalised activations are exact too, so every product is exact and only the fp32 summation
+// order differs from the per-row kernel.  A warp owns 16 vocabulary rows at a time; per 64-column
+// block lane (g, c) loads 16 bytes at 16c of rows g and g+8, which fixes the (consistent) k order
+// of the A and B fragments.  logits = acc * E_s[v]; the argmax keys are merged per CTA and then
+// with atomicMax into best[b].
+// ---------------------------------------------------------------------------------------
+constexpr int kHeadMmaThreads = 256;
+constexpr int kHeadMmaNT = 4;  // 32 batch rows per pass
+
+__device__ __forceinline__ void mma_f16(float (&d)[4], unsigned a0, unsigned a1, unsigned a2, unsigned a3,
+                                        unsigned b0, unsigned b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// two int8 of a biased word (w ^ 0x80808080) as an exact half2: bytes (lo, lo+1) or (lo+2, lo+3)
+__device__ __forceinline__ unsigned i8x2_to_h2(unsigned wb, unsigned sel) {
+  const unsigned h = __byte_perm(wb, 0x64646464u, sel);
+  const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h), __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480)));
+  return *reinterpret_cast<const unsigned*>(&r);
+}
+
+__global__ void __launch_bounds__(kHeadMmaThreads, 1)
+lm_head_mma_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, int vocab, int d,
+                   const __half* __restrict__ xn, int B, float* __restrict__ logits,
+                   unsigned long long* __restrict__ best) {
+  constexpr int NB = 8 * kHeadMmaNT;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int SX = d + 8;  // padded fp16 row stride
+  __half* sx = reinterpret_cast<__half*>(smem);                                        // [NB][SX]
+  unsigned long long* sbest = reinterpret_cast<unsigned long long*>(smem + (size_t)NB * SX * 2);  // [8 warps][NB]
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
+  const int ntiles = (vocab + 15) / 16;
+  for (int bt0 = 0; bt0 < B; bt0 += NB) {
+    const int nb = min(NB, B - bt0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < NB * (d / 8); i += kHeadMmaThreads) {
+      const int b = i / (d / 8), u = i - b * (d / 8);
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (b < nb) v = *reinterpret_cast<const uint4*>(xn + (size_t)(bt0 + b) * d + u * 8);
+      *reinterpret_cast<uint4*>(sx + b * SX + u * 8) = v;
+    }
+    __syncthreads();
+    unsigned long long wbest[kHeadMmaNT][2];
+#pragma unroll
+    for (int tt = 0; tt < kHeadMmaNT; ++tt) wbest[tt][0] = wbest[tt][1] = 0ull;
+    for (int tile = blockIdx.x * 8 + wid; tile < ntiles; tile += gridDim.x * 8) {
+      const int v0 = tile * 16;
+      const int va = min(v0 + g, vocab - 1), vb = min(v0 + g + 8, vocab - 1);
+      const uint4* ra = reinterpret_cast<const uint4*>(Eq + (size_t)va * d);
+      const uint4* rb = reinterpret_cast<const uint4*>(Eq + (size_t)vb * d);
+      float acc[kHeadMmaNT][4];
+#pragma unroll
+      for (int tt = 0; tt < kHeadMmaNT; ++tt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[tt][i] = 0.f;
+      for (int blk = 0; blk < d / 64; ++blk) {
+        const uint4 ea = ldg_stream(ra + blk * 4 + c);
+        const uint4 eb = ldg_stream(rb + blk * 4 + c);
+        const unsigned wa[4] = {ea.x ^ 0x80808080u, ea.y ^ 0x80808080u, ea.z ^ 0x80808080u, ea.w ^ 0x80808080u};
+        const unsigned wb[4] = {eb.x ^ 0x80808080u, eb.y ^ 0x80808080u, eb.z ^ 0x80808080u, eb.w ^ 0x80808080u};
+#pragma unroll
+        for (int s2 = 0; s2 < 4; ++s2) {
+          const unsigned a0 = i8x2_to_h2(wa[s2], 0x4140u), a2 = i8x2_to_h2(wa[s2], 0x4342u);
+          const unsigned a1 = i8x2_to_h2(wb[s2], 0x4140u), a3 = i8x2_to_h2(wb[s2], 0x4342u);
+          const int col = blk * 64 + 16 * c + 4 * s2;
+#pragma unroll
+          for (int tt = 0; tt < kHeadMmaNT; ++tt) {
+            const uint2 bv = *reinterpret_cast<const uint2*>(sx + (tt * 8 + g) * SX + col);
+            mma_f16(acc[tt], a0, a1, a2, a3, bv.x, bv.y);
+          }
+        }
+      }
+      // D fragment: acc[tt][0..1] -> row v0+g, batch 2c, 2c+1 of tile tt; [2..3] -> row v0+g+8
+#pragma unroll
+      for (int tt = 0; tt < kHeadMmaNT; ++tt) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int v = v0 + g + (i >= 2 ? 8 : 0);
+          const int bb = tt * 8 + 2 * c + (i & 1);
+          if (v < vocab && bb < nb) {
+            const float lg = acc[tt][i] * Es[v];
+            logits[(size_t)(bt0 + bb) * vocab + v] = lg;
+            const unsigned long long key = argmax_key(f2h(lg), (uint32_t)v);
+            wbest[tt][i & 1] = key > wbest[tt][i & 1] ? key : wbest[tt][i & 1];
+          }
+        }
+      }
+    }
+    // reduce the per-lane bests over the 8 lanes that share c (same batch columns)
+#pragma unroll
+    for (int tt = 0; tt < kHeadMmaNT; ++tt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        unsigned long long k = wbest[tt][j];
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, o);
+          k = k2 > k ? k2 : k;
+        }
+        if (g == 0) sbest[wid * NB + tt * 8 + 2 * c + j] = k;
+      }
+    __syncthreads();
+    if (threadIdx.x < nb) {
+      unsigned long long k = 0ull;
+      for (int w = 0; w < 8; ++w) k = sbest[w * NB + threadIdx.x] > k ? sbest[w * NB + threadIdx.x] : k;
+      atomicMax(best + bt0 + threadIdx.x, k);
+    }
+  }
+}
+
+inline size_t lm_head_mma_smem(int d) { return (size_t)8 * kHeadMmaNT * (d + 8) * 2 + 8 * 8 * kHeadMmaNT * 8; }
 
 __global__ void finalize_kernel(unsigned long long* __restrict__ best, int B, int* __restrict__ tokens) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
