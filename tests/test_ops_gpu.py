@@ -114,7 +114,8 @@ def test_lm_head_argmax(lib, B, V, d):
     torch.cuda.synchronize()
     ref = (x.astype(np.float64) @ Eq.T.astype(np.float64)) * Es[None, :]
     got = lg.cpu().numpy()
-    np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-4)
+    # fp32 accumulation (tensor-core accumulation for batch >= 8): 1e-5 of the logit scale
+    np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5 * np.abs(ref).max())
     g16 = got.astype(np.float16)
     n = nxt.cpu().numpy()
     # argmax over the kernel's own fp16-rounded logits, first index on ties
