@@ -69,6 +69,20 @@ int effective_mode(const dfssm_engine* e) {
 
 int launch_prep(dfssm_engine* e, const __half* in, int K, const float* w, int quant, const ProjW* p,
                 cudaStream_t s) {
+  if (quant && p && K % 512 == 0) {
+    const int kpt = K / 512;
+#define DFSSM_PREP_FAST(n)                                                                                  \
+  if (kpt == n) {                                                                                          \
+    act_prep_fast_kernel<n><<<e->batch, kPrepFastThreads, 0, s>>>(in, K, w, e->q, e->xs, e->qsum, p->B16, e->t); \
+    CHECK_LAUNCH();                                                                                        \
+    return DFSSM_OK;                                                                                       \
+  }
+    DFSSM_PREP_FAST(1)
+    DFSSM_PREP_FAST(2)
+    DFSSM_PREP_FAST(4)
+    DFSSM_PREP_FAST(8)
+#undef DFSSM_PREP_FAST
+  }
   const size_t sm = (size_t)K * sizeof(__half);
   act_prep_kernel<<<e->batch, kPrepThreads, sm, s>>>(in, K, w, quant, e->xn, e->q, e->xs, e->qsum,
                                                      p ? p->B16 : nullptr, e->t);

@@ -12,7 +12,7 @@
 // Every rounding point follows the reference GPU path
 // (inference/gpu/df_ssm_inference.py:141-210, inference/gpu/df_ssm_kernels.cu:27-103).
 #pragma once
-#include "types.cuh"
+#include "prep.cuh"
 
 namespace dfssm {
 
@@ -102,6 +102,37 @@ act_prep_kernel(const __half* __restrict__ in, int K, const float* __restrict__ 
     }
     acc = warp_sum(acc);
     if (lane == 0) t_out[b * DFSSM_RANK + rk] = f2h(acc);
+  }
+}
+
+// act_prep_fast: the same prologue as act_prep_kernel (quantising variant) for K = 512 * KPT,
+// with 512 threads that each keep KPT columns and their LoRA-B slices in registers and one
+// combined block reduction for the 16 LoRA partials and the q sum.
+template <int KPT>
+__global__ void __launch_bounds__(kPrepFastThreads)
+act_prep_fast_kernel(const __half* __restrict__ in, int K, const float* __restrict__ w, int8_t* __restrict__ q_out,
+                     __half* __restrict__ xs_out, int* __restrict__ qsum_out, const __half* __restrict__ B16,
+                     __half* __restrict__ t_out) {
+  __shared__ float red[(kPrepFastWarps + 1) * (DFSSM_RANK + 1)];
+  __shared__ float s_t[DFSSM_RANK];
+  __shared__ float s_xs[1];
+  __shared__ int s_qsum[1];
+  const int b = blockIdx.x, k0 = threadIdx.x * KPT;
+  float wv[KPT];
+  float vals[1][KPT];
+  typename RankHalves<KPT>::T lb[DFSSM_RANK];
+  load_lora_b<KPT>(B16, K, lb);
+  const __half* xr = in + (size_t)b * K + k0;
+#pragma unroll
+  for (int j = 0; j < KPT; ++j) {
+    wv[j] = __ldg(w + k0 + j);
+    vals[0][j] = h2f(xr[j]);
+  }
+  prep_rows<1, KPT, false>(vals, wv, K, lb, q_out + (size_t)b * K, K, s_xs, s_qsum, s_t, red);
+  if (threadIdx.x < DFSSM_RANK) t_out[b * DFSSM_RANK + threadIdx.x] = f2h(s_t[threadIdx.x]);
+  if (threadIdx.x == 0) {
+    xs_out[b] = f2h(s_xs[0]);
+    qsum_out[b] = s_qsum[0];
   }
 }
 
@@ -290,16 +321,24 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
   const uint4* pa = reinterpret_cast<const uint4*>(p.bits + (size_t)ra * W);
   const uint4* pb = reinterpret_cast<const uint4*>(p.bits + (size_t)rb * W);
 
-  for (int bt0 = 0; bt0 < B; bt0 += NB) {
+  __shared__ uint64_t qbar;
+  if (threadIdx.x == 0) {
+    mbar_init(&qbar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  unsigned phase = 0;
+  for (int bt0 = 0; bt0 < B; bt0 += NB, phase ^= 1u) {
     const int nb = min(NB, B - bt0);
-    __syncthreads();
-    for (int i = threadIdx.x; i < NB * (K / 16); i += kMmaThreads) {
-      const int b = i / (K / 16), u = i - b * (K / 16);
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (b < nb) v = *reinterpret_cast<const uint4*>(q + (size_t)(bt0 + b) * K + u * 16);
-      *reinterpret_cast<uint4*>(sq + b * SQ + u * 16) = v;
+    __syncthreads();  // previous pass done with sq
+    // activation rows -> shared memory by TMA bulk copies (rows >= nb keep stale bytes; their
+    // output columns are never stored)
+    if (wid == 0) {
+      if (lane == 0) mbar_expect_tx(&qbar, (unsigned)(nb * K));
+      __syncwarp();
+      for (int b = lane; b < nb; b += 32) bulk_g2s(sq + b * SQ, q + (size_t)(bt0 + b) * K, (unsigned)K, &qbar);
     }
-    __syncthreads();
+    mbar_wait_bounded(&qbar, phase);
     int acc[kMmaNT][4];
 #pragma unroll
     for (int tt = 0; tt < kMmaNT; ++tt)
@@ -571,16 +610,23 @@ lm_head_mma_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, 
   unsigned long long* sbest = reinterpret_cast<unsigned long long*>(smem + (size_t)NB * SX * 2);  // [8 warps][NB]
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
   const int ntiles = (vocab + 15) / 16;
-  for (int bt0 = 0; bt0 < B; bt0 += NB) {
+  __shared__ uint64_t xbar;
+  if (threadIdx.x == 0) {
+    mbar_init(&xbar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  unsigned phase = 0;
+  for (int bt0 = 0; bt0 < B; bt0 += NB, phase ^= 1u) {
     const int nb = min(NB, B - bt0);
     __syncthreads();
-    for (int i = threadIdx.x; i < NB * (d / 8); i += kHeadMmaThreads) {
-      const int b = i / (d / 8), u = i - b * (d / 8);
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (b < nb) v = *reinterpret_cast<const uint4*>(xn + (size_t)(bt0 + b) * d + u * 8);
-      *reinterpret_cast<uint4*>(sx + b * SX + u * 8) = v;
+    if (wid == 0) {
+      if (lane == 0) mbar_expect_tx(&xbar, (unsigned)(nb * d * 2));
+      __syncwarp();
+      for (int b = lane; b < nb; b += 32)
+        bulk_g2s(sx + b * SX, xn + (size_t)(bt0 + b) * d, (unsigned)(d * 2), &xbar);
     }
-    __syncthreads();
+    mbar_wait_bounded(&xbar, phase);
     unsigned long long wbest[kHeadMmaNT][2];
 #pragma unroll
     for (int tt = 0; tt < kHeadMmaNT; ++tt) wbest[tt][0] = wbest[tt][1] = 0ull;

@@ -24,6 +24,7 @@
 #include <vector>
 
 #include "engine.h"
+#include "prep.cuh"
 
 using namespace dfssm;
 
@@ -82,39 +83,6 @@ __device__ __forceinline__ void stamp(const PParams& P, int idx) {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     P.trace[(size_t)blockIdx.x * (4 + kTracePerLayer * P.n_layer) + idx] = t;
   }
-}
-
-// ------------------------------------------------------------------ PTX helpers
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
-  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 // Wait (thread 0 spins, the block follows) until *cnt >= target; bounded.  Once any wait has
@@ -236,157 +204,6 @@ __device__ __forceinline__ void issue_stage(const PParams& P, const CtaPlan& pl,
   if (i == 0) mbar_expect_tx(bar, (unsigned)pl.tx);
   __syncwarp();
   if (n_) bulk_g2s(st + d_, s_, n_, bar);
-}
-
-// ------------------------------------------------------------------ block reductions (512 threads)
-// Block-wide sum / max of N values per thread with a fixed combination order.  Warp partials
-// go to red[w*N + i]; thread i < N combines column i into red[kWarps*N + i]; every thread then
-// reads the N totals.  `red` holds (kWarps + 1) * N floats.
-template <int N>
-__device__ __forceinline__ void block_sum_n(float (&v)[N], float* red) {
-#pragma unroll
-  for (int i = 0; i < N; ++i) v[i] = warp_sum(v[i]);
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
-  if (l == 0)
-#pragma unroll
-    for (int i = 0; i < N; ++i) red[w * N + i] = v[i];
-  __syncthreads();
-  if (threadIdx.x < N) {
-    float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < kWarps; ++j) s += red[j * N + threadIdx.x];
-    red[kWarps * N + threadIdx.x] = s;
-  }
-  __syncthreads();
-#pragma unroll
-  for (int i = 0; i < N; ++i) v[i] = red[kWarps * N + i];
-}
-template <int N>
-__device__ __forceinline__ void block_max_n(float (&v)[N], float* red) {
-#pragma unroll
-  for (int i = 0; i < N; ++i) v[i] = warp_max(v[i]);
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
-  if (l == 0)
-#pragma unroll
-    for (int i = 0; i < N; ++i) red[w * N + i] = v[i];
-  __syncthreads();
-  if (threadIdx.x < N) {
-    float s = red[threadIdx.x];
-#pragma unroll
-    for (int j = 1; j < kWarps; ++j) s = fmaxf(s, red[j * N + threadIdx.x]);
-    red[kWarps * N + threadIdx.x] = s;
-  }
-  __syncthreads();
-#pragma unroll
-  for (int i = 0; i < N; ++i) v[i] = red[kWarps * N + i];
-}
-
-// Like block_sum_n but only threads i < N receive total i (returned), for the LoRA partials.
-template <int N>
-__device__ __forceinline__ float block_sum_scatter(float (&v)[N], float* red) {
-#pragma unroll
-  for (int i = 0; i < N; ++i) v[i] = warp_sum(v[i]);
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
-  if (l == 0)
-#pragma unroll
-    for (int i = 0; i < N; ++i) red[w * N + i] = v[i];
-  __syncthreads();
-  float s = 0.f;
-  if (threadIdx.x < N)
-#pragma unroll
-    for (int j = 0; j < kWarps; ++j) s += red[j * N + threadIdx.x];
-  return s;
-}
-
-template <int KPT>
-struct RankHalves;  // KPT fp16 LoRA-B values of one rank for this thread's columns
-template <> struct RankHalves<1> { using T = unsigned short; };
-template <> struct RankHalves<2> { using T = unsigned; };
-template <> struct RankHalves<4> { using T = uint2; };
-template <> struct RankHalves<8> { using T = uint4; };
-
-template <int KPT>
-__device__ __forceinline__ void load_lora_b(const __half* B16, int K, typename RankHalves<KPT>::T (&out)[DFSSM_RANK]) {
-  using T = typename RankHalves<KPT>::T;
-  const int k0 = threadIdx.x * KPT;
-#pragma unroll
-  for (int r = 0; r < DFSSM_RANK; ++r) out[r] = __ldg(reinterpret_cast<const T*>(B16 + (size_t)r * K + k0));
-}
-
-template <int KPT>
-__device__ __forceinline__ float half_of(const typename RankHalves<KPT>::T& v, int j) {
-  const unsigned short* h = reinterpret_cast<const unsigned short*>(&v);
-  return __half2float(__ushort_as_half(h[j]));
-}
-
-// Shared-memory position of permuted activation byte p: 16-byte unit u of 128-byte chunk c is
-// stored at unit u ^ (c & 7), so the 8 lanes of a quarter-warp that read unit u of chunks
-// c..c+7 hit 8 different bank groups.
-__device__ __forceinline__ int qswz(int p) {
-  const int c = p >> 7;
-  return (p & ~127) | ((((p >> 4) & 7) ^ (c & 7)) << 4) | (p & 15);
-}
-
-// RMSNorm + per-row int8 quantisation + LoRA down-projection of this thread's KPT columns of
-// B activation rows.  vals[b][j]: fp16-exact inputs of columns k0 + j.  Writes q (permuted) to
-// sq[b][*] and xs/qsum/t to smem; returns after a __syncthreads.
-template <int B, int KPT>
-__device__ void prep_rows(float (&vals)[B][KPT], const float (&w)[KPT], int K,
-                          const typename RankHalves<KPT>::T (&lb)[DFSSM_RANK], int8_t* sq, int Kq,
-                          float* s_xs, int* s_qsum, float* s_t, float* red) {
-  const int k0 = threadIdx.x * KPT;
-  float ss[B];
-#pragma unroll
-  for (int b = 0; b < B; ++b) {
-    float a = 0.f;
-#pragma unroll
-    for (int j = 0; j < KPT; ++j) a = __fadd_rn(a, __fmul_rn(vals[b][j], vals[b][j]));
-    ss[b] = a;
-  }
-  block_sum_n<B>(ss, red);
-  float am[B];
-#pragma unroll
-  for (int b = 0; b < B; ++b) {
-    const float r = rsqrtf(__fadd_rn(__fmul_rn(ss[b], 1.0f / (float)K), 1e-5f));
-    float a = 0.f;
-#pragma unroll
-    for (int j = 0; j < KPT; ++j) {
-      const float xn = round_h(__fmul_rn(__fmul_rn(vals[b][j], r), w[j]));
-      vals[b][j] = xn;
-      a = fmaxf(a, fabsf(xn));
-    }
-    am[b] = a;
-  }
-  block_max_n<B>(am, red);
-  float all[B * DFSSM_RANK + B];  // LoRA partials t[b][r] = sum_j xn_j * q_rj, then the q sums
-#pragma unroll
-  for (int b = 0; b < B; ++b) {
-    const float s = round_h(__fmul_rn(fmaxf(am[b], qscale_floor()), 1.0f / 127.0f));
-    int qsum = 0;
-#pragma unroll
-    for (int j = 0; j < KPT; ++j) {
-      int q = (int)rint_alu(round_h(vals[b][j] / s));
-      q = max(-128, min(127, q));
-      sq[b * Kq + qswz(qperm_index(k0 + j))] = (int8_t)q;
-      qsum += q;
-    }
-    all[B * DFSSM_RANK + b] = (float)qsum;
-    if (threadIdx.x == 0) s_xs[b] = s;
-#pragma unroll
-    for (int r = 0; r < DFSSM_RANK; ++r) {
-      float a = 0.f;
-#pragma unroll
-      for (int j = 0; j < KPT; ++j) a = fmaf(vals[b][j], half_of<KPT>(lb[r], j), a);
-      all[b * DFSSM_RANK + r] = a;
-    }
-  }
-  const float tot = block_sum_scatter<B * DFSSM_RANK + B>(all, red);
-  if (threadIdx.x < B * DFSSM_RANK) s_t[threadIdx.x] = round_h(tot);
-  else if (threadIdx.x < B * DFSSM_RANK + B) s_qsum[threadIdx.x - B * DFSSM_RANK] = (int)tot;
-  __syncthreads();
 }
 
 // 1-bit GEMV of one row held in shared memory for B activation rows: returns the int32
