@@ -49,7 +49,10 @@ def test_single_layer_matches_oracle(B, mode, shape):
         _close(proj[:, d.d_inner:d.d_inner + d.d_xbc], ref["xbc"])
         _close(proj[:, d.d_inner + d.d_xbc:], ref["dt"])
     _close(m.buffer("gated", torch.float16, (m.max_batch, d.d_inner))[:B].cpu().numpy(), ref["gated"], 0.85)
-    _close(xb[:B].cpu().numpy(), ref["x"], 0.85)
+    # one int8 flip in the out_proj input moves every output row by ~1 fp16 ulp of x, so the bound
+    # is in ulps of the residual stream rather than a fraction of bit-identical entries
+    got_x, want_x = xb[:B].cpu().numpy().astype(np.float32), ref["x"].astype(np.float32)
+    assert np.abs(got_x - want_x).max() <= 8 * f16_ulp(np.abs(want_x).max())
     np.testing.assert_allclose(m.h_states[0][:B].cpu().numpy(), hs, rtol=2e-3, atol=2e-4)
     np.testing.assert_allclose(m.conv_states[0][:B].cpu().numpy(), cs, rtol=1e-2, atol=1e-2)
 
