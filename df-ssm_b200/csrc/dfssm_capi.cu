@@ -584,7 +584,7 @@ int dfssm_reset(dfssm_engine* e, void* stream) {
   CU(cudaMemsetAsync(e->ssm, 0, e->ssm_layer * e->d.n_layer * 4, us));
   CU(cudaMemsetAsync(e->conv, 0, e->conv_layer * e->d.n_layer * 4, us));
   CU(cudaMemsetAsync(e->best, 0, (size_t)e->max_batch * 8, us));
-  CU(cudaMemsetAsync(e->sync, 0, 16, us));
+  CU(cudaMemsetAsync(e->sync, 0, 32, us));
   return DFSSM_OK;
 }
 

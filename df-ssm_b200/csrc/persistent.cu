@@ -40,6 +40,7 @@ struct CtaPlan {
   int bc0, nbc;   // B/C rows [bc0, bc0 + nbc) within [0, 2*d_state)
   int o0, no;     // out_proj rows
   int v0, nv;     // LM head rows
+  int tj;         // index among the B/C CTAs (LoRA-t producers are those with tj < n_t), else -1
   int tx;         // bytes of one ring stage (sum of this CTA's copies)
 };
 
@@ -70,6 +71,8 @@ struct PParams {
   int from_x;      // 1: layer l0 starts from x_g instead of the token embedding
   int do_head;     // 1: final norm + LM head + argmax after layer l1-1
   int n_bc;        // number of B/C CTAs
+  int n_t;         // number of LoRA-t producer CTAs (the first n_t B/C CTAs; rank r -> producer r % n_t)
+  float* t_g;      // [2][B][16] published LoRA down-projections (in_proj, out_proj)
   int ns;          // ring stages
   int ring_off;    // byte offset of the ring in dynamic smem
   int tab_off;     // byte offset of the per-layer tables in dynamic smem
@@ -101,14 +104,20 @@ __device__ __forceinline__ void wait_counter(unsigned* cnt, unsigned target, uns
   __syncthreads();
 }
 
-__device__ __forceinline__ void grid_barrier(const PParams& P, unsigned& nbar) {
+__device__ __forceinline__ void grid_arrive(const PParams& P, unsigned& nbar) {
   __syncthreads();
   ++nbar;
   if (threadIdx.x == 0) {
     __threadfence();
     red_release_add(P.sync, 1u);
   }
+}
+__device__ __forceinline__ void grid_wait(const PParams& P, unsigned nbar) {
   wait_counter(P.sync, nbar * gridDim.x, P.sync + 3, 1u);
+}
+__device__ __forceinline__ void grid_barrier(const PParams& P, unsigned& nbar) {
+  grid_arrive(P, nbar);
+  grid_wait(P, nbar);
 }
 
 // Wait for the ring slot of `layer` to hold its data (bounded).
@@ -134,8 +143,8 @@ __device__ __forceinline__ void wait_stage(const PParams& P, uint64_t* bars, int
 template <int B>
 __device__ __forceinline__ void issue_stage(const PParams& P, const CtaPlan& pl, int layer, unsigned char* ring,
                                          uint64_t* bars, const LayerW* layers) {
-  if (layer >= P.l1 || threadIdx.x >= 32) return;
-  const int i = threadIdx.x;
+  if (layer >= P.l1 || threadIdx.x < 32 || threadIdx.x >= 64) return;  // warp 1 issues
+  const int i = threadIdx.x - 32;
   const int slot = (layer - P.l0) % P.ns;
   unsigned char* st = ring + (size_t)slot * P.lay.stage_bytes;
   uint64_t* bar = bars + slot;
@@ -271,6 +280,33 @@ __device__ __forceinline__ float conv_silu(float s0, float s1, float s2, float v
   return o * sig;
 }
 
+// LoRA-t producer: compute this CTA's ranks (r = tj, tj + n_t, ...) of t = fp16(xn . B16^T) and
+// publish them in t_g[which]; one release-increment of the t counter per producer and use.
+template <int B, int KPT>
+__device__ void publish_t(const PParams& P, int tj, const float (&vals)[B][KPT], const __half* B16, int K, int which,
+                          float* red) {
+  for (int r = tj; r < DFSSM_RANK; r += P.n_t) {
+    float t[B];
+    lora_t_rank<B, KPT>(vals, B16, K, r, t, red);
+    if (threadIdx.x == 0)
+#pragma unroll
+      for (int b = 0; b < B; ++b) P.t_g[(which * B + b) * DFSSM_RANK + r] = t[b];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    red_release_add(P.sync + 4, 1u);
+  }
+}
+
+// Wait until `uses` rounds of all producers have published, then copy t_g[which] into s_t.
+template <int B>
+__device__ __forceinline__ void fetch_t(const PParams& P, unsigned uses, int which, float* s_t) {
+  wait_counter(P.sync + 4, uses * (unsigned)P.n_t, P.sync + 3, 8u);
+  if (threadIdx.x < B * DFSSM_RANK) s_t[threadIdx.x] = __ldcg(P.t_g + which * B * DFSSM_RANK + threadIdx.x);
+  __syncthreads();
+}
+
 template <int B, int KI, int KO>
 __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -288,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
   float* s_xc = s_z + B * 64;                       // [B][64]
   float* s_dt = s_xc + B * 64;                      // [B]
   float* s_bc = s_dt + B;                           // [B][2*d_state] (fp32)
-  float* s_hp = s_bc + B * 2 * DFSSM_DSTATE;        // [4] dt_bias, A_log, D, dt-row scale
+  int* s_dot = reinterpret_cast<int*>(s_bc + B * 2 * DFSSM_DSTATE);  // [128][B] GEMV results
   // per-layer tables copied once at kernel start (no dependent global loads inside the loop):
   // the layer pointer table, and this CTA's head scalars (dt_bias, A_log, D, dt-row scale,
   // 16 fp16 dt-row LoRA-A values) for every layer
@@ -340,20 +376,16 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
 
   for (int layer = P.l0; layer < P.l1; ++layer) {
     const LayerW& L = s_layers[layer];
-    stamp(P, 2 + kTracePerLayer * layer + 12);
-    issue_stage<B>(P, pl, layer + P.ns - 1, ring, bars, s_layers);
-    stamp(P, 2 + kTracePerLayer * layer + 13);
     unsigned char* st = ring + (size_t)((layer - P.l0) % P.ns) * P.lay.stage_bytes;
     // ---------------- alpha: per-thread weights are loaded before waiting for x
     float w_in[KI];
-    typename RankHalves<KI>::T lb_in[DFSSM_RANK];
     {
       const int k0 = tid * KI;
 #pragma unroll
       for (int j = 0; j < KI; ++j) w_in[j] = __ldg(L.ln_w + k0 + j);
-      load_lora_b<KI>(L.in.B16, d_model, lb_in);
-
     }
+    const int idx = layer - P.l0;
+    const bool t_producer = pl.role == 1 && pl.tj < P.n_t;
     const int tb = 2 + kTracePerLayer * layer;
     stamp(P, tb + 0);
     if (layer > P.l0) grid_barrier(P, nbar);  // x of the previous layer complete
@@ -370,7 +402,8 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
       for (int b = 0; b < B; ++b)
 #pragma unroll
         for (int j = 0; j < KI; ++j) vals[b][j] = h2f(s_x[b * d_model + tid * KI + j]);
-      prep_rows<B, KI>(vals, w_in, d_model, lb_in, s_q, d_inner, s_xs, s_qsum, s_t, red);
+      prep_quant<B, KI>(vals, w_in, d_model, s_q, d_inner, s_xs, s_qsum, red);
+      if (t_producer) publish_t<B, KI>(P, pl.tj, vals, L.in.B16, d_model, 0, red);
     }
     stamp(P, tb + 3);
     wait_stage(P, bars, layer);
@@ -386,30 +419,32 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
       for (int i = hw; i < ((nrows + 1) & ~1); i += 2 * kWarps) {
         const int row = i < nrows ? i : nrows - 1;
         const Dots<B> dd = row_dot<B>(st + P.lay.in_bits + (size_t)row * RB, d_model, s_q, d_inner, l16, s_qsum);
-        const int* dot = dd.v;
-        if (i < nrows && l16 < B) {
-          const int b = l16;
-          float v;
-          if (row < 2 * np) {
-            v = proj_out(dot[b], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
-          } else {
-            const float* hp = s_hptab + layer * 12;
-            v = proj_out(dot[b], s_xs[b], hp[3], reinterpret_cast<const __half*>(hp + 4), s_t + b * 16);
-          }
-          if (row < np) {
-            s_z[b * 64 + row] = v;
-          } else if (row < 2 * np) {
-            const int j = row - np, ch = pl.h * DFSSM_HEADDIM + pl.p0 + j;
-            const float s0 = cst[(b * 3 + 0) * np + j], s1 = cst[(b * 3 + 1) * np + j],
-                        s2 = cst[(b * 3 + 2) * np + j];
-            float* gcs = P.conv + (long long)layer * P.conv_layer + (long long)b * 3 * P.d_xbc + ch;
-            gcs[0] = s1;
-            gcs[P.d_xbc] = s2;
-            gcs[2 * P.d_xbc] = v;
-            s_xc[b * 64 + j] = round_h(conv_silu(s0, s1, s2, v, cw + j * 4, h2f(cb[j])));
-          } else {
-            s_dt[b] = v;
-          }
+        if (i < nrows && l16 < B) s_dot[row * B + l16] = dd.v[l16];
+      }
+      __syncthreads();
+      fetch_t<B>(P, 2 * idx + 1, 0, s_t);
+      for (int e2 = tid; e2 < nrows * B; e2 += kThreads) {
+        const int row = e2 / B, b = e2 - row * B;
+        const int dot = s_dot[e2];
+        float v;
+        if (row < 2 * np) {
+          v = proj_out(dot, s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
+        } else {
+          const float* hp = s_hptab + layer * 12;
+          v = proj_out(dot, s_xs[b], hp[3], reinterpret_cast<const __half*>(hp + 4), s_t + b * 16);
+        }
+        if (row < np) {
+          s_z[b * 64 + row] = v;
+        } else if (row < 2 * np) {
+          const int j = row - np, ch = pl.h * DFSSM_HEADDIM + pl.p0 + j;
+          const float s0 = cst[(b * 3 + 0) * np + j], s1 = cst[(b * 3 + 1) * np + j], s2 = cst[(b * 3 + 2) * np + j];
+          float* gcs = P.conv + (long long)layer * P.conv_layer + (long long)b * 3 * P.d_xbc + ch;
+          gcs[0] = s1;
+          gcs[P.d_xbc] = s2;
+          gcs[2 * P.d_xbc] = v;
+          s_xc[b * 64 + j] = round_h(conv_silu(s0, s1, s2, v, cw + j * 4, h2f(cb[j])));
+        } else {
+          s_dt[b] = v;
         }
       }
       __syncthreads();
@@ -466,19 +501,20 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
       for (int i = hw; i < ((nb + 1) & ~1); i += 2 * kWarps) {
         const int row = i < nb ? i : nb - 1;
         const Dots<B> dd = row_dot<B>(st + P.lay.in_bits + (size_t)row * RB, d_model, s_q, d_inner, l16, s_qsum);
-        const int* dot = dd.v;
-        if (i < nb && l16 < B) {
-          const int b = l16;
-          const float v = proj_out(dot[b], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
-          const int ch = d_inner + pl.bc0 + row;
-          const float s0 = cst[(b * 3 + 0) * nb + row], s1 = cst[(b * 3 + 1) * nb + row],
-                      s2 = cst[(b * 3 + 2) * nb + row];
-          float* gcs = P.conv + (long long)layer * P.conv_layer + (long long)b * 3 * P.d_xbc + ch;
-          gcs[0] = s1;
-          gcs[P.d_xbc] = s2;
-          gcs[2 * P.d_xbc] = v;
-          P.bc_g[b * 256 + pl.bc0 + row] = f2h(conv_silu(s0, s1, s2, v, cw + row * 4, h2f(cb[row])));
-        }
+        if (i < nb && l16 < B) s_dot[row * B + l16] = dd.v[l16];
+      }
+      __syncthreads();
+      fetch_t<B>(P, 2 * idx + 1, 0, s_t);
+      for (int e2 = tid; e2 < nb * B; e2 += kThreads) {
+        const int row = e2 / B, b = e2 - row * B;
+        const float v = proj_out(s_dot[e2], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
+        const int ch = d_inner + pl.bc0 + row;
+        const float s0 = cst[(b * 3 + 0) * nb + row], s1 = cst[(b * 3 + 1) * nb + row], s2 = cst[(b * 3 + 2) * nb + row];
+        float* gcs = P.conv + (long long)layer * P.conv_layer + (long long)b * 3 * P.d_xbc + ch;
+        gcs[0] = s1;
+        gcs[P.d_xbc] = s2;
+        gcs[2 * P.d_xbc] = v;
+        P.bc_g[b * 256 + pl.bc0 + row] = f2h(conv_silu(s0, s1, s2, v, cw + row * 4, h2f(cb[row])));
       }
       __syncthreads();
       if (tid == 0) {
@@ -489,15 +525,16 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
     stamp(P, tb + 7);
     // ---------------- beta: out_proj rows
     float w_out[KO];
-    typename RankHalves<KO>::T lb_out[DFSSM_RANK];
     {
       const int k0 = tid * KO;
 #pragma unroll
       for (int j = 0; j < KO; ++j) w_out[j] = __ldg(L.norm_w + k0 + j);
-      load_lora_b<KO>(L.out.B16, d_inner, lb_out);
     }
     stamp(P, tb + 8);
-    grid_barrier(P, nbar);  // gated complete
+    // gated complete; warp 1 issues the bulk copies of a later layer while thread 0 waits
+    grid_arrive(P, nbar);
+    issue_stage<B>(P, pl, layer + P.ns - 1, ring, bars, s_layers);
+    grid_wait(P, nbar);
     stamp(P, tb + 9);
     {
       float vals[B][KO];
@@ -515,7 +552,8 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         for (int j = 0; j < KO; ++j) vals[b][j] = h2f(hv[j]);
       }
       __syncthreads();
-      prep_rows<B, KO>(vals, w_out, d_inner, lb_out, s_q, d_inner, s_xs, s_qsum, s_t, red);
+      prep_quant<B, KO>(vals, w_out, d_inner, s_q, d_inner, s_xs, s_qsum, red);
+      if (t_producer) publish_t<B, KO>(P, pl.tj, vals, L.out.B16, d_inner, 1, red);
     }
     stamp(P, tb + 10);
     if (pl.no > 0) {
@@ -525,13 +563,19 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
       for (int i = hw; i < ((pl.no + 1) & ~1); i += 2 * kWarps) {
         const int row = i < pl.no ? i : pl.no - 1;
         const Dots<B> dd = row_dot<B>(st + P.lay.out_bits + (size_t)row * RBO, d_inner, s_q, d_inner, l16, s_qsum);
-        const int* dot = dd.v;
-        if (i < pl.no && l16 < B) {
-          const int b = l16;
-          const float v = proj_out(dot[b], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
-          const int o = pl.o0 + row;
-          P.x_g[(size_t)b * d_model + o] = f2h(h2f(s_x[b * d_model + o]) + v);
-        }
+        if (i < pl.no && l16 < B) s_dot[row * B + l16] = dd.v[l16];
+      }
+    }
+    __syncthreads();
+    fetch_t<B>(P, 2 * idx + 2, 1, s_t);
+    if (pl.no > 0) {
+      const __half* sc = reinterpret_cast<const __half*>(st + P.lay.out_scale);
+      const __half* la = reinterpret_cast<const __half*>(st + P.lay.out_lA);
+      for (int e2 = tid; e2 < pl.no * B; e2 += kThreads) {
+        const int row = e2 / B, b = e2 - row * B;
+        const float v = proj_out(s_dot[e2], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
+        const int o = pl.o0 + row;
+        P.x_g[(size_t)b * d_model + o] = f2h(h2f(s_x[b * d_model + o]) + v);
       }
     }
     __syncthreads();
@@ -689,6 +733,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
       }
       P.sync[0] = 0;
       P.sync[2] = 0;
+      P.sync[4] = 0;
       __threadfence();
       P.sync[1] = 0;
     }
@@ -763,6 +808,7 @@ int build_plan(const dfssm_engine* e, int B, int grid, std::vector<CtaPlan>& pla
       const int j = c - n_items;
       const int b0 = bc_groups * j / n_bc, b1 = bc_groups * (j + 1) / n_bc;
       p.role = 1;
+      p.tj = j;
       p.bc0 = b0 * 8;
       p.nbc = (b1 - b0) * 8;
       max_nbc = p.nbc > max_nbc ? p.nbc : max_nbc;
@@ -798,7 +844,7 @@ int build_plan(const dfssm_engine* e, int B, int grid, std::vector<CtaPlan>& pla
   lay.state = off; off += a16(B * np * DFSSM_DSTATE * 4);
   lay.cstate = off; off += a16(B * 3 * ch * 4);
   lay.stage_bytes = (off + 127) & ~127;
-  const int misc_floats = (kWarps + 1) * (B * 16 + B) + B * 16 + B + B + 16 + B * 64 * 2 + B + B * 256 + 4 + 17 + 4;
+  const int misc_floats = (kWarps + 1) * (B * 16 + B) + B * 16 + B + B + 16 + B * 64 * 2 + B + B * 256 + 128 * B + 8;
   int work = B * d.d_model * 2 + B * d.d_inner + misc_floats * 4;
   work = (work + 127) & ~127;
   tab_off = work;
@@ -882,6 +928,8 @@ int persistent_init(dfssm_engine* e) {
     P.from_x = 0;
     P.do_head = 1;
     P.n_bc = n_bc;
+    P.n_t = n_bc < DFSSM_RANK ? n_bc : DFSSM_RANK;
+    P.t_g = reinterpret_cast<float*>(e->xn);  // 2 x B x 16 floats of the per-op path's xn buffer
     P.ns = ns;
     P.ring_off = smem - ns * lay.stage_bytes;
     P.trace = nullptr;

@@ -163,4 +163,72 @@ __device__ void prep_rows(float (&vals)[B][KPT], const float (&w)[KPT], int K,
 }
 
 
+// RMSNorm + per-row int8 quantisation only (no LoRA): on return vals[b][j] holds the fp16-exact
+// normalised values, q is in sq (swizzled if SWZ), scale and q sum in s_xs / s_qsum.
+template <int B, int KPT, bool SWZ = true>
+__device__ void prep_quant(float (&vals)[B][KPT], const float (&w)[KPT], int K, int8_t* sq, int Kq, float* s_xs,
+                           int* s_qsum, float* red) {
+  const int k0 = threadIdx.x * KPT;
+  float ss[B];
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    float a = 0.f;
+#pragma unroll
+    for (int j = 0; j < KPT; ++j) a = __fadd_rn(a, __fmul_rn(vals[b][j], vals[b][j]));
+    ss[b] = a;
+  }
+  block_sum_n<B>(ss, red);
+  float am[B];
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    const float r = rsqrtf(__fadd_rn(__fmul_rn(ss[b], 1.0f / (float)K), 1e-5f));
+    float a = 0.f;
+#pragma unroll
+    for (int j = 0; j < KPT; ++j) {
+      const float xn = round_h(__fmul_rn(__fmul_rn(vals[b][j], r), w[j]));
+      vals[b][j] = xn;
+      a = fmaxf(a, fabsf(xn));
+    }
+    am[b] = a;
+  }
+  block_max_n<B>(am, red);
+  float qs[B];
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    const float s = round_h(__fmul_rn(fmaxf(am[b], qscale_floor()), 1.0f / 127.0f));
+    int qsum = 0;
+#pragma unroll
+    for (int j = 0; j < KPT; ++j) {
+      int q = (int)rint_alu(round_h(vals[b][j] / s));
+      q = max(-128, min(127, q));
+      sq[b * Kq + (SWZ ? qswz(qperm_index(k0 + j)) : qperm_index(k0 + j))] = (int8_t)q;
+      qsum += q;
+    }
+    qs[b] = (float)qsum;
+    if (threadIdx.x == 0) s_xs[b] = s;
+  }
+  block_sum_n<B>(qs, red);
+  if (threadIdx.x < B) s_qsum[threadIdx.x] = (int)qs[threadIdx.x];
+  __syncthreads();
+}
+
+// One rank r of the LoRA down-projection, t[b] = fp16(sum_k xn[b][k] * B16[r][k]), from the
+// thread-resident normalised values of prep_quant.  Every thread returns the B totals.
+template <int B, int KPT>
+__device__ __forceinline__ void lora_t_rank(const float (&vals)[B][KPT], const __half* B16, int K, int r,
+                                            float (&t)[B], float* red) {
+  typename RankHalves<KPT>::T bv = __ldg(reinterpret_cast<const typename RankHalves<KPT>::T*>(
+      B16 + (size_t)r * K + threadIdx.x * KPT));
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    float a = 0.f;
+#pragma unroll
+    for (int j = 0; j < KPT; ++j) a = fmaf(vals[b][j], half_of<KPT>(bv, j), a);
+    t[b] = a;
+  }
+  block_sum_n<B>(t, red);
+#pragma unroll
+  for (int b = 0; b < B; ++b) t[b] = round_h(t[b]);
+}
+
 }  // namespace dfssm
