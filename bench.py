@@ -154,7 +154,8 @@ def physical_threads() -> int:
 def run_reference_arm(args, cfg, rank, world):
     if rank != 0:
         return
-    batch = cfg["batch"] if cfg["scaling"] == "weak" else cfg["batch"] // world
+    # the whole job's sequences: per-GPU batch x ranks (weak scaling) or the global batch (strong)
+    batch = cfg["batch"] * world if cfg["scaling"] == "weak" else cfg["batch"]
     threads = physical_threads()
     res = cpu_reference_run(cfg, args.steps, args.warmup, threads, batch)
     if "unavailable" in res:

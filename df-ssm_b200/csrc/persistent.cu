@@ -402,8 +402,9 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
       for (int b = 0; b < B; ++b)
 #pragma unroll
         for (int j = 0; j < KI; ++j) vals[b][j] = h2f(s_x[b * d_model + tid * KI + j]);
-      prep_quant<B, KI>(vals, w_in, d_model, s_q, d_inner, s_xs, s_qsum, red);
-      if (t_producer) publish_t<B, KI>(P, pl.tj, vals, L.in.B16, d_model, 0, red);
+      prep_norm<B, KI>(vals, w_in, d_model, red);
+      if (t_producer) publish_t<B, KI>(P, pl.tj, vals, L.in.B16, d_model, 0, red);  // publish before quantising
+      prep_quantize<B, KI>(vals, s_q, d_inner, s_xs, s_qsum, red);
     }
     stamp(P, tb + 3);
     wait_stage(P, bars, layer);
@@ -552,8 +553,9 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         for (int j = 0; j < KO; ++j) vals[b][j] = h2f(hv[j]);
       }
       __syncthreads();
-      prep_quant<B, KO>(vals, w_out, d_inner, s_q, d_inner, s_xs, s_qsum, red);
-      if (t_producer) publish_t<B, KO>(P, pl.tj, vals, L.out.B16, d_inner, 1, red);
+      prep_norm<B, KO>(vals, w_out, d_inner, red);
+      if (t_producer) publish_t<B, KO>(P, pl.tj, vals, L.out.B16, d_inner, 1, red);  // publish before quantising
+      prep_quantize<B, KO>(vals, s_q, d_inner, s_xs, s_qsum, red);
     }
     stamp(P, tb + 10);
     if (pl.no > 0) {

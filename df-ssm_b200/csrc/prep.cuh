@@ -163,12 +163,10 @@ __device__ void prep_rows(float (&vals)[B][KPT], const float (&w)[KPT], int K,
 }
 
 
-// RMSNorm + per-row int8 quantisation only (no LoRA): on return vals[b][j] holds the fp16-exact
-// normalised values, q is in sq (swizzled if SWZ), scale and q sum in s_xs / s_qsum.
-template <int B, int KPT, bool SWZ = true>
-__device__ void prep_quant(float (&vals)[B][KPT], const float (&w)[KPT], int K, int8_t* sq, int Kq, float* s_xs,
-                           int* s_qsum, float* red) {
-  const int k0 = threadIdx.x * KPT;
+// RMSNorm (first half of the quantising prologue): on return vals[b][j] holds the fp16-exact
+// normalised values.
+template <int B, int KPT>
+__device__ __forceinline__ void prep_norm(float (&vals)[B][KPT], const float (&w)[KPT], int K, float* red) {
   float ss[B];
 #pragma unroll
   for (int b = 0; b < B; ++b) {
@@ -178,17 +176,25 @@ __device__ void prep_quant(float (&vals)[B][KPT], const float (&w)[KPT], int K, 
     ss[b] = a;
   }
   block_sum_n<B>(ss, red);
-  float am[B];
 #pragma unroll
   for (int b = 0; b < B; ++b) {
     const float r = rsqrtf(__fadd_rn(__fmul_rn(ss[b], 1.0f / (float)K), 1e-5f));
+#pragma unroll
+    for (int j = 0; j < KPT; ++j) vals[b][j] = round_h(__fmul_rn(__fmul_rn(vals[b][j], r), w[j]));
+  }
+}
+
+// Per-row int8 quantisation of normalised values (second half): q in sq (swizzled if SWZ),
+// scale and q sum in s_xs / s_qsum; returns after a __syncthreads.
+template <int B, int KPT, bool SWZ = true>
+__device__ void prep_quantize(const float (&vals)[B][KPT], int8_t* sq, int Kq, float* s_xs, int* s_qsum, float* red) {
+  const int k0 = threadIdx.x * KPT;
+  float am[B];
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
     float a = 0.f;
 #pragma unroll
-    for (int j = 0; j < KPT; ++j) {
-      const float xn = round_h(__fmul_rn(__fmul_rn(vals[b][j], r), w[j]));
-      vals[b][j] = xn;
-      a = fmaxf(a, fabsf(xn));
-    }
+    for (int j = 0; j < KPT; ++j) a = fmaxf(a, fabsf(vals[b][j]));
     am[b] = a;
   }
   block_max_n<B>(am, red);
@@ -208,7 +214,9 @@ __device__ void prep_quant(float (&vals)[B][KPT], const float (&w)[KPT], int K, 
     if (threadIdx.x == 0) s_xs[b] = s;
   }
   block_sum_n<B>(qs, red);
-  if (threadIdx.x < B) s_qsum[threadIdx.x] = (int)qs[threadIdx.x];
+  if (threadIdx.x == 0)
+#pragma unroll
+    for (int b = 0; b < B; ++b) s_qsum[b] = (int)qs[b];
   __syncthreads();
 }
 
