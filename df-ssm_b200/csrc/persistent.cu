@@ -33,6 +33,7 @@ namespace {
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr unsigned kSpinLimit = 1u << 22;
+constexpr int kMaxRPW = 2;  // SSM rows per warp (np = 32 channels over 16 warps)
 
 struct CtaPlan {
   int role;       // 0 = head item, 1 = B/C rows, 2 = no in_proj rows
@@ -410,6 +411,9 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
     wait_stage(P, bars, layer);
     stamp(P, tb + 4);
     const int RB = d_model / 8;
+    // updated SSM state of a head CTA, written back after it arrives at the gated barrier so that
+    // the barrier's release does not wait for these 16 KB of stores
+    float4 hnew[B][kMaxRPW];
     if (pl.role == 0) {
       const int np = pl.np, nrows = 2 * np + 1;
       const __half* sc = reinterpret_cast<const __half*>(st + P.lay.in_scale);
@@ -468,7 +472,9 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         const float* bb = s_bc + b * 256 + lane * 4;
         const float4 Bn = make_float4(bb[0], bb[1], bb[2], bb[3]);
         const float4 Cn = make_float4(bb[128], bb[129], bb[130], bb[131]);
-        for (int rr = 0; rr < RPW; ++rr) {
+#pragma unroll
+        for (int rr = 0; rr < kMaxRPW; ++rr) {
+          if (rr >= RPW) break;
           const int p = wid * RPW + rr;
           const float4 hv = *reinterpret_cast<const float4*>(sst + ((size_t)b * np + p) * DFSSM_DSTATE + lane * 4);
           const float xv = s_xc[b * 64 + p];
@@ -478,9 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
           o.y = Abar * hv.y + X * Bn.y;
           o.z = Abar * hv.z + X * Bn.z;
           o.w = Abar * hv.w + X * Bn.w;
-          float* gh = P.ssm + (long long)layer * P.ssm_layer +
-                      ((long long)(b * P.nheads + pl.h) * DFSSM_HEADDIM + pl.p0 + p) * DFSSM_DSTATE + lane * 4;
-          __stcs(reinterpret_cast<float4*>(gh), o);
+          hnew[b][rr] = o;
           float part = Cn.x * o.x + Cn.y * o.y + Cn.z * o.z + Cn.w * o.w;
           part = warp_sum(part);
           if (lane == 0) {
@@ -535,6 +539,19 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
     // gated complete; warp 1 issues the bulk copies of a later layer while thread 0 waits
     grid_arrive(P, nbar);
     issue_stage<B>(P, pl, layer + P.ns - 1, ring, bars, s_layers);
+    if (pl.role == 0) {
+      const int RPW = pl.np / kWarps;
+#pragma unroll
+      for (int b = 0; b < B; ++b)
+#pragma unroll
+        for (int rr = 0; rr < kMaxRPW; ++rr) {
+          if (rr >= RPW) break;
+          const int p = wid * RPW + rr;
+          float* gh = P.ssm + (long long)layer * P.ssm_layer +
+                      ((long long)(b * P.nheads + pl.h) * DFSSM_HEADDIM + pl.p0 + p) * DFSSM_DSTATE + lane * 4;
+          __stcs(reinterpret_cast<float4*>(gh), hnew[b][rr]);
+        }
+    }
     grid_wait(P, nbar);
     stamp(P, tb + 9);
     {
@@ -792,11 +809,23 @@ int build_plan(const dfssm_engine* e, int B, int grid, std::vector<CtaPlan>& pla
   plans.assign(grid, CtaPlan{});
   const int og = d.d_model / 8;  // out rows in 8-row groups
   int max_no = 0, max_nbc = 0;
+  // LoRA-t producers (the first min(16, n_bc) B/C CTAs) get no out_proj rows: they publish the
+  // out_proj t while the others run their GEMV, and would otherwise arrive last at the x barrier
+  const int n_t = n_bc < DFSSM_RANK ? n_bc : DFSSM_RANK;
+  const int n_out = grid - n_t;
+  int oc = 0;
   for (int c = 0; c < grid; ++c) {
     CtaPlan& p = plans[c];
-    const int g0 = (int)((long long)og * c / grid), g1 = (int)((long long)og * (c + 1) / grid);
-    p.o0 = g0 * 8;
-    p.no = (g1 - g0) * 8;
+    const bool producer = c >= n_items && c < n_items + n_t;
+    if (producer) {
+      p.o0 = 0;
+      p.no = 0;
+    } else {
+      const int g0 = (int)((long long)og * oc / n_out), g1 = (int)((long long)og * (oc + 1) / n_out);
+      p.o0 = g0 * 8;
+      p.no = (g1 - g0) * 8;
+      ++oc;
+    }
     max_no = p.no > max_no ? p.no : max_no;
     const long long v0 = (long long)d.vocab * c / grid, v1 = (long long)d.vocab * (c + 1) / grid;
     p.v0 = (int)v0;
