@@ -307,36 +307,84 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
                 const __half* __restrict__ conv_b, int d_inner, int d_xbc) {
   constexpr int KS = (kMmaThreads / 32) / RG;  // K slices per CTA
   constexpr int NB = 8 * kMmaNT;               // batch rows per pass
+  constexpr int R = 16 * RG;                   // output rows per CTA
   extern __shared__ __align__(16) unsigned char smem[];
   const int K = p.K, N = p.N, W = K >> 5;
   const int SQ = K + 16;                                         // padded activation row stride
   int8_t* sq = reinterpret_cast<int8_t*>(smem);                  // [NB][SQ]
-  int* red = reinterpret_cast<int*>(smem + NB * SQ);             // [KS][16*RG][NB]
+  int* red = reinterpret_cast<int*>(smem + NB * SQ);             // [KS][R][NB]
+  // epilogue operands, loaded with independent loads before the MMA loop
+  float* e_cs = reinterpret_cast<float*>(red + KS * R * NB);     // [NB][3][R] conv state (MODE 0)
+  float* e_t = e_cs + NB * 3 * R;                                // [NB][16]
+  float* e_a = e_t + NB * DFSSM_RANK;                            // [R][16] LoRA A
+  float* e_cw = e_a + R * DFSSM_RANK;                            // [R][4] conv weights
+  float* e_misc = e_cw + R * 4;                                  // scale[R], conv_b[R], xs[NB], qsum[NB]
+  float* e_scale = e_misc;
+  float* e_cb = e_scale + R;
+  float* e_xs = e_cb + R;
+  int* e_qsum = reinterpret_cast<int*>(e_xs + NB);
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
   const int rg = wid % RG, ks = wid / RG;
-  const int row0 = blockIdx.x * 16 * RG;
+  const int row0 = blockIdx.x * R;
   const int wr = row0 + rg * 16;                                 // this warp's first row
   const int wpw = W / KS, kw0 = ks * wpw;                        // words per warp slice
   const int ra = min(wr + g, N - 1), rb = min(wr + g + 8, N - 1);
   const uint4* pa = reinterpret_cast<const uint4*>(p.bits + (size_t)ra * W);
   const uint4* pb = reinterpret_cast<const uint4*>(p.bits + (size_t)rb * W);
-
   __shared__ uint64_t qbar;
   if (threadIdx.x == 0) {
     mbar_init(&qbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  if (MODE != 2) {  // per-row epilogue operands (independent of the batch pass)
+    for (int i = threadIdx.x; i < R * (DFSSM_RANK + 6); i += kMmaThreads) {
+      const int lr = i / (DFSSM_RANK + 6), f = i - lr * (DFSSM_RANK + 6);
+      const int row = min(row0 + lr, N - 1);
+      if (f < DFSSM_RANK) e_a[lr * DFSSM_RANK + f] = h2f(p.A16[(size_t)row * DFSSM_RANK + f]);
+      else if (f == DFSSM_RANK) e_scale[lr] = h2f(p.scale[row]);
+      else if (MODE == 0) {
+        const int ch = min(max(row - d_inner, 0), d_xbc - 1);
+        if (f == DFSSM_RANK + 5) e_cb[lr] = h2f(conv_b[ch]);
+        else e_cw[lr * 4 + (f - DFSSM_RANK - 1)] = h2f(conv_w[ch * DFSSM_DCONV + (f - DFSSM_RANK - 1)]);
+      }
+    }
+  }
   __syncthreads();
   unsigned phase = 0;
   for (int bt0 = 0; bt0 < B; bt0 += NB, phase ^= 1u) {
     const int nb = min(NB, B - bt0);
-    __syncthreads();  // previous pass done with sq
+    __syncthreads();  // previous pass done with sq and the epilogue operands
     // activation rows -> shared memory by TMA bulk copies (rows >= nb keep stale bytes; their
     // output columns are never stored)
     if (wid == 0) {
       if (lane == 0) mbar_expect_tx(&qbar, (unsigned)(nb * K));
       __syncwarp();
       for (int b = lane; b < nb; b += 32) bulk_g2s(sq + b * SQ, q + (size_t)(bt0 + b) * K, (unsigned)K, &qbar);
+    }
+    // per-batch epilogue operands
+    for (int i = threadIdx.x; i < nb * (DFSSM_RANK + 2); i += kMmaThreads) {
+      const int b = i / (DFSSM_RANK + 2), f = i - b * (DFSSM_RANK + 2);
+      if (f < DFSSM_RANK) {
+        if (MODE != 2) e_t[b * DFSSM_RANK + f] = h2f(t[(bt0 + b) * DFSSM_RANK + f]);
+      } else if (f == DFSSM_RANK) {
+        if (MODE != 2) e_xs[b] = h2f(xs[bt0 + b]);
+      } else {
+        e_qsum[b] = qsum[bt0 + b];
+      }
+    }
+    if (MODE == 1) {  // residual values (the conv-state region is free in this mode)
+      for (int i = threadIdx.x; i < nb * R; i += kMmaThreads) {
+        const int b = i / R, lr = i - b * R;
+        if (row0 + lr < N) e_cs[i] = h2f(out[(size_t)(bt0 + b) * ld_out + row0 + lr]);
+      }
+    }
+    if (MODE == 0) {
+      for (int i = threadIdx.x; i < nb * 3 * R; i += kMmaThreads) {
+        const int b = i / (3 * R), rem = i - b * 3 * R, tap = rem / R, lr = rem - tap * R;
+        const int ch = row0 + lr - d_inner;
+        if (ch >= 0 && ch < d_xbc && row0 + lr < N)
+          e_cs[i] = conv_state[(size_t)(bt0 + b) * 3 * d_xbc + (size_t)tap * d_xbc + ch];
+      }
     }
     mbar_wait_bounded(&qbar, phase);
     int acc[kMmaNT][4];
@@ -364,58 +412,57 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
     // D fragment: acc[tt][0..1] -> row g, batch cols 2c, 2c+1 of tile tt; [2..3] -> row g+8
 #pragma unroll
     for (int tt = 0; tt < kMmaNT; ++tt) {
-      int* r = red + (ks * 16 * RG + rg * 16) * NB + tt * 8 + 2 * c;
+      int* r = red + (ks * R + rg * 16) * NB + tt * 8 + 2 * c;
       r[g * NB] = acc[tt][0];
       r[g * NB + 1] = acc[tt][1];
       r[(g + 8) * NB] = acc[tt][2];
       r[(g + 8) * NB + 1] = acc[tt][3];
     }
     __syncthreads();
-    for (int o = threadIdx.x; o < 16 * RG * NB; o += kMmaThreads) {
+    for (int o = threadIdx.x; o < R * NB; o += kMmaThreads) {
       const int lr = o / NB, bb = o - lr * NB;
       const int row = row0 + lr, b = bt0 + bb;
       if (row >= N || bb >= nb) continue;
       int sacc = 0;
 #pragma unroll
-      for (int k2 = 0; k2 < KS; ++k2) sacc += red[(k2 * 16 * RG + lr) * NB + bb];
-      const int dot = 2 * sacc - qsum[b];
+      for (int k2 = 0; k2 < KS; ++k2) sacc += red[(k2 * R + lr) * NB + bb];
+      const int dot = 2 * sacc - e_qsum[bb];
       if (MODE == 2) {
         reinterpret_cast<int*>(out)[(size_t)b * ld_out + row] = dot;
         continue;
       }
-      const float base = round_h(round_h(round_h((float)dot) * h2f(xs[b])) * h2f(p.scale[row]));
-      const __half* arow = p.A16 + (size_t)row * DFSSM_RANK;
-      const __half* tb = t + b * DFSSM_RANK;
+      const float base = round_h(round_h(round_h((float)dot) * e_xs[bb]) * e_scale[lr]);
       float la = 0.f;
 #pragma unroll
-      for (int r = 0; r < DFSSM_RANK; ++r) la = fmaf(h2f(tb[r]), h2f(arow[r]), la);
+      for (int r = 0; r < DFSSM_RANK; ++r) la = fmaf(e_t[bb * DFSSM_RANK + r], e_a[lr * DFSSM_RANK + r], la);
       const float v = round_h(base + la);
       if (MODE == 0) {
         float res = v;
         const int ch = row - d_inner;
         if (ch >= 0 && ch < d_xbc) {
+          const float* es = e_cs + bb * 3 * R + lr;
+          const float s0 = es[0], s1 = es[R], s2 = es[2 * R];
           float* cs = conv_state + (size_t)b * 3 * d_xbc;
-          const float s0 = cs[ch], s1 = cs[d_xbc + ch], s2 = cs[2 * d_xbc + ch];
           cs[ch] = s1;
           cs[d_xbc + ch] = s2;
           cs[2 * d_xbc + ch] = v;
-          const __half* cw = conv_w + ch * DFSSM_DCONV;
-          const float o2 = s0 * h2f(cw[0]) + s1 * h2f(cw[1]) + s2 * h2f(cw[2]) + v * h2f(cw[3]) + h2f(conv_b[ch]);
+          const float* cw = e_cw + lr * 4;
+          const float o2 = s0 * cw[0] + s1 * cw[1] + s2 * cw[2] + v * cw[3] + e_cb[lr];
           const float sig = 1.0f / (1.0f + expf(-o2));
           res = o2 * sig;
         }
         out[(size_t)b * ld_out + row] = f2h(res);
       } else {
-        __half* xo = out + (size_t)b * ld_out + row;
-        *xo = f2h(h2f(*xo) + v);
+        out[(size_t)b * ld_out + row] = f2h(e_cs[bb * R + lr] + v);
       }
     }
   }
 }
 
 inline size_t proj_mma_smem(int K, int RG) {
-  const int NB = 8 * kMmaNT, KS = (kMmaThreads / 32) / RG;
-  return (size_t)NB * (K + 16) + (size_t)KS * 16 * RG * NB * 4;
+  const int NB = 8 * kMmaNT, KS = (kMmaThreads / 32) / RG, R = 16 * RG;
+  return (size_t)NB * (K + 16) + (size_t)KS * R * NB * 4 +
+         4 * ((size_t)NB * 3 * R + NB * DFSSM_RANK + R * DFSSM_RANK + R * 4 + 2 * R + 2 * NB);
 }
 
 // ---------------------------------------------------------------------------------------
