@@ -182,6 +182,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--config", default="cfg1", choices=list(CONFIGS))
     ap.add_argument("--batch", type=int, default=None, help="override the config's batch (per GPU for weak scaling)")
+    ap.add_argument("--layers", type=int, default=None, help="override the config's layer count (small profiling cases)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--mode", default="auto", choices=["auto", "graph", "eager", "persistent"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -191,6 +192,8 @@ def main():
     cfg = dict(CONFIGS[args.config])
     if args.batch:
         cfg["batch"] = args.batch
+    if args.layers:
+        cfg["layers"] = args.layers
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
