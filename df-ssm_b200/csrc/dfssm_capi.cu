@@ -101,7 +101,7 @@ int gemv_grid(const dfssm_engine* e, int N) {
 constexpr int kMmaMinBatch = 8;
 inline bool mma_ok(int K, int RG) {
   const int KS = (kMmaThreads / 32) / RG;
-  return K % 128 == 0 && ((K / 32) % KS) == 0 && ((K / 32 / KS) % 4) == 0;
+  return K % 128 == 0 && ((K / 32) % KS) == 0 && ((K / 32 / KS) % 4) == 0 && (K / 32 / KS) <= 4 * kMmaMaxBlk;
 }
 // Row groups per CTA for an N x K projection (0 = no tensor-core configuration fits).
 inline int mma_rg(int N, int K) {

@@ -290,6 +290,7 @@ proj_gemv_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ 
 // ---------------------------------------------------------------------------------------
 constexpr int kMmaThreads = 256;
 constexpr int kMmaNT = 4;  // batch tiles of 8 per pass (32 rows)
+constexpr int kMmaMaxBlk = 8;  // 16-byte weight blocks per warp slice (<= 32 words)
 
 __device__ __forceinline__ void mma_s8(int (&d)[4], unsigned a0, unsigned a1, unsigned a2, unsigned a3, unsigned b0,
                                        unsigned b1) {
@@ -386,15 +387,27 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
           e_cs[i] = conv_state[(size_t)(bt0 + b) * 3 * d_xbc + (size_t)tap * d_xbc + ch];
       }
     }
+    // this warp's weight words for the whole K slice, loaded before waiting for the activations
+    // (wpw <= 4 * kMmaMaxBlk words; one round trip instead of one per 4 words)
+    uint4 wva[kMmaMaxBlk], wvb[kMmaMaxBlk];
+#pragma unroll
+    for (int u = 0; u < kMmaMaxBlk; ++u) {
+      if (4 * u < wpw) {
+        wva[u] = ldg_stream(pa + (kw0 >> 2) + u);
+        wvb[u] = ldg_stream(pb + (kw0 >> 2) + u);
+      }
+    }
     mbar_wait_bounded(&qbar, phase);
     int acc[kMmaNT][4];
 #pragma unroll
     for (int tt = 0; tt < kMmaNT; ++tt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[tt][i] = 0;
-    for (int kw = kw0; kw < kw0 + wpw; kw += 4) {
-      const uint4 va = ldg_stream(pa + (kw >> 2));
-      const uint4 vb = ldg_stream(pb + (kw >> 2));
+#pragma unroll
+    for (int u = 0; u < kMmaMaxBlk; ++u) {
+      if (4 * u >= wpw) break;
+      const int kw = kw0 + 4 * u;
+      const uint4 va = wva[u], vb = wvb[u];
       const unsigned wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
