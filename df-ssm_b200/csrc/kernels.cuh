@@ -338,16 +338,29 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (MODE != 2) {  // per-row epilogue operands (independent of the batch pass)
-    for (int i = threadIdx.x; i < R * (DFSSM_RANK + 6); i += kMmaThreads) {
-      const int lr = i / (DFSSM_RANK + 6), f = i - lr * (DFSSM_RANK + 6);
-      const int row = min(row0 + lr, N - 1);
-      if (f < DFSSM_RANK) e_a[lr * DFSSM_RANK + f] = h2f(p.A16[(size_t)row * DFSSM_RANK + f]);
-      else if (f == DFSSM_RANK) e_scale[lr] = h2f(p.scale[row]);
-      else if (MODE == 0) {
-        const int ch = min(max(row - d_inner, 0), d_xbc - 1);
-        if (f == DFSSM_RANK + 5) e_cb[lr] = h2f(conv_b[ch]);
-        else e_cw[lr * 4 + (f - DFSSM_RANK - 1)] = h2f(conv_w[ch * DFSSM_DCONV + (f - DFSSM_RANK - 1)]);
+    constexpr int NF = DFSSM_RANK + 6, U = (R * NF + kMmaThreads - 1) / kMmaThreads;
+    float v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = threadIdx.x + u * kMmaThreads, lr = i / NF, f = i - lr * NF;
+      const int row = min(row0 + lr, N - 1), ch = min(max(row - d_inner, 0), d_xbc - 1);
+      float x = 0.f;
+      if (i < R * NF) {
+        if (f < DFSSM_RANK) x = h2f(p.A16[(size_t)row * DFSSM_RANK + f]);
+        else if (f == DFSSM_RANK) x = h2f(p.scale[row]);
+        else if (MODE == 0 && f == DFSSM_RANK + 5) x = h2f(conv_b[ch]);
+        else if (MODE == 0) x = h2f(conv_w[ch * DFSSM_DCONV + (f - DFSSM_RANK - 1)]);
       }
+      v[u] = x;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = threadIdx.x + u * kMmaThreads, lr = i / NF, f = i - lr * NF;
+      if (i >= R * NF) continue;
+      if (f < DFSSM_RANK) e_a[lr * DFSSM_RANK + f] = v[u];
+      else if (f == DFSSM_RANK) e_scale[lr] = v[u];
+      else if (f == DFSSM_RANK + 5) e_cb[lr] = v[u];
+      else e_cw[lr * 4 + (f - DFSSM_RANK - 1)] = v[u];
     }
   }
   __syncthreads();
@@ -363,29 +376,61 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
       for (int b = lane; b < nb; b += 32) bulk_g2s(sq + b * SQ, q + (size_t)(bt0 + b) * K, (unsigned)K, &qbar);
     }
     // per-batch epilogue operands
-    for (int i = threadIdx.x; i < nb * (DFSSM_RANK + 2); i += kMmaThreads) {
-      const int b = i / (DFSSM_RANK + 2), f = i - b * (DFSSM_RANK + 2);
-      if (f < DFSSM_RANK) {
-        if (MODE != 2) e_t[b * DFSSM_RANK + f] = h2f(t[(bt0 + b) * DFSSM_RANK + f]);
-      } else if (f == DFSSM_RANK) {
-        if (MODE != 2) e_xs[b] = h2f(xs[bt0 + b]);
-      } else {
-        e_qsum[b] = qsum[bt0 + b];
+    {
+      constexpr int NF = DFSSM_RANK + 2, U = (NB * NF + kMmaThreads - 1) / kMmaThreads;
+      float v[U];
+      int vq[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = threadIdx.x + u * kMmaThreads, b = i / NF, f = i - b * NF;
+        v[u] = 0.f;
+        vq[u] = 0;
+        if (b < nb) {
+          if (f < DFSSM_RANK) {
+            if (MODE != 2) v[u] = h2f(t[(bt0 + b) * DFSSM_RANK + f]);
+          } else if (f == DFSSM_RANK) {
+            if (MODE != 2) v[u] = h2f(xs[bt0 + b]);
+          } else {
+            vq[u] = qsum[bt0 + b];
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = threadIdx.x + u * kMmaThreads, b = i / NF, f = i - b * NF;
+        if (b >= NB) continue;
+        if (f < DFSSM_RANK) e_t[b * DFSSM_RANK + f] = v[u];
+        else if (f == DFSSM_RANK) e_xs[b] = v[u];
+        else e_qsum[b] = vq[u];
       }
     }
+    // staging loops issue all their global loads before the shared-memory stores (a load->store
+    // loop with a runtime trip count would otherwise pay one memory round trip per iteration)
     if (MODE == 1) {  // residual values (the conv-state region is free in this mode)
-      for (int i = threadIdx.x; i < nb * R; i += kMmaThreads) {
-        const int b = i / R, lr = i - b * R;
-        if (row0 + lr < N) e_cs[i] = h2f(out[(size_t)(bt0 + b) * ld_out + row0 + lr]);
+      constexpr int U = (NB * R + kMmaThreads - 1) / kMmaThreads;
+      float v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = threadIdx.x + u * kMmaThreads, b = i / R, lr = i - b * R;
+        v[u] = (b < nb && row0 + lr < N) ? h2f(out[(size_t)(bt0 + b) * ld_out + row0 + lr]) : 0.f;
       }
+#pragma unroll
+      for (int u = 0; u < U; ++u) e_cs[threadIdx.x + u * kMmaThreads] = v[u];
     }
     if (MODE == 0) {
-      for (int i = threadIdx.x; i < nb * 3 * R; i += kMmaThreads) {
+      constexpr int U = (NB * 3 * R + kMmaThreads - 1) / kMmaThreads;
+      float v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = threadIdx.x + u * kMmaThreads;
         const int b = i / (3 * R), rem = i - b * 3 * R, tap = rem / R, lr = rem - tap * R;
         const int ch = row0 + lr - d_inner;
-        if (ch >= 0 && ch < d_xbc && row0 + lr < N)
-          e_cs[i] = conv_state[(size_t)(bt0 + b) * 3 * d_xbc + (size_t)tap * d_xbc + ch];
+        v[u] = (b < nb && ch >= 0 && ch < d_xbc && row0 + lr < N)
+                   ? conv_state[(size_t)(bt0 + b) * 3 * d_xbc + (size_t)tap * d_xbc + ch]
+                   : 0.f;
       }
+#pragma unroll
+      for (int u = 0; u < U; ++u) e_cs[threadIdx.x + u * kMmaThreads] = v[u];
     }
     // this warp's weight words for the whole K slice, loaded before waiting for the activations
     // (wpw <= 4 * kMmaMaxBlk words; one round trip instead of one per 4 words)
