@@ -313,12 +313,12 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
   const int K = p.K, N = p.N, W = K >> 5;
   const int SQ = K + 16;                                         // padded activation row stride
   int8_t* sq = reinterpret_cast<int8_t*>(smem);                  // [NB][SQ]
-  int* red = reinterpret_cast<int*>(smem + NB * SQ);             // [KS][R][NB]
+  int* red = reinterpret_cast<int*>(smem + NB * SQ);             // [KS][NB][R] (batch-major)
   // epilogue operands, loaded with independent loads before the MMA loop
   float* e_cs = reinterpret_cast<float*>(red + KS * R * NB);     // [NB][3][R] conv state (MODE 0)
   float* e_t = e_cs + NB * 3 * R;                                // [NB][16]
-  float* e_a = e_t + NB * DFSSM_RANK;                            // [R][16] LoRA A
-  float* e_cw = e_a + R * DFSSM_RANK;                            // [R][4] conv weights
+  float* e_a = e_t + NB * DFSSM_RANK;                            // [R][17] LoRA A (padded row)
+  float* e_cw = e_a + R * (DFSSM_RANK + 1);                      // [R][4] conv weights
   float* e_misc = e_cw + R * 4;                                  // scale[R], conv_b[R], xs[NB], qsum[NB]
   float* e_scale = e_misc;
   float* e_cb = e_scale + R;
@@ -357,7 +357,7 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
     for (int u = 0; u < U; ++u) {
       const int i = threadIdx.x + u * kMmaThreads, lr = i / NF, f = i - lr * NF;
       if (i >= R * NF) continue;
-      if (f < DFSSM_RANK) e_a[lr * DFSSM_RANK + f] = v[u];
+      if (f < DFSSM_RANK) e_a[lr * (DFSSM_RANK + 1) + f] = v[u];
       else if (f == DFSSM_RANK) e_scale[lr] = v[u];
       else if (f == DFSSM_RANK + 5) e_cb[lr] = v[u];
       else e_cw[lr * 4 + (f - DFSSM_RANK - 1)] = v[u];
@@ -470,20 +470,22 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
     // D fragment: acc[tt][0..1] -> row g, batch cols 2c, 2c+1 of tile tt; [2..3] -> row g+8
 #pragma unroll
     for (int tt = 0; tt < kMmaNT; ++tt) {
-      int* r = red + (ks * R + rg * 16) * NB + tt * 8 + 2 * c;
-      r[g * NB] = acc[tt][0];
-      r[g * NB + 1] = acc[tt][1];
-      r[(g + 8) * NB] = acc[tt][2];
-      r[(g + 8) * NB + 1] = acc[tt][3];
+      int* r = red + (ks * NB + tt * 8 + 2 * c) * R + rg * 16 + g;
+      r[0] = acc[tt][0];
+      r[R] = acc[tt][1];
+      r[8] = acc[tt][2];
+      r[R + 8] = acc[tt][3];
     }
     __syncthreads();
+    // consecutive threads take consecutive rows of one batch row: coalesced stores of out and of
+    // the conv state, conflict-free reads of the split-K partials
     for (int o = threadIdx.x; o < R * NB; o += kMmaThreads) {
-      const int lr = o / NB, bb = o - lr * NB;
+      const int bb = o / R, lr = o - bb * R;
       const int row = row0 + lr, b = bt0 + bb;
       if (row >= N || bb >= nb) continue;
       int sacc = 0;
 #pragma unroll
-      for (int k2 = 0; k2 < KS; ++k2) sacc += red[(k2 * R + lr) * NB + bb];
+      for (int k2 = 0; k2 < KS; ++k2) sacc += red[(k2 * NB + bb) * R + lr];
       const int dot = 2 * sacc - e_qsum[bb];
       if (MODE == 2) {
         reinterpret_cast<int*>(out)[(size_t)b * ld_out + row] = dot;
@@ -492,7 +494,7 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
       const float base = round_h(round_h(round_h((float)dot) * e_xs[bb]) * e_scale[lr]);
       float la = 0.f;
 #pragma unroll
-      for (int r = 0; r < DFSSM_RANK; ++r) la = fmaf(e_t[bb * DFSSM_RANK + r], e_a[lr * DFSSM_RANK + r], la);
+      for (int r = 0; r < DFSSM_RANK; ++r) la = fmaf(e_t[bb * DFSSM_RANK + r], e_a[lr * (DFSSM_RANK + 1) + r], la);
       const float v = round_h(base + la);
       if (MODE == 0) {
         float res = v;
@@ -520,7 +522,7 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
 inline size_t proj_mma_smem(int K, int RG) {
   const int NB = 8 * kMmaNT, KS = (kMmaThreads / 32) / RG, R = 16 * RG;
   return (size_t)NB * (K + 16) + (size_t)KS * R * NB * 4 +
-         4 * ((size_t)NB * 3 * R + NB * DFSSM_RANK + R * DFSSM_RANK + R * 4 + 2 * R + 2 * NB);
+         4 * ((size_t)NB * 3 * R + NB * DFSSM_RANK + R * (DFSSM_RANK + 1) + R * 4 + 2 * R + 2 * NB);
 }
 
 // ---------------------------------------------------------------------------------------
