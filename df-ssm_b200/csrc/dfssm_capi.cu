@@ -67,13 +67,20 @@ int effective_mode(const dfssm_engine* e) {
 
 // ------------------------------------------------------------------ kernel launches
 
+// A group is a contiguous range of the batch's sequences [b0, b0 + nb); every per-op kernel works
+// on one group through row offsets of the batch-major buffers.
+struct Group {
+  int b0, nb;
+};
+
 int launch_prep(dfssm_engine* e, const __half* in, int K, const float* w, int quant, const ProjW* p,
-                cudaStream_t s) {
+                cudaStream_t s, Group G) {
   if (quant && p && K % 512 == 0) {
     const int kpt = K / 512;
 #define DFSSM_PREP_FAST(n)                                                                                  \
   if (kpt == n) {                                                                                          \
-    act_prep_fast_kernel<n><<<e->batch, kPrepFastThreads, 0, s>>>(in, K, w, e->q, e->xs, e->qsum, p->B16, e->t); \
+    act_prep_fast_kernel<n><<<G.nb, kPrepFastThreads, 0, s>>>(in + (size_t)G.b0 * K, K, w, e->q + (size_t)G.b0 * K, \
+                                                              e->xs + G.b0, e->qsum + G.b0, p->B16, e->t + G.b0 * kRank); \
     CHECK_LAUNCH();                                                                                        \
     return DFSSM_OK;                                                                                       \
   }
@@ -84,8 +91,9 @@ int launch_prep(dfssm_engine* e, const __half* in, int K, const float* w, int qu
 #undef DFSSM_PREP_FAST
   }
   const size_t sm = (size_t)K * sizeof(__half);
-  act_prep_kernel<<<e->batch, kPrepThreads, sm, s>>>(in, K, w, quant, e->xn, e->q, e->xs, e->qsum,
-                                                     p ? p->B16 : nullptr, e->t);
+  act_prep_kernel<<<G.nb, kPrepThreads, sm, s>>>(in + (size_t)G.b0 * K, K, w, quant, e->xn + (size_t)G.b0 * K,
+                                                 e->q + (size_t)G.b0 * K, e->xs + G.b0, e->qsum + G.b0,
+                                                 p ? p->B16 : nullptr, e->t + G.b0 * kRank);
   CHECK_LAUNCH();
   return DFSSM_OK;
 }
@@ -142,29 +150,46 @@ int launch_gemv(dfssm_engine* e, const ProjW& p, int B, const int8_t* q, const i
   return DFSSM_OK;
 }
 
-int enqueue_layer(dfssm_engine* e, int l, cudaStream_t s) {
+int enqueue_layer(dfssm_engine* e, int l, cudaStream_t s, Group G) {
   const dfssm_dims& d = e->d;
   const LayerW& L = e->layers[l];
-  const int B = e->batch;
+  const int B = G.nb, b0 = G.b0;
+  const size_t hd = (size_t)d.nheads * DFSSM_HEADDIM * DFSSM_DSTATE;
   int rc;
-  if ((rc = launch_prep(e, e->x, d.d_model, L.ln_w, 1, &L.in, s))) return rc;
-  if ((rc = launch_gemv<0>(e, L.in, B, e->q, e->qsum, e->xs, e->t, e->proj, d.n_in,
-                           e->conv + (size_t)l * e->conv_layer, &L, s)))
+  if ((rc = launch_prep(e, e->x, d.d_model, L.ln_w, 1, &L.in, s, G))) return rc;
+  if ((rc = launch_gemv<0>(e, L.in, B, e->q + (size_t)b0 * d.d_model, e->qsum + b0, e->xs + b0, e->t + b0 * kRank,
+                           e->proj + (size_t)b0 * d.n_in, d.n_in,
+                           e->conv + (size_t)l * e->conv_layer + (size_t)b0 * 3 * d.d_xbc, &L, s)))
     return rc;
+  __half* pr = e->proj + (size_t)b0 * d.n_in;
   ssm_gate_kernel<<<dim3(d.nheads, B), kSsmThreads, 0, s>>>(
-      e->proj + d.d_inner, d.n_in, e->proj + d.d_inner + d.d_xbc, d.n_in, e->proj, d.n_in, d.d_inner,
-      d.d_state, d.nheads, L.dt_bias, L.A_log, L.Dp, e->ssm + (size_t)l * e->ssm_layer, e->gated, d.d_inner);
+      pr + d.d_inner, d.n_in, pr + d.d_inner + d.d_xbc, d.n_in, pr, d.n_in, d.d_inner, d.d_state, d.nheads,
+      L.dt_bias, L.A_log, L.Dp, e->ssm + (size_t)l * e->ssm_layer + (size_t)b0 * hd,
+      e->gated + (size_t)b0 * d.d_inner, d.d_inner);
   CHECK_LAUNCH();
-  if ((rc = launch_prep(e, e->gated, d.d_inner, L.norm_w, 1, &L.out, s))) return rc;
-  if ((rc = launch_gemv<1>(e, L.out, B, e->q, e->qsum, e->xs, e->t, e->x, d.d_model, nullptr, nullptr, s)))
+  if ((rc = launch_prep(e, e->gated, d.d_inner, L.norm_w, 1, &L.out, s, G))) return rc;
+  if ((rc = launch_gemv<1>(e, L.out, B, e->q + (size_t)b0 * d.d_inner, e->qsum + b0, e->xs + b0, e->t + b0 * kRank,
+                           e->x + (size_t)b0 * d.d_model, d.d_model, nullptr, nullptr, s)))
     return rc;
   return DFSSM_OK;
+}
+
+// Number of independent sequence groups the per-op step is split into.  Each group's layer chain is
+// captured on its own stream, so the latency-bound projection kernels of one group overlap the
+// bandwidth-bound state update of another.  DFSSM_GROUPS overrides (1..4).
+int step_groups(const dfssm_engine* e) {
+  const char* env = getenv("DFSSM_GROUPS");
+  if (env) {
+    const int g = atoi(env);
+    if (g >= 1 && g <= kMaxGroups && e->batch >= g) return g;
+  }
+  return e->batch >= 16 ? 2 : 1;
 }
 
 int enqueue_head(dfssm_engine* e, cudaStream_t s) {
   const dfssm_dims& d = e->d;
   int rc;
-  if ((rc = launch_prep(e, e->x, d.d_model, e->norm_f, 0, nullptr, s))) return rc;
+  if ((rc = launch_prep(e, e->x, d.d_model, e->norm_f, 0, nullptr, s, Group{0, e->batch}))) return rc;
   if (e->batch >= kMmaMinBatch && d.d_model % 64 == 0) {
     const size_t sm = lm_head_mma_smem(d.d_model);
     CU(cudaFuncSetAttribute(lm_head_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
@@ -186,8 +211,25 @@ int enqueue_step_ops(dfssm_engine* e, cudaStream_t s) {
   embed_kernel<<<e->batch, 256, 0, s>>>(e->tokens, e->Eq, e->Es, d.d_model, d.vocab, e->x);
   CHECK_LAUNCH();
   int rc;
-  for (int l = 0; l < d.n_layer; ++l)
-    if ((rc = enqueue_layer(e, l, s))) return rc;
+  const int G = step_groups(e);
+  if (G == 1) {
+    for (int l = 0; l < d.n_layer; ++l)
+      if ((rc = enqueue_layer(e, l, s, Group{0, e->batch}))) return rc;
+    return enqueue_head(e, s);
+  }
+  // fork: group g runs all layers on stream gs[g] (group 0 on s), then join before the LM head
+  CU(cudaEventRecord(e->ev_fork, s));
+  for (int g = 1; g < G; ++g) CU(cudaStreamWaitEvent(e->gs[g], e->ev_fork, 0));
+  for (int g = 0; g < G; ++g) {
+    const int b0 = (int)((long long)e->batch * g / G), b1 = (int)((long long)e->batch * (g + 1) / G);
+    cudaStream_t gsg = g == 0 ? s : e->gs[g];
+    for (int l = 0; l < d.n_layer; ++l)
+      if ((rc = enqueue_layer(e, l, gsg, Group{b0, b1 - b0}))) return rc;
+  }
+  for (int g = 1; g < G; ++g) {
+    CU(cudaEventRecord(e->ev_join[g], e->gs[g]));
+    CU(cudaStreamWaitEvent(s, e->ev_join[g], 0));
+  }
   return enqueue_head(e, s);
 }
 
@@ -485,6 +527,12 @@ int build_engine(const unsigned char* img, size_t n, int device, int max_batch, 
   if (ce != cudaSuccess) return cleanup(dfssm_fail(DFSSM_ERR_CUDA, "state clear: %s", cudaGetErrorString(ce)));
   ce = cudaMemcpy(e->d_layers, e->layers.data(), sizeof(LayerW) * d.n_layer, cudaMemcpyHostToDevice);
   if (ce != cudaSuccess) return cleanup(dfssm_fail(DFSSM_ERR_CUDA, "layer table upload: %s", cudaGetErrorString(ce)));
+  for (int g = 1; g < kMaxGroups; ++g)
+    if (cudaStreamCreateWithFlags(&e->gs[g], cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&e->ev_join[g], cudaEventDisableTiming) != cudaSuccess)
+      return cleanup(dfssm_fail(DFSSM_ERR_CUDA, "group stream creation failed"));
+  if (cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming) != cudaSuccess)
+    return cleanup(dfssm_fail(DFSSM_ERR_CUDA, "event creation failed"));
   if (cudaStreamCreateWithFlags(&e->s, cudaStreamNonBlocking) != cudaSuccess ||
       cudaEventCreateWithFlags(&e->ev_in, cudaEventDisableTiming) != cudaSuccess ||
       cudaEventCreateWithFlags(&e->ev_out, cudaEventDisableTiming) != cudaSuccess)
@@ -542,6 +590,11 @@ void dfssm_destroy(dfssm_engine* e) {
   if (e->ev_in) cudaEventDestroy(e->ev_in);
   if (e->ev_out) cudaEventDestroy(e->ev_out);
   if (e->s) cudaStreamDestroy(e->s);
+  for (int g = 1; g < kMaxGroups; ++g) {
+    if (e->gs[g]) cudaStreamDestroy(e->gs[g]);
+    if (e->ev_join[g]) cudaEventDestroy(e->ev_join[g]);
+  }
+  if (e->ev_fork) cudaEventDestroy(e->ev_fork);
   persistent_destroy(e);
   if (e->arena) cudaFree(e->arena);
   if (e->work) cudaFree(e->work);
@@ -676,7 +729,7 @@ int dfssm_layer_step(dfssm_engine* e, int layer, void* stream) {
   CU(cudaSetDevice(e->device));
   if (effective_mode(e) == 3)
     return launch_persistent_layers(e, layer, layer + 1, 1, 0, static_cast<cudaStream_t>(stream));
-  return enqueue_layer(e, layer, static_cast<cudaStream_t>(stream));
+  return enqueue_layer(e, layer, static_cast<cudaStream_t>(stream), Group{0, e->batch});
 }
 
 size_t dfssm_trace_entries(const dfssm_engine* e) { return e ? persistent_trace_entries(e) : 0; }

@@ -8,6 +8,8 @@
 #include "../../include/dfssm.h"
 #include "types.cuh"
 
+constexpr int kMaxGroups = 4;
+
 struct dfssm_engine {
   int device = 0;
   dfssm_dims d{};
@@ -37,6 +39,8 @@ struct dfssm_engine {
   // execution
   cudaStream_t s = nullptr;
   cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+  cudaStream_t gs[kMaxGroups] = {};           // streams of sequence groups 1.. (group 0 uses s)
+  cudaEvent_t ev_fork = nullptr, ev_join[kMaxGroups] = {};
   cudaGraphExec_t gexec = nullptr;
   int graph_batch = -1, graph_mode = -1;
   int sm_count = 148;

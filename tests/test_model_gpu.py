@@ -79,6 +79,7 @@ def _check_logits(got, ref):
 
 
 @pytest.mark.parametrize("B,mode,shape", [(1, "graph", "tiny"), (3, "graph", "tiny"), (9, "graph", "small"),
+                                          (18, "graph", "small"),
                                           (1, "persistent", "small"), (2, "persistent", "small")])
 def test_tiny_model_matches_oracle(B, mode, shape):
     w = weights(shape, 2, seed=0)
@@ -205,3 +206,17 @@ def test_persistent_matches_graph_tokens_on_1p3b_two_layers():
     a = model(w, 2, mode="persistent").generate(12, prompt=p, verbose=False)
     b = model(w, 2, mode="graph").generate(12, prompt=p, verbose=False)
     np.testing.assert_array_equal(a, b)
+
+
+@pytest.mark.parametrize("groups", ["2", "4"])
+def test_sequence_groups_are_bitwise_equal_to_one_group(groups, monkeypatch):
+    """Splitting the batch into independent sequence groups (one stream each inside the graph)
+    changes only scheduling, never results."""
+    w = weights("small", 2, seed=8)
+    p = np.random.default_rng(4).integers(0, w.dims.vocab, (16, 3))
+    monkeypatch.setenv("DFSSM_GROUPS", "1")
+    a = _run_engine(model(w, 16, mode="graph"), p, 5)
+    monkeypatch.setenv("DFSSM_GROUPS", groups)
+    b = _run_engine(model(w, 16, mode="graph"), p, 5)
+    np.testing.assert_array_equal(a[0], b[0])
+    np.testing.assert_array_equal(a[1], b[1])
