@@ -28,6 +28,7 @@ SIGNATURES = {
     "dfssm_set_mode": (c_int, [c_void_p, c_int]),
     "dfssm_get_mode": (c_int, [c_void_p, POINTER(c_int)]),
     "dfssm_reset": (c_int, [c_void_p, c_void_p]),
+    "dfssm_reset_slots": (c_int, [c_void_p, c_int, c_int, c_void_p]),
     "dfssm_step": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "dfssm_step_host": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "dfssm_check_finite": (c_int, [c_void_p, c_void_p]),

@@ -642,6 +642,20 @@ int dfssm_reset(dfssm_engine* e, void* stream) {
   return DFSSM_OK;
 }
 
+int dfssm_reset_slots(dfssm_engine* e, int first, int count, void* stream) {
+  if (!e) return dfssm_fail(DFSSM_ERR_ARG, "NULL engine");
+  if (first < 0 || count < 1 || first + count > e->max_batch)
+    return dfssm_fail(DFSSM_ERR_ARG, "slots [%d, %d) outside [0, max_batch=%d)", first, first + count, e->max_batch);
+  CU(cudaSetDevice(e->device));
+  cudaStream_t us = static_cast<cudaStream_t>(stream);
+  const size_t hseq = e->ssm_layer / e->max_batch, cseq = e->conv_layer / e->max_batch;  // floats per sequence
+  for (int l = 0; l < e->d.n_layer; ++l) {
+    CU(cudaMemsetAsync(e->ssm + (size_t)l * e->ssm_layer + (size_t)first * hseq, 0, (size_t)count * hseq * 4, us));
+    CU(cudaMemsetAsync(e->conv + (size_t)l * e->conv_layer + (size_t)first * cseq, 0, (size_t)count * cseq * 4, us));
+  }
+  return DFSSM_OK;
+}
+
 int dfssm_step(dfssm_engine* e, const int32_t* tokens_dev, float* logits_dev, int32_t* next_tokens_dev,
                void* stream) {
   if (!e) return dfssm_fail(DFSSM_ERR_ARG, "NULL engine");

@@ -239,3 +239,41 @@ def pack_signs(signs01: np.ndarray) -> np.ndarray:
     assert k % 32 == 0
     b = np.packbits(signs01.astype(np.uint8), axis=1, bitorder="little")
     return b.view(np.uint32).reshape(n, k // 32).view(np.int32)
+
+
+def main(argv=None):
+    """`python -m dfssm_b200.dfssm_format convert IN OUT [--int8-embedding]`: rewrite a .dfssm file,
+    optionally storing the tied embedding as int8 + per-row fp16 scale (header reserved byte 0 = 1),
+    which halves the embedding bytes (206 -> 103 MB at vocab 50280, d_model 2048)."""
+    import argparse
+    ap = argparse.ArgumentParser(prog="python -m dfssm_b200.dfssm_format")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    c = sub.add_parser("convert")
+    c.add_argument("src")
+    c.add_argument("dst")
+    c.add_argument("--int8-embedding", action="store_true")
+    i = sub.add_parser("info")
+    i.add_argument("src")
+    a = ap.parse_args(argv)
+    if a.cmd == "info":
+        with open(a.src, "rb") as fh:
+            d, kind = parse_header(fh.read(HEADER_SIZE))
+        print(d, "embedding", "int8" if kind == EMB_INT8 else "fp16")
+        return
+    w = read(a.src)
+    if a.int8_embedding and w.emb_q is None:
+        w.emb_q, w.emb_s = quantize_embedding_int8(w.emb_f16)
+    write(a.dst, w, EMB_INT8 if a.int8_embedding else EMB_FP16)
+
+
+def quantize_embedding_int8(E16: np.ndarray):
+    """Per-row symmetric int8 (absmax / 127, fp16 scale) of an fp16 embedding."""
+    Ef = E16.astype(np.float32)
+    s32 = np.abs(Ef).max(axis=1) / np.float32(127.0)            # codes from the fp32 scale
+    s32 = np.where(s32 > 0, s32, np.float32(1.0)).astype(np.float32)
+    q = np.clip(np.rint(Ef / s32[:, None]), -127, 127).astype(np.int8)
+    return q, s32.astype(np.float16)
+
+
+if __name__ == "__main__":
+    main()

@@ -109,6 +109,10 @@ class DFSSMModel:
     def reset_state(self):
         _lib.check(self.lib.dfssm_reset(self._h, self._stream()))
 
+    def reset_sequences(self, first: int, count: int = 1):
+        """Zero the state of sequence slots [first, first + count) only (continuous batching)."""
+        _lib.check(self.lib.dfssm_reset_slots(self._h, first, count, self._stream()))
+
     # ------------------------------------------------------------------ decode
     def step(self, token_ids=None, logits: bool = True):
         """One decode step.  token_ids: [B] ints (host or device) or None to continue from the

@@ -70,6 +70,11 @@ int dfssm_get_mode(const dfssm_engine* e, int* mode);
 /* Zero all SSM and conv state (DFSSMModel.reset_state, df_ssm_inference.py:137-139). */
 int dfssm_reset(dfssm_engine* e, void* stream);
 
+/* Zero the SSM and conv state of sequence slots [first, first + count) only, so that a finished
+ * sequence's slot can take a new sequence while the others keep decoding (continuous batching).
+ * The reference has no per-sequence reset (reset_state, df_ssm_inference.py:137-139, clears all). */
+int dfssm_reset_slots(dfssm_engine* e, int first, int count, void* stream);
+
 /* One decode step for the current batch: embeds tokens_dev[b] (int32 [batch], or the
  * engine's own next-token buffer when NULL, i.e. greedy continuation), runs all layers,
  * the final norm, the LM head and the greedy argmax.  Optional outputs: logits_dev

@@ -90,3 +90,15 @@ def test_reader_rejects_bad_images():
     struct.pack_into("<I", bad, 8 + 4 * 5, 32)  # headdim 32 -> nheads*headdim != d_inner
     with pytest.raises(ValueError):
         fmt.from_bytes(bytes(bad))
+
+
+def test_convert_cli_to_int8_embedding(tmp_path):
+    w = tiny(1)
+    src, dst = tmp_path / "a.dfssm", tmp_path / "b.dfssm"
+    fmt.write(str(src), w, fmt.EMB_FP16)
+    fmt.main(["convert", str(src), str(dst), "--int8-embedding"])
+    w2 = fmt.read(str(dst))
+    assert w2.emb_q is not None and w2.emb_f16 is None
+    # synthetic embeddings are int8 * fp16(0.01) rounded to fp16: the int8 codes are recovered exactly
+    np.testing.assert_array_equal(w2.emb_q, w.emb_q)
+    assert dst.stat().st_size < src.stat().st_size

@@ -220,3 +220,25 @@ def test_sequence_groups_are_bitwise_equal_to_one_group(groups, monkeypatch):
     b = _run_engine(model(w, 16, mode="graph"), p, 5)
     np.testing.assert_array_equal(a[0], b[0])
     np.testing.assert_array_equal(a[1], b[1])
+
+
+def test_reset_one_sequence_slot_continuous_batching():
+    """Resetting slot 1 mid-stream makes it decode like a fresh sequence; slot 0 is untouched."""
+    w = weights("tiny", 2, seed=9)
+    rng = np.random.default_rng(6)
+    p_old, p_new = rng.integers(0, w.dims.vocab, (2, 4)), rng.integers(0, w.dims.vocab, (1, 4))
+    m = model(w, 2, mode="graph")
+    _run_engine(m, p_old, 3)                       # both slots carry state
+    h0 = m.h_states[0][0].cpu().numpy().copy()
+    m.reset_sequences(1)
+    assert float(m.h_states[0][1].abs().max()) == 0.0
+    np.testing.assert_array_equal(m.h_states[0][0].cpu().numpy(), h0)
+    ref = model(w, 1, mode="graph")
+    ref.reset_state()
+    for t in range(4):                             # the fresh sequence alone
+        ref.step(torch.from_numpy(p_new[:, t]), logits=False)
+    # drive slot 1 with the new prompt while slot 0 continues its own greedy stream
+    for t in range(4):
+        cur0 = m._tok_out[:1].cpu().numpy()
+        m.step(torch.from_numpy(np.concatenate([cur0, p_new[:, t]]).astype(np.int64)), logits=False)
+    np.testing.assert_array_equal(m.h_states[1][1].cpu().numpy(), ref.h_states[1][0].cpu().numpy())
