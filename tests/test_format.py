@@ -99,6 +99,9 @@ def test_convert_cli_to_int8_embedding(tmp_path):
     fmt.main(["convert", str(src), str(dst), "--int8-embedding"])
     w2 = fmt.read(str(dst))
     assert w2.emb_q is not None and w2.emb_f16 is None
-    # synthetic embeddings are int8 * fp16(0.01) rounded to fp16: the int8 codes are recovered exactly
-    np.testing.assert_array_equal(w2.emb_q, w.emb_q)
+    # per-row absmax/127 quantisation reconstructs every value within half a step (+ fp16 scale rounding)
+    E = w.embedding_f16().astype(np.float32)
+    deq = w2.emb_q.astype(np.float32) * w2.emb_s.astype(np.float32)[:, None]
+    step = w2.emb_s.astype(np.float32)[:, None]
+    assert np.all(np.abs(deq - E) <= 0.5 * step + 1e-3 * np.abs(E) + 1e-6)
     assert dst.stat().st_size < src.stat().st_size
