@@ -805,6 +805,8 @@ int dfssm_ssm_step(const void* xbc_f16, int ld_xbc, const void* dt_f16, int ld_d
     return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "headdim=%d d_state=%d (built for 64/128)", headdim, d_state);
   if (batch < 1 || nheads < 1) return dfssm_fail(DFSSM_ERR_ARG, "bad sizes");
   if ((uintptr_t)h_state & 15) return dfssm_fail(DFSSM_ERR_ARG, "h_state must be 16-byte aligned");
+  if (ld_xbc % 4 || ((uintptr_t)xbc_f16 & 7))
+    return dfssm_fail(DFSSM_ERR_ARG, "xbc rows must start on 8-byte boundaries (ld_xbc %% 4 == 0)");
   const int d_inner = nheads * headdim;
   ssm_gate_kernel<<<dim3(nheads, batch), kSsmThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __half*>(xbc_f16), ld_xbc, static_cast<const __half*>(dt_f16), ld_dt, nullptr, 0, d_inner,

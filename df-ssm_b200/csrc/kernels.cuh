@@ -540,25 +540,32 @@ ssm_gate_kernel(const __half* __restrict__ xbc, int ld_xbc, const __half* __rest
                 const float* __restrict__ Dp, float* __restrict__ hstate, __half* __restrict__ out, int ld_out) {
   const int h = blockIdx.x, b = blockIdx.y;
   const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const __half* xc = xbc + (size_t)b * ld_xbc;     // conv'd x   [d_inner]
-  const __half* Bc = xc + d_inner;                 // conv'd B   [d_state]
-  const __half* Cc = xc + d_inner + d_state;       // conv'd C   [d_state]
-  float dtv = h2f(dtr[(size_t)b * ld_dt + h]) + dt_bias[h];
-  dtv = log1pf(expf(dtv));
-  const float Abar = expf(dtv * (-expf(A_log[h])));
-  const float Dh = Dp[h];
-
   const int n0 = lane * 4;
-  float Bn[4], Cn[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    Bn[i] = h2f(Bc[n0 + i]);
-    Cn[i] = h2f(Cc[n0 + i]);
-  }
+  // the 32 KB state tile is requested first: its addresses depend on nothing else, so the HBM
+  // stream starts before the small per-head inputs and the dt / exp arithmetic
   float* hs = hstate + ((size_t)b * nheads + h) * (DFSSM_HEADDIM * DFSSM_DSTATE);
   float4 hv[8];
 #pragma unroll
   for (int r = 0; r < 8; ++r) hv[r] = __ldcs(reinterpret_cast<const float4*>(hs + (wid * 8 + r) * DFSSM_DSTATE + n0));
+  const __half* xc = xbc + (size_t)b * ld_xbc;     // conv'd x   [d_inner]
+  const __half* Bc = xc + d_inner;                 // conv'd B   [d_state]
+  const __half* Cc = xc + d_inner + d_state;       // conv'd C   [d_state]
+  const uint2 bq = *reinterpret_cast<const uint2*>(Bc + n0);
+  const uint2 cq = *reinterpret_cast<const uint2*>(Cc + n0);
+  float dtv = h2f(dtr[(size_t)b * ld_dt + h]) + dt_bias[h];
+  dtv = log1pf(expf(dtv));
+  const float Abar = expf(dtv * (-expf(A_log[h])));
+  const float Dh = Dp[h];
+  float Bn[4], Cn[4];
+  {
+    const __half* bh = reinterpret_cast<const __half*>(&bq);
+    const __half* ch = reinterpret_cast<const __half*>(&cq);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      Bn[i] = h2f(bh[i]);
+      Cn[i] = h2f(ch[i]);
+    }
+  }
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
     const int pp = wid * 8 + r;

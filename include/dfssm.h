@@ -150,7 +150,7 @@ int dfssm_conv_step(float* conv_state, void* xbc_f16, int ld_xbc, const void* co
 /* Mamba-2 state update (df_ssm_kernels.cu:53-103, ssm_step), fp32 state:
  * xbc fp16 [B][ld_xbc] holds conv'd x [d_inner] | B [d_state] | C [d_state];
  * dt fp16 [B][ld_dt] raw (before softplus); h fp32 [B][nheads][64][128] in place;
- * y fp16 [B][ld_y] = C.h + D*x.  headdim must be 64 and d_state 128. */
+ * y fp16 [B][ld_y] = C.h + D*x.  headdim must be 64 and d_state 128; ld_xbc % 4 == 0. */
 int dfssm_ssm_step(const void* xbc_f16, int ld_xbc, const void* dt_f16, int ld_dt,
                    const float* dt_bias, const float* A_log, const float* D, float* h_state,
                    void* y_f16, int ld_y, int batch, int nheads, int headdim, int d_state,
