@@ -108,10 +108,9 @@ __device__ __forceinline__ void wait_counter(unsigned* cnt, unsigned target, uns
 __device__ __forceinline__ void grid_arrive(const PParams& P, unsigned& nbar) {
   __syncthreads();
   ++nbar;
-  if (threadIdx.x == 0) {
-    __threadfence();
-    red_release_add(P.sync, 1u);
-  }
+  // bar.sync orders the block's writes before thread 0's release (PTX causality order is
+  // transitive), so the gpu-scope release needs no separate fence.sc
+  if (threadIdx.x == 0) red_release_add(P.sync, 1u);
 }
 __device__ __forceinline__ void grid_wait(const PParams& P, unsigned nbar) {
   wait_counter(P.sync, nbar * gridDim.x, P.sync + 3, 1u);
@@ -283,21 +282,20 @@ __device__ __forceinline__ float conv_silu(float s0, float s1, float s2, float v
 
 // LoRA-t producer: compute this CTA's ranks (r = tj, tj + n_t, ...) of t = fp16(xn . B16^T) and
 // publish them in t_g[which]; one release-increment of the t counter per producer and use.
+// The values of the first rank (r = tj) were loaded into b0 before the barrier, so the
+// producer's critical path holds no HBM round trip for them.
 template <int B, int KPT>
-__device__ void publish_t(const PParams& P, int tj, const float (&vals)[B][KPT], const __half* B16, int K, int which,
-                          float* red) {
+__device__ void publish_t(const PParams& P, int tj, const float (&vals)[B][KPT], typename RankHalves<KPT>::T b0,
+                          const __half* B16, int K, int which, float* red) {
   for (int r = tj; r < DFSSM_RANK; r += P.n_t) {
     float t[B];
-    lora_t_rank<B, KPT>(vals, B16, K, r, t, red);
+    lora_t_rank_v<B, KPT>(vals, r == tj ? b0 : load_rank_b<KPT>(B16, K, r), t, red);
     if (threadIdx.x == 0)
 #pragma unroll
       for (int b = 0; b < B; ++b) P.t_g[(which * B + b) * DFSSM_RANK + r] = t[b];
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    red_release_add(P.sync + 4, 1u);
-  }
+  if (threadIdx.x == 0) red_release_add(P.sync + 4, 1u);
 }
 
 // Wait until `uses` rounds of all producers have published, then copy t_g[which] into s_t.
@@ -387,6 +385,8 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
     }
     const int idx = layer - P.l0;
     const bool t_producer = pl.role == 1 && pl.tj < P.n_t;
+    typename RankHalves<KI>::T tb_in{};
+    if (t_producer) tb_in = load_rank_b<KI>(L.in.B16, d_model, pl.tj);
     const int tb = 2 + kTracePerLayer * layer;
     stamp(P, tb + 0);
     if (layer > P.l0) grid_barrier(P, nbar);  // x of the previous layer complete
@@ -404,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
 #pragma unroll
         for (int j = 0; j < KI; ++j) vals[b][j] = h2f(s_x[b * d_model + tid * KI + j]);
       prep_norm<B, KI>(vals, w_in, d_model, red);
-      if (t_producer) publish_t<B, KI>(P, pl.tj, vals, L.in.B16, d_model, 0, red);  // publish before quantising
+      if (t_producer) publish_t<B, KI>(P, pl.tj, vals, tb_in, L.in.B16, d_model, 0, red);  // publish before quantising
       prep_quantize<B, KI>(vals, s_q, d_inner, s_xs, s_qsum, red);
     }
     stamp(P, tb + 3);
@@ -427,6 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         if (i < nrows && l16 < B) s_dot[row * B + l16] = dd.v[l16];
       }
       __syncthreads();
+      stamp(P, tb + 12);
       fetch_t<B>(P, 2 * idx + 1, 0, s_t);
       for (int e2 = tid; e2 < nrows * B; e2 += kThreads) {
         const int row = e2 / B, b = e2 - row * B;
@@ -509,6 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         if (i < nb && l16 < B) s_dot[row * B + l16] = dd.v[l16];
       }
       __syncthreads();
+      stamp(P, tb + 12);
       fetch_t<B>(P, 2 * idx + 1, 0, s_t);
       for (int e2 = tid; e2 < nb * B; e2 += kThreads) {
         const int row = e2 / B, b = e2 - row * B;
@@ -522,10 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         P.bc_g[b * 256 + pl.bc0 + row] = f2h(conv_silu(s0, s1, s2, v, cw + row * 4, h2f(cb[row])));
       }
       __syncthreads();
-      if (tid == 0) {
-        __threadfence();
-        red_release_add(P.sync + 2, 1u);
-      }
+      if (tid == 0) red_release_add(P.sync + 2, 1u);
     }
     stamp(P, tb + 7);
     // ---------------- beta: out_proj rows
@@ -535,6 +534,8 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
 #pragma unroll
       for (int j = 0; j < KO; ++j) w_out[j] = __ldg(L.norm_w + k0 + j);
     }
+    typename RankHalves<KO>::T tb_out{};
+    if (t_producer) tb_out = load_rank_b<KO>(L.out.B16, d_inner, pl.tj);
     stamp(P, tb + 8);
     // gated complete; warp 1 issues the bulk copies of a later layer while thread 0 waits
     grid_arrive(P, nbar);
@@ -571,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
       }
       __syncthreads();
       prep_norm<B, KO>(vals, w_out, d_inner, red);
-      if (t_producer) publish_t<B, KO>(P, pl.tj, vals, L.out.B16, d_inner, 1, red);  // publish before quantising
+      if (t_producer) publish_t<B, KO>(P, pl.tj, vals, tb_out, L.out.B16, d_inner, 1, red);  // publish before quantising
       prep_quantize<B, KO>(vals, s_q, d_inner, s_xs, s_qsum, red);
     }
     stamp(P, tb + 10);
@@ -586,6 +587,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
       }
     }
     __syncthreads();
+    stamp(P, tb + 13);
     fetch_t<B>(P, 2 * idx + 2, 1, s_t);
     if (pl.no > 0) {
       const __half* sc = reinterpret_cast<const __half*>(st + P.lay.out_scale);

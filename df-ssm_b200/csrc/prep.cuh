@@ -222,11 +222,16 @@ __device__ void prep_quantize(const float (&vals)[B][KPT], int8_t* sq, int Kq, f
 
 // One rank r of the LoRA down-projection, t[b] = fp16(sum_k xn[b][k] * B16[r][k]), from the
 // thread-resident normalised values of prep_quant.  Every thread returns the B totals.
+// This thread's KPT fp16 values of LoRA-B row r (B16 is [16][K]).
+template <int KPT>
+__device__ __forceinline__ typename RankHalves<KPT>::T load_rank_b(const __half* B16, int K, int r) {
+  return __ldg(reinterpret_cast<const typename RankHalves<KPT>::T*>(B16 + (size_t)r * K + threadIdx.x * KPT));
+}
+
+// t[b] = fp16(sum_k vals[b][k] * B16[r][k]) for one rank r whose values bv are already in registers.
 template <int B, int KPT>
-__device__ __forceinline__ void lora_t_rank(const float (&vals)[B][KPT], const __half* B16, int K, int r,
-                                            float (&t)[B], float* red) {
-  typename RankHalves<KPT>::T bv = __ldg(reinterpret_cast<const typename RankHalves<KPT>::T*>(
-      B16 + (size_t)r * K + threadIdx.x * KPT));
+__device__ __forceinline__ void lora_t_rank_v(const float (&vals)[B][KPT], typename RankHalves<KPT>::T bv,
+                                              float (&t)[B], float* red) {
 #pragma unroll
   for (int b = 0; b < B; ++b) {
     float a = 0.f;
@@ -237,6 +242,12 @@ __device__ __forceinline__ void lora_t_rank(const float (&vals)[B][KPT], const _
   block_sum_n<B>(t, red);
 #pragma unroll
   for (int b = 0; b < B; ++b) t[b] = round_h(t[b]);
+}
+
+template <int B, int KPT>
+__device__ __forceinline__ void lora_t_rank(const float (&vals)[B][KPT], const __half* B16, int K, int r,
+                                            float (&t)[B], float* red) {
+  lora_t_rank_v<B, KPT>(vals, load_rank_b<KPT>(B16, K, r), t, red);
 }
 
 }  // namespace dfssm

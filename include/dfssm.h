@@ -109,9 +109,10 @@ int dfssm_layer_step(dfssm_engine* e, int layer, void* stream);
  * that records %globaltimer stamps at its phase boundaries into trace_dev
  * [sm_count][4 + 14 * n_layer]: [0] start, [1] end, [2 + 14l + k] layer l point k
  * (0 alpha entry, 1 after the x barrier, 2 after loading x, 3 after norm/quant/LoRA,
- *  4 after the weight ring wait, 5 after the in_proj GEMV, 6 after the B/C wait, 7 after the
- *  SSM, 8 before the gated barrier, 9 after it, 10 after the beta norm/quant/LoRA,
- *  11 after the out_proj GEMV; 12 and 13 unused);
+ *  4 after the weight ring wait, 12 after the in_proj dot products, 5 after the LoRA-t wait and
+ *  the in_proj epilogue, 6 after the B/C wait, 7 after the SSM, 8 before the gated barrier,
+ *  9 after it, 10 after the beta norm/quant/LoRA, 13 after the out_proj dot products, 11 after
+ *  the LoRA-t wait and the out_proj epilogue);
  * [2 + 14 n_layer] head entry, [3 + 14 n_layer] after its barrier. */
 size_t dfssm_trace_entries(const dfssm_engine* e);
 int dfssm_trace_step(dfssm_engine* e, unsigned long long* trace_dev, void* stream);
