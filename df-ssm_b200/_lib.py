@@ -63,11 +63,13 @@ class Dims(ctypes.Structure):
 _lib = None
 
 
-def load(path: str = LIB_PATH) -> ctypes.CDLL:
-    """Load libdfssm.so and bind every entry point.  Raises if it is absent."""
+def load(path: str = None) -> ctypes.CDLL:
+    """Load libdfssm.so (or the library named by DFSSM_LIB) and bind every entry point.
+    Raises if it is absent."""
     global _lib
     if _lib is not None:
         return _lib
+    path = path or os.environ.get("DFSSM_LIB") or LIB_PATH
     if not os.path.exists(path):
         raise RuntimeError(f"{path} is not built; run `python -m dfssm_b200.build` (no CPU fallback exists)")
     lib = ctypes.CDLL(path)

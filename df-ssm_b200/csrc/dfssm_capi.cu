@@ -504,6 +504,9 @@ int build_engine(const unsigned char* img, size_t n, int device, int max_batch, 
   const size_t o_best = take((size_t)B * 8);
   const size_t o_tok = take((size_t)B * 4);
   const size_t o_sync = take(4096);
+  // tagged exchange words of the persistent kernel: x, B/C, gated and LoRA t for 2 layer
+  // parities x 2 sequences
+  const size_t o_xch = take(persistent_xch_bytes(d));
   const size_t o_layers = take(sizeof(LayerW) * d.n_layer);
   if (cudaMalloc(&e->work, off) != cudaSuccess)
     return cleanup(dfssm_fail(DFSSM_ERR_OOM, "cudaMalloc(%zu) for state/activations failed", off));
@@ -523,6 +526,7 @@ int build_engine(const unsigned char* img, size_t n, int device, int max_batch, 
   e->best = reinterpret_cast<unsigned long long*>(W + o_best);
   e->tokens = reinterpret_cast<int*>(W + o_tok);
   e->sync = reinterpret_cast<unsigned int*>(W + o_sync);
+  e->xch = reinterpret_cast<unsigned long long*>(W + o_xch);
   e->d_layers = reinterpret_cast<LayerW*>(W + o_layers);
   ce = cudaMemset(e->work, 0, off);
   if (ce != cudaSuccess) return cleanup(dfssm_fail(DFSSM_ERR_CUDA, "state clear: %s", cudaGetErrorString(ce)));

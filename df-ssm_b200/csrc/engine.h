@@ -35,7 +35,8 @@ struct dfssm_engine {
   float* logits = nullptr;
   unsigned long long* best = nullptr;
   int* tokens = nullptr;
-  unsigned int* sync = nullptr;  // persistent-kernel barrier words
+  unsigned int* sync = nullptr;  // persistent-kernel words: exit count, error, tag epoch
+  unsigned long long* xch = nullptr;  // persistent-kernel tagged exchange words
   // execution
   cudaStream_t s = nullptr;
   cudaEvent_t ev_in = nullptr, ev_out = nullptr;
@@ -52,6 +53,8 @@ int dfssm_fail(int code, const char* fmt, ...);
 
 // Persistent whole-step kernel (persistent.cu).
 int persistent_init(dfssm_engine* e);
+size_t persistent_xch_words(const dfssm_dims& d);  // tagged exchange words per replica
+size_t persistent_xch_bytes(const dfssm_dims& d);  // whole exchange region (all replicas)
 void persistent_destroy(dfssm_engine* e);
 bool persistent_supported(const dfssm_engine* e);
 int launch_persistent_step(dfssm_engine* e, cudaStream_t s);

@@ -1,19 +1,30 @@
 // Persistent whole-step decode kernel for small batches (B <= 2): one cooperative launch per
 // greedy decode step runs the embedding gather, every layer, the final norm, the LM head and
-// the argmax.  One CTA per SM, 512 threads.
+// the argmax.  One CTA per SM: 16 compute warps (512 threads, named barrier 1) and one warp
+// that only issues the bulk copies of the weight/state ring.
 //
-// Per layer there are two grid-wide barriers:
-//   alpha: every CTA rebuilds RMSNorm(x) -> int8 q and the in_proj LoRA down-projection t.
+// Per layer:
+//   alpha: every CTA rebuilds RMSNorm(x) -> int8 q; 16 "producer" CTAs compute the in_proj
+//          LoRA down-projection t (one rank each) and publish it.
 //          "head" CTAs own half a head (32 channels p of head h): their z/x/dt in_proj rows,
 //          conv1d of their x channels, and their 32x128 slice of the fp32 SSM state.
 //          "BC" CTAs own 8-row groups of the B/C in_proj rows and their conv1d channels and
-//          publish conv'd B/C through global memory + a counter; head CTAs wait on that
-//          counter, then run the state update, C.h + D.x and the SiLU(z) gate.
-//   beta:  every CTA owns 8-row groups of out_proj: gate-RMSNorm of the full gated vector,
-//          quantisation, LoRA, the 1-bit GEMV and the residual add into x.
+//          publish conv'd B/C; head CTAs then run the state update, C.h + D.x and the SiLU(z)
+//          gate and publish the gated vector.
+//   beta:  every non-producer CTA owns 8-row groups of out_proj: gate-RMSNorm of the full
+//          gated vector, quantisation, LoRA, the 1-bit GEMV and the residual add into x.
+// There is no grid barrier.  Every exchanged value (x, LoRA t, conv'd B/C, gated) travels in
+// a 64-bit word {32 data bits, 32-bit tag} written with one relaxed store; a consumer polls
+// its words until every tag equals the tag of the expected (step, layer, kind), so the value
+// and its readiness arrive in a single L2 round trip with no fence.  Tags come from an epoch
+// base in device memory that the last CTA of each launch advances, so words left from
+// earlier steps never match.  Exchange buffers alternate by layer parity; a writer of layer
+// l+2 depends (through the exchange chain) on every reader of layer l having finished it.
 // Weights and state of upcoming layers stream into a shared-memory ring with cp.async.bulk
-// (TMA bulk copies completing on mbarriers) while earlier layers compute, so the HBM stream
-// is off the barrier-to-barrier critical path.  Every wait is bounded: a timeout sets an error
+// (TMA bulk copies completing on "full" mbarriers) while earlier layers compute, so the HBM
+// stream is off the critical path.  The copy warp refills a slot once the compute threads
+// release it on its "empty" mbarrier; issuing some 20 copies per stage takes the TMA unit about
+// a microsecond, which no compute warp waits for.  Every wait is bounded: a timeout sets an error
 // word (reported by dfssm_check_finite) and makes every later wait return at once, so a
 // failed step ends quickly instead of hanging.
 //
@@ -26,12 +37,15 @@
 #include "engine.h"
 #include "prep.cuh"
 
+
+
 using namespace dfssm;
 
 namespace {
 
-constexpr int kThreads = 512;
+constexpr int kThreads = 512;              // compute threads (named barrier 1)
 constexpr int kWarps = kThreads / 32;
+constexpr int kBlockThreads = kThreads + 32;  // + one warp that issues the weight/state copies
 constexpr unsigned kSpinLimit = 1u << 22;
 constexpr int kMaxRPW = 2;  // SSM rows per warp (np = 32 channels over 16 warps)
 
@@ -67,13 +81,18 @@ struct PParams {
   float* logits;    // [B][vocab]
   unsigned long long* best;
   int* tokens;
-  unsigned* sync;  // [0] barrier count, [1] exit count, [2] B/C count, [3] error
+  unsigned* sync;  // [1] exit count, [3] error, [16] tag epoch base (never cleared by resets)
+  // tagged exchange words {data, tag}, each [2 parities][B][...]:
+  unsigned long long* xw;   // x as fp16 pairs        [d_model / 2]
+  unsigned long long* bcw;  // conv'd B/C fp16 pairs  [d_state] (B then C)
+  unsigned long long* gw;   // gated fp16 pairs       [d_inner / 2]
+  unsigned long long* tw;   // LoRA t fp32, [2 parities][2: in, out][B][16]
+  size_t rs;                // words between the replicas of the exchange region
   int l0, l1;      // layers run by this launch
   int from_x;      // 1: layer l0 starts from x_g instead of the token embedding
   int do_head;     // 1: final norm + LM head + argmax after layer l1-1
   int n_bc;        // number of B/C CTAs
   int n_t;         // number of LoRA-t producer CTAs (the first n_t B/C CTAs; rank r -> producer r % n_t)
-  float* t_g;      // [2][B][16] published LoRA down-projections (in_proj, out_proj)
   int ns;          // ring stages
   int ring_off;    // byte offset of the ring in dynamic smem
   int tab_off;     // byte offset of the per-layer tables in dynamic smem
@@ -89,35 +108,81 @@ __device__ __forceinline__ void stamp(const PParams& P, int idx) {
   }
 }
 
-// Wait (thread 0 spins, the block follows) until *cnt >= target; bounded.  Once any wait has
-// timed out (error word != 0) every later wait returns at once.
-__device__ __forceinline__ void wait_counter(unsigned* cnt, unsigned target, unsigned* err, unsigned code) {
-  if (threadIdx.x == 0) {
-    unsigned it = 0;
-    while (ld_acquire(cnt) < target) {
-      if ((++it & 1023u) == 0 && ld_acquire(err) != 0) break;
+// ---- tagged exchange words
+enum : unsigned { kTagX = 1, kTagTin = 2, kTagBC = 3, kTagGated = 4, kTagTout = 5, kTagsPerLayer = 8 };
+__device__ __forceinline__ unsigned tag_of(unsigned base, int layer, unsigned kind) {
+  return base + (unsigned)layer * kTagsPerLayer + kind;
+}
+__device__ __forceinline__ unsigned pack_h2(float a, float b) {
+  return (unsigned)__half_as_ushort(f2h(a)) | ((unsigned)__half_as_ushort(f2h(b)) << 16);
+}
+__device__ __forceinline__ float lo_h(unsigned v) { return h2f(__ushort_as_half((unsigned short)(v & 0xffffu))); }
+__device__ __forceinline__ float hi_h(unsigned v) { return h2f(__ushort_as_half((unsigned short)(v >> 16))); }
+// Every exchange word is written to kReplicas copies kRepStride words apart and CTA c reads
+// copy c % kReplicas: all CTAs polling one copy would concentrate their L2 requests on the
+// few slices that hold it.
+constexpr int kReplicas = 8;
+__device__ __forceinline__ void put_word(unsigned long long* p, size_t rstride, unsigned data, unsigned tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | data;
+#pragma unroll
+  for (int r = 0; r < kReplicas; ++r)
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p + r * rstride), "l"(w) : "memory");
+}
+// Poll G groups of N consecutive words (group g at p + g * gstride; N = 1, 2 or 4, each group
+// 8*N-byte aligned for N > 1) until every tag equals `tag`; the data go to out[][].  All loads
+// of one poll are issued together.  Bounded: after kSpinLimit polls the error word gets
+// `code`, and once the error word is set every poll gives up at its next check.
+template <int G, int N>
+__device__ __forceinline__ void take_words(const unsigned long long* p, size_t gstride, unsigned tag,
+                                           unsigned (&out)[G][N], unsigned* err, unsigned code) {
+  unsigned long long w[G][N];
+  for (unsigned it = 0;; ++it) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const unsigned long long* q = p + g * gstride;
+      if (N == 1) {
+        asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w[g][0]) : "l"(q) : "memory");
+      } else {
+#pragma unroll
+        for (int k = 0; k < N; k += 2)
+          asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];"
+                       : "=l"(w[g][k]), "=l"(w[g][k + 1])
+                       : "l"(q + k)
+                       : "memory");
+      }
+    }
+    bool ok = true;
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int k = 0; k < N; ++k) ok &= (unsigned)(w[g][k] >> 32) == tag;
+    if (ok) break;
+    if ((it & 255u) == 255u) {
+      if (ld_acquire(err) != 0) break;
       if (it > kSpinLimit) {
         atomicOr(err, code);
         break;
       }
     }
   }
-  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int k = 0; k < N; ++k) out[g][k] = (unsigned)w[g][k];
 }
 
-__device__ __forceinline__ void grid_arrive(const PParams& P, unsigned& nbar) {
-  __syncthreads();
-  ++nbar;
-  // bar.sync orders the block's writes before thread 0's release (PTX causality order is
-  // transitive), so the gpu-scope release needs no separate fence.sc
-  if (threadIdx.x == 0) red_release_add(P.sync, 1u);
-}
-__device__ __forceinline__ void grid_wait(const PParams& P, unsigned nbar) {
-  wait_counter(P.sync, nbar * gridDim.x, P.sync + 3, 1u);
-}
-__device__ __forceinline__ void grid_barrier(const PParams& P, unsigned& nbar) {
-  grid_arrive(P, nbar);
-  grid_wait(P, nbar);
+// Collect B x d_model/2 x words (KI = d_model / 512) into s_x.
+template <int B, int KI>
+__device__ __forceinline__ void take_x(const unsigned long long* xw, int n_words, unsigned tag, __half* s_x,
+                                       unsigned* err) {
+  constexpr int XPT = (B * KI) / 2 >= 4 ? 4 : ((B * KI) / 2 >= 2 ? 2 : 1);  // words per thread
+  for (int i = threadIdx.x * XPT; i < n_words; i += kThreads * XPT) {
+    unsigned v[1][XPT];
+    take_words<1, XPT>(xw + i, 0, tag, v, err, 1u);
+#pragma unroll
+    for (int k = 0; k < XPT; ++k) reinterpret_cast<unsigned*>(s_x)[i + k] = v[0][k];
+  }
+  cta_sync();
 }
 
 // Wait for the ring slot of `layer` to hold its data (bounded).
@@ -134,17 +199,16 @@ __device__ __forceinline__ void wait_stage(const PParams& P, uint64_t* bars, int
       }
     }
   }
-  __syncthreads();
+  cta_sync();
 }
 
 // Issue the bulk copies that fill the ring slot of `layer` with this CTA's slice of it.
-// Lane i of warp 0 issues copy i of the table below (all 16-byte aligned, sizes multiples of
+// Copy i of the table below (all 16-byte aligned, sizes multiples of
 // 16); the byte total of a stage is precomputed on the host (CtaPlan::tx).
 template <int B>
 __device__ __forceinline__ void issue_stage(const PParams& P, const CtaPlan& pl, int layer, unsigned char* ring,
-                                         uint64_t* bars, const LayerW* layers) {
-  if (layer >= P.l1 || threadIdx.x < 32 || threadIdx.x >= 64) return;  // warp 1 issues
-  const int i = threadIdx.x - 32;
+                                         uint64_t* bars, const LayerW* layers, int i) {
+  if (layer >= P.l1) return;
   const int slot = (layer - P.l0) % P.ns;
   unsigned char* st = ring + (size_t)slot * P.lay.stage_bytes;
   uint64_t* bar = bars + slot;
@@ -208,10 +272,11 @@ __device__ __forceinline__ void issue_stage(const PParams& P, const CtaPlan& pl,
       default: break;
     }
   }
-  // The slot's previous contents were read by this CTA's threads before a __syncthreads that
-  // precedes this call, which orders those reads before the bulk copies below.
+  // The slot's previous contents were read by the compute threads before they released the
+  // slot (an mbarrier arrive after their barrier), which the issuer observed before this call.
+  // the arrive with the stage's byte total may land before or after the copies complete: the
+  // transaction count of the phase may go negative, and the phase ends only after the arrive
   if (i == 0) mbar_expect_tx(bar, (unsigned)pl.tx);
-  __syncwarp();
   if (n_) bulk_g2s(st + d_, s_, n_, bar);
 }
 
@@ -281,33 +346,66 @@ __device__ __forceinline__ float conv_silu(float s0, float s1, float s2, float v
 }
 
 // LoRA-t producer: compute this CTA's ranks (r = tj, tj + n_t, ...) of t = fp16(xn . B16^T) and
-// publish them in t_g[which]; one release-increment of the t counter per producer and use.
-// The values of the first rank (r = tj) were loaded into b0 before the barrier, so the
-// producer's critical path holds no HBM round trip for them.
+// publish each as a tagged word.  The values of the first rank (r = tj) were loaded into b0
+// before the wait for the activations, so the producer's path holds no HBM round trip for them.
 template <int B, int KPT>
 __device__ void publish_t(const PParams& P, int tj, const float (&vals)[B][KPT], typename RankHalves<KPT>::T b0,
-                          const __half* B16, int K, int which, float* red) {
+                          const __half* B16, int K, unsigned long long* tw, unsigned tag, float* red) {
   for (int r = tj; r < DFSSM_RANK; r += P.n_t) {
     float t[B];
     lora_t_rank_v<B, KPT>(vals, r == tj ? b0 : load_rank_b<KPT>(B16, K, r), t, red);
     if (threadIdx.x == 0)
 #pragma unroll
-      for (int b = 0; b < B; ++b) P.t_g[(which * B + b) * DFSSM_RANK + r] = t[b];
+      for (int b = 0; b < B; ++b) put_word(tw + b * DFSSM_RANK + r, P.rs, __float_as_uint(t[b]), tag);
   }
-  __syncthreads();
-  if (threadIdx.x == 0) red_release_add(P.sync + 4, 1u);
 }
 
-// Wait until `uses` rounds of all producers have published, then copy t_g[which] into s_t.
+// Collect the B x 16 published LoRA t values into s_t.
 template <int B>
-__device__ __forceinline__ void fetch_t(const PParams& P, unsigned uses, int which, float* s_t) {
-  wait_counter(P.sync + 4, uses * (unsigned)P.n_t, P.sync + 3, 8u);
-  if (threadIdx.x < B * DFSSM_RANK) s_t[threadIdx.x] = __ldcg(P.t_g + which * B * DFSSM_RANK + threadIdx.x);
-  __syncthreads();
+__device__ __forceinline__ void fetch_t(const PParams& P, const unsigned long long* tw, unsigned tag, float* s_t) {
+  if (threadIdx.x < B * DFSSM_RANK) {
+    unsigned v[1][1];
+    take_words<1, 1>(tw + (blockIdx.x % kReplicas) * P.rs + threadIdx.x, 0, tag, v, P.sync + 3, 8u);
+    s_t[threadIdx.x] = __uint_as_float(v[0][0]);
+  }
+  cta_sync();
+}
+
+// The copy-issuing warp: fills ring slot (k % ns) with layer l0 + k as soon as the compute
+// threads have released the layer that used the slot before (k >= ns).  Lane i issues copy i of
+// issue_stage.  Bounded: gives up when a wait times out or the error word is set.
+template <int B>
+__device__ void copy_issuer(const PParams& P, const CtaPlan& pl, unsigned char* ring, uint64_t* full,
+                            uint64_t* empty, const LayerW* layers) {
+  const int lane = threadIdx.x & 31;
+  const int nl = P.l1 - P.l0;
+  for (int k = 0; k < nl; ++k) {
+    if (k >= P.ns) {
+      int ok = 1;
+      if (lane == 0) {
+        const unsigned parity = (unsigned)((k / P.ns - 1) & 1);
+        unsigned it = 0;
+        while (!mbar_try_wait(empty + k % P.ns, parity)) {
+          if ((++it & 1023u) == 0 && ld_acquire(P.sync + 3) != 0) {
+            ok = 0;
+            break;
+          }
+          if (it > kSpinLimit) {
+            atomicOr(P.sync + 3, 32u);
+            ok = 0;
+            break;
+          }
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+    }
+    issue_stage<B>(P, pl, P.l0 + k, ring, full, layers, lane);
+    __syncwarp();
+  }
 }
 
 template <int B, int KI, int KO>
-__global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P) {
+__global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PParams P) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int d_model = P.d_model, d_inner = P.d_inner;
   // working smem (carve-up mirrored by build_plan)
@@ -329,25 +427,31 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
   // 16 fp16 dt-row LoRA-A values) for every layer
   LayerW* s_layers = reinterpret_cast<LayerW*>(smem + P.tab_off);
   float* s_hptab = reinterpret_cast<float*>(smem + P.tab_off + ((P.n_layer * (int)sizeof(LayerW) + 15) & ~15));  // [n_layer][12], 16-byte aligned
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.ring_off - 8 * 8);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.ring_off - 8 * 8);      // ring slot full
+  uint64_t* empties = reinterpret_cast<uint64_t*>(smem + P.ring_off - 16 * 8);  // ring slot released
   unsigned char* ring = smem + P.ring_off;
 
   const CtaPlan pl = P.plans[blockIdx.x];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, l16 = lane & 15, hw = tid >> 4;
-  unsigned nbar = 0;
+  const unsigned ebase = __ldcg(P.sync + 16);  // tag epoch of this launch
+  const int XW = d_model / 2, GW = d_inner / 2;
+  const size_t rep_off = (size_t)(blockIdx.x % kReplicas) * P.rs;  // this CTA's copy of the exchange words
 
   if (tid == 0) {
-    for (int i = 0; i < P.ns; ++i) mbar_init(bars + i, 1);
+    for (int i = 0; i < P.ns; ++i) {
+      mbar_init(bars + i, 1);
+      mbar_init(empties + i, 1);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
   stamp(P, 0);
   {
     const int nw = P.n_layer * (int)sizeof(LayerW) / 8;
-    for (int i = tid; i < nw; i += kThreads)
+    for (int i = tid; i < nw; i += kBlockThreads)
       reinterpret_cast<unsigned long long*>(s_layers)[i] = reinterpret_cast<const unsigned long long*>(P.layers)[i];
     if (pl.role == 0) {
-      for (int l = tid; l < P.n_layer; l += kThreads) {
+      for (int l = tid; l < P.n_layer; l += kBlockThreads) {
         const LayerW& G = P.layers[l];
         const int dtrow = d_inner + P.d_xbc + pl.h;
         float* e = s_hptab + l * 12;
@@ -362,7 +466,10 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
     }
   }
   __syncthreads();
-  for (int l = 0; l < P.ns - 1; ++l) issue_stage<B>(P, pl, P.l0 + l, ring, bars, s_layers);
+  if (wid == kWarps) {
+    copy_issuer<B>(P, pl, ring, bars, empties, s_layers);
+    return;
+  }
 
   // embedding gather (every CTA needs the full x of the first layer)
   for (int i = tid; i < B * d_model && !P.from_x; i += kThreads) {
@@ -371,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
     tok = min(max(tok, 0), P.vocab - 1);
     s_x[i] = f2h((float)P.Eq[(size_t)tok * d_model + k] * P.Es[tok]);
   }
-  __syncthreads();
+  cta_sync();
 
   for (int layer = P.l0; layer < P.l1; ++layer) {
     const LayerW& L = s_layers[layer];
@@ -383,19 +490,20 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
 #pragma unroll
       for (int j = 0; j < KI; ++j) w_in[j] = __ldg(L.ln_w + k0 + j);
     }
-    const int idx = layer - P.l0;
     const bool t_producer = pl.role == 1 && pl.tj < P.n_t;
     typename RankHalves<KI>::T tb_in{};
     if (t_producer) tb_in = load_rank_b<KI>(L.in.B16, d_model, pl.tj);
     const int tb = 2 + kTracePerLayer * layer;
     stamp(P, tb + 0);
-    if (layer > P.l0) grid_barrier(P, nbar);  // x of the previous layer complete
-    stamp(P, tb + 1);
-    if (layer > P.l0 || P.from_x) {
+    const int par = layer & 1;
+    if (layer > P.l0) {  // x of this layer, published word by word by the previous layer's out_proj
+      take_x<B, KI>(P.xw + rep_off + (size_t)par * B * XW, B * XW, tag_of(ebase, layer, kTagX), s_x, P.sync + 3);
+    } else if (P.from_x) {
       for (int i = tid; i < B * d_model / 8; i += kThreads)
         reinterpret_cast<uint4*>(s_x)[i] = __ldcg(reinterpret_cast<const uint4*>(P.x_g) + i);
-      __syncthreads();
+      cta_sync();
     }
+    stamp(P, tb + 1);
     stamp(P, tb + 2);
     {
       float vals[B][KI];
@@ -404,7 +512,8 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
 #pragma unroll
         for (int j = 0; j < KI; ++j) vals[b][j] = h2f(s_x[b * d_model + tid * KI + j]);
       prep_norm<B, KI>(vals, w_in, d_model, red);
-      if (t_producer) publish_t<B, KI>(P, pl.tj, vals, tb_in, L.in.B16, d_model, 0, red);  // publish before quantising
+      if (t_producer) publish_t<B, KI>(P, pl.tj, vals, tb_in, L.in.B16, d_model, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK,
+                                         tag_of(ebase, layer, kTagTin), red);  // publish before quantising
       prep_quantize<B, KI>(vals, s_q, d_inner, s_xs, s_qsum, red);
     }
     stamp(P, tb + 3);
@@ -426,9 +535,9 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         const Dots<B> dd = row_dot<B>(st + P.lay.in_bits + (size_t)row * RB, d_model, s_q, d_inner, l16, s_qsum);
         if (i < nrows && l16 < B) s_dot[row * B + l16] = dd.v[l16];
       }
-      __syncthreads();
+      cta_sync();
       stamp(P, tb + 12);
-      fetch_t<B>(P, 2 * idx + 1, 0, s_t);
+      fetch_t<B>(P, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTin), s_t);
       for (int e2 = tid; e2 < nrows * B; e2 += kThreads) {
         const int row = e2 / B, b = e2 - row * B;
         const int dot = s_dot[e2];
@@ -453,15 +562,25 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
           s_dt[b] = v;
         }
       }
-      __syncthreads();
+      cta_sync();
       stamp(P, tb + 5);
       // wait for every B/C CTA of this layer, then fetch conv'd B and C
-      wait_counter(P.sync + 2, (unsigned)(layer - P.l0 + 1) * P.n_bc, P.sync + 3, 4u);
+      {
+        const unsigned long long* bcw = P.bcw + (size_t)par * B * DFSSM_DSTATE;
+        const unsigned tg = tag_of(ebase, layer, kTagBC);
+        for (int i = tid; i < B * DFSSM_DSTATE; i += kThreads) {
+          unsigned v[1][1];
+          take_words<1, 1>(bcw + rep_off + i, 0, tg, v, P.sync + 3, 4u);
+          s_bc[2 * i] = lo_h(v[0][0]);
+          s_bc[2 * i + 1] = hi_h(v[0][0]);
+        }
+      }
+      cta_sync();
       stamp(P, tb + 6);
-      for (int i = tid; i < B * 2 * DFSSM_DSTATE; i += kThreads) s_bc[i] = h2f(__ldcg(P.bc_g + i));
-      __syncthreads();
-      // SSM state update + gate; warp w owns rows p = w*RPW.., lane owns n = 4*lane..
-      const int RPW = np / kWarps;
+      // SSM state update + gate; warp w owns rows p = 2w, 2w+1 (np = 2 * kWarps), lane owns
+      // n = 4*lane..; lane 0 publishes the gated pair as one word
+      unsigned long long* gw = P.gw + (size_t)par * B * GW;
+      const unsigned tg_g = tag_of(ebase, layer, kTagGated);
       const float* sst = reinterpret_cast<const float*>(st + P.lay.state);
       const float* hp = s_hptab + layer * 12;
 #pragma unroll
@@ -473,10 +592,10 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         const float* bb = s_bc + b * 256 + lane * 4;
         const float4 Bn = make_float4(bb[0], bb[1], bb[2], bb[3]);
         const float4 Cn = make_float4(bb[128], bb[129], bb[130], bb[131]);
+        float gv[kMaxRPW];
 #pragma unroll
         for (int rr = 0; rr < kMaxRPW; ++rr) {
-          if (rr >= RPW) break;
-          const int p = wid * RPW + rr;
+          const int p = wid * kMaxRPW + rr;
           const float4 hv = *reinterpret_cast<const float4*>(sst + ((size_t)b * np + p) * DFSSM_DSTATE + lane * 4);
           const float xv = s_xc[b * 64 + p];
           const float X = xv * dtv;
@@ -488,13 +607,17 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
           hnew[b][rr] = o;
           float part = Cn.x * o.x + Cn.y * o.y + Cn.z * o.z + Cn.w * o.w;
           part = warp_sum(part);
-          if (lane == 0) {
-            const float y = part + xv * Dh;
-            const float z = s_z[b * 64 + p];
-            const float sig = round_h(1.0f / (1.0f + expf(-z)));
-            const float silu = round_h(z * sig);
-            P.gated_g[(size_t)b * d_inner + pl.h * DFSSM_HEADDIM + pl.p0 + p] = f2h(round_h(y) * silu);
-          }
+          const float y = part + xv * Dh;
+          const float z = s_z[b * 64 + p];
+          const float sig = round_h(1.0f / (1.0f + expf(-z)));
+          const float silu = round_h(z * sig);
+          gv[rr] = round_h(y) * silu;
+        }
+        if (lane == 0) {
+          const int c = pl.h * DFSSM_HEADDIM + pl.p0 + wid * kMaxRPW;
+          const unsigned w = pack_h2(gv[0], gv[1]);
+          put_word(gw + (size_t)b * GW + c / 2, P.rs, w, tg_g);
+          *reinterpret_cast<unsigned*>(P.gated_g + (size_t)b * d_inner + c) = w;  // plain copy for the host API
         }
       }
     } else if (pl.role == 1) {
@@ -509,22 +632,29 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         const Dots<B> dd = row_dot<B>(st + P.lay.in_bits + (size_t)row * RB, d_model, s_q, d_inner, l16, s_qsum);
         if (i < nb && l16 < B) s_dot[row * B + l16] = dd.v[l16];
       }
-      __syncthreads();
+      cta_sync();
       stamp(P, tb + 12);
-      fetch_t<B>(P, 2 * idx + 1, 0, s_t);
-      for (int e2 = tid; e2 < nb * B; e2 += kThreads) {
-        const int row = e2 / B, b = e2 - row * B;
-        const float v = proj_out(s_dot[e2], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
-        const int ch = d_inner + pl.bc0 + row;
-        const float s0 = cst[(b * 3 + 0) * nb + row], s1 = cst[(b * 3 + 1) * nb + row], s2 = cst[(b * 3 + 2) * nb + row];
-        float* gcs = P.conv + (long long)layer * P.conv_layer + (long long)b * 3 * P.d_xbc + ch;
-        gcs[0] = s1;
-        gcs[P.d_xbc] = s2;
-        gcs[2 * P.d_xbc] = v;
-        P.bc_g[b * 256 + pl.bc0 + row] = f2h(conv_silu(s0, s1, s2, v, cw + row * 4, h2f(cb[row])));
+      fetch_t<B>(P, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTin), s_t);
+      unsigned long long* bcw = P.bcw + (size_t)par * B * DFSSM_DSTATE;
+      const unsigned tg_bc = tag_of(ebase, layer, kTagBC);
+      for (int e2 = tid; e2 < (nb / 2) * B; e2 += kThreads) {
+        const int pr = e2 / B, b = e2 - pr * B;
+        float o2[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int row = 2 * pr + k;
+          const float v = proj_out(s_dot[row * B + b], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
+          const int ch = d_inner + pl.bc0 + row;
+          const float s0 = cst[(b * 3 + 0) * nb + row], s1 = cst[(b * 3 + 1) * nb + row], s2 = cst[(b * 3 + 2) * nb + row];
+          float* gcs = P.conv + (long long)layer * P.conv_layer + (long long)b * 3 * P.d_xbc + ch;
+          gcs[0] = s1;
+          gcs[P.d_xbc] = s2;
+          gcs[2 * P.d_xbc] = v;
+          o2[k] = conv_silu(s0, s1, s2, v, cw + row * 4, h2f(cb[row]));
+        }
+        put_word(bcw + (size_t)b * DFSSM_DSTATE + (pl.bc0 + 2 * pr) / 2, P.rs, pack_h2(o2[0], o2[1]), tg_bc);
       }
-      __syncthreads();
-      if (tid == 0) red_release_add(P.sync + 2, 1u);
+      cta_sync();
     }
     stamp(P, tb + 7);
     // ---------------- beta: out_proj rows
@@ -537,80 +667,84 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
     typename RankHalves<KO>::T tb_out{};
     if (t_producer) tb_out = load_rank_b<KO>(L.out.B16, d_inner, pl.tj);
     stamp(P, tb + 8);
-    // gated complete; warp 1 issues the bulk copies of a later layer while thread 0 waits
-    grid_arrive(P, nbar);
-    issue_stage<B>(P, pl, layer + P.ns - 1, ring, bars, s_layers);
+    // head CTAs write their state back, then every CTA collects the gated vector
+    cta_sync();
+    // release the ring slot of layer - 1 to the copy warp: releasing here, when every CTA is
+    // about to wait for the gated vector, measured faster than at the top of the layer, where the
+    // copies' HBM burst delays the x exchange
+    if (tid == 0 && layer > P.l0) mbar_arrive(empties + (layer - 1 - P.l0) % P.ns);
     if (pl.role == 0) {
-      const int RPW = pl.np / kWarps;
 #pragma unroll
       for (int b = 0; b < B; ++b)
 #pragma unroll
         for (int rr = 0; rr < kMaxRPW; ++rr) {
-          if (rr >= RPW) break;
-          const int p = wid * RPW + rr;
+          const int p = wid * kMaxRPW + rr;
           float* gh = P.ssm + (long long)layer * P.ssm_layer +
                       ((long long)(b * P.nheads + pl.h) * DFSSM_HEADDIM + pl.p0 + p) * DFSSM_DSTATE + lane * 4;
           __stcs(reinterpret_cast<float4*>(gh), hnew[b][rr]);
         }
     }
-    grid_wait(P, nbar);
-    stamp(P, tb + 9);
     {
       float vals[B][KO];
+      const unsigned long long* gw = P.gw + (size_t)par * B * GW;
+      const unsigned tg_g = tag_of(ebase, layer, kTagGated);
+      unsigned v[B][KO / 2];
+      take_words<B, KO / 2>(gw + rep_off + tid * (KO / 2), GW, tg_g, v, P.sync + 3, 16u);
 #pragma unroll
-      for (int b = 0; b < B; ++b) {
-        const __half* g = P.gated_g + (size_t)b * d_inner + tid * KO;
-        __half hv[KO];
-        if (KO == 8) {
-          *reinterpret_cast<uint4*>(hv) = __ldcg(reinterpret_cast<const uint4*>(g));
-        } else {
+      for (int b = 0; b < B; ++b)
 #pragma unroll
-          for (int j = 0; j < KO; ++j) hv[j] = __ldcg(g + j);
+        for (int j = 0; j < KO / 2; ++j) {
+          vals[b][2 * j] = lo_h(v[b][j]);
+          vals[b][2 * j + 1] = hi_h(v[b][j]);
         }
-#pragma unroll
-        for (int j = 0; j < KO; ++j) vals[b][j] = h2f(hv[j]);
-      }
-      __syncthreads();
+      if (P.trace) cta_sync();  // point 9 marks the whole CTA holding the gated vector
+      stamp(P, tb + 9);
       prep_norm<B, KO>(vals, w_out, d_inner, red);
-      if (t_producer) publish_t<B, KO>(P, pl.tj, vals, tb_out, L.out.B16, d_inner, 1, red);  // publish before quantising
+      if (t_producer) publish_t<B, KO>(P, pl.tj, vals, tb_out, L.out.B16, d_inner, P.tw + (size_t)(par * 2 + 1) * B * DFSSM_RANK,
+                                         tag_of(ebase, layer, kTagTout), red);  // publish before quantising
       prep_quantize<B, KO>(vals, s_q, d_inner, s_xs, s_qsum, red);
     }
     stamp(P, tb + 10);
     if (pl.no > 0) {
       const int RBO = d_inner / 8;
-      const __half* sc = reinterpret_cast<const __half*>(st + P.lay.out_scale);
-      const __half* la = reinterpret_cast<const __half*>(st + P.lay.out_lA);
       for (int i = hw; i < ((pl.no + 1) & ~1); i += 2 * kWarps) {
         const int row = i < pl.no ? i : pl.no - 1;
         const Dots<B> dd = row_dot<B>(st + P.lay.out_bits + (size_t)row * RBO, d_inner, s_q, d_inner, l16, s_qsum);
         if (i < pl.no && l16 < B) s_dot[row * B + l16] = dd.v[l16];
       }
     }
-    __syncthreads();
+    cta_sync();
     stamp(P, tb + 13);
-    fetch_t<B>(P, 2 * idx + 2, 1, s_t);
     if (pl.no > 0) {
+      fetch_t<B>(P, P.tw + (size_t)(par * 2 + 1) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTout), s_t);
       const __half* sc = reinterpret_cast<const __half*>(st + P.lay.out_scale);
       const __half* la = reinterpret_cast<const __half*>(st + P.lay.out_lA);
-      for (int e2 = tid; e2 < pl.no * B; e2 += kThreads) {
-        const int row = e2 / B, b = e2 - row * B;
-        const float v = proj_out(s_dot[e2], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
-        const int o = pl.o0 + row;
-        P.x_g[(size_t)b * d_model + o] = f2h(h2f(s_x[b * d_model + o]) + v);
+      unsigned long long* xw = P.xw + (size_t)(par ^ 1) * B * XW;
+      const unsigned tg_x = tag_of(ebase, layer + 1, kTagX);
+      for (int e2 = tid; e2 < (pl.no / 2) * B; e2 += kThreads) {
+        const int pr = e2 / B, b = e2 - pr * B;
+        const int o = pl.o0 + 2 * pr;
+        float xo[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int row = 2 * pr + k;
+          const float v = proj_out(s_dot[row * B + b], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
+          xo[k] = h2f(s_x[b * d_model + o + k]) + v;
+        }
+        const unsigned w = pack_h2(xo[0], xo[1]);
+        put_word(xw + (size_t)b * XW + o / 2, P.rs, w, tg_x);
+        *reinterpret_cast<unsigned*>(P.x_g + (size_t)b * d_model + o) = w;  // plain copy for the host API
       }
     }
-    __syncthreads();
+    cta_sync();
     stamp(P, tb + 11);
   }
 
   // ---------------- final norm + LM head + argmax
   stamp(P, 2 + kTracePerLayer * P.n_layer);
   if (P.do_head) {
-    grid_barrier(P, nbar);
+    take_x<B, KI>(P.xw + rep_off + (size_t)(P.l1 & 1) * B * XW, B * XW, tag_of(ebase, P.l1, kTagX), s_x, P.sync + 3);
     stamp(P, 3 + kTracePerLayer * P.n_layer);
-    for (int i = tid; i < B * d_model / 8; i += kThreads)
-      reinterpret_cast<uint4*>(s_x)[i] = __ldcg(reinterpret_cast<const uint4*>(P.x_g) + i);
-    __syncthreads();
     float* s_no = reinterpret_cast<float*>(ring);  // [B][d_model] fp32 normalised x (ring is idle now)
     {
       float vals[B][KI];
@@ -636,7 +770,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         }
       }
     }
-    __syncthreads();
+    cta_sync();
     unsigned long long mybest[B];
 #pragma unroll
     for (int b = 0; b < B; ++b) mybest[b] = 0ull;
@@ -718,11 +852,11 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
       }
     }
     unsigned long long* sb = reinterpret_cast<unsigned long long*>(red);
-    __syncthreads();
+    cta_sync();
     if (lane == 0)
 #pragma unroll
       for (int b = 0; b < B; ++b) sb[wid * B + b] = mybest[b];
-    __syncthreads();
+    cta_sync();
     if (tid < B) {
       unsigned long long k = 0ull;
       for (int w = 0; w < kWarps; ++w) k = sb[w * B + tid] > k ? sb[w * B + tid] : k;
@@ -730,7 +864,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
     }
   }  // do_head
   stamp(P, 1);
-  __syncthreads();
+  cta_sync();
   // drain: no bulk copy into this CTA's ring may still be in flight when it exits (only
   // possible after a timed-out wait); bounded, ignores the error word
   if (tid == 0) {
@@ -752,9 +886,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_step_kernel(PParams P)
         const unsigned long long k = atomicExch(P.best + b, 0ull);
         P.tokens[b] = (int)argmax_key_index(k);
       }
-      P.sync[0] = 0;
-      P.sync[2] = 0;
-      P.sync[4] = 0;
+      P.sync[16] = ebase + (unsigned)(P.n_layer + 1) * kTagsPerLayer;  // next launch's tags
       __threadfence();
       P.sync[1] = 0;
     }
@@ -883,7 +1015,7 @@ int build_plan(const dfssm_engine* e, int B, int grid, std::vector<CtaPlan>& pla
   tab_off = work;
   work += ((d.n_layer * (int)sizeof(LayerW) + 15) & ~15) + d.n_layer * 12 * 4;
   work = (work + 127) & ~127;
-  const int ring_off = work + 128;  // 8 mbarriers live just below the ring
+  const int ring_off = work + 128;  // 8 full + 8 released mbarriers live just below the ring
   int max_smem = 0;
   cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, e->device);
   ns = (max_smem - ring_off) / lay.stage_bytes;
@@ -923,7 +1055,7 @@ int persistent_init(dfssm_engine* e) {
       continue;
     }
     int nblk = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nblk, fn, kThreads, smem) != cudaSuccess || nblk < 1) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nblk, fn, kBlockThreads, smem) != cudaSuccess || nblk < 1) {
       cudaGetLastError();
       continue;
     }
@@ -950,7 +1082,11 @@ int persistent_init(dfssm_engine* e) {
     P.ssm_layer = (long long)e->ssm_layer;
     P.conv_layer = (long long)e->conv_layer;
     P.x_g = e->x;
-    P.bc_g = e->proj;  // [B][256] fp16 scratch (the per-op path's proj buffer)
+    P.xw = e->xch;
+    P.rs = persistent_xch_words(d);
+    P.bcw = P.xw + 2 * 2 * d.d_model / 2;
+    P.gw = P.bcw + 2 * 2 * d.d_state;
+    P.tw = P.gw + 2 * 2 * d.d_inner / 2;
     P.gated_g = e->gated;
     P.logits = e->logits;
     P.best = e->best;
@@ -962,7 +1098,6 @@ int persistent_init(dfssm_engine* e) {
     P.do_head = 1;
     P.n_bc = n_bc;
     P.n_t = n_bc < DFSSM_RANK ? n_bc : DFSSM_RANK;
-    P.t_g = reinterpret_cast<float*>(e->xn);  // 2 x B x 16 floats of the per-op path's xn buffer
     P.ns = ns;
     P.ring_off = smem - ns * lay.stage_bytes;
     P.trace = nullptr;
@@ -974,6 +1109,11 @@ int persistent_init(dfssm_engine* e) {
   }
   return DFSSM_OK;
 }
+
+size_t persistent_xch_words(const dfssm_dims& d) {
+  return (size_t)2 * 2 * (d.d_model / 2) + 2 * 2 * d.d_state + 2 * 2 * (d.d_inner / 2) + 2 * 2 * 2 * DFSSM_RANK;
+}
+size_t persistent_xch_bytes(const dfssm_dims& d) { return 8 * persistent_xch_words(d) * kReplicas; }
 
 bool persistent_supported(const dfssm_engine* e) {
   return e->persist && e->batch >= 1 && e->batch <= 2 && set_of(e)->st[e->batch].ready;
@@ -989,7 +1129,7 @@ int launch_persistent_layers(dfssm_engine* e, int l0, int l1, int from_x, int do
   P.from_x = from_x;
   P.do_head = do_head;
   void* args[] = {&P};
-  cudaError_t ce = cudaLaunchCooperativeKernel(ps.fn, dim3(ps.grid), dim3(kThreads), args, (size_t)ps.smem, s);
+  cudaError_t ce = cudaLaunchCooperativeKernel(ps.fn, dim3(ps.grid), dim3(kBlockThreads), args, (size_t)ps.smem, s);
   if (ce != cudaSuccess) return dfssm_fail(DFSSM_ERR_CUDA, "cooperative launch failed: %s", cudaGetErrorString(ce));
   return DFSSM_OK;
 }
@@ -1008,7 +1148,7 @@ int launch_persistent_traced(dfssm_engine* e, unsigned long long* trace_dev, cud
   PParams P = ps.params;
   P.trace = trace_dev;
   void* args[] = {&P};
-  cudaError_t ce = cudaLaunchCooperativeKernel(ps.fn, dim3(ps.grid), dim3(kThreads), args, (size_t)ps.smem, s);
+  cudaError_t ce = cudaLaunchCooperativeKernel(ps.fn, dim3(ps.grid), dim3(kBlockThreads), args, (size_t)ps.smem, s);
   if (ce != cudaSuccess) return dfssm_fail(DFSSM_ERR_CUDA, "cooperative launch failed: %s", cudaGetErrorString(ce));
   return DFSSM_OK;
 }

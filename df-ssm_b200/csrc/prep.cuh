@@ -9,6 +9,10 @@ namespace dfssm {
 constexpr int kPrepFastThreads = 512;
 constexpr int kPrepFastWarps = kPrepFastThreads / 32;
 
+// Barrier of the 512 compute threads (named barrier 1).  Blocks of exactly 512 threads use it
+// like __syncthreads; the persistent kernel adds a copy-issuing warp that never joins it.
+__device__ __forceinline__ void cta_sync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+
 // ---- block reductions over kPrepFastThreads (512) threads
 // Block-wide sum / max of N values per thread with a fixed combination order.  Warp partials
 // go to red[w*N + i]; thread i < N combines column i into red[kPrepFastWarps*N + i]; every thread then
@@ -18,18 +22,18 @@ __device__ __forceinline__ void block_sum_n(float (&v)[N], float* red) {
 #pragma unroll
   for (int i = 0; i < N; ++i) v[i] = warp_sum(v[i]);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
+  cta_sync();
   if (l == 0)
 #pragma unroll
     for (int i = 0; i < N; ++i) red[w * N + i] = v[i];
-  __syncthreads();
+  cta_sync();
   if (threadIdx.x < N) {
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < kPrepFastWarps; ++j) s += red[j * N + threadIdx.x];
     red[kPrepFastWarps * N + threadIdx.x] = s;
   }
-  __syncthreads();
+  cta_sync();
 #pragma unroll
   for (int i = 0; i < N; ++i) v[i] = red[kPrepFastWarps * N + i];
 }
@@ -38,18 +42,18 @@ __device__ __forceinline__ void block_max_n(float (&v)[N], float* red) {
 #pragma unroll
   for (int i = 0; i < N; ++i) v[i] = warp_max(v[i]);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
+  cta_sync();
   if (l == 0)
 #pragma unroll
     for (int i = 0; i < N; ++i) red[w * N + i] = v[i];
-  __syncthreads();
+  cta_sync();
   if (threadIdx.x < N) {
     float s = red[threadIdx.x];
 #pragma unroll
     for (int j = 1; j < kPrepFastWarps; ++j) s = fmaxf(s, red[j * N + threadIdx.x]);
     red[kPrepFastWarps * N + threadIdx.x] = s;
   }
-  __syncthreads();
+  cta_sync();
 #pragma unroll
   for (int i = 0; i < N; ++i) v[i] = red[kPrepFastWarps * N + i];
 }
@@ -60,11 +64,11 @@ __device__ __forceinline__ float block_sum_scatter(float (&v)[N], float* red) {
 #pragma unroll
   for (int i = 0; i < N; ++i) v[i] = warp_sum(v[i]);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
+  cta_sync();
   if (l == 0)
 #pragma unroll
     for (int i = 0; i < N; ++i) red[w * N + i] = v[i];
-  __syncthreads();
+  cta_sync();
   float s = 0.f;
   if (threadIdx.x < N)
 #pragma unroll
@@ -103,7 +107,7 @@ __device__ __forceinline__ int qswz(int p) {
 
 // RMSNorm + per-row int8 quantisation + LoRA down-projection of this thread's KPT columns of
 // B activation rows.  vals[b][j]: fp16-exact inputs of columns k0 + j.  Writes q (permuted) to
-// sq[b][*] and xs/qsum/t to smem; returns after a __syncthreads.
+// sq[b][*] and xs/qsum/t to smem; returns after a cta_sync.
 // SWZ: store q in the swizzled shared-memory order of the persistent kernel (qswz) instead of
 // the plain permuted order read by the per-op GEMV kernels.
 template <int B, int KPT, bool SWZ = true>
@@ -159,7 +163,7 @@ __device__ void prep_rows(float (&vals)[B][KPT], const float (&w)[KPT], int K,
   const float tot = block_sum_scatter<B * DFSSM_RANK + B>(all, red);
   if (threadIdx.x < B * DFSSM_RANK) s_t[threadIdx.x] = round_h(tot);
   else if (threadIdx.x < B * DFSSM_RANK + B) s_qsum[threadIdx.x - B * DFSSM_RANK] = (int)tot;
-  __syncthreads();
+  cta_sync();
 }
 
 
@@ -185,7 +189,7 @@ __device__ __forceinline__ void prep_norm(float (&vals)[B][KPT], const float (&w
 }
 
 // Per-row int8 quantisation of normalised values (second half): q in sq (swizzled if SWZ),
-// scale and q sum in s_xs / s_qsum; returns after a __syncthreads.
+// scale and q sum in s_xs / s_qsum; returns after a cta_sync.
 template <int B, int KPT, bool SWZ = true>
 __device__ void prep_quantize(const float (&vals)[B][KPT], int8_t* sq, int Kq, float* s_xs, int* s_qsum, float* red) {
   const int k0 = threadIdx.x * KPT;
@@ -217,7 +221,7 @@ __device__ void prep_quantize(const float (&vals)[B][KPT], int8_t* sq, int Kq, f
   if (threadIdx.x == 0)
 #pragma unroll
     for (int b = 0; b < B; ++b) s_qsum[b] = (int)qs[b];
-  __syncthreads();
+  cta_sync();
 }
 
 // One rank r of the LoRA down-projection, t[b] = fp16(sum_k xn[b][k] * B16[r][k]), from the
