@@ -30,6 +30,19 @@ __device__ __forceinline__ float round_h(float v) {
   const float r = copysignf(__fsub_rn(__fadd_rn(v, M), M), v);  // keeps -0 for tiny negatives
   return fabsf(r) > 65504.f ? copysignf(__int_as_float(0x7f800000), v) : r;
 }
+// The same fp16 rounding with the hardware conversions (cvt.rn.f16.f32, then widening):
+// 2 instructions instead of 8-13, for per-element prologue code that is issue-bound.
+__device__ __forceinline__ float round_hc(float v) { return __half2float(__float2half_rn(v)); }
+// Correctly rounded a / b from rb = RN(1/b) with two FMAs (Markstein's theorem: with rb within
+// half an ulp of 1/b and q0 = RN(a*rb) within an ulp of a/b, the remainder r = a - b*q0 is exact
+// and RN(q0 + r*rb) = RN(a/b)), valid while a/b, a and b stay normal fp32 -- true for fp16
+// operands.  One exception: a = -0 gives +0 (the quantiser maps both zeros to q = 0).  dfssm_selftest_division checks it against IEEE division over every fp16 pair the
+// quantiser can meet.
+__device__ __forceinline__ float div_rn_rcp(float a, float b, float rb) {
+  const float q0 = __fmul_rn(a, rb);
+  const float r = __fmaf_rn(-q0, b, a);
+  return __fmaf_rn(r, rb, q0);
+}
 // Round to the nearest integer, ties to even (|v| < 2^22): same trick with M = 1.5 * 2^23.
 __device__ __forceinline__ float rint_alu(float v) { return __fsub_rn(__fadd_rn(v, 12582912.0f), 12582912.0f); }
 // Signed byte j of w as fp32 without I2F: w ^ 0x80808080 biases the bytes to 0..255, a byte

@@ -926,3 +926,41 @@ extern "C" int dfssm_scaffold_gemm_noalloc(const uint32_t* packed, const int8_t*
   CHECK_LAUNCH();
   return DFSSM_OK;
 }
+
+// ------------------------------------------------------------------ division self-test
+
+namespace {
+__global__ void selftest_division_kernel(unsigned long long* mismatch) {
+  const unsigned short sb = (unsigned short)(blockIdx.x + 1);  // divisor: every positive finite fp16
+  const float b = __half2float(__ushort_as_half(sb));
+  const float rb = __frcp_rn(b);
+  unsigned long long m32 = 0, m16 = 0;
+  for (unsigned a16 = threadIdx.x; a16 < 0x10000u; a16 += blockDim.x) {
+    if ((a16 & 0x7C00u) == 0x7C00u) continue;  // inf / NaN
+    const float a = __half2float(__ushort_as_half((unsigned short)a16));
+    const float q = div_rn_rcp(a, b, rb);
+    const float ref = __fdiv_rn(a, b);
+    // zeros compare equal whatever their sign: -0 / b gives +0 here, and both quantise to 0
+    m32 += q != ref || (q != 0.f && __float_as_uint(q) != __float_as_uint(ref));
+    m16 += __half_as_ushort(__float2half_rn(q)) != __half_as_ushort(__float2half_rn(ref)) && q != 0.f;
+  }
+  if (m32) atomicAdd(mismatch, m32);
+  if (m16) atomicAdd(mismatch + 1, m16);
+}
+}  // namespace
+
+int dfssm_selftest_division(int device, unsigned long long* mismatch) {
+  if (!mismatch) return dfssm_fail(DFSSM_ERR_ARG, "NULL argument");
+  CU(cudaSetDevice(device));
+  unsigned long long* d = nullptr;
+  CU(cudaMalloc(&d, 16));
+  cudaError_t ce = cudaMemset(d, 0, 16);
+  if (ce == cudaSuccess) {
+    selftest_division_kernel<<<0x7BFF, 256>>>(d);
+    ce = cudaGetLastError();
+  }
+  if (ce == cudaSuccess) ce = cudaMemcpy(mismatch, d, 16, cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  if (ce != cudaSuccess) return dfssm_fail(DFSSM_ERR_CUDA, "division self-test: %s", cudaGetErrorString(ce));
+  return DFSSM_OK;
+}

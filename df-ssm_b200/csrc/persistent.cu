@@ -289,7 +289,7 @@ struct Dots {
 
 template <int B>
 __device__ __forceinline__ Dots<B> row_dot(const unsigned char* bits, int K, const int8_t* sq, int Kq, int l16,
-                                        const int* s_qsum) {
+                                        const int (&qs)[B]) {
   Dots<B> dot;
   int acc[B];
 #pragma unroll
@@ -325,18 +325,26 @@ __device__ __forceinline__ Dots<B> row_dot(const unsigned char* bits, int K, con
     a += __shfl_xor_sync(0xffffffffu, a, 4);
     a += __shfl_xor_sync(0xffffffffu, a, 2);
     a += __shfl_xor_sync(0xffffffffu, a, 1);
-    dot.v[b] = 2 * a - s_qsum[b];
+    dot.v[b] = 2 * a - qs[b];
   }
   return dot;
 }
 
-// dequant + LoRA up-projection of one output row (reference rounding points)
+// dequant + LoRA up-projection of one output row (reference rounding points).  A16 (16 fp16,
+// 16-byte aligned) and t live in shared memory; the rank sum runs as 4 independent chains,
+// since few threads run this epilogue and its latency is on the critical path.
 __device__ __forceinline__ float proj_out(int dot, float xs, float wscale, const __half* A16, const float* t) {
-  const float base = round_h(round_h(round_h((float)dot) * xs) * wscale);
-  float la = 0.f;
+  const float base = round_hc(round_hc(round_hc((float)dot) * xs) * wscale);
+  const uint4 a0 = reinterpret_cast<const uint4*>(A16)[0], a1 = reinterpret_cast<const uint4*>(A16)[1];
+  const unsigned aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+  float p[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int r = 0; r < DFSSM_RANK; ++r) la = fmaf(t[r], h2f(A16[r]), la);
-  return round_h(base + la);
+  for (int i = 0; i < 8; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&aw[i]));
+    p[i & 3] = fmaf(t[2 * i], f.x, p[i & 3]);
+    p[i & 3] = fmaf(t[2 * i + 1], f.y, p[i & 3]);
+  }
+  return round_hc(base + ((p[0] + p[1]) + (p[2] + p[3])));
 }
 
 __device__ __forceinline__ float conv_silu(float s0, float s1, float s2, float v, const __half* cw, float cb) {
@@ -351,9 +359,11 @@ __device__ __forceinline__ float conv_silu(float s0, float s1, float s2, float v
 template <int B, int KPT>
 __device__ void publish_t(const PParams& P, int tj, const float (&vals)[B][KPT], typename RankHalves<KPT>::T b0,
                           const __half* B16, int K, unsigned long long* tw, unsigned tag, float* red) {
-  for (int r = tj; r < DFSSM_RANK; r += P.n_t) {
+  // rank reductions alternate between red + 64 and red, the buffers the preceding norm did not
+  // use last
+  for (int r = tj, j = 0; r < DFSSM_RANK; r += P.n_t, ++j) {
     float t[B];
-    lora_t_rank_v<B, KPT>(vals, r == tj ? b0 : load_rank_b<KPT>(B16, K, r), t, red);
+    lora_t_rank_v<B, KPT>(vals, r == tj ? b0 : load_rank_b<KPT>(B16, K, r), t, (j & 1) ? red : red + 64);
     if (threadIdx.x == 0)
 #pragma unroll
       for (int b = 0; b < B; ++b) put_word(tw + b * DFSSM_RANK + r, P.rs, __float_as_uint(t[b]), tag);
@@ -412,11 +422,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
   __half* s_x = reinterpret_cast<__half*>(smem);                   // [B][d_model]
   int8_t* s_q = reinterpret_cast<int8_t*>(smem + B * d_model * 2);  // [B][d_inner]
   float* s_misc = reinterpret_cast<float*>(smem + B * d_model * 2 + B * d_inner);
-  float* red = s_misc;                              // [(kWarps + 1) * (B*16+B)]
+  // reduction buffers: red (norm, odd LoRA ranks), red + 64 (even LoRA ranks), red + 128
+  // (quantisation amax) -- consecutive single-barrier reductions never share one
+  float* red = s_misc;                              // [(kWarps + 1) * (B*16+B)] >= 192
   float* s_t = red + (kWarps + 1) * (B * 16 + B);   // [B*16]
   float* s_xs = s_t + B * 16;                       // [B]
-  int* s_qsum = reinterpret_cast<int*>(s_xs + B);   // [B]
-  float* s_lbs = reinterpret_cast<float*>(s_qsum + B);  // [16]
+  int* s_qpart = reinterpret_cast<int*>(s_xs + B);  // [B][kWarps] per-warp q sums
+  float* s_lbs = reinterpret_cast<float*>(s_qpart + B * kWarps);  // [16]
   float* s_z = s_lbs + 16;                          // [B][64]
   float* s_xc = s_z + B * 64;                       // [B][64]
   float* s_dt = s_xc + B * 64;                      // [B]
@@ -504,7 +516,6 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       cta_sync();
     }
     stamp(P, tb + 1);
-    stamp(P, tb + 2);
     {
       float vals[B][KI];
 #pragma unroll
@@ -514,8 +525,11 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       prep_norm<B, KI>(vals, w_in, d_model, red);
       if (t_producer) publish_t<B, KI>(P, pl.tj, vals, tb_in, L.in.B16, d_model, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK,
                                          tag_of(ebase, layer, kTagTin), red);  // publish before quantising
-      prep_quantize<B, KI>(vals, s_q, d_inner, s_xs, s_qsum, red);
+      prep_quantize<B, KI>(vals, s_q, d_inner, s_xs, s_qpart, red + 128);
     }
+    int qs[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) qs[b] = qsum_of(s_qpart, b);
     stamp(P, tb + 3);
     wait_stage(P, bars, layer);
     stamp(P, tb + 4);
@@ -532,12 +546,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       const float* cst = reinterpret_cast<const float*>(st + P.lay.cstate);
       for (int i = hw; i < ((nrows + 1) & ~1); i += 2 * kWarps) {
         const int row = i < nrows ? i : nrows - 1;
-        const Dots<B> dd = row_dot<B>(st + P.lay.in_bits + (size_t)row * RB, d_model, s_q, d_inner, l16, s_qsum);
+        const Dots<B> dd = row_dot<B>(st + P.lay.in_bits + (size_t)row * RB, d_model, s_q, d_inner, l16, qs);
         if (i < nrows && l16 < B) s_dot[row * B + l16] = dd.v[l16];
       }
       cta_sync();
       stamp(P, tb + 12);
       fetch_t<B>(P, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTin), s_t);
+      stamp(P, tb + 2);
       for (int e2 = tid; e2 < nrows * B; e2 += kThreads) {
         const int row = e2 / B, b = e2 - row * B;
         const int dot = s_dot[e2];
@@ -557,7 +572,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
           gcs[0] = s1;
           gcs[P.d_xbc] = s2;
           gcs[2 * P.d_xbc] = v;
-          s_xc[b * 64 + j] = round_h(conv_silu(s0, s1, s2, v, cw + j * 4, h2f(cb[j])));
+          s_xc[b * 64 + j] = round_hc(conv_silu(s0, s1, s2, v, cw + j * 4, h2f(cb[j])));
         } else {
           s_dt[b] = v;
         }
@@ -629,30 +644,33 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       const float* cst = reinterpret_cast<const float*>(st + P.lay.cstate);
       for (int i = hw; i < ((nb + 1) & ~1); i += 2 * kWarps) {
         const int row = i < nb ? i : nb - 1;
-        const Dots<B> dd = row_dot<B>(st + P.lay.in_bits + (size_t)row * RB, d_model, s_q, d_inner, l16, s_qsum);
+        const Dots<B> dd = row_dot<B>(st + P.lay.in_bits + (size_t)row * RB, d_model, s_q, d_inner, l16, qs);
         if (i < nb && l16 < B) s_dot[row * B + l16] = dd.v[l16];
       }
       cta_sync();
       stamp(P, tb + 12);
       fetch_t<B>(P, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTin), s_t);
+      stamp(P, tb + 2);
       unsigned long long* bcw = P.bcw + (size_t)par * B * DFSSM_DSTATE;
       const unsigned tg_bc = tag_of(ebase, layer, kTagBC);
-      for (int e2 = tid; e2 < (nb / 2) * B; e2 += kThreads) {
-        const int pr = e2 / B, b = e2 - pr * B;
-        float o2[2];
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int row = 2 * pr + k;
-          const float v = proj_out(s_dot[row * B + b], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
+      // one thread per (row, b), e = row * B + b; the partner row of a pair sits B lanes up in
+      // the same warp (32 is a multiple of 2B), and the even row's lane publishes the pair
+      for (int e0 = wid * 32; e0 < nb * B; e0 += kThreads) {
+        const int e2 = e0 + lane, row = e2 / B, b = e2 - row * B;
+        float o = 0.f;
+        if (e2 < nb * B) {
+          const float v = proj_out(s_dot[e2], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
           const int ch = d_inner + pl.bc0 + row;
           const float s0 = cst[(b * 3 + 0) * nb + row], s1 = cst[(b * 3 + 1) * nb + row], s2 = cst[(b * 3 + 2) * nb + row];
           float* gcs = P.conv + (long long)layer * P.conv_layer + (long long)b * 3 * P.d_xbc + ch;
           gcs[0] = s1;
           gcs[P.d_xbc] = s2;
           gcs[2 * P.d_xbc] = v;
-          o2[k] = conv_silu(s0, s1, s2, v, cw + row * 4, h2f(cb[row]));
+          o = conv_silu(s0, s1, s2, v, cw + row * 4, h2f(cb[row]));
         }
-        put_word(bcw + (size_t)b * DFSSM_DSTATE + (pl.bc0 + 2 * pr) / 2, P.rs, pack_h2(o2[0], o2[1]), tg_bc);
+        const float o_next = __shfl_down_sync(0xffffffffu, o, B);
+        if (e2 < nb * B && (row & 1) == 0)
+          put_word(bcw + (size_t)b * DFSSM_DSTATE + (pl.bc0 + row) / 2, P.rs, pack_h2(o, o_next), tg_bc);
       }
       cta_sync();
     }
@@ -702,14 +720,16 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       prep_norm<B, KO>(vals, w_out, d_inner, red);
       if (t_producer) publish_t<B, KO>(P, pl.tj, vals, tb_out, L.out.B16, d_inner, P.tw + (size_t)(par * 2 + 1) * B * DFSSM_RANK,
                                          tag_of(ebase, layer, kTagTout), red);  // publish before quantising
-      prep_quantize<B, KO>(vals, s_q, d_inner, s_xs, s_qsum, red);
+      prep_quantize<B, KO>(vals, s_q, d_inner, s_xs, s_qpart, red + 128);
     }
+#pragma unroll
+    for (int b = 0; b < B; ++b) qs[b] = qsum_of(s_qpart, b);
     stamp(P, tb + 10);
     if (pl.no > 0) {
       const int RBO = d_inner / 8;
       for (int i = hw; i < ((pl.no + 1) & ~1); i += 2 * kWarps) {
         const int row = i < pl.no ? i : pl.no - 1;
-        const Dots<B> dd = row_dot<B>(st + P.lay.out_bits + (size_t)row * RBO, d_inner, s_q, d_inner, l16, s_qsum);
+        const Dots<B> dd = row_dot<B>(st + P.lay.out_bits + (size_t)row * RBO, d_inner, s_q, d_inner, l16, qs);
         if (i < pl.no && l16 < B) s_dot[row * B + l16] = dd.v[l16];
       }
     }
@@ -721,19 +741,21 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       const __half* la = reinterpret_cast<const __half*>(st + P.lay.out_lA);
       unsigned long long* xw = P.xw + (size_t)(par ^ 1) * B * XW;
       const unsigned tg_x = tag_of(ebase, layer + 1, kTagX);
-      for (int e2 = tid; e2 < (pl.no / 2) * B; e2 += kThreads) {
-        const int pr = e2 / B, b = e2 - pr * B;
-        const int o = pl.o0 + 2 * pr;
-        float xo[2];
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int row = 2 * pr + k;
-          const float v = proj_out(s_dot[row * B + b], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
-          xo[k] = h2f(s_x[b * d_model + o + k]) + v;
+      // one thread per (row, b) as in the B/C epilogue; the even row's lane publishes the pair
+      for (int e0 = wid * 32; e0 < pl.no * B; e0 += kThreads) {
+        const int e2 = e0 + lane, row = e2 / B, b = e2 - row * B;
+        const int o = pl.o0 + row;
+        float xo = 0.f;
+        if (e2 < pl.no * B) {
+          const float v = proj_out(s_dot[e2], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
+          xo = h2f(s_x[b * d_model + o]) + v;
         }
-        const unsigned w = pack_h2(xo[0], xo[1]);
-        put_word(xw + (size_t)b * XW + o / 2, P.rs, w, tg_x);
-        *reinterpret_cast<unsigned*>(P.x_g + (size_t)b * d_model + o) = w;  // plain copy for the host API
+        const float xo_next = __shfl_down_sync(0xffffffffu, xo, B);
+        if (e2 < pl.no * B && (row & 1) == 0) {
+          const unsigned w = pack_h2(xo, xo_next);
+          put_word(xw + (size_t)b * XW + o / 2, P.rs, w, tg_x);
+          *reinterpret_cast<unsigned*>(P.x_g + (size_t)b * d_model + o) = w;  // plain copy for the host API
+        }
       }
     }
     cta_sync();
@@ -1009,7 +1031,7 @@ int build_plan(const dfssm_engine* e, int B, int grid, std::vector<CtaPlan>& pla
   lay.state = off; off += a16(B * np * DFSSM_DSTATE * 4);
   lay.cstate = off; off += a16(B * 3 * ch * 4);
   lay.stage_bytes = (off + 127) & ~127;
-  const int misc_floats = (kWarps + 1) * (B * 16 + B) + B * 16 + B + B + 16 + B * 64 * 2 + B + B * 256 + 128 * B + 8;
+  const int misc_floats = (kWarps + 1) * (B * 16 + B) + B * 16 + B + B * kWarps + 16 + B * 64 * 2 + B + B * 256 + 128 * B + 8;
   int work = B * d.d_model * 2 + B * d.d_inner + misc_floats * 4;
   work = (work + 127) & ~127;
   tab_off = work;

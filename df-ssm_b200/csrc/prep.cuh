@@ -58,6 +58,45 @@ __device__ __forceinline__ void block_max_n(float (&v)[N], float* red) {
   for (int i = 0; i < N; ++i) v[i] = red[kPrepFastWarps * N + i];
 }
 
+// Single-barrier block sum / max: warp partials go to red[w*N + i], one cta_sync, then every
+// thread combines the 16 partials of each value itself, in the same fixed order, so all
+// threads hold identical totals.  `red` must not still be read by the previous reduction that
+// used it: callers rotate buffers so that a barrier separates the two uses.
+template <int N>
+__device__ __forceinline__ void block_sum1(float (&v)[N], float* red) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = warp_sum(v[i]);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0)
+#pragma unroll
+    for (int i = 0; i < N; ++i) red[w * N + i] = v[i];
+  cta_sync();
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < kPrepFastWarps; ++j) s += red[j * N + i];
+    v[i] = s;
+  }
+}
+template <int N>
+__device__ __forceinline__ void block_max1(float (&v)[N], float* red) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = warp_max(v[i]);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0)
+#pragma unroll
+    for (int i = 0; i < N; ++i) red[w * N + i] = v[i];
+  cta_sync();
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    float s = red[i];
+#pragma unroll
+    for (int j = 1; j < kPrepFastWarps; ++j) s = fmaxf(s, red[j * N + i]);
+    v[i] = s;
+  }
+}
+
 // Like block_sum_n but only threads i < N receive total i (returned), for the LoRA partials.
 template <int N>
 __device__ __forceinline__ float block_sum_scatter(float (&v)[N], float* red) {
@@ -179,19 +218,20 @@ __device__ __forceinline__ void prep_norm(float (&vals)[B][KPT], const float (&w
     for (int j = 0; j < KPT; ++j) a = __fadd_rn(a, __fmul_rn(vals[b][j], vals[b][j]));
     ss[b] = a;
   }
-  block_sum_n<B>(ss, red);
+  block_sum1<B>(ss, red);
 #pragma unroll
   for (int b = 0; b < B; ++b) {
     const float r = rsqrtf(__fadd_rn(__fmul_rn(ss[b], 1.0f / (float)K), 1e-5f));
 #pragma unroll
-    for (int j = 0; j < KPT; ++j) vals[b][j] = round_h(__fmul_rn(__fmul_rn(vals[b][j], r), w[j]));
+    for (int j = 0; j < KPT; ++j) vals[b][j] = round_hc(__fmul_rn(__fmul_rn(vals[b][j], r), w[j]));
   }
 }
 
 // Per-row int8 quantisation of normalised values (second half): q in sq (swizzled if SWZ),
-// scale and q sum in s_xs / s_qsum; returns after a cta_sync.
+// the scale in s_xs, and per-warp partial q sums in s_qpart[b][warp] (see qsum_of); returns
+// after a cta_sync.  One barrier for the amax, one for the stores.
 template <int B, int KPT, bool SWZ = true>
-__device__ void prep_quantize(const float (&vals)[B][KPT], int8_t* sq, int Kq, float* s_xs, int* s_qsum, float* red) {
+__device__ void prep_quantize(const float (&vals)[B][KPT], int8_t* sq, int Kq, float* s_xs, int* s_qpart, float* red) {
   const int k0 = threadIdx.x * KPT;
   float am[B];
 #pragma unroll
@@ -201,27 +241,34 @@ __device__ void prep_quantize(const float (&vals)[B][KPT], int8_t* sq, int Kq, f
     for (int j = 0; j < KPT; ++j) a = fmaxf(a, fabsf(vals[b][j]));
     am[b] = a;
   }
-  block_max_n<B>(am, red);
-  float qs[B];
+  block_max1<B>(am, red);
 #pragma unroll
   for (int b = 0; b < B; ++b) {
     const float s = round_h(__fmul_rn(fmaxf(am[b], qscale_floor()), 1.0f / 127.0f));
+    const float rs = __frcp_rn(s);
     int qsum = 0;
 #pragma unroll
     for (int j = 0; j < KPT; ++j) {
-      int q = (int)rint_alu(round_h(vals[b][j] / s));
+      // q = rne(fp16(x / s)); |x / s| <= 127 * (1 + 2^-11) since s is amax/127 rounded to fp16,
+      // so the clamp only guards the int8 store
+      int q = __float2int_rn(round_hc(div_rn_rcp(vals[b][j], s, rs)));
       q = max(-128, min(127, q));
       sq[b * Kq + (SWZ ? qswz(qperm_index(k0 + j)) : qperm_index(k0 + j))] = (int8_t)q;
       qsum += q;
     }
-    qs[b] = (float)qsum;
+    qsum = warp_sum(qsum);
+    if ((threadIdx.x & 31) == 0) s_qpart[b * kPrepFastWarps + (threadIdx.x >> 5)] = qsum;
     if (threadIdx.x == 0) s_xs[b] = s;
   }
-  block_sum_n<B>(qs, red);
-  if (threadIdx.x == 0)
-#pragma unroll
-    for (int b = 0; b < B; ++b) s_qsum[b] = (int)qs[b];
   cta_sync();
+}
+
+// Total q sum of activation row b from the per-warp partials of prep_quantize.
+__device__ __forceinline__ int qsum_of(const int* s_qpart, int b) {
+  int s = 0;
+#pragma unroll
+  for (int j = 0; j < kPrepFastWarps; ++j) s += s_qpart[b * kPrepFastWarps + j];
+  return s;
 }
 
 // One rank r of the LoRA down-projection, t[b] = fp16(sum_k xn[b][k] * B16[r][k]), from the
@@ -243,7 +290,7 @@ __device__ __forceinline__ void lora_t_rank_v(const float (&vals)[B][KPT], typen
     for (int j = 0; j < KPT; ++j) a = fmaf(vals[b][j], half_of<KPT>(bv, j), a);
     t[b] = a;
   }
-  block_sum_n<B>(t, red);
+  block_sum1<B>(t, red);
 #pragma unroll
   for (int b = 0; b < B; ++b) t[b] = round_h(t[b]);
 }

@@ -108,11 +108,11 @@ int dfssm_layer_step(dfssm_engine* e, int layer, void* stream);
  * uint64 entries of a persistent-step trace, and one persistent decode step (mode 3 batch)
  * that records %globaltimer stamps at its phase boundaries into trace_dev
  * [sm_count][4 + 14 * n_layer]: [0] start, [1] end, [2 + 14l + k] layer l point k
- * (0 alpha entry, 1 after the x barrier, 2 after loading x, 3 after norm/quant/LoRA,
- *  4 after the weight ring wait, 12 after the in_proj dot products, 5 after the LoRA-t wait and
- *  the in_proj epilogue, 6 after the B/C wait, 7 after the SSM, 8 before the gated barrier,
- *  9 after it, 10 after the beta norm/quant/LoRA, 13 after the out_proj dot products, 11 after
- *  the LoRA-t wait and the out_proj epilogue);
+ * (0 alpha entry, 1 after receiving x, 3 after norm/quant/LoRA, 4 after the weight ring wait,
+ *  12 after the in_proj dot products, 2 after the LoRA-t wait, 5 after the in_proj epilogue,
+ *  6 after receiving B/C, 7 after the SSM, 8 before the gated exchange, 9 after receiving the
+ *  gated vector, 10 after the beta norm/quant/LoRA, 13 after the out_proj dot products, 11
+ *  after the LoRA-t wait and the out_proj epilogue);
  * [2 + 14 n_layer] head entry, [3 + 14 n_layer] after its barrier. */
 size_t dfssm_trace_entries(const dfssm_engine* e);
 int dfssm_trace_step(dfssm_engine* e, unsigned long long* trace_dev, void* stream);
@@ -165,6 +165,13 @@ size_t dfssm_lm_head_workspace(int batch);
  * logits may be NULL.  d % 16 == 0. */
 int dfssm_lm_head_argmax(const int8_t* E_q, const float* E_s, int vocab, int d, const void* x_f16,
                          int batch, float* logits, int32_t* next, void* workspace, void* stream);
+
+/* Self-test (no counterpart in the reference): checks, on device `device`, the kernels'
+ * two-FMA division (common.cuh div_rn_rcp, used by the activation quantiser) against IEEE fp32
+ * division for every pair of finite fp16 operands with a positive divisor.  Writes the number
+ * of pairs whose fp32 quotient differs to mismatch[0] and whose fp16-rounded quotient differs
+ * to mismatch[1], zeros of either sign comparing equal; both must be 0.  Synchronous. */
+int dfssm_selftest_division(int device, unsigned long long* mismatch);
 
 #ifdef __cplusplus
 }

@@ -124,3 +124,12 @@ def test_lm_head_argmax(lib, B, V, d):
     r16 = ref.astype(np.float32).astype(np.float16)
     top = r16.max(-1)
     assert np.all(np.abs(r16[np.arange(B), n].astype(np.float32) - top.astype(np.float32)) <= 0.125)
+
+
+def test_quantiser_division_matches_ieee(lib):
+    """The activation quantiser divides by its scale with two FMAs and a reciprocal
+    (common.cuh div_rn_rcp); over every finite fp16 dividend and positive fp16 divisor its
+    quotient must equal IEEE fp32 division bit for bit."""
+    out = (ctypes.c_ulonglong * 2)()
+    assert lib.dfssm_selftest_division(0, out) == 0, lib.dfssm_last_error()
+    assert (out[0], out[1]) == (0, 0)
