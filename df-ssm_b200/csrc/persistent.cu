@@ -99,7 +99,7 @@ struct PParams {
   unsigned long long* trace;  // optional: per-CTA globaltimer stamps (kTraceStride entries per CTA)
 };
 
-constexpr int kTracePerLayer = 14;
+constexpr int kTracePerLayer = 16;
 __device__ __forceinline__ void stamp(const PParams& P, int idx) {
   if (P.trace && threadIdx.x == 0) {
     unsigned long long t;
@@ -128,14 +128,22 @@ __device__ __forceinline__ void put_word(unsigned long long* p, size_t rstride, 
   for (int r = 0; r < kReplicas; ++r)
     asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p + r * rstride), "l"(w) : "memory");
 }
-// Poll G groups of N consecutive words (group g at p + g * gstride; N = 1, 2 or 4, each group
+// Poll G groups of N consecutive words (FIRST: first wait for word 0 of group 0 alone) (group g at p + g * gstride; N = 1, 2 or 4, each group
 // 8*N-byte aligned for N > 1) until every tag equals `tag`; the data go to out[][].  All loads
 // of one poll are issued together.  Bounded: after kSpinLimit polls the error word gets
 // `code`, and once the error word is set every poll gives up at its next check.
-template <int G, int N>
+template <int G, int N, bool FIRST = false>
 __device__ __forceinline__ void take_words(const unsigned long long* p, size_t gstride, unsigned tag,
                                            unsigned (&out)[G][N], unsigned* err, unsigned code) {
   unsigned long long w[G][N];
+  if (FIRST) {  // wait on the first word alone (an eighth of the poll traffic), then take all
+    for (unsigned it = 0;; ++it) {
+      unsigned long long w0;
+      asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w0) : "l"(p) : "memory");
+      if ((unsigned)(w0 >> 32) == tag) break;
+      if ((it & 255u) == 255u && (ld_acquire(err) != 0 || it > kSpinLimit)) break;
+    }
+  }
   for (unsigned it = 0;; ++it) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -203,15 +211,12 @@ __device__ __forceinline__ void wait_stage(const PParams& P, uint64_t* bars, int
 }
 
 // Issue the bulk copies that fill the ring slot of `layer` with this CTA's slice of it.
-// Copy i of the table below (all 16-byte aligned, sizes multiples of
-// 16); the byte total of a stage is precomputed on the host (CtaPlan::tx).
+// Copy i (0..31) of this CTA's share of layer `layer`: source, byte offset in the ring stage and
+// size (0 = none); all 16-byte aligned, sizes multiples of 16.  The byte total of a stage is
+// precomputed on the host (CtaPlan::tx).
 template <int B>
-__device__ __forceinline__ void issue_stage(const PParams& P, const CtaPlan& pl, int layer, unsigned char* ring,
-                                         uint64_t* bars, const LayerW* layers, int i) {
-  if (layer >= P.l1) return;
-  const int slot = (layer - P.l0) % P.ns;
-  unsigned char* st = ring + (size_t)slot * P.lay.stage_bytes;
-  uint64_t* bar = bars + slot;
+__device__ __forceinline__ void copy_desc(const PParams& P, const CtaPlan& pl, int layer, const LayerW* layers, int i,
+                                          const void*& src, int& dst, unsigned& bytes) {
   const LayerW& L = layers[layer];
   const Layout& Y = P.lay;
   const int RB = P.d_model / 8, RBO = P.d_inner / 8;
@@ -272,13 +277,17 @@ __device__ __forceinline__ void issue_stage(const PParams& P, const CtaPlan& pl,
       default: break;
     }
   }
-  // The slot's previous contents were read by the compute threads before they released the
-  // slot (an mbarrier arrive after their barrier), which the issuer observed before this call.
-  // the arrive with the stage's byte total may land before or after the copies complete: the
-  // transaction count of the phase may go negative, and the phase ends only after the arrive
-  if (i == 0) mbar_expect_tx(bar, (unsigned)pl.tx);
-  if (n_) bulk_g2s(st + d_, s_, n_, bar);
+  src = s_;
+  dst = d_;
+  bytes = n_;
 }
+
+// The ring stage of a layer is cut into pieces of at most kCopyPiece bytes, and piece p belongs
+// to part floor(kParts * (its first byte) / (stage bytes)).  The compute threads release a
+// slot in kParts steps spread over the following layer, so the ring's HBM traffic arrives as
+// kParts small bursts instead of one large burst that would delay every CTA's exchange words.
+constexpr unsigned kCopyPiece = 4096;
+constexpr int kParts = 4;
 
 // 1-bit GEMV of one row held in shared memory for B activation rows: returns the int32
 // sum_k s_k q_k for every b in all 16 lanes of the half-warp.
@@ -381,37 +390,80 @@ __device__ __forceinline__ void fetch_t(const PParams& P, const unsigned long lo
   cta_sync();
 }
 
-// The copy-issuing warp: fills ring slot (k % ns) with layer l0 + k as soon as the compute
-// threads have released the layer that used the slot before (k >= ns).  Lane i issues copy i of
-// issue_stage.  Bounded: gives up when a wait times out or the error word is set.
+// The copy-issuing warp: fills ring slot (k % ns) with layer l0 + k.  The first ns layers go
+// out at once; later ones part by part, each as soon as the compute threads have released that
+// part of the slot (empty barrier slot * kParts + part) while running the layer after the one
+// that used it.  Lane i owns copy i of copy_desc, so a layer costs the warp one pass over the
+// table; the warp shares its SM with 16 busy compute warps and must stay cheap.  The slot's
+// previous contents were read by the compute threads before they released the part (an
+// mbarrier arrive after their barrier), which lane 0 observed before the copies are issued.
+// Bounded: gives up when a wait times out or the error word is set.
 template <int B>
 __device__ void copy_issuer(const PParams& P, const CtaPlan& pl, unsigned char* ring, uint64_t* full,
                             uint64_t* empty, const LayerW* layers) {
   const int lane = threadIdx.x & 31;
   const int nl = P.l1 - P.l0;
+  const unsigned tx = (unsigned)pl.tx;
+  const unsigned b1 = tx / kParts, b2 = 2 * tx / kParts, b3 = 3 * tx / kParts;  // first bytes of parts 1..3
   for (int k = 0; k < nl; ++k) {
-    if (k >= P.ns) {
-      int ok = 1;
-      if (lane == 0) {
-        const unsigned parity = (unsigned)((k / P.ns - 1) & 1);
-        unsigned it = 0;
-        while (!mbar_try_wait(empty + k % P.ns, parity)) {
-          if ((++it & 1023u) == 0 && ld_acquire(P.sync + 3) != 0) {
-            ok = 0;
-            break;
-          }
-          if (it > kSpinLimit) {
-            atomicOr(P.sync + 3, 32u);
-            ok = 0;
-            break;
+    const int layer = P.l0 + k, slot = k % P.ns;
+    unsigned char* st = ring + (size_t)slot * P.lay.stage_bytes;
+    const void* src;
+    int dst;
+    unsigned n;
+    copy_desc<B>(P, pl, layer, layers, lane, src, dst, n);
+    unsigned pre = n;  // inclusive prefix sum of the copy sizes over lanes -> first byte of mine
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned v = __shfl_up_sync(0xffffffffu, pre, o);
+      if (lane >= o) pre += v;
+    }
+    pre -= n;
+    for (int part = 0; part < kParts; ++part) {
+      if (k >= P.ns) {
+        int ok = 1;
+        if (lane == 0) {
+          const unsigned parity = (unsigned)((k / P.ns - 1) & 1);
+          unsigned it = 0;
+          while (!mbar_try_wait(empty + slot * kParts + part, parity)) {
+            if ((++it & 1023u) == 0 && ld_acquire(P.sync + 3) != 0) {
+              ok = 0;
+              break;
+            }
+            if (it > kSpinLimit) {
+              atomicOr(P.sync + 3, 32u);
+              ok = 0;
+              break;
+            }
           }
         }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) return;
       }
-      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      if (part == 0) {
+        if (lane == 0) mbar_expect_tx(full + slot, tx);
+        __syncwarp();
+      }
+      for (unsigned off = 0; off < n; off += kCopyPiece) {
+        const unsigned at = pre + off;
+        const int pp = (at >= b1) + (at >= b2) + (at >= b3);
+        if (pp == part || k < P.ns)
+          bulk_g2s(st + dst + off, reinterpret_cast<const char*>(src) + off, min(kCopyPiece, n - off), full + slot);
+      }
+      if (P.trace && lane == 0 && (part == 0 || part == kParts - 1)) {  // points 14 / 15 of the issued layer
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        P.trace[(size_t)blockIdx.x * (4 + kTracePerLayer * P.n_layer) + 2 + kTracePerLayer * layer + 14 +
+                (part != 0)] = t;
+      }
+      __syncwarp();
+      if (k < P.ns) break;  // the first ns layers: every piece went out with part 0
     }
-    issue_stage<B>(P, pl, P.l0 + k, ring, full, layers, lane);
-    __syncwarp();
   }
+}
+
+// Compute side: release part `part` of the ring slot used by the previous layer.
+__device__ __forceinline__ void release_part(const PParams& P, uint64_t* empties, int layer, int part) {
+  if (threadIdx.x == 0 && layer > P.l0) mbar_arrive(empties + ((layer - 1 - P.l0) % P.ns) * kParts + part);
 }
 
 template <int B, int KI, int KO>
@@ -440,7 +492,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
   LayerW* s_layers = reinterpret_cast<LayerW*>(smem + P.tab_off);
   float* s_hptab = reinterpret_cast<float*>(smem + P.tab_off + ((P.n_layer * (int)sizeof(LayerW) + 15) & ~15));  // [n_layer][12], 16-byte aligned
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.ring_off - 8 * 8);      // ring slot full
-  uint64_t* empties = reinterpret_cast<uint64_t*>(smem + P.ring_off - 16 * 8);  // ring slot released
+  uint64_t* empties = reinterpret_cast<uint64_t*>(smem + P.ring_off - 8 * 8 - 8 * 4 * 8);  // [slot][part] released
   unsigned char* ring = smem + P.ring_off;
 
   const CtaPlan pl = P.plans[blockIdx.x];
@@ -452,7 +504,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
   if (tid == 0) {
     for (int i = 0; i < P.ns; ++i) {
       mbar_init(bars + i, 1);
-      mbar_init(empties + i, 1);
+      for (int j = 0; j < kParts; ++j) mbar_init(empties + i * kParts + j, 1);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -516,6 +568,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       cta_sync();
     }
     stamp(P, tb + 1);
+    release_part(P, empties, layer, 0);
     {
       float vals[B][KI];
 #pragma unroll
@@ -551,6 +604,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       }
       cta_sync();
       stamp(P, tb + 12);
+      release_part(P, empties, layer, 1);
       fetch_t<B>(P, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTin), s_t);
       stamp(P, tb + 2);
       for (int e2 = tid; e2 < nrows * B; e2 += kThreads) {
@@ -649,6 +703,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       }
       cta_sync();
       stamp(P, tb + 12);
+      release_part(P, empties, layer, 1);
       fetch_t<B>(P, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTin), s_t);
       stamp(P, tb + 2);
       unsigned long long* bcw = P.bcw + (size_t)par * B * DFSSM_DSTATE;
@@ -673,6 +728,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
           put_word(bcw + (size_t)b * DFSSM_DSTATE + (pl.bc0 + row) / 2, P.rs, pack_h2(o, o_next), tg_bc);
       }
       cta_sync();
+    } else {
+      release_part(P, empties, layer, 1);  // no in_proj rows
     }
     stamp(P, tb + 7);
     // ---------------- beta: out_proj rows
@@ -687,10 +744,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
     stamp(P, tb + 8);
     // head CTAs write their state back, then every CTA collects the gated vector
     cta_sync();
-    // release the ring slot of layer - 1 to the copy warp: releasing here, when every CTA is
-    // about to wait for the gated vector, measured faster than at the top of the layer, where the
-    // copies' HBM burst delays the x exchange
-    if (tid == 0 && layer > P.l0) mbar_arrive(empties + (layer - 1 - P.l0) % P.ns);
+    release_part(P, empties, layer, 2);
     if (pl.role == 0) {
 #pragma unroll
       for (int b = 0; b < B; ++b)
@@ -707,7 +761,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       const unsigned long long* gw = P.gw + (size_t)par * B * GW;
       const unsigned tg_g = tag_of(ebase, layer, kTagGated);
       unsigned v[B][KO / 2];
-      take_words<B, KO / 2>(gw + rep_off + tid * (KO / 2), GW, tg_g, v, P.sync + 3, 16u);
+      // the gated vector is the largest exchange (every CTA takes all of it while most wait for
+      // the slowest head): poll one word per thread, then load the rest
+      take_words<B, KO / 2, true>(gw + rep_off + tid * (KO / 2), GW, tg_g, v, P.sync + 3, 16u);
 #pragma unroll
       for (int b = 0; b < B; ++b)
 #pragma unroll
@@ -725,6 +781,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
 #pragma unroll
     for (int b = 0; b < B; ++b) qs[b] = qsum_of(s_qpart, b);
     stamp(P, tb + 10);
+    release_part(P, empties, layer, 3);
     if (pl.no > 0) {
       const int RBO = d_inner / 8;
       for (int i = hw; i < ((pl.no + 1) & ~1); i += 2 * kWarps) {
@@ -1037,7 +1094,7 @@ int build_plan(const dfssm_engine* e, int B, int grid, std::vector<CtaPlan>& pla
   tab_off = work;
   work += ((d.n_layer * (int)sizeof(LayerW) + 15) & ~15) + d.n_layer * 12 * 4;
   work = (work + 127) & ~127;
-  const int ring_off = work + 128;  // 8 full + 8 released mbarriers live just below the ring
+  const int ring_off = work + 384;  // 8 full + 8 x 4 released mbarriers live just below the ring
   int max_smem = 0;
   cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, e->device);
   ns = (max_smem - ring_off) / lay.stage_bytes;

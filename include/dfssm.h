@@ -107,13 +107,14 @@ int dfssm_layer_step(dfssm_engine* e, int layer, void* stream);
 /* Diagnostics (no counterpart in the reference, which has no profiler hooks): number of
  * uint64 entries of a persistent-step trace, and one persistent decode step (mode 3 batch)
  * that records %globaltimer stamps at its phase boundaries into trace_dev
- * [sm_count][4 + 14 * n_layer]: [0] start, [1] end, [2 + 14l + k] layer l point k
+ * [sm_count][4 + 16 * n_layer]: [0] start, [1] end, [2 + 16l + k] layer l point k
  * (0 alpha entry, 1 after receiving x, 3 after norm/quant/LoRA, 4 after the weight ring wait,
  *  12 after the in_proj dot products, 2 after the LoRA-t wait, 5 after the in_proj epilogue,
  *  6 after receiving B/C, 7 after the SSM, 8 before the gated exchange, 9 after receiving the
  *  gated vector, 10 after the beta norm/quant/LoRA, 13 after the out_proj dot products, 11
- *  after the LoRA-t wait and the out_proj epilogue);
- * [2 + 14 n_layer] head entry, [3 + 14 n_layer] after its barrier. */
+ *  after the LoRA-t wait and the out_proj epilogue; 14 / 15: the copy warp issued the first /
+ *  last part of this layer's ring stage, 0 for the first ring-depth layers);
+ * [2 + 16 n_layer] head entry, [3 + 16 n_layer] after receiving the final x. */
 size_t dfssm_trace_entries(const dfssm_engine* e);
 int dfssm_trace_step(dfssm_engine* e, unsigned long long* trace_dev, void* stream);
 
