@@ -299,8 +299,10 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], unsigned a0, unsigned a1, un
                : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Two CTAs per SM (caps registers at 128): the in_proj grid has 266 CTAs, which one CTA per SM
+// would run as two waves.
 template <int MODE, int RG>
-__global__ void __launch_bounds__(kMmaThreads)
+__global__ void __launch_bounds__(kMmaThreads, 2)
 proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ qsum,
                 const __half* __restrict__ xs, const __half* __restrict__ t, int B,
                 __half* __restrict__ out, int ld_out,

@@ -170,7 +170,7 @@ __device__ void prep_rows(float (&vals)[B][KPT], const float (&w)[KPT], int K,
     float a = 0.f;
 #pragma unroll
     for (int j = 0; j < KPT; ++j) {
-      const float xn = round_h(__fmul_rn(__fmul_rn(vals[b][j], r), w[j]));
+      const float xn = round_hc(__fmul_rn(__fmul_rn(vals[b][j], r), w[j]));
       vals[b][j] = xn;
       a = fmaxf(a, fabsf(xn));
     }
@@ -181,10 +181,11 @@ __device__ void prep_rows(float (&vals)[B][KPT], const float (&w)[KPT], int K,
 #pragma unroll
   for (int b = 0; b < B; ++b) {
     const float s = round_h(__fmul_rn(fmaxf(am[b], qscale_floor()), 1.0f / 127.0f));
+    const float rs = __frcp_rn(s);
     int qsum = 0;
 #pragma unroll
     for (int j = 0; j < KPT; ++j) {
-      int q = (int)rint_alu(round_h(vals[b][j] / s));
+      int q = __float2int_rn(round_hc(div_rn_rcp(vals[b][j], s, rs)));
       q = max(-128, min(127, q));
       sq[b * Kq + (SWZ ? qswz(qperm_index(k0 + j)) : qperm_index(k0 + j))] = (int8_t)q;
       qsum += q;
