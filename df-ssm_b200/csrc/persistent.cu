@@ -379,14 +379,33 @@ __device__ void publish_t(const PParams& P, int tj, const float (&vals)[B][KPT],
   }
 }
 
-// Collect the B x 16 published LoRA t values into s_t.
+// One relaxed read of an exchange word, issued ahead of independent work so that its L2 round
+// trip overlaps that work; take_word() then polls again only if the tag did not match yet.
+__device__ __forceinline__ unsigned long long peek_word(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+__device__ __forceinline__ unsigned take_word(const unsigned long long* p, unsigned long long early, unsigned tag,
+                                              unsigned* err, unsigned code) {
+  if ((unsigned)(early >> 32) == tag) return (unsigned)early;
+  unsigned v[1][1];
+  take_words<1, 1>(p, 0, tag, v, err, code);
+  return v[0][0];
+}
+
+// This thread's LoRA-t word (threads < B x 16) of this CTA's replica.
 template <int B>
-__device__ __forceinline__ void fetch_t(const PParams& P, const unsigned long long* tw, unsigned tag, float* s_t) {
-  if (threadIdx.x < B * DFSSM_RANK) {
-    unsigned v[1][1];
-    take_words<1, 1>(tw + (blockIdx.x % kReplicas) * P.rs + threadIdx.x, 0, tag, v, P.sync + 3, 8u);
-    s_t[threadIdx.x] = __uint_as_float(v[0][0]);
-  }
+__device__ __forceinline__ const unsigned long long* t_word(const PParams& P, const unsigned long long* tw) {
+  return tw + (blockIdx.x % kReplicas) * P.rs + (threadIdx.x < B * DFSSM_RANK ? threadIdx.x : 0);
+}
+
+// Collect the B x 16 published LoRA t values into s_t; `early` is peek_word(t_word(...)) issued
+// before the dot products.
+template <int B>
+__device__ __forceinline__ void fetch_t(const PParams& P, const unsigned long long* tw, unsigned tag, float* s_t,
+                                        unsigned long long early) {
+  if (threadIdx.x < B * DFSSM_RANK) s_t[threadIdx.x] = __uint_as_float(take_word(t_word<B>(P, tw), early, tag, P.sync + 3, 8u));
   cta_sync();
 }
 
@@ -597,6 +616,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       const __half* cw = reinterpret_cast<const __half*>(st + P.lay.conv_w);
       const __half* cb = reinterpret_cast<const __half*>(st + P.lay.conv_b);
       const float* cst = reinterpret_cast<const float*>(st + P.lay.cstate);
+      const unsigned long long t_early = peek_word(t_word<B>(P, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK));
       for (int i = hw; i < ((nrows + 1) & ~1); i += 2 * kWarps) {
         const int row = i < nrows ? i : nrows - 1;
         const Dots<B> dd = row_dot<B>(st + P.lay.in_bits + (size_t)row * RB, d_model, s_q, d_inner, l16, qs);
@@ -605,8 +625,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       cta_sync();
       stamp(P, tb + 12);
       release_part(P, empties, layer, 1);
-      fetch_t<B>(P, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTin), s_t);
+      fetch_t<B>(P, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTin), s_t, t_early);
       stamp(P, tb + 2);
+      const unsigned long long* bcw_mine = P.bcw + (size_t)par * B * DFSSM_DSTATE + rep_off + (tid < B * DFSSM_DSTATE ? tid : 0);
+      const unsigned long long bc_early = tid < B * DFSSM_DSTATE ? peek_word(bcw_mine) : 0ull;
       for (int e2 = tid; e2 < nrows * B; e2 += kThreads) {
         const int row = e2 / B, b = e2 - row * B;
         const int dot = s_dot[e2];
@@ -633,16 +655,11 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       }
       cta_sync();
       stamp(P, tb + 5);
-      // wait for every B/C CTA of this layer, then fetch conv'd B and C
-      {
-        const unsigned long long* bcw = P.bcw + (size_t)par * B * DFSSM_DSTATE;
-        const unsigned tg = tag_of(ebase, layer, kTagBC);
-        for (int i = tid; i < B * DFSSM_DSTATE; i += kThreads) {
-          unsigned v[1][1];
-          take_words<1, 1>(bcw + rep_off + i, 0, tg, v, P.sync + 3, 4u);
-          s_bc[2 * i] = lo_h(v[0][0]);
-          s_bc[2 * i + 1] = hi_h(v[0][0]);
-        }
+      // wait for every B/C CTA of this layer, then fetch conv'd B and C (B * d_state <= 512 words)
+      if (tid < B * DFSSM_DSTATE) {
+        const unsigned v = take_word(bcw_mine, bc_early, tag_of(ebase, layer, kTagBC), P.sync + 3, 4u);
+        s_bc[2 * tid] = lo_h(v);
+        s_bc[2 * tid + 1] = hi_h(v);
       }
       cta_sync();
       stamp(P, tb + 6);
@@ -696,6 +713,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       const __half* cw = reinterpret_cast<const __half*>(st + P.lay.conv_w);
       const __half* cb = reinterpret_cast<const __half*>(st + P.lay.conv_b);
       const float* cst = reinterpret_cast<const float*>(st + P.lay.cstate);
+      const unsigned long long t_early = peek_word(t_word<B>(P, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK));
       for (int i = hw; i < ((nb + 1) & ~1); i += 2 * kWarps) {
         const int row = i < nb ? i : nb - 1;
         const Dots<B> dd = row_dot<B>(st + P.lay.in_bits + (size_t)row * RB, d_model, s_q, d_inner, l16, qs);
@@ -704,7 +722,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       cta_sync();
       stamp(P, tb + 12);
       release_part(P, empties, layer, 1);
-      fetch_t<B>(P, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTin), s_t);
+      fetch_t<B>(P, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTin), s_t, t_early);
       stamp(P, tb + 2);
       unsigned long long* bcw = P.bcw + (size_t)par * B * DFSSM_DSTATE;
       const unsigned tg_bc = tag_of(ebase, layer, kTagBC);
@@ -782,6 +800,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
     for (int b = 0; b < B; ++b) qs[b] = qsum_of(s_qpart, b);
     stamp(P, tb + 10);
     release_part(P, empties, layer, 3);
+    const unsigned long long to_early = pl.no > 0 ? peek_word(t_word<B>(P, P.tw + (size_t)(par * 2 + 1) * B * DFSSM_RANK)) : 0ull;
     if (pl.no > 0) {
       const int RBO = d_inner / 8;
       for (int i = hw; i < ((pl.no + 1) & ~1); i += 2 * kWarps) {
@@ -793,7 +812,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
     cta_sync();
     stamp(P, tb + 13);
     if (pl.no > 0) {
-      fetch_t<B>(P, P.tw + (size_t)(par * 2 + 1) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTout), s_t);
+      fetch_t<B>(P, P.tw + (size_t)(par * 2 + 1) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTout), s_t, to_early);
       const __half* sc = reinterpret_cast<const __half*>(st + P.lay.out_scale);
       const __half* la = reinterpret_cast<const __half*>(st + P.lay.out_lA);
       unsigned long long* xw = P.xw + (size_t)(par ^ 1) * B * XW;
