@@ -6,11 +6,11 @@
 // Per layer:
 //   alpha: every CTA rebuilds RMSNorm(x) -> int8 q; 16 "producer" CTAs compute the in_proj
 //          LoRA down-projection t (one rank each) and publish it.
-//          "head" CTAs own half a head (32 channels p of head h): their z/x/dt in_proj rows,
+//          "head" CTAs own half a head (32 channels p of head h): their z/x in_proj rows,
 //          conv1d of their x channels, and their 32x128 slice of the fp32 SSM state.
-//          "BC" CTAs own 8-row groups of the B/C in_proj rows and their conv1d channels and
-//          publish conv'd B/C; head CTAs then run the state update, C.h + D.x and the SiLU(z)
-//          gate and publish the gated vector.
+//          "BC" CTAs own 8-row groups of the B, C and dt in_proj rows (and the conv1d channels
+//          of B/C) and publish conv'd B/C and raw dt; head CTAs then run the state update,
+//          C.h + D.x and the SiLU(z) gate and publish the gated vector.
 //   beta:  every non-producer CTA owns 8-row groups of out_proj: gate-RMSNorm of the full
 //          gated vector, quantisation, LoRA, the 1-bit GEMV and the residual add into x.
 // There is no grid barrier.  Every exchanged value (x, LoRA t, conv'd B/C, gated) travels in
@@ -32,6 +32,7 @@
 // only fp32 summation orders differ.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "engine.h"
@@ -84,7 +85,8 @@ struct PParams {
   unsigned* sync;  // [1] exit count, [3] error, [16] tag epoch base (never cleared by resets)
   // tagged exchange words {data, tag}, each [2 parities][B][...]:
   unsigned long long* xw;   // x as fp16 pairs        [d_model / 2]
-  unsigned long long* bcw;  // conv'd B/C fp16 pairs  [d_state] (B then C)
+  unsigned long long* bcw;  // conv'd B/C then raw dt, fp16 pairs [bcw_per_seq = d_state + nheads / 2]
+  int bcw_per_seq;
   unsigned long long* gw;   // gated fp16 pairs       [d_inner / 2]
   unsigned long long* tw;   // LoRA t fp32, [2 parities][2: in, out][B][16]
   size_t rs;                // words between the replicas of the exchange region
@@ -229,7 +231,6 @@ __device__ __forceinline__ void copy_desc(const PParams& P, const CtaPlan& pl, i
     switch (i) {
       case 0: s_ = inb + (size_t)c0 * RB; d_ = Y.in_bits; n_ = np * RB; break;
       case 1: s_ = inb + (size_t)(P.d_inner + c0) * RB; d_ = Y.in_bits + np * RB; n_ = np * RB; break;
-      case 2: s_ = inb + (size_t)(P.d_inner + P.d_xbc + pl.h) * RB; d_ = Y.in_bits + 2 * np * RB; n_ = RB; break;
       case 3: s_ = L.in.scale + c0; d_ = Y.in_scale; n_ = np * 2; break;
       case 4: s_ = L.in.scale + P.d_inner + c0; d_ = Y.in_scale + np * 2; n_ = np * 2; break;
       case 5: s_ = L.in.A16 + (size_t)c0 * 16; d_ = Y.in_lA; n_ = np * 32; break;
@@ -252,20 +253,22 @@ __device__ __forceinline__ void copy_desc(const PParams& P, const CtaPlan& pl, i
       n_ = np * 4;
     }
   } else if (pl.role == 1) {
+    // rows [bc0, bc0 + nbc) of the B/C/dt block; only the B/C channels have conv1d operands
     const int r0 = 2 * P.d_inner + pl.bc0, c0 = P.d_inner + pl.bc0, nb = pl.nbc;
+    const int nconv = max(0, min(nb, 2 * DFSSM_DSTATE - pl.bc0));
     switch (i) {
       case 0: s_ = inb + (size_t)r0 * RB; d_ = Y.in_bits; n_ = nb * RB; break;
       case 3: s_ = L.in.scale + r0; d_ = Y.in_scale; n_ = nb * 2; break;
       case 5: s_ = L.in.A16 + (size_t)r0 * 16; d_ = Y.in_lA; n_ = nb * 32; break;
-      case 9: s_ = L.conv_w + (size_t)c0 * 4; d_ = Y.conv_w; n_ = nb * 8; break;
-      case 10: s_ = L.conv_b + c0; d_ = Y.conv_b; n_ = nb * 2; break;
+      case 9: s_ = L.conv_w + (size_t)c0 * 4; d_ = Y.conv_w; n_ = nconv * 8; break;
+      case 10: s_ = L.conv_b + c0; d_ = Y.conv_b; n_ = nconv * 2; break;
       default: break;
     }
     const int k = i - 15 - B;
     if (k >= 0 && k < 3 * B) {
       s_ = P.conv + (long long)layer * P.conv_layer + (long long)k * P.d_xbc + c0;
       d_ = Y.cstate + k * nb * 4;
-      n_ = nb * 4;
+      n_ = nconv * 4;
     }
   }
   if (pl.no > 0) {
@@ -506,10 +509,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
   float* s_bc = s_dt + B;                           // [B][2*d_state] (fp32)
   int* s_dot = reinterpret_cast<int*>(s_bc + B * 2 * DFSSM_DSTATE);  // [128][B] GEMV results
   // per-layer tables copied once at kernel start (no dependent global loads inside the loop):
-  // the layer pointer table, and this CTA's head scalars (dt_bias, A_log, D, dt-row scale,
-  // 16 fp16 dt-row LoRA-A values) for every layer
+  // the layer pointer table, and this CTA's head scalars (dt_bias, A_log, D) for every layer
   LayerW* s_layers = reinterpret_cast<LayerW*>(smem + P.tab_off);
-  float* s_hptab = reinterpret_cast<float*>(smem + P.tab_off + ((P.n_layer * (int)sizeof(LayerW) + 15) & ~15));  // [n_layer][12], 16-byte aligned
+  float* s_hptab = reinterpret_cast<float*>(smem + P.tab_off + ((P.n_layer * (int)sizeof(LayerW) + 15) & ~15));  // [n_layer][4], 16-byte aligned
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.ring_off - 8 * 8);      // ring slot full
   uint64_t* empties = reinterpret_cast<uint64_t*>(smem + P.ring_off - 8 * 8 - 8 * 4 * 8);  // [slot][part] released
   unsigned char* ring = smem + P.ring_off;
@@ -536,15 +538,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
     if (pl.role == 0) {
       for (int l = tid; l < P.n_layer; l += kBlockThreads) {
         const LayerW& G = P.layers[l];
-        const int dtrow = d_inner + P.d_xbc + pl.h;
-        float* e = s_hptab + l * 12;
+        float* e = s_hptab + l * 4;
         e[0] = G.dt_bias[pl.h];
         e[1] = G.A_log[pl.h];
         e[2] = G.Dp[pl.h];
-        e[3] = h2f(G.in.scale[dtrow]);
-        const uint4* a16 = reinterpret_cast<const uint4*>(G.in.A16 + (size_t)dtrow * 16);
-        reinterpret_cast<uint4*>(e + 4)[0] = a16[0];
-        reinterpret_cast<uint4*>(e + 4)[1] = a16[1];
       }
     }
   }
@@ -610,7 +607,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
     // the barrier's release does not wait for these 16 KB of stores
     float4 hnew[B][kMaxRPW];
     if (pl.role == 0) {
-      const int np = pl.np, nrows = 2 * np + 1;
+      const int np = pl.np, nrows = 2 * np;  // z and x rows (the dt rows belong to the B/C CTAs)
       const __half* sc = reinterpret_cast<const __half*>(st + P.lay.in_scale);
       const __half* la = reinterpret_cast<const __half*>(st + P.lay.in_lA);
       const __half* cw = reinterpret_cast<const __half*>(st + P.lay.conv_w);
@@ -627,21 +624,20 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       release_part(P, empties, layer, 1);
       fetch_t<B>(P, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTin), s_t, t_early);
       stamp(P, tb + 2);
-      const unsigned long long* bcw_mine = P.bcw + (size_t)par * B * DFSSM_DSTATE + rep_off + (tid < B * DFSSM_DSTATE ? tid : 0);
-      const unsigned long long bc_early = tid < B * DFSSM_DSTATE ? peek_word(bcw_mine) : 0ull;
+      // threads < B * d_state take the B/C words, the next B threads the word holding dt of head h
+      const int bc_b = tid < B * DFSSM_DSTATE ? tid / DFSSM_DSTATE : tid - B * DFSSM_DSTATE;
+      const int bc_j = tid < B * DFSSM_DSTATE ? tid - bc_b * DFSSM_DSTATE : DFSSM_DSTATE + pl.h / 2;
+      const bool bc_taker = tid < B * (DFSSM_DSTATE + 1);
+      const unsigned long long* bcw_mine =
+          P.bcw + ((size_t)par * B + (bc_taker ? bc_b : 0)) * P.bcw_per_seq + rep_off + (bc_taker ? bc_j : 0);
+      const unsigned long long bc_early = bc_taker ? peek_word(bcw_mine) : 0ull;
       for (int e2 = tid; e2 < nrows * B; e2 += kThreads) {
         const int row = e2 / B, b = e2 - row * B;
         const int dot = s_dot[e2];
-        float v;
-        if (row < 2 * np) {
-          v = proj_out(dot, s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
-        } else {
-          const float* hp = s_hptab + layer * 12;
-          v = proj_out(dot, s_xs[b], hp[3], reinterpret_cast<const __half*>(hp + 4), s_t + b * 16);
-        }
+        const float v = proj_out(dot, s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
         if (row < np) {
           s_z[b * 64 + row] = v;
-        } else if (row < 2 * np) {
+        } else {
           const int j = row - np, ch = pl.h * DFSSM_HEADDIM + pl.p0 + j;
           const float s0 = cst[(b * 3 + 0) * np + j], s1 = cst[(b * 3 + 1) * np + j], s2 = cst[(b * 3 + 2) * np + j];
           float* gcs = P.conv + (long long)layer * P.conv_layer + (long long)b * 3 * P.d_xbc + ch;
@@ -649,17 +645,20 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
           gcs[P.d_xbc] = s2;
           gcs[2 * P.d_xbc] = v;
           s_xc[b * 64 + j] = round_hc(conv_silu(s0, s1, s2, v, cw + j * 4, h2f(cb[j])));
-        } else {
-          s_dt[b] = v;
         }
       }
       cta_sync();
       stamp(P, tb + 5);
-      // wait for every B/C CTA of this layer, then fetch conv'd B and C (B * d_state <= 512 words)
-      if (tid < B * DFSSM_DSTATE) {
+      // wait for every B/C CTA of this layer, then fetch conv'd B and C and dt (B * (d_state + 1)
+      // <= 512 words)
+      if (bc_taker) {
         const unsigned v = take_word(bcw_mine, bc_early, tag_of(ebase, layer, kTagBC), P.sync + 3, 4u);
-        s_bc[2 * tid] = lo_h(v);
-        s_bc[2 * tid + 1] = hi_h(v);
+        if (tid < B * DFSSM_DSTATE) {
+          s_bc[2 * tid] = lo_h(v);
+          s_bc[2 * tid + 1] = hi_h(v);
+        } else {
+          s_dt[bc_b] = (pl.h & 1) ? hi_h(v) : lo_h(v);
+        }
       }
       cta_sync();
       stamp(P, tb + 6);
@@ -668,7 +667,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       unsigned long long* gw = P.gw + (size_t)par * B * GW;
       const unsigned tg_g = tag_of(ebase, layer, kTagGated);
       const float* sst = reinterpret_cast<const float*>(st + P.lay.state);
-      const float* hp = s_hptab + layer * 12;
+      const float* hp = s_hptab + layer * 4;
 #pragma unroll
       for (int b = 0; b < B; ++b) {
         float dtv = s_dt[b] + hp[0];
@@ -724,7 +723,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       release_part(P, empties, layer, 1);
       fetch_t<B>(P, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTin), s_t, t_early);
       stamp(P, tb + 2);
-      unsigned long long* bcw = P.bcw + (size_t)par * B * DFSSM_DSTATE;
+      unsigned long long* bcw = P.bcw + (size_t)par * B * P.bcw_per_seq;
       const unsigned tg_bc = tag_of(ebase, layer, kTagBC);
       // one thread per (row, b), e = row * B + b; the partner row of a pair sits B lanes up in
       // the same warp (32 is a multiple of 2B), and the even row's lane publishes the pair
@@ -733,17 +732,21 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
         float o = 0.f;
         if (e2 < nb * B) {
           const float v = proj_out(s_dot[e2], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
-          const int ch = d_inner + pl.bc0 + row;
-          const float s0 = cst[(b * 3 + 0) * nb + row], s1 = cst[(b * 3 + 1) * nb + row], s2 = cst[(b * 3 + 2) * nb + row];
-          float* gcs = P.conv + (long long)layer * P.conv_layer + (long long)b * 3 * P.d_xbc + ch;
-          gcs[0] = s1;
-          gcs[P.d_xbc] = s2;
-          gcs[2 * P.d_xbc] = v;
-          o = conv_silu(s0, s1, s2, v, cw + row * 4, h2f(cb[row]));
+          if (pl.bc0 + row < 2 * DFSSM_DSTATE) {  // B/C channel: conv1d + SiLU
+            const int ch = d_inner + pl.bc0 + row;
+            const float s0 = cst[(b * 3 + 0) * nb + row], s1 = cst[(b * 3 + 1) * nb + row], s2 = cst[(b * 3 + 2) * nb + row];
+            float* gcs = P.conv + (long long)layer * P.conv_layer + (long long)b * 3 * P.d_xbc + ch;
+            gcs[0] = s1;
+            gcs[P.d_xbc] = s2;
+            gcs[2 * P.d_xbc] = v;
+            o = conv_silu(s0, s1, s2, v, cw + row * 4, h2f(cb[row]));
+          } else {  // dt row of head bc0 + row - 2 d_state: raw projection (fp16-exact)
+            o = v;
+          }
         }
         const float o_next = __shfl_down_sync(0xffffffffu, o, B);
         if (e2 < nb * B && (row & 1) == 0)
-          put_word(bcw + (size_t)b * DFSSM_DSTATE + (pl.bc0 + row) / 2, P.rs, pack_h2(o, o_next), tg_bc);
+          put_word(bcw + (size_t)b * P.bcw_per_seq + (pl.bc0 + row) / 2, P.rs, pack_h2(o, o_next), tg_bc);
       }
       cta_sync();
     } else {
@@ -1035,7 +1038,8 @@ int build_plan(const dfssm_engine* e, int B, int grid, std::vector<CtaPlan>& pla
   const int S = 2, np = DFSSM_HEADDIM / S;
   const int n_items = d.nheads * S;
   n_bc = grid - n_items;
-  const int bc_groups = 2 * d.d_state / 8;
+  if (d.d_state != DFSSM_DSTATE || d.nheads % 8) return 0;
+  const int bc_groups = (2 * d.d_state + d.nheads) / 8;  // 8-row groups of the B, C and dt rows
   if (n_bc < 1) return 0;
   if (n_bc > bc_groups) n_bc = bc_groups;
   plans.assign(grid, CtaPlan{});
@@ -1083,14 +1087,16 @@ int build_plan(const dfssm_engine* e, int B, int grid, std::vector<CtaPlan>& pla
   for (CtaPlan& p : plans) {
     long long tx = 0;
     if (p.role == 0)
-      tx += (long long)(2 * p.np + 1) * RB + 2 * p.np * (2 + 32) + p.np * 8 + p.np * 2 +
+      tx += (long long)(2 * p.np) * RB + 2 * p.np * (2 + 32) + p.np * 8 + p.np * 2 +
             (long long)B * p.np * DFSSM_DSTATE * 4 + 3LL * B * p.np * 4;
-    else if (p.role == 1)
-      tx += (long long)p.nbc * RB + p.nbc * (2 + 32) + p.nbc * 8 + p.nbc * 2 + 3LL * B * p.nbc * 4;
+    else if (p.role == 1) {
+      const int nconv = std::max(0, std::min(p.nbc, 2 * d.d_state - p.bc0));
+      tx += (long long)p.nbc * RB + p.nbc * (2 + 32) + nconv * 8 + nconv * 2 + 3LL * B * nconv * 4;
+    }
     if (p.no > 0) tx += (long long)p.no * RBO + p.no * (2 + 32);
     p.tx = (int)tx;
   }
-  const int rows_in = (2 * np + 1) > max_nbc ? (2 * np + 1) : max_nbc;
+  const int rows_in = 2 * np > max_nbc ? 2 * np : max_nbc;
   const int ch = np > max_nbc ? np : max_nbc;
   auto a16 = [](int x) { return (x + 15) & ~15; };
   int off = 0;
@@ -1111,7 +1117,7 @@ int build_plan(const dfssm_engine* e, int B, int grid, std::vector<CtaPlan>& pla
   int work = B * d.d_model * 2 + B * d.d_inner + misc_floats * 4;
   work = (work + 127) & ~127;
   tab_off = work;
-  work += ((d.n_layer * (int)sizeof(LayerW) + 15) & ~15) + d.n_layer * 12 * 4;
+  work += ((d.n_layer * (int)sizeof(LayerW) + 15) & ~15) + d.n_layer * 4 * 4;
   work = (work + 127) & ~127;
   const int ring_off = work + 384;  // 8 full + 8 x 4 released mbarriers live just below the ring
   int max_smem = 0;
@@ -1183,7 +1189,8 @@ int persistent_init(dfssm_engine* e) {
     P.xw = e->xch;
     P.rs = persistent_xch_words(d);
     P.bcw = P.xw + 2 * 2 * d.d_model / 2;
-    P.gw = P.bcw + 2 * 2 * d.d_state;
+    P.bcw_per_seq = d.d_state + d.nheads / 2;
+    P.gw = P.bcw + 2 * 2 * P.bcw_per_seq;
     P.tw = P.gw + 2 * 2 * d.d_inner / 2;
     P.gated_g = e->gated;
     P.logits = e->logits;
@@ -1209,7 +1216,8 @@ int persistent_init(dfssm_engine* e) {
 }
 
 size_t persistent_xch_words(const dfssm_dims& d) {
-  return (size_t)2 * 2 * (d.d_model / 2) + 2 * 2 * d.d_state + 2 * 2 * (d.d_inner / 2) + 2 * 2 * 2 * DFSSM_RANK;
+  return (size_t)2 * 2 * (d.d_model / 2) + 2 * 2 * (d.d_state + d.nheads / 2) + 2 * 2 * (d.d_inner / 2) +
+         2 * 2 * 2 * DFSSM_RANK;
 }
 size_t persistent_xch_bytes(const dfssm_dims& d) { return 8 * persistent_xch_words(d) * kReplicas; }
 
