@@ -427,9 +427,43 @@ __device__ void copy_issuer(const PParams& P, const CtaPlan& pl, unsigned char* 
   const int nl = P.l1 - P.l0;
   const unsigned tx = (unsigned)pl.tx;
   const unsigned b1 = tx / kParts, b2 = 2 * tx / kParts, b3 = 3 * tx / kParts;  // first bytes of parts 1..3
-  for (int k = 0; k < nl; ++k) {
+  const int RC = P.lay.stage_bytes / P.d_model;                 // embedding rows per head chunk
+  const int nch = P.do_head ? (pl.nv + RC - 1) / RC : 0;
+  for (int k = 0; k < nl + nch; ++k) {
     const int layer = P.l0 + k, slot = k % P.ns;
     unsigned char* st = ring + (size_t)slot * P.lay.stage_bytes;
+    if (k >= nl) {  // LM head chunk: rows [r0, r0 + nr) of this CTA's vocabulary slice
+      if (k >= P.ns) {
+        int ok = 1;
+        if (lane == 0) {
+          const unsigned parity = (unsigned)((k / P.ns - 1) & 1);
+          for (int part = 0; part < kParts && ok; ++part) {
+            unsigned it = 0;
+            while (!mbar_try_wait(empty + slot * kParts + part, parity)) {
+              if ((++it & 1023u) == 0 && ld_acquire(P.sync + 3) != 0) {
+                ok = 0;
+                break;
+              }
+              if (it > kSpinLimit) {
+                atomicOr(P.sync + 3, 32u);
+                ok = 0;
+                break;
+              }
+            }
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+      }
+      const int r0 = pl.v0 + (k - nl) * RC, nr = min(RC, pl.v0 + pl.nv - r0);
+      const unsigned bytes = (unsigned)nr * (unsigned)P.d_model;
+      if (lane == 0) mbar_expect_tx(full + slot, bytes);
+      __syncwarp();
+      const char* src = reinterpret_cast<const char*>(P.Eq) + (size_t)r0 * P.d_model;
+      for (unsigned off = lane * kCopyPiece; off < bytes; off += 32 * kCopyPiece)
+        bulk_g2s(st + off, src + off, min(kCopyPiece, bytes - off), full + slot);
+      __syncwarp();
+      continue;
+    }
     const void* src;
     int dst;
     unsigned n;
@@ -842,12 +876,17 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
   }
 
   // ---------------- final norm + LM head + argmax
+  // The copy warp streams this CTA's embedding rows through the ring as items nl, nl + 1, ...
+  // (RC rows each) once the compute threads release the slots, as it does for layers.
   stamp(P, 2 + kTracePerLayer * P.n_layer);
+  const int nl = P.l1 - P.l0;
+  if (tid == 0)  // the last layer's slot is free now
+    for (int j = 0; j < kParts; ++j) mbar_arrive(empties + ((nl - 1) % P.ns) * kParts + j);
   if (P.do_head) {
     take_x<B, KI>(P.xw + rep_off + (size_t)(P.l1 & 1) * B * XW, B * XW, tag_of(ebase, P.l1, kTagX), s_x, P.sync + 3);
     stamp(P, 3 + kTracePerLayer * P.n_layer);
-    float* s_no = reinterpret_cast<float*>(ring);  // [B][d_model] fp32 normalised x (ring is idle now)
     {
+      // normalised x, fp16-exact, written back over x in s_x (each thread rewrites its own columns)
       float vals[B][KI];
       float ss[B];
 #pragma unroll
@@ -867,7 +906,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
 #pragma unroll
         for (int j = 0; j < KI; ++j) {
           const int k = tid * KI + j;
-          s_no[b * d_model + k] = round_h(__fmul_rn(__fmul_rn(vals[b][j], r), P.norm_f[k]));
+          s_x[b * d_model + k] = f2h(__fmul_rn(__fmul_rn(vals[b][j], r), P.norm_f[k]));
         }
       }
     }
@@ -875,42 +914,35 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
     unsigned long long mybest[B];
 #pragma unroll
     for (int b = 0; b < B; ++b) mybest[b] = 0ull;
-    // Each warp takes 2 rows per iteration; with d_model = 512*KI a row is 32*KI 16-byte chunks,
-    // KI per lane, and all 2*KI loads are issued before any arithmetic.
+    // A warp takes whole rows of a chunk; with d_model = 512*KI a row is 32*KI 16-byte units,
+    // KI per lane.  Batch 1 keeps this lane's KI*16 activations in registers for all rows.
     constexpr int CPL = KI;
-    const int C = d_model >> 4;
-    const int vend = pl.v0 + pl.nv;
-    // batch 1: this lane's KI*16 normalised activations stay in registers for all rows
+    const int RC = P.lay.stage_bytes / d_model, nch = (pl.nv + RC - 1) / RC;
     float xr[B == 1 ? KI : 1][16];
     if (B == 1) {
 #pragma unroll
       for (int u = 0; u < (B == 1 ? KI : 1); ++u)
 #pragma unroll
-        for (int q = 0; q < 16; ++q) xr[u][q] = s_no[(lane + 32 * u) * 16 + q];
+        for (int q = 0; q < 16; ++q) xr[u][q] = h2f(s_x[(lane + 32 * u) * 16 + q]);
     }
-    for (int v = pl.v0 + 2 * wid; v < vend; v += 2 * kWarps) {
-      uint4 ev[2][CPL];
+    for (int c = 0; c < nch; ++c) {
+      const int item = nl + c;
+      wait_stage(P, bars, P.l0 + item);
+      const unsigned char* st = ring + (size_t)(item % P.ns) * P.lay.stage_bytes;
+      const int r0 = pl.v0 + c * RC, nr = min(RC, pl.v0 + pl.nv - r0);
+      for (int r = wid; r < nr; r += kWarps) {
+        const uint4* er = reinterpret_cast<const uint4*>(st + (size_t)r * d_model);
+        uint4 ev[B == 1 ? CPL : 1];  // batch 1: all units up front; batch 2: one at a time (registers)
+        if (B == 1)
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int vr = v + r < vend ? v + r : v;
-        const uint4* er = reinterpret_cast<const uint4*>(P.Eq + (size_t)vr * d_model);
-#pragma unroll
-        for (int u = 0; u < CPL; ++u) {
-          const int c = lane + 32 * u;
-          ev[r][u] = c < C ? ldg_stream(er + c) : make_uint4(0, 0, 0, 0);
-        }
-      }
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
+          for (int u = 0; u < CPL; ++u) ev[B == 1 ? u : 0] = er[lane + 32 * u];
         float acc[B];
 #pragma unroll
         for (int b = 0; b < B; ++b) acc[b] = 0.f;
 #pragma unroll
         for (int u = 0; u < CPL; ++u) {
-          const int c = lane + 32 * u;
-          if (c >= C) continue;
-          const unsigned w4[4] = {ev[r][u].x ^ 0x80808080u, ev[r][u].y ^ 0x80808080u, ev[r][u].z ^ 0x80808080u,
-                                  ev[r][u].w ^ 0x80808080u};
+          const uint4 e4 = B == 1 ? ev[B == 1 ? u : 0] : er[lane + 32 * u];
+          const unsigned w4[4] = {e4.x ^ 0x80808080u, e4.y ^ 0x80808080u, e4.z ^ 0x80808080u, e4.w ^ 0x80808080u};
           if (B == 1) {
             float a = acc[0];
 #pragma unroll
@@ -924,22 +956,21 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
           } else {
 #pragma unroll
             for (int b = 0; b < B; ++b) {
-              const float4* xv = reinterpret_cast<const float4*>(s_no + b * d_model + c * 16);
+              const __half2* xv = reinterpret_cast<const __half2*>(s_x + b * d_model + (lane + 32 * u) * 16);
               float a = acc[b];
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
-                const float4 xx = xv[q];
-                a = fmaf(i8_to_f(w4[q], 0), xx.x, a);
-                a = fmaf(i8_to_f(w4[q], 1), xx.y, a);
-                a = fmaf(i8_to_f(w4[q], 2), xx.z, a);
-                a = fmaf(i8_to_f(w4[q], 3), xx.w, a);
+                const float2 x01 = __half22float2(xv[2 * q]), x23 = __half22float2(xv[2 * q + 1]);
+                a = fmaf(i8_to_f(w4[q], 0), x01.x, a);
+                a = fmaf(i8_to_f(w4[q], 1), x01.y, a);
+                a = fmaf(i8_to_f(w4[q], 2), x23.x, a);
+                a = fmaf(i8_to_f(w4[q], 3), x23.y, a);
               }
               acc[b] = a;
             }
           }
         }
-        const int vr = v + r;
-        if (vr >= vend) break;
+        const int vr = r0 + r;
         const float sv = P.Es[vr];
 #pragma unroll
         for (int b = 0; b < B; ++b) {
@@ -951,6 +982,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
           }
         }
       }
+      cta_sync();  // every warp is done with the chunk: release its slot
+      if (tid == 0)
+        for (int j = 0; j < kParts; ++j) mbar_arrive(empties + (item % P.ns) * kParts + j);
     }
     unsigned long long* sb = reinterpret_cast<unsigned long long*>(red);
     cta_sync();
@@ -969,9 +1003,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
   // drain: no bulk copy into this CTA's ring may still be in flight when it exits (only
   // possible after a timed-out wait); bounded, ignores the error word
   if (tid == 0) {
-    const int nl = P.l1 - P.l0;
-    for (int s = 0; s < P.ns && s < nl; ++s) {
-      const int last = s + ((nl - 1 - s) / P.ns) * P.ns;
+    const int RC = P.lay.stage_bytes / d_model;
+    const int ni = nl + (P.do_head ? (pl.nv + RC - 1) / RC : 0);  // ring items: layers, then head chunks
+    for (int s = 0; s < P.ns && s < ni; ++s) {
+      const int last = s + ((ni - 1 - s) / P.ns) * P.ns;
       unsigned it = 0;
       while (!mbar_try_wait(bars + s, (unsigned)((last / P.ns) & 1)) && ++it < kSpinLimit) {
       }
