@@ -335,10 +335,33 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
   const uint4* pa = reinterpret_cast<const uint4*>(p.bits + (size_t)ra * W);
   const uint4* pb = reinterpret_cast<const uint4*>(p.bits + (size_t)rb * W);
   __shared__ uint64_t qbar;
+  // The first pass's activation copies and weight words go out before anything else, so their
+  // round trips overlap the staging of the epilogue operands.
+  auto issue_q = [&](int bt0, int nb) {
+    if (wid == 0) {
+      if (lane == 0) mbar_expect_tx(&qbar, (unsigned)(nb * K));
+      __syncwarp();
+      for (int b = lane; b < nb; b += 32) bulk_g2s(sq + b * SQ, q + (size_t)(bt0 + b) * K, (unsigned)K, &qbar);
+    }
+  };
+  // this warp's weight words for the whole K slice (wpw <= 4 * kMmaMaxBlk words)
+  uint4 wva[kMmaMaxBlk], wvb[kMmaMaxBlk];
+  auto load_w = [&]() {
+#pragma unroll
+    for (int u = 0; u < kMmaMaxBlk; ++u) {
+      if (4 * u < wpw) {
+        wva[u] = ldg_stream(pa + (kw0 >> 2) + u);
+        wvb[u] = ldg_stream(pb + (kw0 >> 2) + u);
+      }
+    }
+  };
   if (threadIdx.x == 0) {
     mbar_init(&qbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  __syncwarp();
+  issue_q(0, min(NB, B));
+  load_w();
   if (MODE != 2) {  // per-row epilogue operands (independent of the batch pass)
     constexpr int NF = DFSSM_RANK + 6, U = (R * NF + kMmaThreads - 1) / kMmaThreads;
     float v[U];
@@ -371,12 +394,8 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
     const int nb = min(NB, B - bt0);
     __syncthreads();  // previous pass done with sq and the epilogue operands
     // activation rows -> shared memory by TMA bulk copies (rows >= nb keep stale bytes; their
-    // output columns are never stored)
-    if (wid == 0) {
-      if (lane == 0) mbar_expect_tx(&qbar, (unsigned)(nb * K));
-      __syncwarp();
-      for (int b = lane; b < nb; b += 32) bulk_g2s(sq + b * SQ, q + (size_t)(bt0 + b) * K, (unsigned)K, &qbar);
-    }
+    // output columns are never stored); the first pass's went out at kernel entry
+    if (bt0 > 0) issue_q(bt0, nb);
     // per-batch epilogue operands
     {
       constexpr int NF = DFSSM_RANK + 2, U = (NB * NF + kMmaThreads - 1) / kMmaThreads;
@@ -434,16 +453,7 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
 #pragma unroll
       for (int u = 0; u < U; ++u) e_cs[threadIdx.x + u * kMmaThreads] = v[u];
     }
-    // this warp's weight words for the whole K slice, loaded before waiting for the activations
-    // (wpw <= 4 * kMmaMaxBlk words; one round trip instead of one per 4 words)
-    uint4 wva[kMmaMaxBlk], wvb[kMmaMaxBlk];
-#pragma unroll
-    for (int u = 0; u < kMmaMaxBlk; ++u) {
-      if (4 * u < wpw) {
-        wva[u] = ldg_stream(pa + (kw0 >> 2) + u);
-        wvb[u] = ldg_stream(pb + (kw0 >> 2) + u);
-      }
-    }
+    if (bt0 > 0) load_w();
     mbar_wait_bounded(&qbar, phase);
     int acc[kMmaNT][4];
 #pragma unroll
