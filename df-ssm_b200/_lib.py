@@ -33,6 +33,9 @@ SIGNATURES = {
     "dfssm_step_host": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "dfssm_check_finite": (c_int, [c_void_p, c_void_p]),
     "dfssm_selftest_division": (c_int, [c_int, c_void_p]),
+    "dfssm_sample": (c_int, [c_void_p, c_int, c_int, c_void_p, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                             ctypes.c_uint64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "dfssm_set_sampling": (c_int, [c_void_p, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_uint64]),
     "dfssm_state_ptrs": (c_int, [c_void_p, c_int, POINTER(c_void_p), POINTER(c_void_p)]),
     "dfssm_get_buffer": (c_int, [c_void_p, c_char_p, POINTER(c_void_p), POINTER(c_size_t)]),
     "dfssm_layer_step": (c_int, [c_void_p, c_int, c_void_p]),

@@ -14,6 +14,7 @@
 
 #include "engine.h"
 #include "kernels.cuh"
+#include "sample.cuh"
 
 using namespace dfssm;
 
@@ -507,6 +508,9 @@ int build_engine(const unsigned char* img, size_t n, int device, int max_batch, 
   // tagged exchange words of the persistent kernel: x, B/C, gated and LoRA t for 2 layer
   // parities x 2 sequences
   const size_t o_xch = take(persistent_xch_bytes(d));
+  const int seen_words = (d.vocab + 31) / 32;
+  const size_t o_seen = take((size_t)B * seen_words * 4);
+  const size_t o_ctr = take((size_t)B * 8);
   const size_t o_layers = take(sizeof(LayerW) * d.n_layer);
   if (cudaMalloc(&e->work, off) != cudaSuccess)
     return cleanup(dfssm_fail(DFSSM_ERR_OOM, "cudaMalloc(%zu) for state/activations failed", off));
@@ -527,6 +531,9 @@ int build_engine(const unsigned char* img, size_t n, int device, int max_batch, 
   e->tokens = reinterpret_cast<int*>(W + o_tok);
   e->sync = reinterpret_cast<unsigned int*>(W + o_sync);
   e->xch = reinterpret_cast<unsigned long long*>(W + o_xch);
+  e->seen = reinterpret_cast<uint32_t*>(W + o_seen);
+  e->seen_words = seen_words;
+  e->counters = reinterpret_cast<unsigned long long*>(W + o_ctr);
   e->d_layers = reinterpret_cast<LayerW*>(W + o_layers);
   ce = cudaMemset(e->work, 0, off);
   if (ce != cudaSuccess) return cleanup(dfssm_fail(DFSSM_ERR_CUDA, "state clear: %s", cudaGetErrorString(ce)));
@@ -643,6 +650,8 @@ int dfssm_reset(dfssm_engine* e, void* stream) {
   CU(cudaMemsetAsync(e->conv, 0, e->conv_layer * e->d.n_layer * 4, us));
   CU(cudaMemsetAsync(e->best, 0, (size_t)e->max_batch * 8, us));
   CU(cudaMemsetAsync(e->sync, 0, 32, us));
+  CU(cudaMemsetAsync(e->seen, 0, (size_t)e->max_batch * e->seen_words * 4, us));
+  CU(cudaMemsetAsync(e->counters, 0, (size_t)e->max_batch * 8, us));
   return DFSSM_OK;
 }
 
@@ -657,6 +666,8 @@ int dfssm_reset_slots(dfssm_engine* e, int first, int count, void* stream) {
     CU(cudaMemsetAsync(e->ssm + (size_t)l * e->ssm_layer + (size_t)first * hseq, 0, (size_t)count * hseq * 4, us));
     CU(cudaMemsetAsync(e->conv + (size_t)l * e->conv_layer + (size_t)first * cseq, 0, (size_t)count * cseq * 4, us));
   }
+  CU(cudaMemsetAsync(e->seen + (size_t)first * e->seen_words, 0, (size_t)count * e->seen_words * 4, us));
+  CU(cudaMemsetAsync(e->counters + first, 0, (size_t)count * 8, us));
   return DFSSM_OK;
 }
 
@@ -672,6 +683,11 @@ int dfssm_step(dfssm_engine* e, const int32_t* tokens_dev, float* logits_dev, in
   CU(cudaStreamWaitEvent(e->s, e->ev_in, 0));
   if (tokens_dev)
     CU(cudaMemcpyAsync(e->tokens, tokens_dev, (size_t)e->batch * 4, cudaMemcpyDeviceToDevice, e->s));
+  const bool sampling = e->s_temp > 0.f;
+  if (sampling) {  // the input tokens join each sequence's seen set before the penalty applies
+    mark_seen_kernel<<<(e->batch + 127) / 128, 128, 0, e->s>>>(e->tokens, e->batch, e->d.vocab, e->seen, e->seen_words);
+    CHECK_LAUNCH();
+  }
   int rc;
   if (mode == 2) {
     if ((rc = enqueue_step(e, 1, e->s))) return rc;
@@ -681,6 +697,10 @@ int dfssm_step(dfssm_engine* e, const int32_t* tokens_dev, float* logits_dev, in
     if ((rc = ensure_graph(e, mode))) return rc;
     CU(cudaGraphLaunch(e->gexec, e->s));
   }
+  if (sampling &&
+      (rc = dfssm_sample(e->logits, e->batch, e->d.vocab, e->seen, e->s_temp, e->s_top_p, e->s_rep, e->s_seed,
+                         reinterpret_cast<uint64_t*>(e->counters), e->tokens, nullptr, nullptr, e->s)))
+    return rc;
   if (logits_dev)
     CU(cudaMemcpyAsync(logits_dev, e->logits, (size_t)e->batch * e->d.vocab * 4, cudaMemcpyDeviceToDevice, e->s));
   if (next_tokens_dev)
@@ -962,5 +982,41 @@ int dfssm_selftest_division(int device, unsigned long long* mismatch) {
   if (ce == cudaSuccess) ce = cudaMemcpy(mismatch, d, 16, cudaMemcpyDeviceToHost);
   cudaFree(d);
   if (ce != cudaSuccess) return dfssm_fail(DFSSM_ERR_CUDA, "division self-test: %s", cudaGetErrorString(ce));
+  return DFSSM_OK;
+}
+
+// ------------------------------------------------------------------ sampling epilogue
+
+int dfssm_sample(const float* logits, int batch, int vocab, uint32_t* seen_bits, float temperature, float top_p,
+                 float rep_penalty, uint64_t seed, uint64_t* counters, int32_t* next, float* kept_mass,
+                 int32_t* kept_count, void* stream) {
+  if (!logits || !seen_bits || !counters || !next) return dfssm_fail(DFSSM_ERR_ARG, "NULL argument");
+  if (batch < 1 || vocab < 1) return dfssm_fail(DFSSM_ERR_ARG, "batch %d vocab %d", batch, vocab);
+  if (!(temperature > 0.f) || !(rep_penalty > 0.f) || !(top_p >= 0.f))
+    return dfssm_fail(DFSSM_ERR_ARG, "temperature and rep_penalty must be > 0, top_p >= 0");
+  const size_t sm = (size_t)vocab * 4;
+  int dev = 0, max_sm = 0;
+  CU(cudaGetDevice(&dev));
+  CU(cudaDeviceGetAttribute(&max_sm, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+  if (sm + 1024 > (size_t)max_sm)
+    return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "vocab %d needs %zu bytes of shared memory (max %d)", vocab, sm, max_sm);
+  CU(cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  sample_kernel<<<batch, kSampleThreads, sm, static_cast<cudaStream_t>(stream)>>>(
+      logits, vocab, seen_bits, (vocab + 31) / 32, temperature, top_p, rep_penalty,
+      (unsigned long long)seed, reinterpret_cast<unsigned long long*>(counters), next, kept_mass, kept_count);
+  CHECK_LAUNCH();
+  return DFSSM_OK;
+}
+
+int dfssm_set_sampling(dfssm_engine* e, float temperature, float top_p, float rep_penalty, uint64_t seed) {
+  if (!e) return dfssm_fail(DFSSM_ERR_ARG, "NULL engine");
+  if (temperature > 0.f && (!(rep_penalty > 0.f) || !(top_p >= 0.f)))
+    return dfssm_fail(DFSSM_ERR_ARG, "rep_penalty must be > 0 and top_p >= 0");
+  if (temperature > 0.f && (size_t)e->d.vocab * 4 + 1024 > 232448)
+    return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "vocab %d too large for the sampling epilogue", e->d.vocab);
+  e->s_temp = temperature > 0.f ? temperature : 0.f;
+  e->s_top_p = top_p;
+  e->s_rep = rep_penalty;
+  e->s_seed = seed;
   return DFSSM_OK;
 }

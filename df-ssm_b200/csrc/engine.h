@@ -37,6 +37,12 @@ struct dfssm_engine {
   int* tokens = nullptr;
   unsigned int* sync = nullptr;  // persistent-kernel words: exit count, error, tag epoch
   unsigned long long* xch = nullptr;  // persistent-kernel tagged exchange words
+  // sampling epilogue (dfssm_set_sampling); temperature <= 0 = greedy argmax
+  float s_temp = 0.f, s_top_p = 1.f, s_rep = 1.f;
+  unsigned long long s_seed = 0;
+  uint32_t* seen = nullptr;               // [max_batch][seen_words] tokens already in each sequence
+  int seen_words = 0;
+  unsigned long long* counters = nullptr;  // [max_batch] draws so far
   // execution
   cudaStream_t s = nullptr;
   cudaEvent_t ev_in = nullptr, ev_out = nullptr;

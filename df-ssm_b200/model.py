@@ -157,11 +157,22 @@ class DFSSMModel:
             nxt = self.step(prompt[:, t], logits=False)
         return nxt
 
-    def generate(self, n_tokens: int = 128, prompt=None, verbose: bool = True, logits: bool = False):
-        """Greedy decode: reset, consume `prompt` ([B, T]; token 0 if None), then n_tokens steps.
-        Returns int32 tokens [B, n_tokens] (host numpy)."""
+    def set_sampling(self, temperature: float = 0.0, top_p: float = 1.0, rep_penalty: float = 1.0, seed: int = 0):
+        """Token choice of later steps: greedy argmax for temperature <= 0 (the default, as the
+        reference DFSSMModel.generate), else the sampling of eval/gen_test.py:54-95 (temperature,
+        repetition penalty over the tokens already in each sequence, top-p nucleus, multinomial),
+        on the device.  Draws are reproducible for a seed after reset_state()."""
+        _lib.check(self.lib.dfssm_set_sampling(self._h, float(temperature), float(top_p), float(rep_penalty),
+                                               int(seed) & (2**64 - 1)))
+
+    def generate(self, n_tokens: int = 128, prompt=None, verbose: bool = True, logits: bool = False,
+                 temperature: float = 0.0, top_p: float = 0.9, rep_penalty: float = 1.2, seed: int = 0):
+        """Decode: reset, consume `prompt` ([B, T]; token 0 if None), then n_tokens steps.  Greedy
+        by default; temperature > 0 samples as eval/gen_test.py's generate() (defaults 0.7 / 0.9 /
+        1.2 there).  Returns int32 tokens [B, n_tokens] (host numpy)."""
         torch = self.torch
         B = self.batch_size
+        self.set_sampling(temperature, top_p, rep_penalty, seed)
         self.reset_state()
         if prompt is None:
             prompt = torch.zeros(B, 1, dtype=torch.int64)
@@ -205,8 +216,13 @@ def main(argv: Optional[Sequence[str]] = None):
     p.add_argument("--batch_size", type=int, default=1)
     p.add_argument("--n_tokens", type=int, default=128)
     p.add_argument("--mode", default="auto", choices=list(DFSSMModel.MODES))
+    p.add_argument("--temperature", type=float, default=0.0, help="> 0 samples (eval/gen_test.py); 0 = greedy")
+    p.add_argument("--top_p", type=float, default=0.9)
+    p.add_argument("--rep_penalty", type=float, default=1.2)
+    p.add_argument("--seed", type=int, default=0)
     a = p.parse_args(argv)
-    DFSSMModel(a.model, batch_size=a.batch_size, mode=a.mode).generate(n_tokens=a.n_tokens)
+    DFSSMModel(a.model, batch_size=a.batch_size, mode=a.mode).generate(
+        n_tokens=a.n_tokens, temperature=a.temperature, top_p=a.top_p, rep_penalty=a.rep_penalty, seed=a.seed)
 
 
 if __name__ == "__main__":

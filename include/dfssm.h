@@ -167,6 +167,25 @@ size_t dfssm_lm_head_workspace(int batch);
 int dfssm_lm_head_argmax(const int8_t* E_q, const float* E_s, int vocab, int d, const void* x_f16,
                          int batch, float* logits, int32_t* next, void* workspace, void* stream);
 
+/* Sampling epilogue (eval/gen_test.py:54-95, the reference's generate(): temperature,
+ * repetition penalty, top-p nucleus, multinomial draw), one draw per row:
+ *   l = logits / temperature;  l[v] /= rep_penalty for every v set in the row's seen bitmap;
+ *   p = softmax(l);  kept = the top-p nucleus (in descending p, a token is kept while the mass
+ *   ranked before it is <= top_p; tokens tied at the boundary are all kept);  next = a draw
+ *   from p restricted to kept, u from splitmix64(seed, row, counters[row]), counters[row]++.
+ * logits fp32 [batch][vocab]; seen_bits uint32 [batch][ceil(vocab/32)] (bit v%32 of word v/32;
+ * read only); counters uint64 [batch]; next int32 [batch]; kept_mass (fraction of the
+ * probability mass kept) and kept_count float/int32 [batch] may be NULL.  vocab * 4 bytes must
+ * fit in one CTA's shared memory (vocab <= 57,000).  temperature and rep_penalty > 0. */
+int dfssm_sample(const float* logits, int batch, int vocab, uint32_t* seen_bits, float temperature, float top_p,
+                 float rep_penalty, uint64_t seed, uint64_t* counters, int32_t* next, float* kept_mass,
+                 int32_t* kept_count, void* stream);
+/* Switch the engine's token choice from greedy argmax to dfssm_sample (temperature <= 0 switches
+ * back).  The engine keeps each sequence's seen bitmap (every token fed to dfssm_step, prompt
+ * included, as the reference's ids) and draw counter; dfssm_reset / dfssm_reset_slots clear them.
+ * The returned logits stay the raw fp32 logits. */
+int dfssm_set_sampling(dfssm_engine* e, float temperature, float top_p, float rep_penalty, uint64_t seed);
+
 /* Self-test (no counterpart in the reference): checks, on device `device`, the kernels'
  * two-FMA division (common.cuh div_rn_rcp, used by the activation quantiser) against IEEE fp32
  * division for every pair of finite fp16 operands with a positive divisor.  Writes the number

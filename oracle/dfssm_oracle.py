@@ -27,6 +27,7 @@ following the same points can be compared tightly:
   residual      df_ssm_inference.py:207       x = fp16(x + out)
   head          df_ssm_inference.py:210,224,236  final rms_norm, logits = fp16(norm_out.E^T),
                                                greedy argmax (first index on ties)
+  sampling      eval/gen_test.py:54-95         temperature, repetition penalty, top-p nucleus
 
 Options select the documented deviations of the B200 engine from the literal
 reference: ``state_dtype`` ("f16" is the reference, "f32" the engine contract) and
@@ -135,6 +136,24 @@ def gate(y16: np.ndarray, z16: np.ndarray) -> np.ndarray:
         sig = (F32(1.0) / (F32(1.0) + np.exp(-zf, dtype=F32))).astype(F16)
     silu_z = (zf * sig.astype(F32)).astype(F16)
     return (y16.astype(F32) * silu_z.astype(F32)).astype(F16)
+
+
+def sample_nucleus(logits: np.ndarray, seen: np.ndarray, temperature: float, top_p: float, rep_penalty: float):
+    """The token-choice rule of the reference's generate() (eval/gen_test.py:69-87) for one row:
+    logits / T (:69), seen tokens' logits / rep_penalty (:71-72), softmax (:74), descending sort,
+    cumsum, drop tokens whose preceding mass exceeds top_p (:75-78), renormalise (:79-82).
+    Returns (kept token ids in descending-probability order, softmax probabilities, kept mass).
+    The draw itself (torch.multinomial, :84) is random; tests check its distribution."""
+    l = logits.astype(np.float32) / np.float32(temperature)
+    l = l.copy()
+    l[seen] = l[seen] / np.float32(rep_penalty)
+    e = np.exp((l - l.max()).astype(np.float64))
+    p = e / e.sum()
+    order = np.argsort(-p, kind="stable")
+    sp = p[order]
+    cs = np.cumsum(sp)
+    keep = (cs - sp) <= top_p
+    return order[keep], p, float(sp[keep].sum())
 
 
 def argmax_first(v: np.ndarray) -> np.ndarray:

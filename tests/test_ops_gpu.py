@@ -133,3 +133,76 @@ def test_quantiser_division_matches_ieee(lib):
     out = (ctypes.c_ulonglong * 2)()
     assert lib.dfssm_selftest_division(0, out) == 0, lib.dfssm_last_error()
     assert (out[0], out[1]) == (0, 0)
+
+
+# ---------------------------------------------------------------- sampling epilogue
+
+def _sample(lib, logits, seen_mask, T, top_p, rep, seed=0, counters=None):
+    import torch
+    B, V = logits.shape
+    W = (V + 31) // 32
+    bits = np.zeros((B, W), np.uint32)
+    for b, v in zip(*np.nonzero(seen_mask)):
+        bits[b, v >> 5] |= np.uint32(1 << (v & 31))
+    dev = "cuda"
+    tl = torch.from_numpy(logits.astype(np.float32)).to(dev)
+    tb = torch.from_numpy(bits.view(np.int32)).to(dev)
+    ctr = counters if counters is not None else torch.zeros(B, dtype=torch.int64, device=dev)
+    nxt = torch.empty(B, dtype=torch.int32, device=dev)
+    mass = torch.empty(B, dtype=torch.float32, device=dev)
+    cnt = torch.empty(B, dtype=torch.int32, device=dev)
+    _lib.check(lib.dfssm_sample(ptr(tl), B, V, ptr(tb), T, top_p, rep, seed, ptr(ctr), ptr(nxt), ptr(mass),
+                                ptr(cnt), stream()))
+    torch.cuda.synchronize()
+    return nxt.cpu().numpy(), mass.cpu().numpy(), cnt.cpu().numpy()
+
+
+@pytest.mark.parametrize("top_p", [0.0, 0.3, 0.9, 1.0])
+def test_sampling_nucleus_matches_reference_rule(lib, top_p):
+    """Kept set (count, mass) and the drawn token against the sort-based rule of
+    eval/gen_test.py:69-87 restated in the oracle; random logits have distinct probabilities."""
+    rng = np.random.default_rng(1)
+    B, V = 4, 3001
+    logits = (rng.standard_normal((B, V)) * 3).astype(np.float32)
+    seen = rng.random((B, V)) < 0.1
+    for seed in range(3):
+        nxt, mass, cnt = _sample(lib, logits, seen, 0.7, top_p, 1.2, seed=seed)
+        for b in range(B):
+            kept, p, kmass = O.sample_nucleus(logits[b], seen[b], 0.7, top_p, 1.2)
+            # the boundary token may flip only if its preceding mass is within fp32 summation error
+            assert abs(int(cnt[b]) - len(kept)) <= 1, (b, cnt[b], len(kept))
+            assert abs(float(mass[b]) - kmass) < 2e-4 + (p[kept[-1]] if abs(int(cnt[b]) - len(kept)) else 0)
+            extended = set(kept.tolist()) | set(np.argsort(-p, kind="stable")[:len(kept) + 1].tolist())
+            assert int(nxt[b]) in extended
+
+
+def test_sampling_top_p_zero_is_penalised_argmax(lib):
+    """top_p = 0 keeps only the most likely token; the repetition penalty divides the logit of a
+    seen token whatever its sign (eval/gen_test.py:71-72), so a seen token with a negative logit
+    becomes the most likely one when the others are more negative."""
+    logits = np.full((2, 500), -8.0, np.float32)
+    logits[0, 17] = -1.0          # unseen, best
+    logits[1, 17] = -1.0
+    logits[1, 42] = -2.0          # seen in row 1: -2 / 4 = -0.5 beats -1
+    seen = np.zeros((2, 500), bool)
+    seen[1, 42] = True
+    nxt, mass, cnt = _sample(lib, logits, seen, 1.0, 0.0, 4.0)
+    assert nxt.tolist() == [17, 42] and cnt.tolist() == [1, 1]
+
+
+def test_sampling_distribution_matches_softmax(lib):
+    """2000 draws (the per-row counter advances each call) follow the softmax within 5 sigma."""
+    import torch
+    logits = np.array([[1.0, 0.5, 0.0, -0.5, -1.0, 2.0]], np.float32)
+    seen = np.zeros_like(logits, bool)
+    ctr = torch.zeros(1, dtype=torch.int64, device="cuda")
+    n = 2000
+    counts = np.zeros(6)
+    for _ in range(n):
+        nxt, _, _ = _sample(lib, logits, seen, 1.0, 1.0, 1.0, seed=7, counters=ctr)
+        counts[nxt[0]] += 1
+    assert int(ctr.item()) == n
+    p = np.exp(logits[0] - logits[0].max())
+    p /= p.sum()
+    sigma = np.sqrt(n * p * (1 - p))
+    assert np.all(np.abs(counts - n * p) < 5 * sigma), (counts, n * p)
