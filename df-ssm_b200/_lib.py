@@ -36,6 +36,7 @@ SIGNATURES = {
     "dfssm_sample": (c_int, [c_void_p, c_int, c_int, c_void_p, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                              ctypes.c_uint64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "dfssm_set_sampling": (c_int, [c_void_p, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_uint64]),
+    "dfssm_prefill": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "dfssm_state_ptrs": (c_int, [c_void_p, c_int, POINTER(c_void_p), POINTER(c_void_p)]),
     "dfssm_get_buffer": (c_int, [c_void_p, c_char_p, POINTER(c_void_p), POINTER(c_size_t)]),
     "dfssm_layer_step": (c_int, [c_void_p, c_int, c_void_p]),

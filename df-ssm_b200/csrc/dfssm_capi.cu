@@ -15,6 +15,7 @@
 #include "engine.h"
 #include "kernels.cuh"
 #include "sample.cuh"
+#include "prefill.cuh"
 
 using namespace dfssm;
 
@@ -74,14 +75,24 @@ struct Group {
   int b0, nb;
 };
 
+// Outputs of the quantising prologue for a set of activation rows (row r at offset r).
+struct RowBufs {
+  __half* xn;
+  int8_t* q;
+  __half* xs;
+  int* qsum;
+  __half* t;
+};
+RowBufs engine_rows(dfssm_engine* e) { return RowBufs{e->xn, e->q, e->xs, e->qsum, e->t}; }
+
 int launch_prep(dfssm_engine* e, const __half* in, int K, const float* w, int quant, const ProjW* p,
-                cudaStream_t s, Group G) {
+                cudaStream_t s, Group G, const RowBufs& R) {
   if (quant && p && K % 512 == 0) {
     const int kpt = K / 512;
 #define DFSSM_PREP_FAST(n)                                                                                  \
   if (kpt == n) {                                                                                          \
-    act_prep_fast_kernel<n><<<G.nb, kPrepFastThreads, 0, s>>>(in + (size_t)G.b0 * K, K, w, e->q + (size_t)G.b0 * K, \
-                                                              e->xs + G.b0, e->qsum + G.b0, p->B16, e->t + G.b0 * kRank); \
+    act_prep_fast_kernel<n><<<G.nb, kPrepFastThreads, 0, s>>>(in + (size_t)G.b0 * K, K, w, R.q + (size_t)G.b0 * K, \
+                                                              R.xs + G.b0, R.qsum + G.b0, p->B16, R.t + G.b0 * kRank); \
     CHECK_LAUNCH();                                                                                        \
     return DFSSM_OK;                                                                                       \
   }
@@ -92,9 +103,9 @@ int launch_prep(dfssm_engine* e, const __half* in, int K, const float* w, int qu
 #undef DFSSM_PREP_FAST
   }
   const size_t sm = (size_t)K * sizeof(__half);
-  act_prep_kernel<<<G.nb, kPrepThreads, sm, s>>>(in + (size_t)G.b0 * K, K, w, quant, e->xn + (size_t)G.b0 * K,
-                                                 e->q + (size_t)G.b0 * K, e->xs + G.b0, e->qsum + G.b0,
-                                                 p ? p->B16 : nullptr, e->t + G.b0 * kRank);
+  act_prep_kernel<<<G.nb, kPrepThreads, sm, s>>>(in + (size_t)G.b0 * K, K, w, quant, R.xn + (size_t)G.b0 * K,
+                                                 R.q + (size_t)G.b0 * K, R.xs + G.b0, R.qsum + G.b0,
+                                                 p ? p->B16 : nullptr, R.t + G.b0 * kRank);
   CHECK_LAUNCH();
   return DFSSM_OK;
 }
@@ -157,7 +168,7 @@ int enqueue_layer(dfssm_engine* e, int l, cudaStream_t s, Group G) {
   const int B = G.nb, b0 = G.b0;
   const size_t hd = (size_t)d.nheads * DFSSM_HEADDIM * DFSSM_DSTATE;
   int rc;
-  if ((rc = launch_prep(e, e->x, d.d_model, L.ln_w, 1, &L.in, s, G))) return rc;
+  if ((rc = launch_prep(e, e->x, d.d_model, L.ln_w, 1, &L.in, s, G, engine_rows(e)))) return rc;
   if ((rc = launch_gemv<0>(e, L.in, B, e->q + (size_t)b0 * d.d_model, e->qsum + b0, e->xs + b0, e->t + b0 * kRank,
                            e->proj + (size_t)b0 * d.n_in, d.n_in,
                            e->conv + (size_t)l * e->conv_layer + (size_t)b0 * 3 * d.d_xbc, &L, s)))
@@ -168,7 +179,7 @@ int enqueue_layer(dfssm_engine* e, int l, cudaStream_t s, Group G) {
       L.dt_bias, L.A_log, L.Dp, e->ssm + (size_t)l * e->ssm_layer + (size_t)b0 * hd,
       e->gated + (size_t)b0 * d.d_inner, d.d_inner);
   CHECK_LAUNCH();
-  if ((rc = launch_prep(e, e->gated, d.d_inner, L.norm_w, 1, &L.out, s, G))) return rc;
+  if ((rc = launch_prep(e, e->gated, d.d_inner, L.norm_w, 1, &L.out, s, G, engine_rows(e)))) return rc;
   if ((rc = launch_gemv<1>(e, L.out, B, e->q + (size_t)b0 * d.d_inner, e->qsum + b0, e->xs + b0, e->t + b0 * kRank,
                            e->x + (size_t)b0 * d.d_model, d.d_model, nullptr, nullptr, s)))
     return rc;
@@ -191,7 +202,7 @@ int step_groups(const dfssm_engine* e) {
 int enqueue_head(dfssm_engine* e, cudaStream_t s) {
   const dfssm_dims& d = e->d;
   int rc;
-  if ((rc = launch_prep(e, e->x, d.d_model, e->norm_f, 0, nullptr, s, Group{0, e->batch}))) return rc;
+  if ((rc = launch_prep(e, e->x, d.d_model, e->norm_f, 0, nullptr, s, Group{0, e->batch}, engine_rows(e)))) return rc;
   if (e->batch >= kMmaMinBatch && d.d_model % 64 == 0) {
     const size_t sm = lm_head_mma_smem(d.d_model);
     CU(cudaFuncSetAttribute(lm_head_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
@@ -610,6 +621,7 @@ void dfssm_destroy(dfssm_engine* e) {
   persistent_destroy(e);
   if (e->arena) cudaFree(e->arena);
   if (e->work) cudaFree(e->work);
+  if (e->pf) cudaFree(e->pf);
   delete e;
 }
 
@@ -1018,5 +1030,140 @@ int dfssm_set_sampling(dfssm_engine* e, float temperature, float top_p, float re
   e->s_top_p = top_p;
   e->s_rep = rep_penalty;
   e->s_seed = seed;
+  return DFSSM_OK;
+}
+
+// ------------------------------------------------------------------ prompt prefill
+
+namespace {
+
+struct PrefillBufs {
+  __half *x, *xn, *xs, *t, *proj, *gated;
+  int8_t* q;
+  int* qsum;
+  int* tok;
+};
+
+int prefill_bufs(dfssm_engine* e, int rows, PrefillBufs& P) {
+  const dfssm_dims& d = e->d;
+  const size_t kmax = d.d_inner > d.d_model ? d.d_inner : d.d_model;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  const size_t ox = take((size_t)rows * d.d_model * 2), oxn = take((size_t)rows * kmax * 2),
+               oq = take((size_t)rows * kmax), oxs = take((size_t)rows * 2), oqs = take((size_t)rows * 4),
+               ot = take((size_t)rows * kRank * 2), op = take((size_t)rows * d.n_in * 2),
+               og = take((size_t)rows * d.d_inner * 2), otk = take((size_t)rows * 4);
+  if (off > e->pf_bytes) {
+    if (e->pf) CU(cudaFree(e->pf));
+    e->pf = nullptr;
+    e->pf_bytes = 0;
+    if (cudaMalloc(&e->pf, off) != cudaSuccess)
+      return dfssm_fail(DFSSM_ERR_OOM, "cudaMalloc(%zu) for prefill rows failed", off);
+    e->pf_bytes = off;
+  }
+  char* W = e->pf;
+  P = PrefillBufs{reinterpret_cast<__half*>(W + ox), reinterpret_cast<__half*>(W + oxn), reinterpret_cast<__half*>(W + oxs),
+                  reinterpret_cast<__half*>(W + ot), reinterpret_cast<__half*>(W + op), reinterpret_cast<__half*>(W + og),
+                  reinterpret_cast<int8_t*>(W + oq), reinterpret_cast<int*>(W + oqs), reinterpret_cast<int*>(W + otk)};
+  return DFSSM_OK;
+}
+
+// All layers over the B x T prompt rows of one chunk; the state carries over from the previous chunk.
+int prefill_chunk(dfssm_engine* e, const PrefillBufs& P, int T, cudaStream_t s) {
+  const dfssm_dims& d = e->d;
+  const int B = e->batch, R = B * T;
+  const RowBufs rb{P.xn, P.q, P.xs, P.qsum, P.t};
+  embed_rows_kernel<<<R, 256, 0, s>>>(P.tok, e->Eq, e->Es, d.d_model, d.vocab, P.x);
+  CHECK_LAUNCH();
+  const size_t sm = prefill_scan_smem(T, d.d_state);
+  CU(cudaFuncSetAttribute(prefill_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  int rc;
+  for (int l = 0; l < d.n_layer; ++l) {
+    const LayerW& L = e->layers[l];
+    if ((rc = launch_prep(e, P.x, d.d_model, L.ln_w, 1, &L.in, s, Group{0, R}, rb))) return rc;
+    if ((rc = launch_mma<3>(L.in, R, P.q, P.qsum, P.xs, P.t, P.proj, d.n_in, nullptr, nullptr, nullptr, d.d_inner,
+                            d.d_xbc, s)))
+      return rc;
+    prefill_scan_kernel<<<dim3(d.nheads, B), kScanThreads, sm, s>>>(
+        P.proj, d.n_in, T, d.d_inner, d.d_state, d.nheads, L.conv_w, L.conv_b, L.dt_bias, L.A_log, L.Dp,
+        e->conv + (size_t)l * e->conv_layer, e->ssm + (size_t)l * e->ssm_layer, P.gated);
+    CHECK_LAUNCH();
+    if ((rc = launch_prep(e, P.gated, d.d_inner, L.norm_w, 1, &L.out, s, Group{0, R}, rb))) return rc;
+    if ((rc = launch_mma<1>(L.out, R, P.q, P.qsum, P.xs, P.t, P.x, d.d_model, nullptr, nullptr, nullptr, d.d_inner,
+                            d.d_xbc, s)))
+      return rc;
+  }
+  return DFSSM_OK;
+}
+
+}  // namespace
+
+int dfssm_prefill(dfssm_engine* e, const int32_t* tokens_dev, int T, float* logits_dev, int32_t* next_tokens_dev,
+                  void* stream) {
+  if (!e || !tokens_dev) return dfssm_fail(DFSSM_ERR_ARG, "NULL argument");
+  if (T < 1) return dfssm_fail(DFSSM_ERR_ARG, "prompt length %d", T);
+  CU(cudaSetDevice(e->device));
+  cudaStream_t us = static_cast<cudaStream_t>(stream);
+  const dfssm_dims& d = e->d;
+  const int B = e->batch;
+  const int Tc = T < kScanMaxT ? T : kScanMaxT;
+  const bool batched = B * (T < Tc ? T : Tc) >= kMmaMinBatch && mma_rg(d.n_in, d.d_model) && mma_rg(d.d_model, d.d_inner) &&
+                       prefill_scan_smem(Tc, d.d_state) <= 227 * 1024;
+  if (!batched) {  // too few rows for the batched kernels: token by token through dfssm_step
+    for (int t = 0; t < T; ++t) {
+      CU(cudaMemcpy2DAsync(e->tokens, 4, tokens_dev + t, (size_t)T * 4, 4, B, cudaMemcpyDeviceToDevice, us));
+      int rc = dfssm_step(e, nullptr, t == T - 1 ? logits_dev : nullptr, t == T - 1 ? next_tokens_dev : nullptr, stream);
+      if (rc) return rc;
+    }
+    return DFSSM_OK;
+  }
+  PrefillBufs P;
+  int rc;
+  if ((rc = prefill_bufs(e, B * Tc, P))) return rc;
+  CU(cudaEventRecord(e->ev_in, us));
+  CU(cudaStreamWaitEvent(e->s, e->ev_in, 0));
+  for (int t0 = 0; t0 < T; t0 += Tc) {
+    const int tc = T - t0 < Tc ? T - t0 : Tc;
+    if (B * tc < kMmaMinBatch) {  // a short tail chunk: token by token
+      for (int t = t0; t < T; ++t) {
+        CU(cudaMemcpy2DAsync(e->tokens, 4, tokens_dev + t, (size_t)T * 4, 4, B, cudaMemcpyDeviceToDevice, e->s));
+        CU(cudaEventRecord(e->ev_out, e->s));
+        CU(cudaStreamWaitEvent(us, e->ev_out, 0));
+        if ((rc = dfssm_step(e, nullptr, t == T - 1 ? logits_dev : nullptr, t == T - 1 ? next_tokens_dev : nullptr,
+                             stream)))
+          return rc;
+        CU(cudaEventRecord(e->ev_in, us));
+        CU(cudaStreamWaitEvent(e->s, e->ev_in, 0));
+      }
+      CU(cudaEventRecord(e->ev_out, e->s));
+      CU(cudaStreamWaitEvent(us, e->ev_out, 0));
+      return DFSSM_OK;
+    }
+    CU(cudaMemcpy2DAsync(P.tok, (size_t)tc * 4, tokens_dev + t0, (size_t)T * 4, (size_t)tc * 4, B,
+                         cudaMemcpyDeviceToDevice, e->s));
+    if (e->s_temp > 0.f) {
+      mark_seen_rows_kernel<<<(B * tc + 127) / 128, 128, 0, e->s>>>(P.tok, B, tc, d.vocab, e->seen, e->seen_words);
+      CHECK_LAUNCH();
+    }
+    if ((rc = prefill_chunk(e, P, tc, e->s))) return rc;
+    if (t0 + tc == T) {  // the last token of every sequence: final norm, LM head, next token
+      last_rows_kernel<<<B, 256, 0, e->s>>>(P.x, tc, d.d_model, e->x);
+      CHECK_LAUNCH();
+      if ((rc = enqueue_head(e, e->s))) return rc;
+      if (e->s_temp > 0.f &&
+          (rc = dfssm_sample(e->logits, B, d.vocab, e->seen, e->s_temp, e->s_top_p, e->s_rep, e->s_seed,
+                             reinterpret_cast<uint64_t*>(e->counters), e->tokens, nullptr, nullptr, e->s)))
+        return rc;
+    }
+  }
+  if (logits_dev)
+    CU(cudaMemcpyAsync(logits_dev, e->logits, (size_t)B * d.vocab * 4, cudaMemcpyDeviceToDevice, e->s));
+  if (next_tokens_dev) CU(cudaMemcpyAsync(next_tokens_dev, e->tokens, (size_t)B * 4, cudaMemcpyDeviceToDevice, e->s));
+  CU(cudaEventRecord(e->ev_out, e->s));
+  CU(cudaStreamWaitEvent(us, e->ev_out, 0));
   return DFSSM_OK;
 }

@@ -43,6 +43,9 @@ struct dfssm_engine {
   uint32_t* seen = nullptr;               // [max_batch][seen_words] tokens already in each sequence
   int seen_words = 0;
   unsigned long long* counters = nullptr;  // [max_batch] draws so far
+  // prompt prefill rows (dfssm_prefill), grown on demand
+  char* pf = nullptr;
+  size_t pf_bytes = 0;
   // execution
   cudaStream_t s = nullptr;
   cudaEvent_t ev_in = nullptr, ev_out = nullptr;

@@ -287,6 +287,8 @@ proj_gemv_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ 
 // sum_k s_k q_k = 2 * sum_{bit=1} q_k - sum_k q_k as in proj_gemv; the K slices of a CTA's warps
 // are added exactly in int32 through shared memory before the shared epilogue.
 // Activation rows sit in shared memory with a stride of K + 16 bytes (bank-conflict-free B loads).
+// MODE 0: in_proj epilogue with the conv1d step; 1: out_proj with the residual add; 2: raw int32
+// accumulators; 3: dequantised projection only (prompt rows, whose conv runs in the prefill scan).
 // ---------------------------------------------------------------------------------------
 constexpr int kMmaThreads = 256;
 constexpr int kMmaNT = 4;  // batch tiles of 8 per pass (32 rows)
@@ -524,6 +526,8 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
           res = o2 * sig;
         }
         out[(size_t)b * ld_out + row] = f2h(res);
+      } else if (MODE == 3) {  // plain projection (the prefill scan applies the conv over time)
+        out[(size_t)b * ld_out + row] = f2h(v);
       } else {
         out[(size_t)b * ld_out + row] = f2h(e_cs[bb * R + lr] + v);
       }

@@ -147,15 +147,24 @@ class DFSSMModel:
 
     __call__ = forward
 
-    def prefill(self, prompt) -> "object":
-        """Feed prompt tokens [B, T] one at a time; returns the greedy token after the prompt."""
-        prompt = self.torch.as_tensor(prompt)
+    def prefill(self, prompt, chunked: bool = True, logits: bool = False) -> "object":
+        """Consume prompt tokens [B, T] (dfssm_prefill: batched projections and a per-head scan
+        over time; chunked=False feeds them one step at a time); returns the token chosen after
+        the prompt (device int32 [B]) and fills self.logits if `logits`."""
+        torch = self.torch
+        prompt = torch.as_tensor(prompt)
         if prompt.dim() == 1:
             prompt = prompt.reshape(self.batch_size, -1)
-        nxt = None
-        for t in range(prompt.shape[1]):
-            nxt = self.step(prompt[:, t], logits=False)
-        return nxt
+        if not chunked:
+            nxt = None
+            for t in range(prompt.shape[1]):
+                nxt = self.step(prompt[:, t], logits=logits)
+            return nxt
+        tok = prompt.to(device=self.device, dtype=torch.int32).contiguous()
+        lg = ctypes.c_void_p(self.logits.data_ptr()) if logits else None
+        _lib.check(self.lib.dfssm_prefill(self._h, ctypes.c_void_p(tok.data_ptr()), int(tok.shape[1]), lg,
+                                          ctypes.c_void_p(self._tok_out.data_ptr()), self._stream()))
+        return self._tok_out[: self.batch_size]
 
     def set_sampling(self, temperature: float = 0.0, top_p: float = 1.0, rep_penalty: float = 1.0, seed: int = 0):
         """Token choice of later steps: greedy argmax for temperature <= 0 (the default, as the

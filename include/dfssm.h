@@ -167,6 +167,19 @@ size_t dfssm_lm_head_workspace(int batch);
 int dfssm_lm_head_argmax(const int8_t* E_q, const float* E_s, int vocab, int d, const void* x_f16,
                          int batch, float* logits, int32_t* next, void* workspace, void* stream);
 
+/* Prompt prefill (replaces feeding a prompt token by token through DFSSMModel.forward,
+ * df_ssm_inference.py:219-231): tokens_dev int32 [batch][T] are consumed in order, as T calls of
+ * dfssm_step would, and the logits / next token after the last one are returned (either may be
+ * NULL).  The projections of all batch x T token rows run as batched GEMMs and each head runs its
+ * conv1d and state recurrence over the T tokens with the state in registers (chunks of 64
+ * tokens), so a layer's state is read and written once per chunk.  Per token the arithmetic
+ * follows the decode kernels; fp32 summation orders of the LoRA down-projection differ from the
+ * batch-1 decode prologue.  Fewer than 8 rows per chunk run token by token.  Device memory for
+ * the prompt rows is allocated on first use (not capturable); the state continues into
+ * dfssm_step. */
+int dfssm_prefill(dfssm_engine* e, const int32_t* tokens_dev, int T, float* logits_dev, int32_t* next_tokens_dev,
+                  void* stream);
+
 /* Sampling epilogue (eval/gen_test.py:54-95, the reference's generate(): temperature,
  * repetition penalty, top-p nucleus, multinomial draw), one draw per row:
  *   l = logits / temperature;  l[v] /= rep_penalty for every v set in the row's seen bitmap;

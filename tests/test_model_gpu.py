@@ -263,3 +263,29 @@ def test_engine_sampling_is_reproducible_and_greedy_unchanged(mode):
     assert (a != c).any() and (a != greedy).any()
     assert ((a >= 0) & (a < w.dims.vocab)).all()
     np.testing.assert_array_equal(m.generate(10, prompt=p, verbose=False), greedy)
+
+
+@pytest.mark.parametrize("B,T,mode", [(2, 12, "graph"), (2, 70, "persistent"), (1, 4, "graph"), (9, 3, "graph")])
+def test_prefill_matches_token_by_token(B, T, mode):
+    """dfssm_prefill (batched projections + per-head scan over the prompt, 64-token chunks) leaves
+    the same state and next token as feeding the prompt one dfssm_step at a time, within the
+    fp32-summation-order tolerance of the LoRA down-projection; short prompts fall back to steps."""
+    w = weights("small", 2, seed=4)
+    p = np.random.default_rng(5).integers(0, w.dims.vocab, (B, T))
+    a, b = model(w, B, mode=mode), model(w, B, mode=mode)
+    a.reset_state()
+    b.reset_state()
+    ta = a.prefill(p, chunked=True, logits=True).cpu().numpy()
+    tb = b.prefill(p, chunked=False, logits=True).cpu().numpy()
+    la, lb = a.logits[:B].cpu().numpy(), b.logits[:B].cpu().numpy()
+    np.testing.assert_allclose(la, lb, atol=2e-2 * float(np.abs(lb).max()))
+    np.testing.assert_array_equal(ta, tb)
+    for l in range(w.dims.n_layer):
+        ha, hb = a.h_states[l][:B].cpu().numpy(), b.h_states[l][:B].cpu().numpy()
+        assert np.abs(ha - hb).max() <= 2e-3 * np.abs(hb).max() + 1e-6, l
+        ca, cb = a.conv_states[l][:B].cpu().numpy(), b.conv_states[l][:B].cpu().numpy()
+        assert np.abs(ca - cb).max() <= 2e-3 * np.abs(cb).max() + 1e-6, l
+    # decoding continues from the prefilled state
+    na = [a.step(None, logits=False).cpu().numpy() for _ in range(3)]
+    nb = [b.step(None, logits=False).cpu().numpy() for _ in range(3)]
+    np.testing.assert_array_equal(np.array(na), np.array(nb))
