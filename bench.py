@@ -60,6 +60,32 @@ def step_bytes(d, batch: int) -> dict:
     return dict(weights=weights, embedding=emb, state=batch * state_seq, total=weights + emb + batch * state_seq)
 
 
+def rank_batch(cfg: dict, world: int) -> tuple:
+    """(sequences per rank, sequences of the whole job): weak scaling keeps the config's batch per
+    rank, strong scaling splits the config's batch over the ranks."""
+    if cfg["scaling"] == "weak":
+        return cfg["batch"], cfg["batch"] * world
+    if cfg["batch"] % world:
+        raise SystemExit(f"batch {cfg['batch']} not divisible by {world} ranks")
+    return cfg["batch"] // world, cfg["batch"]
+
+
+def rank_rows(rank: int, per_rank: int) -> slice:
+    """This rank's contiguous slice of the job's sequences (no data-path collective needed)."""
+    return slice(rank * per_rank, (rank + 1) * per_rank)
+
+
+def max_over_ranks(value: float, world: int, device) -> float:
+    """Max of a per-rank timing over all ranks (all_reduce MAX on the process group's backend)."""
+    if world <= 1:
+        return float(value)
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -161,7 +187,7 @@ def run_reference_arm(args, cfg, rank, world):
     if rank != 0:
         return
     # the whole job's sequences: per-GPU batch x ranks (weak scaling) or the global batch (strong)
-    batch = cfg["batch"] * world if cfg["scaling"] == "weak" else cfg["batch"]
+    batch = rank_batch(cfg, world)[1]
     threads = physical_threads()
     res = cpu_reference_run(cfg, args.steps, args.warmup, threads, batch)
     if "unavailable" in res:
@@ -290,17 +316,11 @@ def main():
     from dfssm_b200 import synthetic
     from dfssm_b200.model import DFSSMModel
 
-    if cfg["scaling"] == "weak":
-        batch = cfg["batch"]
-    else:
-        if cfg["batch"] % world:
-            raise SystemExit(f"batch {cfg['batch']} not divisible by {world} ranks")
-        batch = cfg["batch"] // world
+    batch, job_batch = rank_batch(cfg, world)
     dims = synthetic.make_dims(cfg["shape"], cfg["layers"])
     w = synthetic.make_weights(dims, seed=0)
-    prompts = synthetic.make_prompts(dims.vocab, cfg["batch"] if cfg["scaling"] == "strong" else batch * world,
-                                     PROMPT_LEN, seed=0)
-    my_prompts = prompts[rank * batch:(rank + 1) * batch]
+    prompts = synthetic.make_prompts(dims.vocab, job_batch, PROMPT_LEN, seed=0)
+    my_prompts = prompts[rank_rows(rank, batch)]
     m = DFSSMModel(w, device=f"cuda:{local}", batch_size=batch, mode=args.mode)
     del w
     stream = torch.cuda.current_stream()
@@ -332,11 +352,7 @@ def main():
     e1.record(stream)
     barrier()
     clk = clocks.stop()
-    ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = max_over_ranks(e0.elapsed_time(e1), world, torch.device("cuda", local))
 
     # ---------------- end-to-end through the public host-buffer API (tokens in/out via pinned host memory)
     tok_h = torch.empty(batch, dtype=torch.int32).pin_memory().numpy()
@@ -349,10 +365,7 @@ def main():
         tok_h[:] = nxt_h
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
-    te = torch.tensor([e2e_s], device="cuda")
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_s = float(te.item())
+    e2e_s = max_over_ranks(e2e_s, world, torch.device("cuda", local))
     m.check_finite()
 
     tokens_total = batch * world * args.steps
