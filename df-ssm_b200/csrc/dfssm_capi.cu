@@ -91,7 +91,7 @@ int launch_prep(dfssm_engine* e, const __half* in, int K, const float* w, int qu
     const int kpt = K / 512;
 #define DFSSM_PREP_FAST(n)                                                                                  \
   if (kpt == n) {                                                                                          \
-    act_prep_fast_kernel<n><<<G.nb, kPrepFastThreads, 0, s>>>(in + (size_t)G.b0 * K, K, w, R.q + (size_t)G.b0 * K, \
+    act_prep_fast_kernel<n><<<dim3(G.nb, 2), kPrepFastThreads, 0, s>>>(in + (size_t)G.b0 * K, K, w, R.q + (size_t)G.b0 * K, \
                                                               R.xs + G.b0, R.qsum + G.b0, p->B16, R.t + G.b0 * kRank); \
     CHECK_LAUNCH();                                                                                        \
     return DFSSM_OK;                                                                                       \

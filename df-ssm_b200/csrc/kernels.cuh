@@ -107,32 +107,41 @@ act_prep_kernel(const __half* __restrict__ in, int K, const float* __restrict__ 
 
 // act_prep_fast: the same prologue as act_prep_kernel (quantising variant) for K = 512 * KPT,
 // with 512 threads that each keep KPT columns and their LoRA-B slices in registers and one
-// combined block reduction for the 16 LoRA partials and the q sum.
+// combined block reduction for the LoRA partials and the q sum.  Grid (rows, 2): CTA (b, p)
+// computes ranks 8p..8p+7 of row b's LoRA down-projection (halving each CTA's LoRA-B stream);
+// both compute the identical q, xs and qsum, which CTA p = 0 stores.
 template <int KPT>
 __global__ void __launch_bounds__(kPrepFastThreads)
 act_prep_fast_kernel(const __half* __restrict__ in, int K, const float* __restrict__ w, int8_t* __restrict__ q_out,
                      __half* __restrict__ xs_out, int* __restrict__ qsum_out, const __half* __restrict__ B16,
                      __half* __restrict__ t_out) {
-  __shared__ float red[(kPrepFastWarps + 1) * (DFSSM_RANK + 1)];
-  __shared__ float s_t[DFSSM_RANK];
+  constexpr int NR = DFSSM_RANK / 2;
+  __shared__ float red[(kPrepFastWarps + 1) * (NR + 1)];
+  __shared__ float s_t[NR];
   __shared__ float s_xs[1];
   __shared__ int s_qsum[1];
-  const int b = blockIdx.x, k0 = threadIdx.x * KPT;
+  __shared__ __align__(16) int8_t s_q[KPT * kPrepFastThreads];
+  const int b = blockIdx.x, part = blockIdx.y, k0 = threadIdx.x * KPT;
   float wv[KPT];
   float vals[1][KPT];
-  typename RankHalves<KPT>::T lb[DFSSM_RANK];
-  load_lora_b<KPT>(B16, K, lb);
+  typename RankHalves<KPT>::T lb[NR];
+  load_lora_b_ranks<KPT, NR>(B16, K, part * NR, lb);
   const __half* xr = in + (size_t)b * K + k0;
 #pragma unroll
   for (int j = 0; j < KPT; ++j) {
     wv[j] = __ldg(w + k0 + j);
     vals[0][j] = h2f(xr[j]);
   }
-  prep_rows<1, KPT, false>(vals, wv, K, lb, q_out + (size_t)b * K, K, s_xs, s_qsum, s_t, red);
-  if (threadIdx.x < DFSSM_RANK) t_out[b * DFSSM_RANK + threadIdx.x] = f2h(s_t[threadIdx.x]);
-  if (threadIdx.x == 0) {
-    xs_out[b] = f2h(s_xs[0]);
-    qsum_out[b] = s_qsum[0];
+  prep_rows<1, KPT, false, NR>(vals, wv, K, lb, s_q, K, s_xs, s_qsum, s_t, red);
+  if (threadIdx.x < NR) t_out[b * DFSSM_RANK + part * NR + threadIdx.x] = f2h(s_t[threadIdx.x]);
+  if (part == 0) {
+    int4* dst = reinterpret_cast<int4*>(q_out + (size_t)b * K);
+    const int4* src = reinterpret_cast<const int4*>(s_q);
+    for (int i = threadIdx.x; i < K / 16; i += kPrepFastThreads) dst[i] = src[i];
+    if (threadIdx.x == 0) {
+      xs_out[b] = f2h(s_xs[0]);
+      qsum_out[b] = s_qsum[0];
+    }
   }
 }
 

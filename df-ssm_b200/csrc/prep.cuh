@@ -129,6 +129,15 @@ __device__ __forceinline__ void load_lora_b(const __half* B16, int K, typename R
 #pragma unroll
   for (int r = 0; r < DFSSM_RANK; ++r) out[r] = __ldg(reinterpret_cast<const T*>(B16 + (size_t)r * K + k0));
 }
+// NR rank rows starting at r0.
+template <int KPT, int NR>
+__device__ __forceinline__ void load_lora_b_ranks(const __half* B16, int K, int r0,
+                                                  typename RankHalves<KPT>::T (&out)[NR]) {
+  using T = typename RankHalves<KPT>::T;
+  const int k0 = threadIdx.x * KPT;
+#pragma unroll
+  for (int r = 0; r < NR; ++r) out[r] = __ldg(reinterpret_cast<const T*>(B16 + (size_t)(r0 + r) * K + k0));
+}
 
 template <int KPT>
 __device__ __forceinline__ float half_of(const typename RankHalves<KPT>::T& v, int j) {
@@ -148,10 +157,11 @@ __device__ __forceinline__ int qswz(int p) {
 // B activation rows.  vals[b][j]: fp16-exact inputs of columns k0 + j.  Writes q (permuted) to
 // sq[b][*] and xs/qsum/t to smem; returns after a cta_sync.
 // SWZ: store q in the swizzled shared-memory order of the persistent kernel (qswz) instead of
-// the plain permuted order read by the per-op GEMV kernels.
-template <int B, int KPT, bool SWZ = true>
+// the plain permuted order read by the per-op GEMV kernels.  NR: LoRA ranks computed here (lb
+// holds NR consecutive rank rows; s_t receives [B][NR]).
+template <int B, int KPT, bool SWZ = true, int NR = DFSSM_RANK>
 __device__ void prep_rows(float (&vals)[B][KPT], const float (&w)[KPT], int K,
-                          const typename RankHalves<KPT>::T (&lb)[DFSSM_RANK], int8_t* sq, int Kq,
+                          const typename RankHalves<KPT>::T (&lb)[NR], int8_t* sq, int Kq,
                           float* s_xs, int* s_qsum, float* s_t, float* red) {
   const int k0 = threadIdx.x * KPT;
   float ss[B];
@@ -177,7 +187,7 @@ __device__ void prep_rows(float (&vals)[B][KPT], const float (&w)[KPT], int K,
     am[b] = a;
   }
   block_max_n<B>(am, red);
-  float all[B * DFSSM_RANK + B];  // LoRA partials t[b][r] = sum_j xn_j * q_rj, then the q sums
+  float all[B * NR + B];  // LoRA partials t[b][r] = sum_j xn_j * q_rj, then the q sums
 #pragma unroll
   for (int b = 0; b < B; ++b) {
     const float s = round_h(__fmul_rn(fmaxf(am[b], qscale_floor()), 1.0f / 127.0f));
@@ -190,19 +200,19 @@ __device__ void prep_rows(float (&vals)[B][KPT], const float (&w)[KPT], int K,
       sq[b * Kq + (SWZ ? qswz(qperm_index(k0 + j)) : qperm_index(k0 + j))] = (int8_t)q;
       qsum += q;
     }
-    all[B * DFSSM_RANK + b] = (float)qsum;
+    all[B * NR + b] = (float)qsum;
     if (threadIdx.x == 0) s_xs[b] = s;
 #pragma unroll
-    for (int r = 0; r < DFSSM_RANK; ++r) {
+    for (int r = 0; r < NR; ++r) {
       float a = 0.f;
 #pragma unroll
       for (int j = 0; j < KPT; ++j) a = fmaf(vals[b][j], half_of<KPT>(lb[r], j), a);
-      all[b * DFSSM_RANK + r] = a;
+      all[b * NR + r] = a;
     }
   }
-  const float tot = block_sum_scatter<B * DFSSM_RANK + B>(all, red);
-  if (threadIdx.x < B * DFSSM_RANK) s_t[threadIdx.x] = round_h(tot);
-  else if (threadIdx.x < B * DFSSM_RANK + B) s_qsum[threadIdx.x - B * DFSSM_RANK] = (int)tot;
+  const float tot = block_sum_scatter<B * NR + B>(all, red);
+  if (threadIdx.x < B * NR) s_t[threadIdx.x] = round_h(tot);
+  else if (threadIdx.x < B * NR + B) s_qsum[threadIdx.x - B * NR] = (int)tot;
   cta_sync();
 }
 
