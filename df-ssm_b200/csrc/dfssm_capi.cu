@@ -16,6 +16,7 @@
 #include "kernels.cuh"
 #include "sample.cuh"
 #include "prefill.cuh"
+#include "umma.cuh"
 
 using namespace dfssm;
 
@@ -129,10 +130,40 @@ inline int mma_rg(int N, int K) {
   return mma_ok(K, pref) ? pref : (mma_ok(K, other) ? other : 0);
 }
 
+// error word of the tcgen05 projection (a wait that ran out); read by dfssm_check_finite
+__device__ unsigned g_umma_err;
+
+// Split-K scratch of the tcgen05 projection: int32 partial sums [rows][N] and one counter per
+// output tile, all zero between uses (the kernel clears what it used).
+struct UmmaScratch {
+  int* acc = nullptr;
+  unsigned* cnt = nullptr;
+};
+constexpr int kUmmaMaxTiles = 4096;
+
 template <int MODE>
 int launch_mma(const ProjW& p, int B, const int8_t* q, const int* qsum, const __half* xs, const __half* t, void* out,
                int ld_out, float* conv_state, const __half* conv_w, const __half* conv_b, int d_inner, int d_xbc,
-               cudaStream_t s) {
+               cudaStream_t s, UmmaScratch us = UmmaScratch{}) {
+  if (B >= kUmmaMinBatch && p.K % kUmmaKC == 0) {  // tcgen05 path
+    constexpr int NT = 128;
+    const int tiles = ((p.N + 127) / 128) * ((B + NT - 1) / NT);
+    // split K until about one CTA per SM: MODE 2 adds the partials into `out`, the others need the
+    // scratch
+    int ks = 1;
+    const bool can_split = MODE == 2 || (us.acc && us.cnt && tiles <= kUmmaMaxTiles);
+    while (can_split && tiles * ks * 2 <= 160 && (p.K / (2 * ks)) % kUmmaKC == 0 && ks < 8) ks *= 2;
+    if (MODE == 2 && ks > 1) CU(cudaMemsetAsync(out, 0, (size_t)B * ld_out * 4, s));
+    const size_t sm = proj_umma_smem(NT);
+    unsigned* err = nullptr;
+    CU(cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_umma_err));
+    CU(cudaFuncSetAttribute(proj_umma_kernel<MODE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    proj_umma_kernel<MODE, NT><<<dim3((p.N + 127) / 128, (B + NT - 1) / NT, ks), kUmmaThreads, sm, s>>>(
+        p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out), ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, ks,
+        us.acc, us.cnt, err);
+    CHECK_LAUNCH();
+    return DFSSM_OK;
+  }
   const int RG = mma_rg(p.N, p.K);
   const size_t sm = proj_mma_smem(p.K, RG);
   if (RG == 2) {
@@ -150,10 +181,11 @@ int launch_mma(const ProjW& p, int B, const int8_t* q, const int* qsum, const __
 
 template <int MODE>
 int launch_gemv(dfssm_engine* e, const ProjW& p, int B, const int8_t* q, const int* qsum, const __half* xs,
-                const __half* t, void* out, int ld_out, float* conv_state, const LayerW* L, cudaStream_t s) {
+                const __half* t, void* out, int ld_out, float* conv_state, const LayerW* L, cudaStream_t s,
+                UmmaScratch us) {
   if (B >= kMmaMinBatch && mma_rg(p.N, p.K))
     return launch_mma<MODE>(p, B, q, qsum, xs, t, out, ld_out, conv_state, L ? L->conv_w : nullptr,
-                            L ? L->conv_b : nullptr, e->d.d_inner, e->d.d_xbc, s);
+                            L ? L->conv_b : nullptr, e->d.d_inner, e->d.d_xbc, s, us);
   const size_t sm = (size_t)kGemvBT * p.K;
   proj_gemv_kernel<MODE><<<gemv_grid(e, p.N), kGemvThreads, sm, s>>>(
       p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out), ld_out, conv_state, L ? L->conv_w : nullptr,
@@ -166,12 +198,14 @@ int enqueue_layer(dfssm_engine* e, int l, cudaStream_t s, Group G) {
   const dfssm_dims& d = e->d;
   const LayerW& L = e->layers[l];
   const int B = G.nb, b0 = G.b0;
+  // the split-K scratch is shared: only a step that runs the whole batch as one group uses it
+  const UmmaScratch us = (b0 == 0 && B == e->batch) ? UmmaScratch{e->uacc, e->ucnt} : UmmaScratch{};
   const size_t hd = (size_t)d.nheads * DFSSM_HEADDIM * DFSSM_DSTATE;
   int rc;
   if ((rc = launch_prep(e, e->x, d.d_model, L.ln_w, 1, &L.in, s, G, engine_rows(e)))) return rc;
   if ((rc = launch_gemv<0>(e, L.in, B, e->q + (size_t)b0 * d.d_model, e->qsum + b0, e->xs + b0, e->t + b0 * kRank,
                            e->proj + (size_t)b0 * d.n_in, d.n_in,
-                           e->conv + (size_t)l * e->conv_layer + (size_t)b0 * 3 * d.d_xbc, &L, s)))
+                           e->conv + (size_t)l * e->conv_layer + (size_t)b0 * 3 * d.d_xbc, &L, s, us)))
     return rc;
   __half* pr = e->proj + (size_t)b0 * d.n_in;
   ssm_gate_kernel<<<dim3(d.nheads, B), kSsmThreads, 0, s>>>(
@@ -181,7 +215,7 @@ int enqueue_layer(dfssm_engine* e, int l, cudaStream_t s, Group G) {
   CHECK_LAUNCH();
   if ((rc = launch_prep(e, e->gated, d.d_inner, L.norm_w, 1, &L.out, s, G, engine_rows(e)))) return rc;
   if ((rc = launch_gemv<1>(e, L.out, B, e->q + (size_t)b0 * d.d_inner, e->qsum + b0, e->xs + b0, e->t + b0 * kRank,
-                           e->x + (size_t)b0 * d.d_model, d.d_model, nullptr, nullptr, s)))
+                           e->x + (size_t)b0 * d.d_model, d.d_model, nullptr, nullptr, s, us)))
     return rc;
   return DFSSM_OK;
 }
@@ -519,6 +553,9 @@ int build_engine(const unsigned char* img, size_t n, int device, int max_batch, 
   // tagged exchange words of the persistent kernel: x, B/C, gated and LoRA t for 2 layer
   // parities x 2 sequences
   const size_t o_xch = take(persistent_xch_bytes(d));
+  const size_t umma_rows = B >= kUmmaMinBatch ? (size_t)B : 0;
+  const size_t o_uacc = take(umma_rows * (d.n_in > d.d_model ? d.n_in : d.d_model) * 4);
+  const size_t o_ucnt = take(umma_rows ? (size_t)kUmmaMaxTiles * 4 : 0);
   const int seen_words = (d.vocab + 31) / 32;
   const size_t o_seen = take((size_t)B * seen_words * 4);
   const size_t o_ctr = take((size_t)B * 8);
@@ -543,6 +580,8 @@ int build_engine(const unsigned char* img, size_t n, int device, int max_batch, 
   e->sync = reinterpret_cast<unsigned int*>(W + o_sync);
   e->xch = reinterpret_cast<unsigned long long*>(W + o_xch);
   e->seen = reinterpret_cast<uint32_t*>(W + o_seen);
+  e->uacc = umma_rows ? reinterpret_cast<int*>(W + o_uacc) : nullptr;
+  e->ucnt = umma_rows ? reinterpret_cast<unsigned*>(W + o_ucnt) : nullptr;
   e->seen_words = seen_words;
   e->counters = reinterpret_cast<unsigned long long*>(W + o_ctr);
   e->d_layers = reinterpret_cast<LayerW*>(W + o_layers);
@@ -744,8 +783,10 @@ int dfssm_check_finite(dfssm_engine* e, void* stream) {
   std::vector<float> h((size_t)e->batch * e->d.vocab);
   CU(cudaMemcpyAsync(h.data(), e->logits, h.size() * 4, cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream)));
   CU(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
-  unsigned sync_err = 0;
+  unsigned sync_err = 0, umma_err = 0;
   CU(cudaMemcpy(&sync_err, e->sync + 3, 4, cudaMemcpyDeviceToHost));
+  CU(cudaMemcpyFromSymbol(&umma_err, g_umma_err, 4));
+  if (umma_err) return dfssm_fail(DFSSM_ERR_STATE, "tcgen05 projection kernel recorded a timed-out wait");
   if (sync_err)
     return dfssm_fail(DFSSM_ERR_STATE, "persistent step kernel recorded a timed-out wait (code %u)", sync_err);
   for (size_t i = 0; i < h.size(); ++i)
@@ -1042,6 +1083,7 @@ struct PrefillBufs {
   int8_t* q;
   int* qsum;
   int* tok;
+  UmmaScratch us;
 };
 
 int prefill_bufs(dfssm_engine* e, int rows, PrefillBufs& P) {
@@ -1056,19 +1098,23 @@ int prefill_bufs(dfssm_engine* e, int rows, PrefillBufs& P) {
   const size_t ox = take((size_t)rows * d.d_model * 2), oxn = take((size_t)rows * kmax * 2),
                oq = take((size_t)rows * kmax), oxs = take((size_t)rows * 2), oqs = take((size_t)rows * 4),
                ot = take((size_t)rows * kRank * 2), op = take((size_t)rows * d.n_in * 2),
-               og = take((size_t)rows * d.d_inner * 2), otk = take((size_t)rows * 4);
+               og = take((size_t)rows * d.d_inner * 2), otk = take((size_t)rows * 4),
+               oua = take((size_t)rows * (d.n_in > d.d_model ? d.n_in : d.d_model) * 4),
+               ouc = take((size_t)kUmmaMaxTiles * 4);
   if (off > e->pf_bytes) {
     if (e->pf) CU(cudaFree(e->pf));
     e->pf = nullptr;
     e->pf_bytes = 0;
     if (cudaMalloc(&e->pf, off) != cudaSuccess)
       return dfssm_fail(DFSSM_ERR_OOM, "cudaMalloc(%zu) for prefill rows failed", off);
+    CU(cudaMemset(e->pf, 0, off));  // the split-K scratch starts (and stays) zero
     e->pf_bytes = off;
   }
   char* W = e->pf;
   P = PrefillBufs{reinterpret_cast<__half*>(W + ox), reinterpret_cast<__half*>(W + oxn), reinterpret_cast<__half*>(W + oxs),
                   reinterpret_cast<__half*>(W + ot), reinterpret_cast<__half*>(W + op), reinterpret_cast<__half*>(W + og),
-                  reinterpret_cast<int8_t*>(W + oq), reinterpret_cast<int*>(W + oqs), reinterpret_cast<int*>(W + otk)};
+                  reinterpret_cast<int8_t*>(W + oq), reinterpret_cast<int*>(W + oqs), reinterpret_cast<int*>(W + otk),
+                  UmmaScratch{reinterpret_cast<int*>(W + oua), reinterpret_cast<unsigned*>(W + ouc)}};
   return DFSSM_OK;
 }
 
@@ -1086,7 +1132,7 @@ int prefill_chunk(dfssm_engine* e, const PrefillBufs& P, int T, cudaStream_t s) 
     const LayerW& L = e->layers[l];
     if ((rc = launch_prep(e, P.x, d.d_model, L.ln_w, 1, &L.in, s, Group{0, R}, rb))) return rc;
     if ((rc = launch_mma<3>(L.in, R, P.q, P.qsum, P.xs, P.t, P.proj, d.n_in, nullptr, nullptr, nullptr, d.d_inner,
-                            d.d_xbc, s)))
+                            d.d_xbc, s, P.us)))
       return rc;
     prefill_scan_kernel<<<dim3(d.nheads, B), kScanThreads, sm, s>>>(
         P.proj, d.n_in, T, d.d_inner, d.d_state, d.nheads, L.conv_w, L.conv_b, L.dt_bias, L.A_log, L.Dp,
@@ -1094,7 +1140,7 @@ int prefill_chunk(dfssm_engine* e, const PrefillBufs& P, int T, cudaStream_t s) 
     CHECK_LAUNCH();
     if ((rc = launch_prep(e, P.gated, d.d_inner, L.norm_w, 1, &L.out, s, Group{0, R}, rb))) return rc;
     if ((rc = launch_mma<1>(L.out, R, P.q, P.qsum, P.xs, P.t, P.x, d.d_model, nullptr, nullptr, nullptr, d.d_inner,
-                            d.d_xbc, s)))
+                            d.d_xbc, s, P.us)))
       return rc;
   }
   return DFSSM_OK;

@@ -43,6 +43,8 @@ struct dfssm_engine {
   uint32_t* seen = nullptr;               // [max_batch][seen_words] tokens already in each sequence
   int seen_words = 0;
   unsigned long long* counters = nullptr;  // [max_batch] draws so far
+  int* uacc = nullptr;          // split-K scratch of the tcgen05 projection [max_batch][max(n_in, d_model)]
+  unsigned* ucnt = nullptr;     // its per-tile counters
   // prompt prefill rows (dfssm_prefill), grown on demand
   char* pf = nullptr;
   size_t pf_bytes = 0;
