@@ -60,7 +60,7 @@ proj_umma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ 
                  unsigned* __restrict__ err) {
   constexpr int ABYTES = 128 * kUmmaKC, BBYTES = NT * kUmmaKC, SBO = kUmmaKC / 16 * 128;
   constexpr int WPR = kUmmaKC / 32, CPR = kUmmaKC / 16;  // words / 16-byte units per row and chunk
-  extern __shared__ __align__(1024) unsigned char smem[];
+  extern __shared__ __align__(16) unsigned char smem[];  // no-swizzle operands need 16-byte alignment
   // buffer k: A at smem + k (ABYTES + BBYTES), B right after it
   auto sA = [&](int k) { return smem + k * (ABYTES + BBYTES); };
   auto sB = [&](int k) { return smem + k * (ABYTES + BBYTES) + ABYTES; };
