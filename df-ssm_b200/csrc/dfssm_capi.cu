@@ -141,28 +141,45 @@ struct UmmaScratch {
 };
 constexpr int kUmmaMaxTiles = 4096;
 
+// Batch at and above which the projections use the tcgen05 kernel (DFSSM_UMMA_MIN overrides).
+int umma_min_batch() {
+  static const int v = [] {
+    const char* e = getenv("DFSSM_UMMA_MIN");
+    return e ? atoi(e) : kUmmaMinBatch;
+  }();
+  return v;
+}
+
+template <int MODE, int NT>
+int launch_umma(const ProjW& p, int B, const int8_t* q, const int* qsum, const __half* xs, const __half* t, void* out,
+                int ld_out, float* conv_state, const __half* conv_w, const __half* conv_b, int d_inner, int d_xbc,
+                cudaStream_t s, UmmaScratch us) {
+  const int tiles = ((p.N + 127) / 128) * ((B + NT - 1) / NT);
+  // split K until about one CTA per SM: MODE 2 adds the partials into `out`, the others need the
+  // scratch
+  int ks = 1;
+  const bool can_split = MODE == 2 || (us.acc && us.cnt && tiles <= kUmmaMaxTiles);
+  while (can_split && tiles * ks * 2 <= 160 && (p.K / (2 * ks)) % kUmmaKC == 0 && ks < 8) ks *= 2;
+  if (MODE == 2 && ks > 1) CU(cudaMemsetAsync(out, 0, (size_t)B * ld_out * 4, s));
+  const size_t sm = proj_umma_smem(NT);
+  unsigned* err = nullptr;
+  CU(cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_umma_err));
+  CU(cudaFuncSetAttribute(proj_umma_kernel<MODE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  proj_umma_kernel<MODE, NT><<<dim3((p.N + 127) / 128, (B + NT - 1) / NT, ks), kUmmaThreads, sm, s>>>(
+      p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out), ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, ks,
+      us.acc, us.cnt, err);
+  CHECK_LAUNCH();
+  return DFSSM_OK;
+}
+
 template <int MODE>
 int launch_mma(const ProjW& p, int B, const int8_t* q, const int* qsum, const __half* xs, const __half* t, void* out,
                int ld_out, float* conv_state, const __half* conv_w, const __half* conv_b, int d_inner, int d_xbc,
                cudaStream_t s, UmmaScratch us = UmmaScratch{}) {
-  if (B >= kUmmaMinBatch && p.K % kUmmaKC == 0) {  // tcgen05 path
-    constexpr int NT = 128;
-    const int tiles = ((p.N + 127) / 128) * ((B + NT - 1) / NT);
-    // split K until about one CTA per SM: MODE 2 adds the partials into `out`, the others need the
-    // scratch
-    int ks = 1;
-    const bool can_split = MODE == 2 || (us.acc && us.cnt && tiles <= kUmmaMaxTiles);
-    while (can_split && tiles * ks * 2 <= 160 && (p.K / (2 * ks)) % kUmmaKC == 0 && ks < 8) ks *= 2;
-    if (MODE == 2 && ks > 1) CU(cudaMemsetAsync(out, 0, (size_t)B * ld_out * 4, s));
-    const size_t sm = proj_umma_smem(NT);
-    unsigned* err = nullptr;
-    CU(cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_umma_err));
-    CU(cudaFuncSetAttribute(proj_umma_kernel<MODE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-    proj_umma_kernel<MODE, NT><<<dim3((p.N + 127) / 128, (B + NT - 1) / NT, ks), kUmmaThreads, sm, s>>>(
-        p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out), ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, ks,
-        us.acc, us.cnt, err);
-    CHECK_LAUNCH();
-    return DFSSM_OK;
+  if (B >= umma_min_batch() && p.K % kUmmaKC == 0) {  // tcgen05 path
+    if (B >= 128) return launch_umma<MODE, 128>(p, B, q, qsum, xs, t, out, ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, s, us);
+    if (B >= 64) return launch_umma<MODE, 64>(p, B, q, qsum, xs, t, out, ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, s, us);
+    return launch_umma<MODE, 32>(p, B, q, qsum, xs, t, out, ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, s, us);
   }
   const int RG = mma_rg(p.N, p.K);
   const size_t sm = proj_mma_smem(p.K, RG);
@@ -553,7 +570,7 @@ int build_engine(const unsigned char* img, size_t n, int device, int max_batch, 
   // tagged exchange words of the persistent kernel: x, B/C, gated and LoRA t for 2 layer
   // parities x 2 sequences
   const size_t o_xch = take(persistent_xch_bytes(d));
-  const size_t umma_rows = B >= kUmmaMinBatch ? (size_t)B : 0;
+  const size_t umma_rows = B >= kMmaMinBatch ? (size_t)B : 0;  // any batch that may take the tcgen05 path
   const size_t o_uacc = take(umma_rows * (d.n_in > d.d_model ? d.n_in : d.d_model) * 4);
   const size_t o_ucnt = take(umma_rows ? (size_t)kUmmaMaxTiles * 4 : 0);
   const int seen_words = (d.vocab + 31) / 32;
