@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -43,6 +44,22 @@ namespace {
   } while (0)
 
 #define CHECK_LAUNCH() CU(cudaGetLastError())
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (device, kernel, size): the call costs
+// microseconds of host time, which the stand-alone ops would otherwise pay on every launch.
+cudaError_t ensure_smem(const void* fn, size_t bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, size_t> done;
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return ce;
+  std::lock_guard<std::mutex> lk(mu);
+  size_t& have = done[{dev, fn}];
+  if (have >= bytes) return cudaSuccess;
+  ce = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (ce == cudaSuccess) have = bytes;
+  return ce;
+}
 
 constexpr size_t kHeader = 64;
 constexpr int kRank = DFSSM_RANK;
@@ -150,6 +167,25 @@ int umma_min_batch() {
   return v;
 }
 
+// Device address of g_umma_err on the current device (looked up once per device).
+cudaError_t umma_err_word(unsigned** out) {
+  static std::mutex mu;
+  static std::map<int, unsigned*> addr;
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return ce;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = addr.find(dev);
+  if (it == addr.end()) {
+    unsigned* a = nullptr;
+    ce = cudaGetSymbolAddress(reinterpret_cast<void**>(&a), g_umma_err);
+    if (ce != cudaSuccess) return ce;
+    it = addr.emplace(dev, a).first;
+  }
+  *out = it->second;
+  return cudaSuccess;
+}
+
 template <int MODE, int NT>
 int launch_umma(const ProjW& p, int B, const int8_t* q, const int* qsum, const __half* xs, const __half* t, void* out,
                 int ld_out, float* conv_state, const __half* conv_w, const __half* conv_b, int d_inner, int d_xbc,
@@ -159,12 +195,16 @@ int launch_umma(const ProjW& p, int B, const int8_t* q, const int* qsum, const _
   // scratch
   int ks = 1;
   const bool can_split = MODE == 2 || (us.acc && us.cnt && tiles <= kUmmaMaxTiles);
-  while (can_split && tiles * ks * 2 <= 160 && (p.K / (2 * ks)) % kUmmaKC == 0 && ks < 8) ks *= 2;
+  static const int target = [] {
+    const char* e = getenv("DFSSM_UMMA_CTAS");
+    return e ? atoi(e) : 160;
+  }();
+  while (can_split && tiles * ks * 2 <= target && (p.K / (2 * ks)) % kUmmaKC == 0 && ks < 16) ks *= 2;
   if (MODE == 2 && ks > 1) CU(cudaMemsetAsync(out, 0, (size_t)B * ld_out * 4, s));
   const size_t sm = proj_umma_smem(NT);
   unsigned* err = nullptr;
-  CU(cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_umma_err));
-  CU(cudaFuncSetAttribute(proj_umma_kernel<MODE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  CU(umma_err_word(&err));
+  CU(ensure_smem(reinterpret_cast<const void*>(proj_umma_kernel<MODE, NT>), sm));
   proj_umma_kernel<MODE, NT><<<dim3((p.N + 127) / 128, (B + NT - 1) / NT, ks), kUmmaThreads, sm, s>>>(
       p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out), ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, ks,
       us.acc, us.cnt, err);
@@ -184,11 +224,11 @@ int launch_mma(const ProjW& p, int B, const int8_t* q, const int* qsum, const __
   const int RG = mma_rg(p.N, p.K);
   const size_t sm = proj_mma_smem(p.K, RG);
   if (RG == 2) {
-    CU(cudaFuncSetAttribute(proj_mma_kernel<MODE, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    CU(ensure_smem(reinterpret_cast<const void*>(proj_mma_kernel<MODE, 2>), sm));
     proj_mma_kernel<MODE, 2><<<(p.N + 31) / 32, kMmaThreads, sm, s>>>(p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out),
                                                                      ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc);
   } else {
-    CU(cudaFuncSetAttribute(proj_mma_kernel<MODE, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    CU(ensure_smem(reinterpret_cast<const void*>(proj_mma_kernel<MODE, 1>), sm));
     proj_mma_kernel<MODE, 1><<<(p.N + 15) / 16, kMmaThreads, sm, s>>>(p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out),
                                                                      ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc);
   }
@@ -256,7 +296,7 @@ int enqueue_head(dfssm_engine* e, cudaStream_t s) {
   if ((rc = launch_prep(e, e->x, d.d_model, e->norm_f, 0, nullptr, s, Group{0, e->batch}, engine_rows(e)))) return rc;
   if (e->batch >= kMmaMinBatch && d.d_model % 64 == 0) {
     const size_t sm = lm_head_mma_smem(d.d_model);
-    CU(cudaFuncSetAttribute(lm_head_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    CU(ensure_smem(reinterpret_cast<const void*>(lm_head_mma_kernel), sm));
     lm_head_mma_kernel<<<e->sm_count, kHeadMmaThreads, sm, s>>>(e->Eq, e->Es, d.vocab, d.d_model, e->xn, e->batch,
                                                                e->logits, e->best);
   } else {
@@ -872,7 +912,7 @@ int dfssm_scaffold_gemm(const uint32_t* packed, const int8_t* q, int M, int N, i
   if (M >= kMmaMinBatch && mma_rg(N, K))
     return launch_mma<2>(p, M, qp, qsum, nullptr, nullptr, acc, N, nullptr, nullptr, nullptr, 0, 0, s);
   const size_t sm = (size_t)kGemvBT * K;
-  if (sm > 48 * 1024) CU(cudaFuncSetAttribute(proj_gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  if (sm > 48 * 1024) CU(ensure_smem(reinterpret_cast<const void*>(proj_gemv_kernel<2>), sm));
   const int rows_per_cta = 2 * (kGemvThreads / 32);
   proj_gemv_kernel<2><<<(N + rows_per_cta - 1) / rows_per_cta, kGemvThreads, sm, s>>>(
       p, qp, qsum, nullptr, nullptr, M, reinterpret_cast<__half*>(acc), N, nullptr, nullptr, nullptr, 0, 0);
@@ -922,14 +962,14 @@ int dfssm_lm_head_argmax(const int8_t* E_q, const float* E_s, int vocab, int d, 
   float* lg = logits;
   if (!lg) return dfssm_fail(DFSSM_ERR_ARG, "logits output is required by this build");
   const size_t sm = (size_t)kHeadBT * d * sizeof(float);
-  if (sm > 48 * 1024) CU(cudaFuncSetAttribute(lm_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  if (sm > 48 * 1024) CU(ensure_smem(reinterpret_cast<const void*>(lm_head_kernel), sm));
   int sms = 148;
   int dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (batch >= kMmaMinBatch && d % 64 == 0) {
     const size_t sm2 = lm_head_mma_smem(d);
-    CU(cudaFuncSetAttribute(lm_head_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2));
+    CU(ensure_smem(reinterpret_cast<const void*>(lm_head_mma_kernel), sm2));
     lm_head_mma_kernel<<<sms, kHeadMmaThreads, sm2, s>>>(E_q, E_s, vocab, d, static_cast<const __half*>(x_f16), batch,
                                                           lg, best);
   } else {
@@ -1009,7 +1049,7 @@ extern "C" int dfssm_scaffold_gemm_noalloc(const uint32_t* packed, const int8_t*
   p.N = N;
   p.K = K;
   const size_t sm = (size_t)kGemvBT * K;
-  if (sm > 48 * 1024) CU(cudaFuncSetAttribute(proj_gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  if (sm > 48 * 1024) CU(ensure_smem(reinterpret_cast<const void*>(proj_gemv_kernel<2>), sm));
   const int rows_per_cta = 2 * (kGemvThreads / 32);
   proj_gemv_kernel<2><<<(N + rows_per_cta - 1) / rows_per_cta, kGemvThreads, sm, s>>>(
       p, qp, qsum, nullptr, nullptr, M, reinterpret_cast<__half*>(acc), N, nullptr, nullptr, nullptr, 0, 0);
@@ -1070,7 +1110,7 @@ int dfssm_sample(const float* logits, int batch, int vocab, uint32_t* seen_bits,
   CU(cudaDeviceGetAttribute(&max_sm, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
   if (sm + 1024 > (size_t)max_sm)
     return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "vocab %d needs %zu bytes of shared memory (max %d)", vocab, sm, max_sm);
-  CU(cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  CU(ensure_smem(reinterpret_cast<const void*>(sample_kernel), sm));
   sample_kernel<<<batch, kSampleThreads, sm, static_cast<cudaStream_t>(stream)>>>(
       logits, vocab, seen_bits, (vocab + 31) / 32, temperature, top_p, rep_penalty,
       (unsigned long long)seed, reinterpret_cast<unsigned long long*>(counters), next, kept_mass, kept_count);
@@ -1143,7 +1183,7 @@ int prefill_chunk(dfssm_engine* e, const PrefillBufs& P, int T, cudaStream_t s) 
   embed_rows_kernel<<<R, 256, 0, s>>>(P.tok, e->Eq, e->Es, d.d_model, d.vocab, P.x);
   CHECK_LAUNCH();
   const size_t sm = prefill_scan_smem(T, d.d_state);
-  CU(cudaFuncSetAttribute(prefill_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  CU(ensure_smem(reinterpret_cast<const void*>(prefill_scan_kernel), sm));
   int rc;
   for (int l = 0; l < d.n_layer; ++l) {
     const LayerW& L = e->layers[l];
