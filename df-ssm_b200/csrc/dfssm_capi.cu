@@ -186,6 +186,37 @@ cudaError_t umma_err_word(unsigned** out) {
   return cudaSuccess;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link); null if absent.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    cudaGetLastError();
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
+// Tensor map over the activation rows q [rows][K] int8: box 128 bytes x NT rows, 128-byte swizzle,
+// rows past `rows` read as zeros.  False if it cannot be made (then the threads stage B).
+bool make_q_map(CUtensorMap* m, const int8_t* q, int rows, int K, int NT) {
+  const EncodeTiledFn fn = encode_tiled();
+  if (!fn || (reinterpret_cast<uintptr_t>(q) & 15) || K % 128) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)K};
+  const cuuint32_t box[2] = {128u, (cuuint32_t)NT};
+  const cuuint32_t estr[2] = {1u, 1u};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int MODE, int NT>
 int launch_umma(const ProjW& p, int B, const int8_t* q, const int* qsum, const __half* xs, const __half* t, void* out,
                 int ld_out, float* conv_state, const __half* conv_w, const __half* conv_b, int d_inner, int d_xbc,
@@ -204,10 +235,24 @@ int launch_umma(const ProjW& p, int B, const int8_t* q, const int* qsum, const _
   const size_t sm = proj_umma_smem(NT);
   unsigned* err = nullptr;
   CU(umma_err_word(&err));
-  CU(ensure_smem(reinterpret_cast<const void*>(proj_umma_kernel<MODE, NT>), sm));
-  proj_umma_kernel<MODE, NT><<<dim3((p.N + 127) / 128, (B + NT - 1) / NT, ks), kUmmaThreads, sm, s>>>(
-      p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out), ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, ks,
-      us.acc, us.cnt, err);
+  CUtensorMap tm;
+  memset(&tm, 0, sizeof(tm));
+  static const bool tma_on = [] {
+    const char* e = getenv("DFSSM_UMMA_TMA");
+    return !e || atoi(e) != 0;
+  }();
+  const dim3 grid((p.N + 127) / 128, (B + NT - 1) / NT, ks);
+  if (tma_on && make_q_map(&tm, q, B, p.K, NT)) {
+    CU(ensure_smem(reinterpret_cast<const void*>(proj_umma_kernel<MODE, NT, true>), sm));
+    proj_umma_kernel<MODE, NT, true><<<grid, kUmmaThreads, sm, s>>>(
+        tm, p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out), ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc,
+        ks, us.acc, us.cnt, err);
+  } else {
+    CU(ensure_smem(reinterpret_cast<const void*>(proj_umma_kernel<MODE, NT, false>), sm));
+    proj_umma_kernel<MODE, NT, false><<<grid, kUmmaThreads, sm, s>>>(
+        tm, p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out), ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc,
+        ks, us.acc, us.cnt, err);
+  }
   CHECK_LAUNCH();
   return DFSSM_OK;
 }

@@ -17,6 +17,8 @@
 // i.e. output rows; each thread holds its row's dequant/LoRA/conv operands in registers) and
 // runs the same per-element arithmetic as proj_mma_kernel.
 #pragma once
+#include <cuda.h>  // CUtensorMap (the map is encoded on the host through the driver entry point)
+
 #include "common.cuh"
 
 namespace dfssm {
@@ -29,11 +31,11 @@ constexpr int kUmmaKC = DFSSM_UMMA_KC;  // K bytes per chunk (KC / 32 MMAs of K 
 constexpr int kUmmaMinBatch = 64;   // batches below this use proj_mma_kernel (mma.sync)
 constexpr int kUmmaSpin = 1 << 22;  // bound of every mbarrier wait
 
-__device__ __forceinline__ uint64_t umma_sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+__device__ __forceinline__ uint64_t umma_sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout = 0) {
   // start address, leading / stride byte offsets (16-byte units), descriptor version 1
-  // (tcgen05), base offset 0, no swizzle
+  // (tcgen05), base offset 0, layout type (0 = no swizzle, 2 = 128-byte swizzle)
   return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
 }
 
 __device__ __forceinline__ bool umma_wait(uint64_t* bar, unsigned parity) {
@@ -42,7 +44,9 @@ __device__ __forceinline__ bool umma_wait(uint64_t* bar, unsigned parity) {
   return false;
 }
 
-inline size_t proj_umma_smem(int NT) { return (size_t)2 * (128 + NT) * kUmmaKC + 2 * NT * 4 + NT * DFSSM_RANK * 4; }
+inline size_t proj_umma_smem(int NT) {
+  return 1024 + (size_t)2 * (128 + NT) * kUmmaKC + 2 * NT * 4 + NT * DFSSM_RANK * 4;  // + base alignment
+}
 
 // MODE as proj_mma_kernel: 0 in_proj + conv1d, 1 out_proj + residual, 2 raw int32, 3 plain.
 // Grid (ceil(N / 128), ceil(B / NT), ksplit); (K / ksplit) % 256 == 0.  With ksplit > 1 the CTAs
@@ -51,16 +55,24 @@ inline size_t proj_umma_smem(int NT) { return (size_t)2 * (128 + NT) * kUmmaKC +
 // by the caller), else into ws [B][N] int32 with a per-tile counter cnt, and the last CTA of the
 // tile runs the epilogue and clears its part of ws and its counter.  err: set to 1 if a wait ran
 // out.
-template <int MODE, int NT>
+// TMAB: the activation tiles arrive by TMA (tensor map tmq over q [B][K] int8, box 128 bytes x NT
+// rows, 128-byte swizzle; rows past B read as zeros) and both operands use the 128-byte-swizzled
+// K-major layout (8-row atoms of 1 KB, 16-byte unit u of row r at unit u ^ (r % 8)); otherwise the
+// threads stage them in the no-swizzle core-matrix layout.
+template <int MODE, int NT, bool TMAB>
 __global__ void __launch_bounds__(kUmmaThreads, 1)
-proj_umma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ qsum, const __half* __restrict__ xs,
+proj_umma_kernel(const __grid_constant__ CUtensorMap tmq, ProjW p, const int8_t* __restrict__ q,
+                 const int* __restrict__ qsum, const __half* __restrict__ xs,
                  const __half* __restrict__ t, int B, __half* __restrict__ out, int ld_out,
                  float* __restrict__ conv_state, const __half* __restrict__ conv_w, const __half* __restrict__ conv_b,
                  int d_inner, int d_xbc, int ksplit, int* __restrict__ ws, unsigned* __restrict__ cnt,
                  unsigned* __restrict__ err) {
   constexpr int ABYTES = 128 * kUmmaKC, BBYTES = NT * kUmmaKC, SBO = kUmmaKC / 16 * 128;
   constexpr int WPR = kUmmaKC / 32, CPR = kUmmaKC / 16;  // words / 16-byte units per row and chunk
-  extern __shared__ __align__(16) unsigned char smem[];  // no-swizzle operands need 16-byte alignment
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  // 1 KB-aligned base (the 128-byte swizzle atoms and TMA destinations need it)
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  static_assert(!TMAB || kUmmaKC == 128, "the swizzled layout holds one 128-byte row per chunk");
   // buffer k: A at smem + k (ABYTES + BBYTES), B right after it
   auto sA = [&](int k) { return smem + k * (ABYTES + BBYTES); };
   auto sB = [&](int k) { return smem + k * (ABYTES + BBYTES) + ABYTES; };
@@ -68,6 +80,7 @@ proj_umma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ 
   int* e_qsum = reinterpret_cast<int*>(e_xs + NT);                         // [NT]
   float* e_t = reinterpret_cast<float*>(e_qsum + NT);                      // [NT][16]
   __shared__ uint64_t bars[2];
+  __shared__ uint64_t fulls[2];  // TMAB: the B tile of a buffer has landed
   __shared__ uint32_t s_tmem;
   __shared__ int s_last;
   const int tid = threadIdx.x, wid = tid >> 5, lane = tid & 31;
@@ -80,6 +93,8 @@ proj_umma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ 
   if (tid == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
+    mbar_init(&fulls[0], 1);
+    mbar_init(&fulls[1], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   // per-column operands of this batch tile
@@ -109,28 +124,38 @@ proj_umma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ 
       const int i = tid + u * kUmmaThreads, r = i / WPR, j = i - r * WPR;
       rw[u] = __ldg(p.bits + (size_t)min(row0 + r, N - 1) * W + (kc >> 5) + j);
     }
+    if (!TMAB)
 #pragma unroll
-    for (int u = 0; u < BU; ++u) {
-      const int i = tid + u * kUmmaThreads, b = i / CPR, c = i - b * CPR;
-      rv[u] = __ldg(reinterpret_cast<const uint4*>(q + (size_t)(b0 + min(b, nb - 1)) * K + kc) + c);
-    }
+      for (int u = 0; u < BU; ++u) {
+        const int i = tid + u * kUmmaThreads, b = i / CPR, c = i - b * CPR;
+        rv[u] = __ldg(reinterpret_cast<const uint4*>(q + (size_t)(b0 + min(b, nb - 1)) * K + kc) + c);
+      }
   };
   auto store = [&](int buf) {
 #pragma unroll
     for (int u = 0; u < AW; ++u) {
       const int i = tid + u * kUmmaThreads, r = i / WPR, j = i - r * WPR;
-      unsigned char* dst = sA(buf) + (r >> 3) * SBO + (2 * j) * 128 + (r & 7) * 16;
       const uint32_t x = rw[u];
-      *reinterpret_cast<uint4*>(dst) = make_uint4(x & 0x01010101u, (x >> 1) & 0x01010101u, (x >> 2) & 0x01010101u,
-                                                  (x >> 3) & 0x01010101u);
-      *reinterpret_cast<uint4*>(dst + 128) = make_uint4((x >> 4) & 0x01010101u, (x >> 5) & 0x01010101u,
-                                                        (x >> 6) & 0x01010101u, (x >> 7) & 0x01010101u);
+      const uint4 lo = make_uint4(x & 0x01010101u, (x >> 1) & 0x01010101u, (x >> 2) & 0x01010101u,
+                                  (x >> 3) & 0x01010101u);
+      const uint4 hi = make_uint4((x >> 4) & 0x01010101u, (x >> 5) & 0x01010101u, (x >> 6) & 0x01010101u,
+                                  (x >> 7) & 0x01010101u);
+      if (TMAB) {  // units 2j, 2j + 1 of row r, swizzled
+        unsigned char* rowp = sA(buf) + (r >> 3) * 1024 + (r & 7) * 128;
+        *reinterpret_cast<uint4*>(rowp + (((2 * j) ^ (r & 7)) << 4)) = lo;
+        *reinterpret_cast<uint4*>(rowp + (((2 * j + 1) ^ (r & 7)) << 4)) = hi;
+      } else {
+        unsigned char* dst = sA(buf) + (r >> 3) * SBO + (2 * j) * 128 + (r & 7) * 16;
+        *reinterpret_cast<uint4*>(dst) = lo;
+        *reinterpret_cast<uint4*>(dst + 128) = hi;
+      }
     }
+    if (!TMAB)
 #pragma unroll
-    for (int u = 0; u < BU; ++u) {
-      const int i = tid + u * kUmmaThreads, b = i / CPR, c = i - b * CPR;
-      *reinterpret_cast<uint4*>(sB(buf) + (b >> 3) * SBO + c * 128 + (b & 7) * 16) = rv[u];
-    }
+      for (int u = 0; u < BU; ++u) {
+        const int i = tid + u * kUmmaThreads, b = i / CPR, c = i - b * CPR;
+        *reinterpret_cast<uint4*>(sB(buf) + (b >> 3) * SBO + c * 128 + (b & 7) * 16) = rv[u];
+      }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
   };
 
@@ -144,18 +169,41 @@ proj_umma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ 
     else ph0 ^= 1u;
     return r;
   };
+  unsigned fph0 = 0u, fph1 = 0u;  // TMAB: next phase of fulls[0] / fulls[1]
+  auto issue_b = [&](int kc, int buf) {  // thread 0: the B tile of chunk kc into buffer buf
+    if (TMAB && tid == 0) {
+      mbar_expect_tx(&fulls[buf], (unsigned)BBYTES);
+      asm volatile(
+          "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+              smem_u32(sB(buf))),
+          "l"(reinterpret_cast<uint64_t>(&tmq)), "r"(kc), "r"(b0), "r"(smem_u32(&fulls[buf]))
+          : "memory");
+    }
+  };
+  issue_b(kbeg, 0);
   load(kbeg);
   store(0);
-  if (nch > 1) load(kbeg + kUmmaKC);
+  if (nch > 1) {
+    issue_b(kbeg + kUmmaKC, 1);
+    load(kbeg + kUmmaKC);
+  }
   for (int c = 0; c < nch; ++c) {
     const int buf = c & 1;
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;");
     if (tid == 0) {
+      if (TMAB) {  // the chunk's B tile
+        ok = umma_wait(&fulls[buf], buf ? fph1 : fph0) && ok;
+        if (buf) fph1 ^= 1u;
+        else fph0 ^= 1u;
+      }
 #pragma unroll
       for (int s = 0; s < kUmmaKC / 32; ++s) {
-        const uint64_t da = umma_sdesc(smem_u32(sA(buf)) + s * 256, 128, SBO);
-        const uint64_t db = umma_sdesc(smem_u32(sB(buf)) + s * 256, 128, SBO);
+        // no swizzle: the K step is 2 core matrices (256 B); swizzled: 32 bytes along the 128-byte row
+        const uint64_t da = TMAB ? umma_sdesc(smem_u32(sA(buf)) + s * 32, 16, 1024, 2)
+                                 : umma_sdesc(smem_u32(sA(buf)) + s * 256, 128, SBO);
+        const uint64_t db = TMAB ? umma_sdesc(smem_u32(sB(buf)) + s * 32, 16, 1024, 2)
+                                 : umma_sdesc(smem_u32(sB(buf)) + s * 256, 128, SBO);
         const uint32_t accum = (c > 0 || s > 0) ? 1u : 0u;
         asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
                      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem),
@@ -167,7 +215,10 @@ proj_umma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ 
     }
     if (c + 1 < nch) {
       // the other buffer was last read by the MMAs of chunk c - 1
-      if (c >= 1) ok = wait_buf(buf ^ 1) && ok;
+      if (c >= 1) {
+        ok = wait_buf(buf ^ 1) && ok;
+        issue_b(kbeg + (c + 1) * kUmmaKC, buf ^ 1);
+      }
       store(buf ^ 1);
       if (c + 2 < nch) load(kbeg + (c + 2) * kUmmaKC);
     }
