@@ -16,8 +16,11 @@ constexpr int kScanMaxT = 64;  // tokens per scan launch (longer prompts run in 
 // proj fp16 [B*T rows][n_in]: z [d_inner] | x [d_inner] | B [d_state] | C [d_state] | dt [nheads]
 // (row b*T + t).  Writes gated fp16 [B*T][d_inner]; updates this layer's conv state
 // [B][3][d_xbc] (tap-major) and SSM state [B][nheads][64][128].
-// Dynamic shared memory: (64 + 2*d_state) channels x (T + 3) fp32 raw inputs, then the same
-// channels x T conv outputs.
+// Everything the token loop reads is staged in shared memory first, by coalesced row reads, so the
+// loop itself touches no global memory: raw conv inputs (channel-major, 3 taps + T), conv + SiLU
+// outputs (time-major, so a lane's 4 B/C values of one token are one conflict-free float4), the
+// SiLU(z) gate factors, softplus(dt) and exp(A dt) per token, and the gated outputs (written to HBM
+// as whole rows at the end).
 __global__ void __launch_bounds__(kScanThreads)
 prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inner, int d_state, int nheads,
                     const __half* __restrict__ conv_w, const __half* __restrict__ conv_b,
@@ -28,8 +31,12 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
   const int d_xbc = d_inner + 2 * d_state;
   const int NC = DFSSM_HEADDIM + 2 * d_state;  // this head's x channels, then all B and C channels
   const int TS = T + 3;
-  float* raw = sm;                  // [NC][T + 3]: 3 taps of conv state, then the T raw inputs
-  float* cvo = sm + NC * TS;        // [NC][T]: fp16-exact conv + SiLU outputs
+  float* raw = sm;                          // [NC][T + 3]: 3 taps of conv state, then the T raw inputs
+  float* cvo = raw + NC * TS;               // [T][NC]: fp16-exact conv + SiLU outputs
+  float* zg = cvo + NC * T;                 // [T][64]: fp16-exact SiLU(z)
+  float* dts = zg + T * DFSSM_HEADDIM;      // [T]: softplus(dt + bias)
+  float* abar = dts + T;                    // [T]: exp(A dt)
+  __half* gs = reinterpret_cast<__half*>(raw);  // [T][64] gated outputs (raw is dead by then)
   auto chan = [&](int c) { return c < DFSSM_HEADDIM ? h * DFSSM_HEADDIM + c : d_inner + (c - DFSSM_HEADDIM); };
   // state tile: first, so the HBM stream starts before anything else
   const int wid = tid >> 5, lane = tid & 31, n0 = lane * 4;
@@ -37,14 +44,31 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
   float4 hv[8];
 #pragma unroll
   for (int r = 0; r < 8; ++r) hv[r] = __ldcs(reinterpret_cast<const float4*>(hs + (wid * 8 + r) * DFSSM_DSTATE + n0));
+  const float Ah = -expf(A_log[h]), Dh = Dp[h], dtb = dt_bias[h];
+  const __half* pb = proj + (size_t)b * T * n_in;
   const float* cs = conv_state + (size_t)b * 3 * d_xbc;
-  for (int i = tid; i < NC * TS; i += kScanThreads) {
-    const int c = i / TS, k = i - c * TS, ch = chan(c);
-    raw[i] = k < 3 ? cs[(size_t)k * d_xbc + ch] : h2f(proj[((size_t)b * T + (k - 3)) * n_in + d_inner + ch]);
+  for (int i = tid; i < NC * 3; i += kScanThreads) {
+    const int k = i / NC, c = i - k * NC;
+    raw[c * TS + k] = cs[(size_t)k * d_xbc + chan(c)];
+  }
+  for (int i = tid; i < NC * T; i += kScanThreads) {  // row t, channel c: contiguous in c
+    const int t = i / NC, c = i - t * NC;
+    raw[c * TS + 3 + t] = h2f(pb[(size_t)t * n_in + d_inner + chan(c)]);
+  }
+  for (int i = tid; i < T * DFSSM_HEADDIM; i += kScanThreads) {
+    const int t = i / DFSSM_HEADDIM, p = i - t * DFSSM_HEADDIM;
+    const float z = h2f(pb[(size_t)t * n_in + h * DFSSM_HEADDIM + p]);
+    const float sig = round_h(1.0f / (1.0f + expf(-z)));
+    zg[i] = round_h(z * sig);
+  }
+  for (int t = tid; t < T; t += kScanThreads) {
+    const float dtv = log1pf(expf(h2f(pb[(size_t)t * n_in + d_inner + d_xbc + h]) + dtb));
+    dts[t] = dtv;
+    abar[t] = expf(dtv * Ah);
   }
   __syncthreads();
   for (int i = tid; i < NC * T; i += kScanThreads) {
-    const int c = i / T, t = i - c * T, ch = chan(c);
+    const int t = i / NC, c = i - t * NC, ch = chan(c);
     const float* rr = raw + c * TS + t;
     const __half* cw = conv_w + ch * DFSSM_DCONV;
     const float s0 = rr[0], s1 = rr[1], s2 = rr[2], v = rr[3];
@@ -52,59 +76,51 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
     const float sig = 1.0f / (1.0f + expf(-o2));
     cvo[i] = h2f(f2h(o2 * sig));
   }
-  __syncthreads();
   // conv state after the prompt: the last three raw inputs (B/C channels written by head 0)
   float* csw = conv_state + (size_t)b * 3 * d_xbc;
   for (int i = tid; i < NC * 3; i += kScanThreads) {
-    const int c = i / 3, k = i - c * 3;
+    const int k = i / NC, c = i - k * NC;
     if (c >= DFSSM_HEADDIM && h != 0) continue;
     csw[(size_t)k * d_xbc + chan(c)] = raw[c * TS + T + k];
   }
-  const float Ah = -expf(A_log[h]), Dh = Dp[h], dtb = dt_bias[h];
-  const float* Bs = cvo + DFSSM_HEADDIM * T;  // channel-major: B channel n at Bs[n * T + t]
-  const float* Cs = Bs + d_state * T;
+  __syncthreads();
   for (int t = 0; t < T; ++t) {
-    const size_t row = (size_t)b * T + t;
-    const __half* pr = proj + row * n_in;
-    float dtv = h2f(pr[d_inner + d_xbc + h]) + dtb;
-    dtv = log1pf(expf(dtv));
-    const float Abar = expf(dtv * Ah);
-    float Bn[4], Cn[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      Bn[i] = Bs[(n0 + i) * T + t];
-      Cn[i] = Cs[(n0 + i) * T + t];
-    }
+    const float* ct = cvo + t * NC;
+    const float dtv = dts[t], Abar = abar[t];
+    const float4 Bn = *reinterpret_cast<const float4*>(ct + DFSSM_HEADDIM + n0);
+    const float4 Cn = *reinterpret_cast<const float4*>(ct + DFSSM_HEADDIM + d_state + n0);
+    float yv = 0.f;
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
-      const int pp = wid * 8 + r;
-      const float xv = cvo[pp * T + t];
+      const float xv = ct[wid * 8 + r];
       const float X = xv * dtv;
       float4 o;
-      o.x = Abar * hv[r].x + X * Bn[0];
-      o.y = Abar * hv[r].y + X * Bn[1];
-      o.z = Abar * hv[r].z + X * Bn[2];
-      o.w = Abar * hv[r].w + X * Bn[3];
+      o.x = Abar * hv[r].x + X * Bn.x;
+      o.y = Abar * hv[r].y + X * Bn.y;
+      o.z = Abar * hv[r].z + X * Bn.z;
+      o.w = Abar * hv[r].w + X * Bn.w;
       hv[r] = o;
-      float part = Cn[0] * o.x + Cn[1] * o.y + Cn[2] * o.z + Cn[3] * o.w;
-      part = warp_sum(part);
-      if (lane == r) {
-        const float y = part + xv * Dh;
-        __half o16 = f2h(y);
-        const float z = h2f(pr[h * DFSSM_HEADDIM + pp]);
-        const float sig = round_h(1.0f / (1.0f + expf(-z)));
-        const float silu = round_h(z * sig);
-        o16 = f2h(h2f(o16) * silu);
-        gated[row * d_inner + h * DFSSM_HEADDIM + pp] = o16;
-      }
+      const float part = warp_sum(Cn.x * o.x + Cn.y * o.y + Cn.z * o.z + Cn.w * o.w);
+      if (lane == r) yv = part + xv * Dh;
+    }
+    if (lane < 8) {
+      const int pp = wid * 8 + lane;
+      gs[t * DFSSM_HEADDIM + pp] = f2h(h2f(f2h(yv)) * zg[t * DFSSM_HEADDIM + pp]);
     }
   }
 #pragma unroll
   for (int r = 0; r < 8; ++r) __stcs(reinterpret_cast<float4*>(hs + (wid * 8 + r) * DFSSM_DSTATE + n0), hv[r]);
+  __syncthreads();
+  for (int i = tid; i < T * DFSSM_HEADDIM / 2; i += kScanThreads) {
+    const int t = i / (DFSSM_HEADDIM / 2), p2 = i - t * (DFSSM_HEADDIM / 2);
+    reinterpret_cast<__half2*>(gated + ((size_t)b * T + t) * d_inner + h * DFSSM_HEADDIM)[p2] =
+        reinterpret_cast<const __half2*>(gs)[i];
+  }
 }
 
 inline size_t prefill_scan_smem(int T, int d_state) {
-  return (size_t)(DFSSM_HEADDIM + 2 * d_state) * (2 * T + 3) * sizeof(float);
+  const size_t nc = DFSSM_HEADDIM + 2 * d_state;
+  return (nc * (2 * T + 3) + (size_t)T * DFSSM_HEADDIM + 2 * T) * sizeof(float);
 }
 
 // x rows b*T + t = the embedding of tokens[b][t] (fp16, as embed_kernel).
