@@ -48,6 +48,9 @@ constexpr int kThreads = 512;              // compute threads (named barrier 1)
 constexpr int kWarps = kThreads / 32;
 constexpr int kBlockThreads = kThreads + 32;  // + one warp that issues the weight/state copies
 constexpr unsigned kSpinLimit = 1u << 22;
+#ifndef DFSSM_GFIRST
+#define DFSSM_GFIRST 1  // gated vector: poll one word per thread before loading the rest
+#endif
 constexpr int kMaxRPW = 2;  // SSM rows per warp (np = 32 channels over 16 warps)
 
 struct CtaPlan {
@@ -123,7 +126,10 @@ __device__ __forceinline__ float hi_h(unsigned v) { return h2f(__ushort_as_half(
 // Every exchange word is written to kReplicas copies kRepStride words apart and CTA c reads
 // copy c % kReplicas: all CTAs polling one copy would concentrate their L2 requests on the
 // few slices that hold it.
-constexpr int kReplicas = 8;
+#ifndef DFSSM_XREPL
+#define DFSSM_XREPL 8
+#endif
+constexpr int kReplicas = DFSSM_XREPL;
 __device__ __forceinline__ void put_word(unsigned long long* p, size_t rstride, unsigned data, unsigned tag) {
   const unsigned long long w = ((unsigned long long)tag << 32) | data;
 #pragma unroll
@@ -818,7 +824,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       unsigned v[B][KO / 2];
       // the gated vector is the largest exchange (every CTA takes all of it while most wait for
       // the slowest head): poll one word per thread, then load the rest
-      take_words<B, KO / 2, true>(gw + rep_off + tid * (KO / 2), GW, tg_g, v, P.sync + 3, 16u);
+      take_words<B, KO / 2, DFSSM_GFIRST != 0>(gw + rep_off + tid * (KO / 2), GW, tg_g, v, P.sync + 3, 16u);
 #pragma unroll
       for (int b = 0; b < B; ++b)
 #pragma unroll

@@ -10,7 +10,8 @@
 
 namespace dfssm {
 
-constexpr int kScanThreads = 256;
+constexpr int kScanThreads = 512;
+constexpr int kScanRPW = DFSSM_HEADDIM / (kScanThreads / 32);  // state rows per warp
 constexpr int kScanMaxT = 64;  // tokens per scan launch (longer prompts run in chunks)
 
 // proj fp16 [B*T rows][n_in]: z [d_inner] | x [d_inner] | B [d_state] | C [d_state] | dt [nheads]
@@ -41,9 +42,10 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
   // state tile: first, so the HBM stream starts before anything else
   const int wid = tid >> 5, lane = tid & 31, n0 = lane * 4;
   float* hs = hstate + ((size_t)b * nheads + h) * (DFSSM_HEADDIM * DFSSM_DSTATE);
-  float4 hv[8];
+  float4 hv[kScanRPW];
 #pragma unroll
-  for (int r = 0; r < 8; ++r) hv[r] = __ldcs(reinterpret_cast<const float4*>(hs + (wid * 8 + r) * DFSSM_DSTATE + n0));
+  for (int r = 0; r < kScanRPW; ++r)
+    hv[r] = __ldcs(reinterpret_cast<const float4*>(hs + (wid * kScanRPW + r) * DFSSM_DSTATE + n0));
   const float Ah = -expf(A_log[h]), Dh = Dp[h], dtb = dt_bias[h];
   const __half* pb = proj + (size_t)b * T * n_in;
   const float* cs = conv_state + (size_t)b * 3 * d_xbc;
@@ -51,15 +53,45 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
     const int k = i / NC, c = i - k * NC;
     raw[c * TS + k] = cs[(size_t)k * d_xbc + chan(c)];
   }
-  for (int i = tid; i < NC * T; i += kScanThreads) {  // row t, channel c: contiguous in c
-    const int t = i / NC, c = i - t * NC;
-    raw[c * TS + 3 + t] = h2f(pb[(size_t)t * n_in + d_inner + chan(c)]);
-  }
-  for (int i = tid; i < T * DFSSM_HEADDIM; i += kScanThreads) {
-    const int t = i / DFSSM_HEADDIM, p = i - t * DFSSM_HEADDIM;
-    const float z = h2f(pb[(size_t)t * n_in + h * DFSSM_HEADDIM + p]);
-    const float sig = round_h(1.0f / (1.0f + expf(-z)));
-    zg[i] = round_h(z * sig);
+  // raw inputs and z by 16-byte loads, kU of them in flight per thread: a row t holds 8 units
+  // of this head's x channels, d_state/4 units of B and C, and 8 units of z
+  {
+    constexpr int kU = 4;
+    const int ux = DFSSM_HEADDIM / 8, ubc = 2 * d_state / 8, upr = ux + ubc + ux;  // units per row
+    const int nu = T * upr;
+    for (int u0 = tid; u0 < nu; u0 += kScanThreads * kU) {
+      uint4 v[kU];
+#pragma unroll
+      for (int j = 0; j < kU; ++j) {
+        const int u = u0 + j * kScanThreads;
+        if (u < nu) {
+          const int t = u / upr, k = u - t * upr;
+          const size_t col = k < ux ? (size_t)d_inner + h * DFSSM_HEADDIM + 8 * k
+                                    : (k < ux + ubc ? (size_t)2 * d_inner + 8 * (k - ux)
+                                                    : (size_t)h * DFSSM_HEADDIM + 8 * (k - ux - ubc));
+          v[j] = __ldcs(reinterpret_cast<const uint4*>(pb + (size_t)t * n_in + col));
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kU; ++j) {
+        const int u = u0 + j * kScanThreads;
+        if (u < nu) {
+          const int t = u / upr, k = u - t * upr;
+          const __half* hv8 = reinterpret_cast<const __half*>(&v[j]);
+          if (k < ux + ubc) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) raw[(8 * k + e) * TS + 3 + t] = h2f(hv8[e]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float z = h2f(hv8[e]);
+              const float sig = round_h(1.0f / (1.0f + expf(-z)));
+              zg[t * DFSSM_HEADDIM + 8 * (k - ux - ubc) + e] = round_h(z * sig);
+            }
+          }
+        }
+      }
+    }
   }
   for (int t = tid; t < T; t += kScanThreads) {
     const float dtv = log1pf(expf(h2f(pb[(size_t)t * n_in + d_inner + d_xbc + h]) + dtb));
@@ -67,14 +99,25 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
     abar[t] = expf(dtv * Ah);
   }
   __syncthreads();
-  for (int i = tid; i < NC * T; i += kScanThreads) {
-    const int t = i / NC, c = i - t * NC, ch = chan(c);
-    const float* rr = raw + c * TS + t;
-    const __half* cw = conv_w + ch * DFSSM_DCONV;
-    const float s0 = rr[0], s1 = rr[1], s2 = rr[2], v = rr[3];
-    const float o2 = s0 * h2f(cw[0]) + s1 * h2f(cw[1]) + s2 * h2f(cw[2]) + v * h2f(cw[3]) + h2f(conv_b[ch]);
-    const float sig = 1.0f / (1.0f + expf(-o2));
-    cvo[i] = h2f(f2h(o2 * sig));
+  // conv + SiLU: a thread owns a channel over a run of TL tokens and slides the 4-tap window
+  const int nseg = T >= 32 ? 4 : 1, TL = (T + nseg - 1) / nseg;
+  for (int item = tid; item < NC * nseg; item += kScanThreads) {
+    const int seg = item / NC, c = item - seg * NC, ch = chan(c);
+    const uint2 wv = *reinterpret_cast<const uint2*>(conv_w + ch * DFSSM_DCONV);
+    const __half* w4 = reinterpret_cast<const __half*>(&wv);
+    const float w0 = h2f(w4[0]), w1 = h2f(w4[1]), w2 = h2f(w4[2]), w3 = h2f(w4[3]), cb = h2f(conv_b[ch]);
+    const int t0 = seg * TL, t1 = min(T, t0 + TL);
+    const float* rr = raw + c * TS;
+    float s0 = rr[t0], s1 = rr[t0 + 1], s2 = rr[t0 + 2];
+    for (int t = t0; t < t1; ++t) {
+      const float v = rr[3 + t];
+      const float o2 = s0 * w0 + s1 * w1 + s2 * w2 + v * w3 + cb;
+      const float sig = 1.0f / (1.0f + expf(-o2));
+      cvo[t * NC + c] = h2f(f2h(o2 * sig));
+      s0 = s1;
+      s1 = s2;
+      s2 = v;
+    }
   }
   // conv state after the prompt: the last three raw inputs (B/C channels written by head 0)
   float* csw = conv_state + (size_t)b * 3 * d_xbc;
@@ -89,27 +132,44 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
     const float dtv = dts[t], Abar = abar[t];
     const float4 Bn = *reinterpret_cast<const float4*>(ct + DFSSM_HEADDIM + n0);
     const float4 Cn = *reinterpret_cast<const float4*>(ct + DFSSM_HEADDIM + d_state + n0);
-    float yv = 0.f;
+    float part[kScanRPW];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const float xv = ct[wid * 8 + r];
-      const float X = xv * dtv;
+    for (int r = 0; r < kScanRPW; ++r) {
+      const float X = ct[wid * kScanRPW + r] * dtv;
       float4 o;
       o.x = Abar * hv[r].x + X * Bn.x;
       o.y = Abar * hv[r].y + X * Bn.y;
       o.z = Abar * hv[r].z + X * Bn.z;
       o.w = Abar * hv[r].w + X * Bn.w;
       hv[r] = o;
-      const float part = warp_sum(Cn.x * o.x + Cn.y * o.y + Cn.z * o.z + Cn.w * o.w);
-      if (lane == r) yv = part + xv * Dh;
+      part[r] = Cn.x * o.x + Cn.y * o.y + Cn.z * o.z + Cn.w * o.w;
     }
-    if (lane < 8) {
-      const int pp = wid * 8 + lane;
-      gs[t * DFSSM_HEADDIM + pp] = f2h(h2f(f2h(yv)) * zg[t * DFSSM_HEADDIM + pp]);
+    // C.h of the warp's rows summed over the 32 lanes as a transposing butterfly: each exchange
+    // halves the values a lane holds, so kScanRPW rows cost kScanRPW - 1 + 5 - log2(kScanRPW)
+    // shuffles instead of 5 kScanRPW; lane ends with the sum of row `rw`
+    int rw = 0, off = 16;
+#pragma unroll
+    for (int n = kScanRPW; n > 1; n >>= 1, off >>= 1) {
+      const bool hi = (lane & off) != 0;
+#pragma unroll
+      for (int i = 0; i < n / 2; ++i) {
+        const float send = hi ? part[i] : part[i + n / 2];
+        const float keep = hi ? part[i + n / 2] : part[i];
+        part[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+      }
+      rw += hi ? n / 2 : 0;
+    }
+#pragma unroll
+    for (int o = off; o > 0; o >>= 1) part[0] += __shfl_xor_sync(0xffffffffu, part[0], o);
+    if ((lane & (2 * off - 1)) == 0) {  // one lane per row
+      const int pp = wid * kScanRPW + rw;
+      const float y = part[0] + ct[pp] * Dh;
+      gs[t * DFSSM_HEADDIM + pp] = f2h(h2f(f2h(y)) * zg[t * DFSSM_HEADDIM + pp]);
     }
   }
 #pragma unroll
-  for (int r = 0; r < 8; ++r) __stcs(reinterpret_cast<float4*>(hs + (wid * 8 + r) * DFSSM_DSTATE + n0), hv[r]);
+  for (int r = 0; r < kScanRPW; ++r)
+    __stcs(reinterpret_cast<float4*>(hs + (wid * kScanRPW + r) * DFSSM_DSTATE + n0), hv[r]);
   __syncthreads();
   for (int i = tid; i < T * DFSSM_HEADDIM / 2; i += kScanThreads) {
     const int t = i / (DFSSM_HEADDIM / 2), p2 = i - t * (DFSSM_HEADDIM / 2);
