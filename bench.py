@@ -13,6 +13,8 @@ above the 126 MB L2), so no explicit L2 flush is needed.
 Configs (synthetic weights of the stated shapes, seed 0):
   cfg0  2-layer 1.3B width, batch 1           cfg1  48-layer 1.3B, batch 1 (default)
   cfg2  48-layer 1.3B, batch 32               cfg4  64-layer 2.7B, batch 256 split over ranks
+  --prefill T  instead of decode steps, time K prompt prefills (reset + dfssm_prefill of a [batch, T]
+        random prompt; metric prompt tok/s)
   cfg3  isolated scaffold GEMM (1-bit x int8 -> int32, dfssm_scaffold_gemm) at the 1.3B in_proj and
         out_proj shapes for M in {1, 8, 32, 128, 512}; one JSON line with the sweep
 Multi-GPU: one process per GPU, each with a full weight replica and its own sequences;
@@ -281,6 +283,45 @@ def run_scaffold_bench(args, rank, world):
     print(json.dumps(line))
 
 
+def run_prefill_bench(args, cfg, m, batch, world, rank, local, dims):
+    """K timed prompt prefills (reset + dfssm_prefill of one [batch, T] prompt each), device time,
+    max over ranks; prompts of T > 64 tokens run in 64-token chunks."""
+    import torch
+    import torch.distributed as dist
+    T = args.prefill
+    prompt = torch.from_numpy(np.random.default_rng(1 + rank).integers(0, dims.vocab, (batch, T))).to(
+        device=f"cuda:{local}", dtype=torch.int32)
+    for _ in range(args.warmup):
+        m.reset_state()
+        m.prefill(prompt)
+    stream = torch.cuda.current_stream()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        m.reset_state()
+        m.prefill(prompt)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world, torch.device("cuda", local))
+    m.check_finite()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "prompt prefill tok/s", "value": batch * world * T * args.steps / (ms / 1e3), "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 x 1-bit -> int32 scaffold, fp16 activations, fp32 state",
+            "data": "synthetic (seeded random weights of the named shape and random prompts)",
+            "config": {"workload": args.config, "shape": cfg["shape"], "layers": cfg["layers"],
+                       "batch_per_gpu": batch, "prompt": T, "mode": m.mode}}))
+    m.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -292,6 +333,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--mode", default="auto", choices=["auto", "graph", "eager", "persistent"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill", type=int, default=0, metavar="T",
+                    help="time K prompt prefills of T tokens per sequence instead of decode steps")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -315,6 +358,11 @@ def main():
         run_scaffold_bench(args, rank, world)
         return
     if args.impl == "reference":
+        if args.prefill:
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference has no prompt prefill: its "
+                                  "drivers feed a prompt one decode step per token"}))
+            return
         run_reference_arm(args, cfg, rank, world)
         return
 
@@ -334,6 +382,9 @@ def main():
     m = DFSSMModel(w, device=f"cuda:{local}", batch_size=batch, mode=args.mode)
     del w
     stream = torch.cuda.current_stream()
+    if args.prefill:
+        run_prefill_bench(args, cfg, m, batch, world, rank, local, dims)
+        return
 
     # prompt + warm-up (untimed)
     m.reset_state()

@@ -1227,8 +1227,12 @@ int prefill_chunk(dfssm_engine* e, const PrefillBufs& P, int T, cudaStream_t s) 
   const RowBufs rb{P.xn, P.q, P.xs, P.qsum, P.t};
   embed_rows_kernel<<<R, 256, 0, s>>>(P.tok, e->Eq, e->Es, d.d_model, d.vocab, P.x);
   CHECK_LAUNCH();
-  const size_t sm = prefill_scan_smem(T, d.d_state);
-  CU(ensure_smem(reinterpret_cast<const void*>(prefill_scan_kernel), sm));
+  // two CTAs per (head, sequence) while one each would leave SMs idle (the B/C conv is repeated)
+  const int split = d.nheads * B < e->sm_count ? 2 : 1;
+  const size_t sm = prefill_scan_smem(T, d.d_state, split);
+  const void* scan = split == 2 ? reinterpret_cast<const void*>(prefill_scan_kernel<2>)
+                                : reinterpret_cast<const void*>(prefill_scan_kernel<1>);
+  CU(ensure_smem(scan, sm));
   int rc;
   for (int l = 0; l < d.n_layer; ++l) {
     const LayerW& L = e->layers[l];
@@ -1236,9 +1240,14 @@ int prefill_chunk(dfssm_engine* e, const PrefillBufs& P, int T, cudaStream_t s) 
     if ((rc = launch_mma<3>(L.in, R, P.q, P.qsum, P.xs, P.t, P.proj, d.n_in, nullptr, nullptr, nullptr, d.d_inner,
                             d.d_xbc, s, P.us)))
       return rc;
-    prefill_scan_kernel<<<dim3(d.nheads, B), kScanThreads, sm, s>>>(
-        P.proj, d.n_in, T, d.d_inner, d.d_state, d.nheads, L.conv_w, L.conv_b, L.dt_bias, L.A_log, L.Dp,
-        e->conv + (size_t)l * e->conv_layer, e->ssm + (size_t)l * e->ssm_layer, P.gated);
+    if (split == 2)
+      prefill_scan_kernel<2><<<dim3(d.nheads * 2, B), kScanThreads, sm, s>>>(
+          P.proj, d.n_in, T, d.d_inner, d.d_state, d.nheads, L.conv_w, L.conv_b, L.dt_bias, L.A_log, L.Dp,
+          e->conv + (size_t)l * e->conv_layer, e->ssm + (size_t)l * e->ssm_layer, P.gated);
+    else
+      prefill_scan_kernel<1><<<dim3(d.nheads, B), kScanThreads, sm, s>>>(
+          P.proj, d.n_in, T, d.d_inner, d.d_state, d.nheads, L.conv_w, L.conv_b, L.dt_bias, L.A_log, L.Dp,
+          e->conv + (size_t)l * e->conv_layer, e->ssm + (size_t)l * e->ssm_layer, P.gated);
     CHECK_LAUNCH();
     if ((rc = launch_prep(e, P.gated, d.d_inner, L.norm_w, 1, &L.out, s, Group{0, R}, rb))) return rc;
     if ((rc = launch_mma<1>(L.out, R, P.q, P.qsum, P.xs, P.t, P.x, d.d_model, nullptr, nullptr, nullptr, d.d_inner,
@@ -1260,7 +1269,7 @@ int dfssm_prefill(dfssm_engine* e, const int32_t* tokens_dev, int T, float* logi
   const int B = e->batch;
   const int Tc = T < kScanMaxT ? T : kScanMaxT;
   const bool batched = B * (T < Tc ? T : Tc) >= kMmaMinBatch && mma_rg(d.n_in, d.d_model) && mma_rg(d.d_model, d.d_inner) &&
-                       prefill_scan_smem(Tc, d.d_state) <= 227 * 1024;
+                       prefill_scan_smem(Tc, d.d_state, 1) <= 227 * 1024;
   if (!batched) {  // too few rows for the batched kernels: token by token through dfssm_step
     for (int t = 0; t < T; ++t) {
       CU(cudaMemcpy2DAsync(e->tokens, 4, tokens_dev + t, (size_t)T * 4, 4, B, cudaMemcpyDeviceToDevice, us));

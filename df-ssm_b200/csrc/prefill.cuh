@@ -11,37 +11,45 @@
 namespace dfssm {
 
 constexpr int kScanThreads = 512;
-constexpr int kScanRPW = DFSSM_HEADDIM / (kScanThreads / 32);  // state rows per warp
 constexpr int kScanMaxT = 64;  // tokens per scan launch (longer prompts run in chunks)
 
 // proj fp16 [B*T rows][n_in]: z [d_inner] | x [d_inner] | B [d_state] | C [d_state] | dt [nheads]
 // (row b*T + t).  Writes gated fp16 [B*T][d_inner]; updates this layer's conv state
 // [B][3][d_xbc] (tap-major) and SSM state [B][nheads][64][128].
+// Grid (nheads * SPLIT, B): CTA (h * SPLIT + part, b) owns channels p in [part * kScanRows,
+// +kScanRows) of head h, kScanRows = 64 / SPLIT; SPLIT = 2 when one CTA per (head, sequence) leaves
+// SMs idle and runs the conv of its x channels and of all B/C
+// channels (the B/C conv is repeated by every CTA of the sequence; head 0 part 0 stores its state).
 // Everything the token loop reads is staged in shared memory first, by coalesced row reads, so the
 // loop itself touches no global memory: raw conv inputs (channel-major, 3 taps + T), conv + SiLU
 // outputs (time-major, so a lane's 4 B/C values of one token are one conflict-free float4), the
 // SiLU(z) gate factors, softplus(dt) and exp(A dt) per token, and the gated outputs (written to HBM
 // as whole rows at the end).
+template <int SPLIT>
 __global__ void __launch_bounds__(kScanThreads)
 prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inner, int d_state, int nheads,
                     const __half* __restrict__ conv_w, const __half* __restrict__ conv_b,
                     const float* __restrict__ dt_bias, const float* __restrict__ A_log, const float* __restrict__ Dp,
                     float* __restrict__ conv_state, float* __restrict__ hstate, __half* __restrict__ gated) {
+  constexpr int kScanRows = DFSSM_HEADDIM / SPLIT;           // state rows (head channels) per CTA
+  constexpr int kScanRPW = kScanRows / (kScanThreads / 32);  // state rows per warp
   extern __shared__ float sm[];
-  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  const int h = blockIdx.x / SPLIT, part = blockIdx.x - h * SPLIT, b = blockIdx.y, tid = threadIdx.x;
+  const int c0 = h * DFSSM_HEADDIM + part * kScanRows;  // first head channel of this CTA
   const int d_xbc = d_inner + 2 * d_state;
-  const int NC = DFSSM_HEADDIM + 2 * d_state;  // this head's x channels, then all B and C channels
+  const int NC = kScanRows + 2 * d_state;  // this CTA's x channels, then all B and C channels
   const int TS = T + 3;
   float* raw = sm;                          // [NC][T + 3]: 3 taps of conv state, then the T raw inputs
   float* cvo = raw + NC * TS;               // [T][NC]: fp16-exact conv + SiLU outputs
-  float* zg = cvo + NC * T;                 // [T][64]: fp16-exact SiLU(z)
-  float* dts = zg + T * DFSSM_HEADDIM;      // [T]: softplus(dt + bias)
+  float* zg = cvo + NC * T;                 // [T][kScanRows]: fp16-exact SiLU(z)
+  float* dts = zg + T * kScanRows;          // [T]: softplus(dt + bias)
   float* abar = dts + T;                    // [T]: exp(A dt)
-  __half* gs = reinterpret_cast<__half*>(raw);  // [T][64] gated outputs (raw is dead by then)
-  auto chan = [&](int c) { return c < DFSSM_HEADDIM ? h * DFSSM_HEADDIM + c : d_inner + (c - DFSSM_HEADDIM); };
+  __half* gs = reinterpret_cast<__half*>(raw);  // [T][kScanRows] gated outputs (raw is dead by then)
+  auto chan = [&](int c) { return c < kScanRows ? c0 + c : d_inner + (c - kScanRows); };
   // state tile: first, so the HBM stream starts before anything else
   const int wid = tid >> 5, lane = tid & 31, n0 = lane * 4;
-  float* hs = hstate + ((size_t)b * nheads + h) * (DFSSM_HEADDIM * DFSSM_DSTATE);
+  float* hs = hstate + ((size_t)b * nheads + h) * (DFSSM_HEADDIM * DFSSM_DSTATE) +
+              (size_t)part * kScanRows * DFSSM_DSTATE;
   float4 hv[kScanRPW];
 #pragma unroll
   for (int r = 0; r < kScanRPW; ++r)
@@ -53,11 +61,12 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
     const int k = i / NC, c = i - k * NC;
     raw[c * TS + k] = cs[(size_t)k * d_xbc + chan(c)];
   }
-  // raw inputs and z by 16-byte loads, kU of them in flight per thread: a row t holds 8 units
-  // of this head's x channels, d_state/4 units of B and C, and 8 units of z
+  // raw inputs and z by 16-byte loads, kU of them in flight per thread: a row t holds ux units of
+  // this CTA's x channels, d_state/4 units of B and C, and ux units of z
   {
     constexpr int kU = 4;
-    const int ux = DFSSM_HEADDIM / 8, ubc = 2 * d_state / 8, upr = ux + ubc + ux;  // units per row
+    constexpr int ux = kScanRows / 8;
+    const int ubc = 2 * d_state / 8, upr = ux + ubc + ux;  // units per row
     const int nu = T * upr;
     for (int u0 = tid; u0 < nu; u0 += kScanThreads * kU) {
       uint4 v[kU];
@@ -66,9 +75,9 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
         const int u = u0 + j * kScanThreads;
         if (u < nu) {
           const int t = u / upr, k = u - t * upr;
-          const size_t col = k < ux ? (size_t)d_inner + h * DFSSM_HEADDIM + 8 * k
+          const size_t col = k < ux ? (size_t)d_inner + c0 + 8 * k
                                     : (k < ux + ubc ? (size_t)2 * d_inner + 8 * (k - ux)
-                                                    : (size_t)h * DFSSM_HEADDIM + 8 * (k - ux - ubc));
+                                                    : (size_t)c0 + 8 * (k - ux - ubc));
           v[j] = __ldcs(reinterpret_cast<const uint4*>(pb + (size_t)t * n_in + col));
         }
       }
@@ -86,7 +95,7 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
             for (int e = 0; e < 8; ++e) {
               const float z = h2f(hv8[e]);
               const float sig = round_h(1.0f / (1.0f + expf(-z)));
-              zg[t * DFSSM_HEADDIM + 8 * (k - ux - ubc) + e] = round_h(z * sig);
+              zg[t * kScanRows + 8 * (k - ux - ubc) + e] = round_h(z * sig);
             }
           }
         }
@@ -119,20 +128,20 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
       s2 = v;
     }
   }
-  // conv state after the prompt: the last three raw inputs (B/C channels written by head 0)
+  // conv state after the prompt: the last three raw inputs (B/C channels written by one CTA)
   float* csw = conv_state + (size_t)b * 3 * d_xbc;
   for (int i = tid; i < NC * 3; i += kScanThreads) {
     const int k = i / NC, c = i - k * NC;
-    if (c >= DFSSM_HEADDIM && h != 0) continue;
+    if (c >= kScanRows && blockIdx.x != 0) continue;
     csw[(size_t)k * d_xbc + chan(c)] = raw[c * TS + T + k];
   }
   __syncthreads();
   for (int t = 0; t < T; ++t) {
     const float* ct = cvo + t * NC;
     const float dtv = dts[t], Abar = abar[t];
-    const float4 Bn = *reinterpret_cast<const float4*>(ct + DFSSM_HEADDIM + n0);
-    const float4 Cn = *reinterpret_cast<const float4*>(ct + DFSSM_HEADDIM + d_state + n0);
-    float part[kScanRPW];
+    const float4 Bn = *reinterpret_cast<const float4*>(ct + kScanRows + n0);
+    const float4 Cn = *reinterpret_cast<const float4*>(ct + kScanRows + d_state + n0);
+    float part_[kScanRPW];
 #pragma unroll
     for (int r = 0; r < kScanRPW; ++r) {
       const float X = ct[wid * kScanRPW + r] * dtv;
@@ -142,45 +151,44 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
       o.z = Abar * hv[r].z + X * Bn.z;
       o.w = Abar * hv[r].w + X * Bn.w;
       hv[r] = o;
-      part[r] = Cn.x * o.x + Cn.y * o.y + Cn.z * o.z + Cn.w * o.w;
+      part_[r] = Cn.x * o.x + Cn.y * o.y + Cn.z * o.z + Cn.w * o.w;
     }
     // C.h of the warp's rows summed over the 32 lanes as a transposing butterfly: each exchange
     // halves the values a lane holds, so kScanRPW rows cost kScanRPW - 1 + 5 - log2(kScanRPW)
-    // shuffles instead of 5 kScanRPW; lane ends with the sum of row `rw`
+    // shuffles instead of 5 kScanRPW; the lane ends with the sum of row `rw`
     int rw = 0, off = 16;
 #pragma unroll
     for (int n = kScanRPW; n > 1; n >>= 1, off >>= 1) {
       const bool hi = (lane & off) != 0;
 #pragma unroll
       for (int i = 0; i < n / 2; ++i) {
-        const float send = hi ? part[i] : part[i + n / 2];
-        const float keep = hi ? part[i + n / 2] : part[i];
-        part[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        const float send = hi ? part_[i] : part_[i + n / 2];
+        const float keep = hi ? part_[i + n / 2] : part_[i];
+        part_[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
       }
       rw += hi ? n / 2 : 0;
     }
 #pragma unroll
-    for (int o = off; o > 0; o >>= 1) part[0] += __shfl_xor_sync(0xffffffffu, part[0], o);
+    for (int o = off; o > 0; o >>= 1) part_[0] += __shfl_xor_sync(0xffffffffu, part_[0], o);
     if ((lane & (2 * off - 1)) == 0) {  // one lane per row
       const int pp = wid * kScanRPW + rw;
-      const float y = part[0] + ct[pp] * Dh;
-      gs[t * DFSSM_HEADDIM + pp] = f2h(h2f(f2h(y)) * zg[t * DFSSM_HEADDIM + pp]);
+      const float y = part_[0] + ct[pp] * Dh;
+      gs[t * kScanRows + pp] = f2h(h2f(f2h(y)) * zg[t * kScanRows + pp]);
     }
   }
 #pragma unroll
   for (int r = 0; r < kScanRPW; ++r)
     __stcs(reinterpret_cast<float4*>(hs + (wid * kScanRPW + r) * DFSSM_DSTATE + n0), hv[r]);
   __syncthreads();
-  for (int i = tid; i < T * DFSSM_HEADDIM / 2; i += kScanThreads) {
-    const int t = i / (DFSSM_HEADDIM / 2), p2 = i - t * (DFSSM_HEADDIM / 2);
-    reinterpret_cast<__half2*>(gated + ((size_t)b * T + t) * d_inner + h * DFSSM_HEADDIM)[p2] =
-        reinterpret_cast<const __half2*>(gs)[i];
+  for (int i = tid; i < T * kScanRows / 2; i += kScanThreads) {
+    const int t = i / (kScanRows / 2), p2 = i - t * (kScanRows / 2);
+    reinterpret_cast<__half2*>(gated + ((size_t)b * T + t) * d_inner + c0)[p2] = reinterpret_cast<const __half2*>(gs)[i];
   }
 }
 
-inline size_t prefill_scan_smem(int T, int d_state) {
-  const size_t nc = DFSSM_HEADDIM + 2 * d_state;
-  return (nc * (2 * T + 3) + (size_t)T * DFSSM_HEADDIM + 2 * T) * sizeof(float);
+inline size_t prefill_scan_smem(int T, int d_state, int split) {
+  const size_t rows = DFSSM_HEADDIM / split, nc = rows + 2 * d_state;
+  return (nc * (2 * T + 3) + (size_t)T * rows + 2 * T) * sizeof(float);
 }
 
 // x rows b*T + t = the embedding of tokens[b][t] (fp16, as embed_kernel).

@@ -266,7 +266,10 @@ def test_engine_sampling_is_reproducible_and_greedy_unchanged(mode):
     np.testing.assert_array_equal(m.generate(10, prompt=p, verbose=False), greedy)
 
 
-@pytest.mark.parametrize("B,T,mode", [(2, 12, "graph"), (2, 70, "persistent"), (1, 4, "graph"), (9, 3, "graph")])
+# (10, 5): 16 heads x 10 sequences fill the 148 SMs, so the scan runs one CTA per (head, sequence);
+# the smaller cases split each head over two CTAs
+@pytest.mark.parametrize("B,T,mode", [(2, 12, "graph"), (2, 70, "persistent"), (1, 4, "graph"), (9, 3, "graph"),
+                                      (10, 5, "graph")])
 def test_prefill_matches_token_by_token(B, T, mode):
     """dfssm_prefill (batched projections + per-head scan over the prompt, 64-token chunks) leaves
     the same state and next token as feeding the prompt one dfssm_step at a time, within the
