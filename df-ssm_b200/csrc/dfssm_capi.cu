@@ -204,7 +204,7 @@ EncodeTiledFn encode_tiled() {
 }
 
 // Tensor map over the activation rows q [rows][K] int8: box 128 bytes x NT rows, 128-byte swizzle,
-// rows past `rows` read as zeros.  False if it cannot be made (then the threads stage B).
+// rows past `rows` read as zeros.  False if it cannot be made.
 bool make_q_map(CUtensorMap* m, const int8_t* q, int rows, int K, int NT) {
   const EncodeTiledFn fn = encode_tiled();
   if (!fn || (reinterpret_cast<uintptr_t>(q) & 15) || K % 128) return false;
@@ -214,6 +214,22 @@ bool make_q_map(CUtensorMap* m, const int8_t* q, int rows, int K, int NT) {
   const cuuint32_t estr[2] = {1u, 1u};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Returns -1 (nothing launched) when the tcgen05 kernel cannot take this call: no tensor map (the
+// driver entry point is missing, or misaligned operands); the caller then uses the mma.sync kernel.
+// Tensor map over packed 1-bit weights [N rows][K / 8 bytes]: box 16 bytes x 128 rows, no swizzle,
+// rows past N read as zeros.
+bool make_w_map(CUtensorMap* m, const uint32_t* bits, int N, int K) {
+  const EncodeTiledFn fn = encode_tiled();
+  if (!fn || (reinterpret_cast<uintptr_t>(bits) & 15) || K % 128) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)(K / 8), (cuuint64_t)N};
+  const cuuint64_t strides[1] = {(cuuint64_t)(K / 8)};
+  const cuuint32_t box[2] = {16u, 128u};
+  const cuuint32_t estr[2] = {1u, 1u};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint32_t*>(bits), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -231,28 +247,19 @@ int launch_umma(const ProjW& p, int B, const int8_t* q, const int* qsum, const _
     return e ? atoi(e) : 160;
   }();
   while (can_split && tiles * ks * 2 <= target && (p.K / (2 * ks)) % kUmmaKC == 0 && ks < 16) ks *= 2;
-  if (MODE == 2 && ks > 1) CU(cudaMemsetAsync(out, 0, (size_t)B * ld_out * 4, s));
   const size_t sm = proj_umma_smem(NT);
+  CUtensorMap tm, tw;
+  memset(&tm, 0, sizeof(tm));
+  memset(&tw, 0, sizeof(tw));
+  if (!make_q_map(&tm, q, B, p.K, NT) || !make_w_map(&tw, p.bits, p.N, p.K)) return -1;
+  if (MODE == 2 && ks > 1) CU(cudaMemsetAsync(out, 0, (size_t)B * ld_out * 4, s));
   unsigned* err = nullptr;
   CU(umma_err_word(&err));
-  CUtensorMap tm;
-  memset(&tm, 0, sizeof(tm));
-  static const bool tma_on = [] {
-    const char* e = getenv("DFSSM_UMMA_TMA");
-    return !e || atoi(e) != 0;
-  }();
   const dim3 grid((p.N + 127) / 128, (B + NT - 1) / NT, ks);
-  if (tma_on && make_q_map(&tm, q, B, p.K, NT)) {
-    CU(ensure_smem(reinterpret_cast<const void*>(proj_umma_kernel<MODE, NT, true>), sm));
-    proj_umma_kernel<MODE, NT, true><<<grid, kUmmaThreads, sm, s>>>(
-        tm, p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out), ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc,
-        ks, us.acc, us.cnt, err);
-  } else {
-    CU(ensure_smem(reinterpret_cast<const void*>(proj_umma_kernel<MODE, NT, false>), sm));
-    proj_umma_kernel<MODE, NT, false><<<grid, kUmmaThreads, sm, s>>>(
-        tm, p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out), ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc,
-        ks, us.acc, us.cnt, err);
-  }
+  CU(ensure_smem(reinterpret_cast<const void*>(proj_umma_kernel<MODE, NT>), sm));
+  proj_umma_kernel<MODE, NT><<<grid, kUmmaThreads, sm, s>>>(tm, tw, p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out),
+                                                             ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, ks,
+                                                             us.acc, us.cnt, err);
   CHECK_LAUNCH();
   return DFSSM_OK;
 }
@@ -262,9 +269,10 @@ int launch_mma(const ProjW& p, int B, const int8_t* q, const int* qsum, const __
                int ld_out, float* conv_state, const __half* conv_w, const __half* conv_b, int d_inner, int d_xbc,
                cudaStream_t s, UmmaScratch us = UmmaScratch{}) {
   if (B >= umma_min_batch() && p.K % kUmmaKC == 0) {  // tcgen05 path
-    if (B >= 128) return launch_umma<MODE, 128>(p, B, q, qsum, xs, t, out, ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, s, us);
-    if (B >= 64) return launch_umma<MODE, 64>(p, B, q, qsum, xs, t, out, ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, s, us);
-    return launch_umma<MODE, 32>(p, B, q, qsum, xs, t, out, ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, s, us);
+    const int rc = B >= 128 ? launch_umma<MODE, 128>(p, B, q, qsum, xs, t, out, ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, s, us)
+                 : B >= 64  ? launch_umma<MODE, 64>(p, B, q, qsum, xs, t, out, ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, s, us)
+                            : launch_umma<MODE, 32>(p, B, q, qsum, xs, t, out, ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, s, us);
+    if (rc != -1) return rc;  // -1: not taken, fall through to mma.sync
   }
   const int RG = mma_rg(p.N, p.K);
   const size_t sm = proj_mma_smem(p.K, RG);

@@ -9,13 +9,17 @@
 //   B (activations): the permuted int8 q rows, as s8.
 //   D (s32): sum over k of mask * q; the signed product is 2 D - sum_k q, as in the GEMV paths,
 //     so the int32 result equals torch._int_mm on the +-1 weights bit for bit.
-// Both operands use the K-major, no-swizzle canonical layout of 8-row x 16-byte core matrices:
-// a row group's 16 core matrices along the chunk are contiguous (leading-byte offset 128 B) and
-// row groups follow at 2 KB (stride-byte offset).  Two chunk buffers: threads fill one while the
-// tensor core reads the other; an MMA batch signals its buffer free through tcgen05.commit on an
-// mbarrier.  The epilogue reads D with tcgen05.ld (warp w and w + 4 own TMEM lanes 32(w % 4)..,
-// i.e. output rows; each thread holds its row's dequant/LoRA/conv operands in registers) and
-// runs the same per-element arithmetic as proj_mma_kernel.
+// Both operands use the K-major 128-byte-swizzled layout (8-row atoms of 1 KB; 16-byte unit u of
+// row r sits at unit u ^ (r % 8)), one 128-byte row per K chunk.  Data movement per CTA:
+//   - per K chunk, one ring slot receives by TMA the activation tile (NT rows x 128 bytes, tensor
+//     map over q, 128-byte swizzle) and the weight rows' packed bits (128 rows x 16 bytes, tensor
+//     map over the bits, no swizzle) on one mbarrier; the ring is kUmmaSB slots deep and chunks are
+//     issued kUmmaSB - 1 ahead of the MMAs that read them;
+//   - the threads expand a chunk's bits into the u8 masks (shared to shared) in one of two A buffers.
+// tcgen05.commit of chunk c's MMAs on an mbarrier frees its A buffer and ring slot.  The epilogue
+// reads D with tcgen05.ld (warp w and w + 4 own TMEM lanes 32(w % 4).., i.e. output rows; each
+// thread holds its row's dequant/LoRA/conv operands in registers) and runs the same per-element
+// arithmetic as proj_mma_kernel.
 #pragma once
 #include <cuda.h>  // CUtensorMap (the map is encoded on the host through the driver entry point)
 
@@ -30,6 +34,8 @@ constexpr int kUmmaThreads = 256;
 constexpr int kUmmaKC = DFSSM_UMMA_KC;  // K bytes per chunk (KC / 32 MMAs of K = 32)
 constexpr int kUmmaMinBatch = 64;   // batches below this use proj_mma_kernel (mma.sync)
 constexpr int kUmmaSpin = 1 << 22;  // bound of every mbarrier wait
+constexpr int kUmmaSB = 3;          // ring depth (chunks in flight)
+constexpr int kUmmaRawBytes = 128 * kUmmaKC / 8;  // one chunk of the 128 weight rows' bits
 
 __device__ __forceinline__ uint64_t umma_sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout = 0) {
   // start address, leading / stride byte offsets (16-byte units), descriptor version 1
@@ -45,7 +51,8 @@ __device__ __forceinline__ bool umma_wait(uint64_t* bar, unsigned parity) {
 }
 
 inline size_t proj_umma_smem(int NT) {
-  return 1024 + (size_t)2 * (128 + NT) * kUmmaKC + 2 * NT * 4 + NT * DFSSM_RANK * 4;  // + base alignment
+  return 1024 + (size_t)2 * 128 * kUmmaKC + (size_t)kUmmaSB * (NT * kUmmaKC + kUmmaRawBytes) + 2 * NT * 4 +
+         NT * DFSSM_RANK * 4;  // + base alignment
 }
 
 // MODE as proj_mma_kernel: 0 in_proj + conv1d, 1 out_proj + residual, 2 raw int32, 3 plain.
@@ -55,46 +62,46 @@ inline size_t proj_umma_smem(int NT) {
 // by the caller), else into ws [B][N] int32 with a per-tile counter cnt, and the last CTA of the
 // tile runs the epilogue and clears its part of ws and its counter.  err: set to 1 if a wait ran
 // out.
-// TMAB: the activation tiles arrive by TMA (tensor map tmq over q [B][K] int8, box 128 bytes x NT
-// rows, 128-byte swizzle; rows past B read as zeros) and both operands use the 128-byte-swizzled
-// K-major layout (8-row atoms of 1 KB, 16-byte unit u of row r at unit u ^ (r % 8)); otherwise the
-// threads stage them in the no-swizzle core-matrix layout.
-template <int MODE, int NT, bool TMAB>
+// tmq: tensor map over q [B][K] int8, box 128 bytes x NT rows, 128-byte swizzle (rows past B read
+// as zeros).  tmw: tensor map over the packed bits [N][K / 8] bytes, box 16 bytes x 128 rows, no
+// swizzle (rows past N read as zeros).  K / ksplit is a multiple of 128.
+template <int MODE, int NT>
 __global__ void __launch_bounds__(kUmmaThreads, 1)
-proj_umma_kernel(const __grid_constant__ CUtensorMap tmq, ProjW p, const int8_t* __restrict__ q,
+proj_umma_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmw, ProjW p, const int8_t* __restrict__ q,
                  const int* __restrict__ qsum, const __half* __restrict__ xs,
                  const __half* __restrict__ t, int B, __half* __restrict__ out, int ld_out,
                  float* __restrict__ conv_state, const __half* __restrict__ conv_w, const __half* __restrict__ conv_b,
                  int d_inner, int d_xbc, int ksplit, int* __restrict__ ws, unsigned* __restrict__ cnt,
                  unsigned* __restrict__ err) {
-  constexpr int ABYTES = 128 * kUmmaKC, BBYTES = NT * kUmmaKC, SBO = kUmmaKC / 16 * 128;
-  constexpr int WPR = kUmmaKC / 32, CPR = kUmmaKC / 16;  // words / 16-byte units per row and chunk
+  static_assert(kUmmaKC == 128, "the swizzled layout holds one 128-byte row per chunk");
+  constexpr int ABYTES = 128 * kUmmaKC, BBYTES = NT * kUmmaKC;
+  constexpr int WPR = kUmmaKC / 32;  // bit words per row and chunk
   extern __shared__ __align__(16) unsigned char smem_raw[];
   // 1 KB-aligned base (the 128-byte swizzle atoms and TMA destinations need it)
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  static_assert(!TMAB || kUmmaKC == 128, "the swizzled layout holds one 128-byte row per chunk");
-  // buffer k: A at smem + k (ABYTES + BBYTES), B right after it
-  auto sA = [&](int k) { return smem + k * (ABYTES + BBYTES); };
-  auto sB = [&](int k) { return smem + k * (ABYTES + BBYTES) + ABYTES; };
-  float* e_xs = reinterpret_cast<float*>(smem + 2 * (ABYTES + BBYTES));  // [NT]
-  int* e_qsum = reinterpret_cast<int*>(e_xs + NT);                         // [NT]
-  float* e_t = reinterpret_cast<float*>(e_qsum + NT);                      // [NT][16]
-  __shared__ uint64_t bars[2];
-  __shared__ uint64_t fulls[2];  // TMAB: the B tile of a buffer has landed
+  const int N = p.N, K = p.K;
+  const int klen = K / ksplit, kbeg = blockIdx.z * klen, nch = klen / kUmmaKC;
+  auto sA = [&](int k) { return smem + k * ABYTES; };                          // 2 mask buffers
+  auto sB = [&](int k) { return smem + 2 * ABYTES + k * BBYTES; };              // ring: activation tiles
+  auto sW = [&](int k) { return smem + 2 * ABYTES + kUmmaSB * BBYTES + k * kUmmaRawBytes; };  // ring: bits
+  float* e_xs = reinterpret_cast<float*>(sW(kUmmaSB));                           // [NT]
+  int* e_qsum = reinterpret_cast<int*>(e_xs + NT);                               // [NT]
+  float* e_t = reinterpret_cast<float*>(e_qsum + NT);                            // [NT][16]
+  __shared__ uint64_t mbars[kUmmaSB];  // MMAs of the chunk in slot s complete
+  __shared__ uint64_t fulls[kUmmaSB];  // activation tile and weight bits of slot s landed
   __shared__ uint32_t s_tmem;
   __shared__ int s_last;
   const int tid = threadIdx.x, wid = tid >> 5, lane = tid & 31;
-  const int N = p.N, K = p.K, W = K >> 5;
   const int row0 = blockIdx.x * 128, b0 = blockIdx.y * NT, nb = min(NT, B - b0);
   if (wid == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)), "r"(NT));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
-    mbar_init(&fulls[0], 1);
-    mbar_init(&fulls[1], 1);
+    for (int i = 0; i < kUmmaSB; ++i) {
+      mbar_init(&mbars[i], 1);
+      mbar_init(&fulls[i], 1);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   // per-column operands of this batch tile
@@ -111,124 +118,75 @@ proj_umma_kernel(const __grid_constant__ CUtensorMap tmq, ProjW p, const int8_t*
   const uint32_t tmem = s_tmem;
   const uint32_t idesc = (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(NT >> 3) << 17) | ((128u >> 4) << 24);
 
-  // A chunk: 128 rows x WPR words; B chunk: NT rows x CPR 16-byte units.  A chunk's global loads
-  // go to registers one chunk ahead of its shared-memory stores, so their latency overlaps the
-  // tensor core working on the previous chunk.
-  constexpr int AW = 128 * WPR / kUmmaThreads;  // words per thread
-  constexpr int BU = NT * CPR / kUmmaThreads;   // 16-byte units per thread
-  uint32_t rw[AW];
-  uint4 rv[BU];
-  auto load = [&](int kc) {
-#pragma unroll
-    for (int u = 0; u < AW; ++u) {
-      const int i = tid + u * kUmmaThreads, r = i / WPR, j = i - r * WPR;
-      rw[u] = __ldg(p.bits + (size_t)min(row0 + r, N - 1) * W + (kc >> 5) + j);
-    }
-    if (!TMAB)
-#pragma unroll
-      for (int u = 0; u < BU; ++u) {
-        const int i = tid + u * kUmmaThreads, b = i / CPR, c = i - b * CPR;
-        rv[u] = __ldg(reinterpret_cast<const uint4*>(q + (size_t)(b0 + min(b, nb - 1)) * K + kc) + c);
-      }
+  auto issue = [&](int c) {  // thread 0: chunk c's activation tile and weight bits into slot c % kUmmaSB
+    const int sl = c % kUmmaSB, kc = kbeg + c * kUmmaKC;
+    mbar_expect_tx(&fulls[sl], (unsigned)(BBYTES + kUmmaRawBytes));
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(sB(sl))),
+        "l"(reinterpret_cast<uint64_t>(&tmq)), "r"(kc), "r"(b0), "r"(smem_u32(&fulls[sl]))
+        : "memory");
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(sW(sl))),
+        "l"(reinterpret_cast<uint64_t>(&tmw)), "r"(kc >> 3), "r"(row0), "r"(smem_u32(&fulls[sl]))
+        : "memory");
   };
-  auto store = [&](int buf) {
+  if (tid == 0)
+    for (int c = 0; c < kUmmaSB && c < nch; ++c) issue(c);
+  // chunk c's masks into A buffer c & 1: thread i expands word j = i % WPR of row i / WPR (+64)
+  auto expand = [&](int c) {
+    const unsigned char* raw = sW(c % kUmmaSB);
 #pragma unroll
-    for (int u = 0; u < AW; ++u) {
+    for (int u = 0; u < 128 * WPR / kUmmaThreads; ++u) {
       const int i = tid + u * kUmmaThreads, r = i / WPR, j = i - r * WPR;
-      const uint32_t x = rw[u];
+      const uint32_t x = *reinterpret_cast<const uint32_t*>(raw + r * (kUmmaKC / 8) + 4 * j);
       const uint4 lo = make_uint4(x & 0x01010101u, (x >> 1) & 0x01010101u, (x >> 2) & 0x01010101u,
                                   (x >> 3) & 0x01010101u);
       const uint4 hi = make_uint4((x >> 4) & 0x01010101u, (x >> 5) & 0x01010101u, (x >> 6) & 0x01010101u,
                                   (x >> 7) & 0x01010101u);
-      if (TMAB) {  // units 2j, 2j + 1 of row r, swizzled
-        unsigned char* rowp = sA(buf) + (r >> 3) * 1024 + (r & 7) * 128;
-        *reinterpret_cast<uint4*>(rowp + (((2 * j) ^ (r & 7)) << 4)) = lo;
-        *reinterpret_cast<uint4*>(rowp + (((2 * j + 1) ^ (r & 7)) << 4)) = hi;
-      } else {
-        unsigned char* dst = sA(buf) + (r >> 3) * SBO + (2 * j) * 128 + (r & 7) * 16;
-        *reinterpret_cast<uint4*>(dst) = lo;
-        *reinterpret_cast<uint4*>(dst + 128) = hi;
-      }
+      unsigned char* rowp = sA(c & 1) + (r >> 3) * 1024 + (r & 7) * 128;  // units 2j, 2j + 1, swizzled
+      *reinterpret_cast<uint4*>(rowp + (((2 * j) ^ (r & 7)) << 4)) = lo;
+      *reinterpret_cast<uint4*>(rowp + (((2 * j + 1) ^ (r & 7)) << 4)) = hi;
     }
-    if (!TMAB)
-#pragma unroll
-      for (int u = 0; u < BU; ++u) {
-        const int i = tid + u * kUmmaThreads, b = i / CPR, c = i - b * CPR;
-        *reinterpret_cast<uint4*>(sB(buf) + (b >> 3) * SBO + c * 128 + (b & 7) * 16) = rv[u];
-      }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
   };
-
-  const int klen = K / ksplit, kbeg = blockIdx.z * klen;
-  const int nch = klen / kUmmaKC;
-  bool ok = true;
-  unsigned ph0 = 0u, ph1 = 0u;  // next phase to wait for on bars[0] / bars[1]
-  auto wait_buf = [&](int k) {
-    const bool r = umma_wait(&bars[k], k ? ph1 : ph0);
-    if (k) ph1 ^= 1u;
-    else ph0 ^= 1u;
-    return r;
-  };
-  unsigned fph0 = 0u, fph1 = 0u;  // TMAB: next phase of fulls[0] / fulls[1]
-  auto issue_b = [&](int kc, int buf) {  // thread 0: the B tile of chunk kc into buffer buf
-    if (TMAB && tid == 0) {
-      mbar_expect_tx(&fulls[buf], (unsigned)BBYTES);
-      asm volatile(
-          "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-              smem_u32(sB(buf))),
-          "l"(reinterpret_cast<uint64_t>(&tmq)), "r"(kc), "r"(b0), "r"(smem_u32(&fulls[buf]))
-          : "memory");
-    }
-  };
-  issue_b(kbeg, 0);
-  load(kbeg);
-  store(0);
-  if (nch > 1) {
-    issue_b(kbeg + kUmmaKC, 1);
-    load(kbeg + kUmmaKC);
-  }
+  auto slot_par = [](int c) { return (unsigned)((c / kUmmaSB) & 1); };
+  bool ok = umma_wait(&fulls[0], 0u);
+  expand(0);
   for (int c = 0; c < nch; ++c) {
-    const int buf = c & 1;
-    __syncthreads();
+    const int sl = c % kUmmaSB;
+    __syncthreads();  // chunk c's masks are stored
     asm volatile("tcgen05.fence::after_thread_sync;");
     if (tid == 0) {
-      if (TMAB) {  // the chunk's B tile
-        ok = umma_wait(&fulls[buf], buf ? fph1 : fph0) && ok;
-        if (buf) fph1 ^= 1u;
-        else fph0 ^= 1u;
-      }
+      // chunk c's activation tile (its slot's barrier completed before expand(c) read the bits)
 #pragma unroll
-      for (int s = 0; s < kUmmaKC / 32; ++s) {
-        // no swizzle: the K step is 2 core matrices (256 B); swizzled: 32 bytes along the 128-byte row
-        const uint64_t da = TMAB ? umma_sdesc(smem_u32(sA(buf)) + s * 32, 16, 1024, 2)
-                                 : umma_sdesc(smem_u32(sA(buf)) + s * 256, 128, SBO);
-        const uint64_t db = TMAB ? umma_sdesc(smem_u32(sB(buf)) + s * 32, 16, 1024, 2)
-                                 : umma_sdesc(smem_u32(sB(buf)) + s * 256, 128, SBO);
-        const uint32_t accum = (c > 0 || s > 0) ? 1u : 0u;
+      for (int k = 0; k < kUmmaKC / 32; ++k) {  // K = 32 per MMA: 32 bytes along the 128-byte row
+        const uint64_t da = umma_sdesc(smem_u32(sA(c & 1)) + k * 32, 16, 1024, 2);
+        const uint64_t db = umma_sdesc(smem_u32(sB(sl)) + k * 32, 16, 1024, 2);
+        const uint32_t accum = (c > 0 || k > 0) ? 1u : 0u;
         asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
                      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem),
                      "l"(da), "l"(db), "r"(idesc), "r"(accum));
       }
       asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                       smem_u32(&bars[buf]))
+                       smem_u32(&mbars[sl]))
                    : "memory");
     }
+    if (c >= 1) {
+      // chunk c - 1's MMAs are done: its A buffer (that of chunk c + 1) and its ring slot (that of
+      // chunk c - 1 + kUmmaSB) are free
+      const int pc = c - 1;
+      ok = umma_wait(&mbars[pc % kUmmaSB], slot_par(pc)) && ok;
+      if (tid == 0 && pc + kUmmaSB < nch) issue(pc + kUmmaSB);
+    }
     if (c + 1 < nch) {
-      // the other buffer was last read by the MMAs of chunk c - 1
-      if (c >= 1) {
-        ok = wait_buf(buf ^ 1) && ok;
-        issue_b(kbeg + (c + 1) * kUmmaKC, buf ^ 1);
-      }
-      store(buf ^ 1);
-      if (c + 2 < nch) load(kbeg + (c + 2) * kUmmaKC);
+      ok = umma_wait(&fulls[(c + 1) % kUmmaSB], slot_par(c + 1)) && ok;
+      expand(c + 1);
     }
   }
   // the last chunk's MMAs (and with them all earlier ones) complete
-  {
-    const int lb = (nch - 1) & 1;
-    if (nch >= 2) ok = wait_buf(lb ^ 1) && ok;  // chunk nch - 2, not yet waited for
-    ok = wait_buf(lb) && ok;
-  }
+  ok = umma_wait(&mbars[(nch - 1) % kUmmaSB], (unsigned)(((nch - 1) / kUmmaSB) & 1)) && ok;
   asm volatile("tcgen05.fence::after_thread_sync;");
   if (!ok && tid == 0) atomicOr(err, 1u);
   // warp w and w + 4 share TMEM lanes 32 (w % 4)..: thread = output row lr, w < 4 takes the
