@@ -660,28 +660,41 @@ lm_head_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, int 
 #pragma unroll
       for (int b = 0; b < kHeadBT; ++b) acc[b] = 0.f;
       const uint4* er = reinterpret_cast<const uint4*>(Eq + (size_t)v * d);
-      for (int c = lane; c < C; c += 32) {
-        const uint4 ev = ldg_stream(er + c);
-        float e[16];
-        const unsigned w4[4] = {ev.x ^ 0x80808080u, ev.y ^ 0x80808080u, ev.z ^ 0x80808080u, ev.w ^ 0x80808080u};
+      // four 16-byte units per lane in flight (d = 2048 is one group); the sum runs over the
+      // units in the same order as one at a time
+      for (int cg = 0; cg < C; cg += 32 * 4) {
+        uint4 evs[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int g = 0; g < 4; ++g) {
+          const int c = cg + lane + 32 * g;
+          if (c < C) evs[g] = ldg_stream(er + c);
+        }
 #pragma unroll
-          for (int i = 0; i < 4; ++i) e[j * 4 + i] = i8_to_f(w4[j], i);
+        for (int g = 0; g < 4; ++g) {
+          const int c = cg + lane + 32 * g;
+          if (c >= C) break;
+          const uint4 ev = evs[g];
+          float e[16];
+          const unsigned w4[4] = {ev.x ^ 0x80808080u, ev.y ^ 0x80808080u, ev.z ^ 0x80808080u, ev.w ^ 0x80808080u};
 #pragma unroll
-        for (int b = 0; b < kHeadBT; ++b) {
-          if (b < nb) {
-            const float4* xv = reinterpret_cast<const float4*>(sx + b * d + c * 16);
-            float a = acc[b];
+          for (int j = 0; j < 4; ++j)
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const float4 xx = xv[u];
-              a = fmaf(e[4 * u + 0], xx.x, a);
-              a = fmaf(e[4 * u + 1], xx.y, a);
-              a = fmaf(e[4 * u + 2], xx.z, a);
-              a = fmaf(e[4 * u + 3], xx.w, a);
+            for (int i = 0; i < 4; ++i) e[j * 4 + i] = i8_to_f(w4[j], i);
+#pragma unroll
+          for (int b = 0; b < kHeadBT; ++b) {
+            if (b < nb) {
+              const float4* xv = reinterpret_cast<const float4*>(sx + b * d + c * 16);
+              float a = acc[b];
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const float4 xx = xv[u];
+                a = fmaf(e[4 * u + 0], xx.x, a);
+                a = fmaf(e[4 * u + 1], xx.y, a);
+                a = fmaf(e[4 * u + 2], xx.z, a);
+                a = fmaf(e[4 * u + 3], xx.w, a);
+              }
+              acc[b] = a;
             }
-            acc[b] = a;
           }
         }
       }

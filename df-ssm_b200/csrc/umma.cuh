@@ -152,6 +152,33 @@ proj_umma_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
   };
   auto slot_par = [](int c) { return (unsigned)((c / kUmmaSB) & 1); };
+  // warp w and w + 4 share TMEM lanes 32 (w % 4)..: thread = output row lr, w < 4 takes the
+  // batch columns [0, NT/2), w >= 4 the rest
+  const int quarter = wid & 3, half = wid >> 2;
+  const int lr = quarter * 32 + lane, row = row0 + lr;
+  const bool rvalid = row < N;
+  const int rr = min(row, N - 1);
+  // this row's epilogue operands, loaded before the main loop so their latency overlaps it
+  float scale = 0.f, a[DFSSM_RANK], cw[4] = {0.f, 0.f, 0.f, 0.f}, cb = 0.f;
+  int ch = -1;
+  if (MODE != 2) {
+    scale = h2f(p.scale[rr]);
+    const uint4 a0 = reinterpret_cast<const uint4*>(p.A16 + (size_t)rr * DFSSM_RANK)[0];
+    const uint4 a1 = reinterpret_cast<const uint4*>(p.A16 + (size_t)rr * DFSSM_RANK)[1];
+    const unsigned aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&aw[i]));
+      a[2 * i] = f.x;
+      a[2 * i + 1] = f.y;
+    }
+    if (MODE == 0 && rr - d_inner >= 0 && rr - d_inner < d_xbc) {
+      ch = rr - d_inner;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) cw[k] = h2f(conv_w[ch * DFSSM_DCONV + k]);
+      cb = h2f(conv_b[ch]);
+    }
+  }
   bool ok = umma_wait(&fulls[0], 0u);
   expand(0);
   for (int c = 0; c < nch; ++c) {
@@ -189,12 +216,6 @@ proj_umma_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
   ok = umma_wait(&mbars[(nch - 1) % kUmmaSB], (unsigned)(((nch - 1) / kUmmaSB) & 1)) && ok;
   asm volatile("tcgen05.fence::after_thread_sync;");
   if (!ok && tid == 0) atomicOr(err, 1u);
-  // warp w and w + 4 share TMEM lanes 32 (w % 4)..: thread = output row lr, w < 4 takes the
-  // batch columns [0, NT/2), w >= 4 the rest
-  const int quarter = wid & 3, half = wid >> 2;
-  const int lr = quarter * 32 + lane, row = row0 + lr;
-  const bool rvalid = row < N;
-  const int rr = min(row, N - 1);
   const int tile = blockIdx.y * gridDim.x + blockIdx.x;
   bool emit_here = ksplit == 1 || MODE == 2;
   if (!emit_here) {
@@ -217,26 +238,6 @@ proj_umma_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
     __threadfence();
   }
   {
-    float scale = 0.f, a[DFSSM_RANK], cw[4] = {0.f, 0.f, 0.f, 0.f}, cb = 0.f;
-    int ch = -1;
-    if (MODE != 2) {
-      scale = h2f(p.scale[rr]);
-      const uint4 a0 = reinterpret_cast<const uint4*>(p.A16 + (size_t)rr * DFSSM_RANK)[0];
-      const uint4 a1 = reinterpret_cast<const uint4*>(p.A16 + (size_t)rr * DFSSM_RANK)[1];
-      const unsigned aw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&aw[i]));
-        a[2 * i] = f.x;
-        a[2 * i + 1] = f.y;
-      }
-      if (MODE == 0 && rr - d_inner >= 0 && rr - d_inner < d_xbc) {
-        ch = rr - d_inner;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) cw[k] = h2f(conv_w[ch * DFSSM_DCONV + k]);
-        cb = h2f(conv_b[ch]);
-      }
-    }
     for (int c0 = half * (NT / 2); c0 < (half + 1) * (NT / 2); c0 += 8) {
       uint32_t v[8];
       if (ksplit == 1 || MODE == 2) {
