@@ -269,9 +269,18 @@ int launch_mma(const ProjW& p, int B, const int8_t* q, const int* qsum, const __
                int ld_out, float* conv_state, const __half* conv_w, const __half* conv_b, int d_inner, int d_xbc,
                cudaStream_t s, UmmaScratch us = UmmaScratch{}) {
   if (B >= umma_min_batch() && p.K % kUmmaKC == 0) {  // tcgen05 path
-    const int rc = B >= 128 ? launch_umma<MODE, 128>(p, B, q, qsum, xs, t, out, ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, s, us)
-                 : B >= 64  ? launch_umma<MODE, 64>(p, B, q, qsum, xs, t, out, ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, s, us)
-                            : launch_umma<MODE, 32>(p, B, q, qsum, xs, t, out, ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, s, us);
+    // the widest batch tile that still gives enough tiles to fill the GPU without splitting K: a
+    // split leaves the epilogue to the last CTA of each tile
+    static const int min_tiles = [] {
+      const char* e = getenv("DFSSM_UMMA_TILES");
+      return e ? atoi(e) : 120;
+    }();
+    auto tiles = [&](int nt) { return ((p.N + 127) / 128) * ((B + nt - 1) / nt); };
+    int NT = B >= 128 ? 128 : (B >= 64 ? 64 : 32);
+    while (NT > 32 && tiles(NT) < min_tiles) NT /= 2;
+    const int rc = NT == 128 ? launch_umma<MODE, 128>(p, B, q, qsum, xs, t, out, ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, s, us)
+                 : NT == 64  ? launch_umma<MODE, 64>(p, B, q, qsum, xs, t, out, ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, s, us)
+                             : launch_umma<MODE, 32>(p, B, q, qsum, xs, t, out, ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, s, us);
     if (rc != -1) return rc;  // -1: not taken, fall through to mma.sync
   }
   const int RG = mma_rg(p.N, p.K);

@@ -1,5 +1,5 @@
 // Batched scaffold projection on the 5th-generation tensor cores (tcgen05, kind::i8), for batches
-// of 64 and more (decode at large batch, prompt prefill rows, the stand-alone scaffold GEMM).
+// of 96 and more (decode at large batch, prompt prefill rows, the stand-alone scaffold GEMM).
 //
 // One CTA computes a 128-row x NT-column tile of D = mask . q^T with the accumulator in tensor
 // memory (TMEM): MMA M = 128 weight rows, N = NT batch rows, K in 256-byte chunks.
@@ -32,7 +32,7 @@ constexpr int kUmmaThreads = 256;
 #define DFSSM_UMMA_KC 128
 #endif
 constexpr int kUmmaKC = DFSSM_UMMA_KC;  // K bytes per chunk (KC / 32 MMAs of K = 32)
-constexpr int kUmmaMinBatch = 64;   // batches below this use proj_mma_kernel (mma.sync)
+constexpr int kUmmaMinBatch = 96;   // batches below this use proj_mma_kernel (mma.sync)
 constexpr int kUmmaSpin = 1 << 22;  // bound of every mbarrier wait
 constexpr int kUmmaSB = 3;          // ring depth (chunks in flight)
 constexpr int kUmmaRawBytes = 128 * kUmmaKC / 8;  // one chunk of the 128 weight rows' bits
@@ -247,10 +247,26 @@ proj_umma_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
       } else {
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          int* wp = ws + (size_t)(b0 + min(c0 + jj, nb - 1)) * N + rr;
-          v[jj] = (rvalid && c0 + jj < nb) ? (uint32_t)__ldcg(wp) : 0u;
-          if (rvalid && c0 + jj < nb) *wp = 0;  // clean for the next use
+        for (int jj = 0; jj < 8; ++jj)
+          v[jj] = (rvalid && c0 + jj < nb) ? (uint32_t)__ldcg(ws + (size_t)(b0 + c0 + jj) * N + rr) : 0u;
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj)  // clean for the next use (after all 8 loads are out)
+          if (rvalid && c0 + jj < nb) ws[(size_t)(b0 + c0 + jj) * N + rr] = 0;
+      }
+      // the group's other global operands (conv taps, residual), all requested before any is used
+      float g0[8], g1[8], g2[8];
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        g0[jj] = g1[jj] = g2[jj] = 0.f;
+        const int b = b0 + c0 + jj;
+        if (!rvalid || c0 + jj >= nb) continue;
+        if (MODE == 0 && ch >= 0) {
+          const float* cs = conv_state + (size_t)b * 3 * d_xbc;
+          g0[jj] = cs[ch];
+          g1[jj] = cs[d_xbc + ch];
+          g2[jj] = cs[2 * d_xbc + ch];
+        } else if (MODE == 1) {
+          g0[jj] = h2f(out[(size_t)b * ld_out + row]);
         }
       }
 #pragma unroll
@@ -274,7 +290,7 @@ proj_umma_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
           float res = vv;
           if (ch >= 0) {
             float* cs = conv_state + (size_t)b * 3 * d_xbc;
-            const float s0 = cs[ch], s1 = cs[d_xbc + ch], s2 = cs[2 * d_xbc + ch];
+            const float s0 = g0[jj], s1 = g1[jj], s2 = g2[jj];
             cs[ch] = s1;
             cs[d_xbc + ch] = s2;
             cs[2 * d_xbc + ch] = vv;
@@ -286,8 +302,7 @@ proj_umma_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
         } else if (MODE == 3) {
           out[(size_t)b * ld_out + row] = f2h(vv);
         } else {
-          __half* xo = out + (size_t)b * ld_out + row;
-          *xo = f2h(h2f(*xo) + vv);
+          out[(size_t)b * ld_out + row] = f2h(g0[jj] + vv);
         }
       }
     }
