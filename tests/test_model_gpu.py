@@ -24,7 +24,7 @@ def _close(got, ref, frac_exact=0.9, rel=1e-2):
 
 @pytest.mark.parametrize("B,mode,shape", [(1, "graph", "tiny"), (3, "graph", "tiny"), (17, "graph", "tiny"),
                                           (17, "graph", "small"), (40, "graph", "small"), (80, "graph", "small"),
-                                          (130, "graph", "tiny"),
+                                          (100, "graph", "small"), (130, "graph", "tiny"),
                                           (1, "persistent", "small"), (2, "persistent", "small")])
 def test_single_layer_matches_oracle(B, mode, shape):
     w = weights(shape, 1, seed=2)

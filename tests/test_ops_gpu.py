@@ -22,7 +22,8 @@ def lib():
 @pytest.mark.parametrize("M", [1, 8, 32, 64, 100, 128, 512])
 def test_scaffold_gemm_bit_exact(lib, M, N, K):
     """Config 3: 1-bit packed x int8 -> int32, bit-exact vs the oracle and torch._int_mm
-    (M < 8: dp4a GEMV; 8..63: mma.sync; >= 64: tcgen05 with the accumulator in TMEM)."""
+    (M < 8: dp4a GEMV; 8..95: mma.sync; >= 96: tcgen05 with the accumulator in TMEM, batch tiles of
+    32, 64 or 128 rows by the tile count)."""
     rng = np.random.default_rng(M * 7 + N)
     packed = rng.integers(0, 2**32, size=(N, K // 32), dtype=np.uint32)
     x = rng.standard_normal((M, K)).astype(np.float16)
