@@ -257,7 +257,7 @@ int launch_umma(const ProjW& p, int B, const int8_t* q, const int* qsum, const _
   CU(umma_err_word(&err));
   const dim3 grid((p.N + 127) / 128, (B + NT - 1) / NT, ks);
   CU(ensure_smem(reinterpret_cast<const void*>(proj_umma_kernel<MODE, NT>), sm));
-  proj_umma_kernel<MODE, NT><<<grid, kUmmaThreads, sm, s>>>(tm, tw, p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out),
+  proj_umma_kernel<MODE, NT><<<grid, kUmmaThreads, sm, s>>>(tm, tw, p, qsum, xs, t, B, reinterpret_cast<__half*>(out),
                                                              ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc, ks,
                                                              us.acc, us.cnt, err);
   CHECK_LAUNCH();

@@ -2,7 +2,7 @@
 // of 96 and more (decode at large batch, prompt prefill rows, the stand-alone scaffold GEMM).
 //
 // One CTA computes a 128-row x NT-column tile of D = mask . q^T with the accumulator in tensor
-// memory (TMEM): MMA M = 128 weight rows, N = NT batch rows, K in 256-byte chunks.
+// memory (TMEM): MMA M = 128 weight rows, N = NT batch rows, K in 128-byte chunks.
 //   A (weights): the 0/1 sign masks as u8, built in shared memory from the packed bits: word w of
 //     a row gives the 32 bytes (w >> j) & 0x01010101, j = 0..7 -- the permuted column order that
 //     the quantised activations are stored in (qperm_index), so A and B columns line up.
@@ -13,8 +13,8 @@
 // row r sits at unit u ^ (r % 8)), one 128-byte row per K chunk.  Data movement per CTA:
 //   - per K chunk, one ring slot receives by TMA the activation tile (NT rows x 128 bytes, tensor
 //     map over q, 128-byte swizzle) and the weight rows' packed bits (128 rows x 16 bytes, tensor
-//     map over the bits, no swizzle) on one mbarrier; the ring is kUmmaSB slots deep and chunks are
-//     issued kUmmaSB - 1 ahead of the MMAs that read them;
+//     map over the bits, no swizzle) on one mbarrier; the ring is kUmmaSB slots deep, and a slot is
+//     refilled (kUmmaSB chunks on) as soon as the MMAs that read it have committed;
 //   - the threads expand a chunk's bits into the u8 masks (shared to shared) in one of two A buffers.
 // tcgen05.commit of chunk c's MMAs on an mbarrier frees its A buffer and ring slot.  The epilogue
 // reads D with tcgen05.ld (warp w and w + 4 own TMEM lanes 32(w % 4).., i.e. output rows; each
@@ -56,7 +56,7 @@ inline size_t proj_umma_smem(int NT) {
 }
 
 // MODE as proj_mma_kernel: 0 in_proj + conv1d, 1 out_proj + residual, 2 raw int32, 3 plain.
-// Grid (ceil(N / 128), ceil(B / NT), ksplit); (K / ksplit) % 256 == 0.  With ksplit > 1 the CTAs
+// Grid (ceil(N / 128), ceil(B / NT), ksplit); (K / ksplit) % 128 == 0.  With ksplit > 1 the CTAs
 // of a tile each take a K range (narrow projections would otherwise leave most SMs idle): the
 // integer partials meet exactly, in any order, through atomicAdd -- into `out` for MODE 2 (zeroed
 // by the caller), else into ws [B][N] int32 with a per-tile counter cnt, and the last CTA of the
@@ -67,7 +67,7 @@ inline size_t proj_umma_smem(int NT) {
 // swizzle (rows past N read as zeros).  K / ksplit is a multiple of 128.
 template <int MODE, int NT>
 __global__ void __launch_bounds__(kUmmaThreads, 1)
-proj_umma_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmw, ProjW p, const int8_t* __restrict__ q,
+proj_umma_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmw, ProjW p,
                  const int* __restrict__ qsum, const __half* __restrict__ xs,
                  const __half* __restrict__ t, int B, __half* __restrict__ out, int ld_out,
                  float* __restrict__ conv_state, const __half* __restrict__ conv_w, const __half* __restrict__ conv_b,
