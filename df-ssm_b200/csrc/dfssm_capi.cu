@@ -118,6 +118,8 @@ int launch_prep(dfssm_engine* e, const __half* in, int K, const float* w, int qu
     DFSSM_PREP_FAST(2)
     DFSSM_PREP_FAST(4)
     DFSSM_PREP_FAST(8)
+    DFSSM_PREP_FAST(5)
+    DFSSM_PREP_FAST(10)
 #undef DFSSM_PREP_FAST
   }
   const size_t sm = (size_t)K * sizeof(__half);

@@ -121,22 +121,51 @@ template <> struct RankHalves<1> { using T = unsigned short; };
 template <> struct RankHalves<2> { using T = unsigned; };
 template <> struct RankHalves<4> { using T = uint2; };
 template <> struct RankHalves<8> { using T = uint4; };
+// widths that are not a power of two (the 2.7B shape: d_model 2560 = 512 x 5, d_inner 5120 = 512 x 10):
+// the halves packed in pairs into 32-bit words, half j in the low (j even) or high half of word j / 2
+template <int N>
+struct HalfPack {
+  unsigned w[(N + 1) / 2];
+};
+template <> struct RankHalves<5> { using T = HalfPack<5>; };
+template <> struct RankHalves<10> { using T = HalfPack<10>; };
+
+// KPT consecutive fp16 values at p (read-only data), in this thread's RankHalves form
+template <int KPT>
+__device__ __forceinline__ typename RankHalves<KPT>::T ld_halves(const __half* p) {
+  using T = typename RankHalves<KPT>::T;
+  if constexpr (KPT == 5 || KPT == 10) {
+    T v;
+    const unsigned short* h = reinterpret_cast<const unsigned short*>(p);
+    if constexpr (KPT % 2 == 0) {  // 4-byte aligned: one word per pair
+#pragma unroll
+      for (int i = 0; i < KPT / 2; ++i) v.w[i] = __ldg(reinterpret_cast<const unsigned*>(p) + i);
+    } else {
+#pragma unroll
+      for (int i = 0; i < (KPT + 1) / 2; ++i) {
+        const unsigned lo = __ldg(h + 2 * i), hi = 2 * i + 1 < KPT ? __ldg(h + 2 * i + 1) : 0u;
+        v.w[i] = lo | (hi << 16);
+      }
+    }
+    return v;
+  } else {
+    return __ldg(reinterpret_cast<const T*>(p));
+  }
+}
 
 template <int KPT>
 __device__ __forceinline__ void load_lora_b(const __half* B16, int K, typename RankHalves<KPT>::T (&out)[DFSSM_RANK]) {
-  using T = typename RankHalves<KPT>::T;
   const int k0 = threadIdx.x * KPT;
 #pragma unroll
-  for (int r = 0; r < DFSSM_RANK; ++r) out[r] = __ldg(reinterpret_cast<const T*>(B16 + (size_t)r * K + k0));
+  for (int r = 0; r < DFSSM_RANK; ++r) out[r] = ld_halves<KPT>(B16 + (size_t)r * K + k0);
 }
 // NR rank rows starting at r0.
 template <int KPT, int NR>
 __device__ __forceinline__ void load_lora_b_ranks(const __half* B16, int K, int r0,
                                                   typename RankHalves<KPT>::T (&out)[NR]) {
-  using T = typename RankHalves<KPT>::T;
   const int k0 = threadIdx.x * KPT;
 #pragma unroll
-  for (int r = 0; r < NR; ++r) out[r] = __ldg(reinterpret_cast<const T*>(B16 + (size_t)(r0 + r) * K + k0));
+  for (int r = 0; r < NR; ++r) out[r] = ld_halves<KPT>(B16 + (size_t)(r0 + r) * K + k0);
 }
 
 template <int KPT>
@@ -287,7 +316,7 @@ __device__ __forceinline__ int qsum_of(const int* s_qpart, int b) {
 // This thread's KPT fp16 values of LoRA-B row r (B16 is [16][K]).
 template <int KPT>
 __device__ __forceinline__ typename RankHalves<KPT>::T load_rank_b(const __half* B16, int K, int r) {
-  return __ldg(reinterpret_cast<const typename RankHalves<KPT>::T*>(B16 + (size_t)r * K + threadIdx.x * KPT));
+  return ld_halves<KPT>(B16 + (size_t)r * K + threadIdx.x * KPT);
 }
 
 // t[b] = fp16(sum_k vals[b][k] * B16[r][k]) for one rank r whose values bv are already in registers.

@@ -25,6 +25,8 @@ def _close(got, ref, frac_exact=0.9, rel=1e-2):
 @pytest.mark.parametrize("B,mode,shape", [(1, "graph", "tiny"), (3, "graph", "tiny"), (17, "graph", "tiny"),
                                           (17, "graph", "small"), (40, "graph", "small"), (80, "graph", "small"),
                                           (100, "graph", "small"), (130, "graph", "tiny"),
+                                          # 2.7B widths: prologues with 5 and 10 columns per thread
+                                          (3, "graph", "2.7b"), (100, "graph", "2.7b"),
                                           (1, "persistent", "small"), (2, "persistent", "small")])
 def test_single_layer_matches_oracle(B, mode, shape):
     w = weights(shape, 1, seed=2)
