@@ -28,10 +28,7 @@
 namespace dfssm {
 
 constexpr int kUmmaThreads = 256;
-#ifndef DFSSM_UMMA_KC
-#define DFSSM_UMMA_KC 128
-#endif
-constexpr int kUmmaKC = DFSSM_UMMA_KC;  // K bytes per chunk (KC / 32 MMAs of K = 32)
+constexpr int kUmmaKC = 128;        // K bytes per chunk (4 MMAs of K = 32; one 128-byte swizzle row)
 constexpr int kUmmaMinBatch = 96;   // batches below this use proj_mma_kernel (mma.sync)
 constexpr int kUmmaSpin = 1 << 22;  // bound of every mbarrier wait
 constexpr int kUmmaSB = 3;          // ring depth (chunks in flight)
