@@ -41,8 +41,9 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
   const int TS = T + 3;
   float* raw = sm;                          // [NC][T + 3]: 3 taps of conv state, then the T raw inputs
   float* cvo = raw + NC * TS;               // [T][NC]: fp16-exact conv + SiLU outputs
-  float* zg = cvo + NC * T;                 // [T][kScanRows]: fp16-exact SiLU(z)
-  float* dts = zg + T * kScanRows;          // [T]: softplus(dt + bias)
+  constexpr int ZS = kScanRows + 1;         // padded: the staging stores run along t
+  float* zg = cvo + NC * T;                 // [T][ZS]: fp16-exact SiLU(z)
+  float* dts = zg + T * ZS;                 // [T]: softplus(dt + bias)
   float* abar = dts + T;                    // [T]: exp(A dt)
   __half* gs = reinterpret_cast<__half*>(raw);  // [T][kScanRows] gated outputs (raw is dead by then)
   auto chan = [&](int c) { return c < kScanRows ? c0 + c : d_inner + (c - kScanRows); };
@@ -62,7 +63,8 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
     raw[c * TS + k] = cs[(size_t)k * d_xbc + chan(c)];
   }
   // raw inputs and z by 16-byte loads, kU of them in flight per thread: a row t holds ux units of
-  // this CTA's x channels, d_state/4 units of B and C, and ux units of z
+  // this CTA's x channels, d_state/4 units of B and C, and ux units of z.  Unit u is (unit k = u / T,
+  // token t = u % T), so a warp's shared-memory stores of one channel hit consecutive words.
   {
     constexpr int kU = 4;
     constexpr int ux = kScanRows / 8;
@@ -74,7 +76,7 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
       for (int j = 0; j < kU; ++j) {
         const int u = u0 + j * kScanThreads;
         if (u < nu) {
-          const int t = u / upr, k = u - t * upr;
+          const int k = u / T, t = u - k * T;  // consecutive threads: consecutive tokens of one unit
           const size_t col = k < ux ? (size_t)d_inner + c0 + 8 * k
                                     : (k < ux + ubc ? (size_t)2 * d_inner + 8 * (k - ux)
                                                     : (size_t)c0 + 8 * (k - ux - ubc));
@@ -85,7 +87,7 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
       for (int j = 0; j < kU; ++j) {
         const int u = u0 + j * kScanThreads;
         if (u < nu) {
-          const int t = u / upr, k = u - t * upr;
+          const int k = u / T, t = u - k * T;
           const __half* hv8 = reinterpret_cast<const __half*>(&v[j]);
           if (k < ux + ubc) {
 #pragma unroll
@@ -95,7 +97,7 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
             for (int e = 0; e < 8; ++e) {
               const float z = h2f(hv8[e]);
               const float sig = round_h(1.0f / (1.0f + expf(-z)));
-              zg[t * kScanRows + 8 * (k - ux - ubc) + e] = round_h(z * sig);
+              zg[t * ZS + 8 * (k - ux - ubc) + e] = round_h(z * sig);
             }
           }
         }
@@ -173,7 +175,7 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
     if ((lane & (2 * off - 1)) == 0) {  // one lane per row
       const int pp = wid * kScanRPW + rw;
       const float y = part_[0] + ct[pp] * Dh;
-      gs[t * kScanRows + pp] = f2h(h2f(f2h(y)) * zg[t * kScanRows + pp]);
+      gs[t * kScanRows + pp] = f2h(h2f(f2h(y)) * zg[t * ZS + pp]);
     }
   }
 #pragma unroll
@@ -188,7 +190,7 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
 
 inline size_t prefill_scan_smem(int T, int d_state, int split) {
   const size_t rows = DFSSM_HEADDIM / split, nc = rows + 2 * d_state;
-  return (nc * (2 * T + 3) + (size_t)T * rows + 2 * T) * sizeof(float);
+  return (nc * (2 * T + 3) + (size_t)T * (rows + 1) + 2 * T) * sizeof(float);
 }
 
 // x rows b*T + t = the embedding of tokens[b][t] (fp16, as embed_kernel).
