@@ -65,3 +65,14 @@ def test_reference_arm_under_torchrun_prints_one_job_line():
     assert line["impl"] == "reference"
     if "unavailable" not in line:
         assert line["config"]["batch"] == 2 and line["n_gpus"] == 2 and line["value"] > 0
+
+
+@pytest.mark.parametrize("config", ["cfg3", "cfg1 --prefill 16"])
+def test_reference_arm_without_a_counterpart_prints_unavailable(config):
+    """The reference has no stand-alone scaffold GEMM entry point and no prompt prefill, so the
+    reference arm of those workloads prints one 'unavailable' line and exits 0 (no GPU needed)."""
+    cmd = [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--config", *config.split()]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=120, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [json.loads(l) for l in r.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1 and lines[0]["impl"] == "reference" and lines[0]["unavailable"]
