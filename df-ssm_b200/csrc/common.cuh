@@ -179,4 +179,18 @@ __device__ __forceinline__ void mbar_wait_bounded(uint64_t* bar, unsigned parity
   }
 }
 
+// fp16 tensor-core MMA m16n8k16 with fp32 accumulation (the LM head kernels)
+__device__ __forceinline__ void mma_f16(float (&d)[4], unsigned a0, unsigned a1, unsigned a2, unsigned a3,
+                                        unsigned b0, unsigned b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// two int8 of a biased word (w ^ 0x80808080) as an exact half2: bytes (lo, lo+1) or (lo+2, lo+3)
+__device__ __forceinline__ unsigned i8x2_to_h2(unsigned wb, unsigned sel) {
+  const unsigned h = __byte_perm(wb, 0x64646464u, sel);
+  const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h), __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480)));
+  return *reinterpret_cast<const unsigned*>(&r);
+}
+
 }  // namespace dfssm

@@ -920,78 +920,84 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
     unsigned long long mybest[B];
 #pragma unroll
     for (int b = 0; b < B; ++b) mybest[b] = 0ull;
-    // A warp takes whole rows of a chunk; with d_model = 512*KI a row is 32*KI 16-byte units,
-    // KI per lane.  Batch 1 keeps this lane's KI*16 activations in registers for all rows.
-    constexpr int CPL = KI;
+    // Logits on the fp16 tensor cores (mma.sync m16n8k16, fp32 accumulation; the int8 rows become
+    // exact fp16 by a byte permute, the normalised x is fp16, so every product is exact).  The rows
+    // of a chunk go in 16-row tiles, two tiles per pass: warp w takes tile w / 8 of the pass and the
+    // K slice w % 8 (d_model / 512 blocks of 64 columns), lane (g, c) loads 16 bytes at 16c of a
+    // block's rows g and g + 8 (the k order of A and B agrees), batch column n = g of B (zero for
+    // g >= B).  Partial sums [2][8 slices][16 rows][B] meet in s_q (free in the head phase) and are
+    // added over the slices in a fixed order by one thread per (tile, row, sequence).
     const int RC = P.lay.stage_bytes / d_model, nch = (pl.nv + RC - 1) / RC;
-    float xr[B == 1 ? KI : 1][16];
-    if (B == 1) {
-#pragma unroll
-      for (int u = 0; u < (B == 1 ? KI : 1); ++u)
-#pragma unroll
-        for (int q = 0; q < 16; ++q) xr[u][q] = h2f(s_x[(lane + 32 * u) * 16 + q]);
-    }
-    for (int c = 0; c < nch; ++c) {
-      const int item = nl + c;
+    const int g = lane >> 2, c = lane & 3;
+    const int nblk = d_model / 64, bps = nblk / 8;  // 64-column blocks, blocks per K slice
+    const int wtile = wid >> 3, slice = wid & 7;
+    float* part = reinterpret_cast<float*>(s_q);  // [2][8][16][B]
+    for (int ch = 0; ch < nch; ++ch) {
+      const int item = nl + ch;
       wait_stage(P, bars, P.l0 + item);
       const unsigned char* st = ring + (size_t)(item % P.ns) * P.lay.stage_bytes;
-      const int r0 = pl.v0 + c * RC, nr = min(RC, pl.v0 + pl.nv - r0);
-      for (int r = wid; r < nr; r += kWarps) {
-        const uint4* er = reinterpret_cast<const uint4*>(st + (size_t)r * d_model);
-        uint4 ev[B == 1 ? CPL : 1];  // batch 1: all units up front; batch 2: one at a time (registers)
-        if (B == 1)
+      const int r0 = pl.v0 + ch * RC, nr = min(RC, pl.v0 + pl.nv - r0);
+      for (int t0 = 0; t0 < nr; t0 += 32) {  // a pass: tiles t0 / 16 and t0 / 16 + 1
+        const int tr0 = t0 + 16 * wtile;      // this warp's tile's first row
+        if (tr0 < nr) {
+          const uint4* ra = reinterpret_cast<const uint4*>(st + (size_t)min(tr0 + g, nr - 1) * d_model);
+          const uint4* rb = reinterpret_cast<const uint4*>(st + (size_t)min(tr0 + g + 8, nr - 1) * d_model);
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+          for (int blk = slice * bps; blk < (slice + 1) * bps; ++blk) {
+            const uint4 ea = ra[blk * 4 + c], eb = rb[blk * 4 + c];
+            const unsigned wa[4] = {ea.x ^ 0x80808080u, ea.y ^ 0x80808080u, ea.z ^ 0x80808080u, ea.w ^ 0x80808080u};
+            const unsigned wb[4] = {eb.x ^ 0x80808080u, eb.y ^ 0x80808080u, eb.z ^ 0x80808080u, eb.w ^ 0x80808080u};
 #pragma unroll
-          for (int u = 0; u < CPL; ++u) ev[B == 1 ? u : 0] = er[lane + 32 * u];
-        float acc[B];
-#pragma unroll
-        for (int b = 0; b < B; ++b) acc[b] = 0.f;
-#pragma unroll
-        for (int u = 0; u < CPL; ++u) {
-          const uint4 e4 = B == 1 ? ev[B == 1 ? u : 0] : er[lane + 32 * u];
-          const unsigned w4[4] = {e4.x ^ 0x80808080u, e4.y ^ 0x80808080u, e4.z ^ 0x80808080u, e4.w ^ 0x80808080u};
-          if (B == 1) {
-            float a = acc[0];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              a = fmaf(i8_to_f(w4[q], 0), xr[B == 1 ? u : 0][4 * q + 0], a);
-              a = fmaf(i8_to_f(w4[q], 1), xr[B == 1 ? u : 0][4 * q + 1], a);
-              a = fmaf(i8_to_f(w4[q], 2), xr[B == 1 ? u : 0][4 * q + 2], a);
-              a = fmaf(i8_to_f(w4[q], 3), xr[B == 1 ? u : 0][4 * q + 3], a);
+            for (int s2 = 0; s2 < 4; ++s2) {
+              const unsigned a0 = i8x2_to_h2(wa[s2], 0x4140u), a2 = i8x2_to_h2(wa[s2], 0x4342u);
+              const unsigned a1 = i8x2_to_h2(wb[s2], 0x4140u), a3 = i8x2_to_h2(wb[s2], 0x4342u);
+              uint2 bv = make_uint2(0u, 0u);
+              if (g < B) bv = *reinterpret_cast<const uint2*>(s_x + g * d_model + blk * 64 + 16 * c + 4 * s2);
+              mma_f16(acc, a0, a1, a2, a3, bv.x, bv.y);
             }
-            acc[0] = a;
-          } else {
+          }
+          // D: acc[0..1] -> row g, columns 2c, 2c + 1; acc[2..3] -> row g + 8; only c = 0 holds
+          // batch columns 0 and 1
+          if (c == 0) {
+            float* pp = part + ((size_t)(wtile * 8 + slice) * 16) * B;
 #pragma unroll
             for (int b = 0; b < B; ++b) {
-              const __half2* xv = reinterpret_cast<const __half2*>(s_x + b * d_model + (lane + 32 * u) * 16);
-              float a = acc[b];
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const float2 x01 = __half22float2(xv[2 * q]), x23 = __half22float2(xv[2 * q + 1]);
-                a = fmaf(i8_to_f(w4[q], 0), x01.x, a);
-                a = fmaf(i8_to_f(w4[q], 1), x01.y, a);
-                a = fmaf(i8_to_f(w4[q], 2), x23.x, a);
-                a = fmaf(i8_to_f(w4[q], 3), x23.y, a);
-              }
-              acc[b] = a;
+              pp[g * B + b] = acc[b];
+              pp[(g + 8) * B + b] = acc[2 + b];
             }
           }
         }
-        const int vr = r0 + r;
-        const float sv = P.Es[vr];
+        cta_sync();
+        if (tid < 32 * B) {  // (tile, row, sequence)
+          const int tile = tid / (16 * B), rem = tid - tile * 16 * B, row = rem / B, b = rem - row * B;
+          const int r = t0 + 16 * tile + row;
+          if (r < nr) {
+            const float* pp = part + ((size_t)(tile * 8) * 16 + row) * B + b;
+            float sum = 0.f;
 #pragma unroll
-        for (int b = 0; b < B; ++b) {
-          const float lg = warp_sum(acc[b]) * sv;
-          if (lane == 0) {
+            for (int sl = 0; sl < 8; ++sl) sum += pp[(size_t)sl * 16 * B];
+            const int vr = r0 + r;
+            const float lg = sum * P.Es[vr];
             P.logits[(size_t)b * P.vocab + vr] = lg;
             const unsigned long long key = argmax_key(f2h(lg), (uint32_t)vr);
-            mybest[b] = key > mybest[b] ? key : mybest[b];
+#pragma unroll
+            for (int bb = 0; bb < B; ++bb)  // static indices keep mybest in registers
+              if (bb == b) mybest[bb] = key > mybest[bb] ? key : mybest[bb];
           }
         }
+        cta_sync();  // the partials are read before the next pass (or chunk) writes them
       }
-      cta_sync();  // every warp is done with the chunk: release its slot
-      if (tid == 0)
+      if (tid == 0)  // every warp is done with the chunk: release its slot
         for (int j = 0; j < kParts; ++j) mbar_arrive(empties + (item % P.ns) * kParts + j);
     }
+    // each thread's best keys -> the warp's best per sequence (lane 0)
+#pragma unroll
+    for (int b = 0; b < B; ++b)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, mybest[b], o);
+        mybest[b] = k2 > mybest[b] ? k2 : mybest[b];
+      }
     unsigned long long* sb = reinterpret_cast<unsigned long long*>(red);
     cta_sync();
     if (lane == 0)
