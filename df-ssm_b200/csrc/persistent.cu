@@ -1,4 +1,5 @@
-// Persistent whole-step decode kernel for small batches (B <= 2): one cooperative launch per
+// Persistent whole-step decode kernel for small batches (B <= 2 per launch; batches up to 6 run one
+// launch per group of two sequences): one cooperative launch per
 // greedy decode step runs the embedding gather, every layer, the final norm, the LM head and
 // the argmax.  One CTA per SM: 16 compute warps (512 threads, named barrier 1) and one warp
 // that only issues the bulk copies of the weight/state ring.
@@ -1268,22 +1269,42 @@ size_t persistent_xch_words(const dfssm_dims& d) {
 }
 size_t persistent_xch_bytes(const dfssm_dims& d) { return 8 * persistent_xch_words(d) * kReplicas; }
 
+// Batches of 3 to kPersistMaxBatch sequences run as consecutive launches over groups of two (the
+// last may hold one): at the 1.3B shape two launches of the batch-2 kernel (2 x 0.73 ms) beat the
+// per-op graph at batch 4 (2.8 ms, bound by its per-kernel latency chain).
+constexpr int kPersistMaxBatch = 6;
+
 bool persistent_supported(const dfssm_engine* e) {
-  return e->persist && e->batch >= 1 && e->batch <= 2 && set_of(e)->st[e->batch].ready;
+  if (!e->persist || e->batch < 1 || e->batch > kPersistMaxBatch) return false;
+  const PersistentSet* ps = set_of(e);
+  if (e->batch <= 2) return ps->st[e->batch].ready;
+  return ps->st[2].ready && (e->batch % 2 == 0 || ps->st[1].ready);
 }
 
 int launch_persistent_layers(dfssm_engine* e, int l0, int l1, int from_x, int do_head, cudaStream_t s) {
   if (!persistent_supported(e)) return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "persistent kernel unavailable");
   if (l0 < 0 || l1 > e->d.n_layer || l0 >= l1) return dfssm_fail(DFSSM_ERR_ARG, "bad layer range [%d, %d)", l0, l1);
-  PersistentState& ps = set_of(e)->st[e->batch];
-  PParams P = ps.params;
-  P.l0 = l0;
-  P.l1 = l1;
-  P.from_x = from_x;
-  P.do_head = do_head;
-  void* args[] = {&P};
-  cudaError_t ce = cudaLaunchCooperativeKernel(ps.fn, dim3(ps.grid), dim3(kBlockThreads), args, (size_t)ps.smem, s);
-  if (ce != cudaSuccess) return dfssm_fail(DFSSM_ERR_CUDA, "cooperative launch failed: %s", cudaGetErrorString(ce));
+  const dfssm_dims& d = e->d;
+  for (int b0 = 0; b0 < e->batch; b0 += 2) {
+    const int nb = e->batch - b0 < 2 ? e->batch - b0 : 2;
+    PersistentState& ps = set_of(e)->st[nb];
+    PParams P = ps.params;
+    // this group's rows of every per-sequence buffer (the layer strides stay those of max_batch)
+    P.ssm += (size_t)b0 * d.nheads * DFSSM_HEADDIM * DFSSM_DSTATE;
+    P.conv += (size_t)b0 * 3 * d.d_xbc;
+    P.x_g += (size_t)b0 * d.d_model;
+    P.gated_g += (size_t)b0 * d.d_inner;
+    P.logits += (size_t)b0 * d.vocab;
+    P.best += b0;
+    P.tokens += b0;
+    P.l0 = l0;
+    P.l1 = l1;
+    P.from_x = from_x;
+    P.do_head = do_head;
+    void* args[] = {&P};
+    cudaError_t ce = cudaLaunchCooperativeKernel(ps.fn, dim3(ps.grid), dim3(kBlockThreads), args, (size_t)ps.smem, s);
+    if (ce != cudaSuccess) return dfssm_fail(DFSSM_ERR_CUDA, "cooperative launch failed: %s", cudaGetErrorString(ce));
+  }
   return DFSSM_OK;
 }
 
@@ -1296,7 +1317,8 @@ size_t persistent_trace_entries(const dfssm_engine* e) {
 }
 
 int launch_persistent_traced(dfssm_engine* e, unsigned long long* trace_dev, cudaStream_t s) {
-  if (!persistent_supported(e)) return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "persistent kernel unavailable");
+  if (!persistent_supported(e) || e->batch > 2)
+    return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "the phase trace runs the persistent kernel at batch 1 or 2");
   PersistentState& ps = set_of(e)->st[e->batch];
   PParams P = ps.params;
   P.trace = trace_dev;

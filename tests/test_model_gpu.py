@@ -27,7 +27,9 @@ def _close(got, ref, frac_exact=0.9, rel=1e-2):
                                           (100, "graph", "small"), (130, "graph", "tiny"),
                                           # 2.7B widths: prologues with 5 and 10 columns per thread
                                           (3, "graph", "2.7b"), (100, "graph", "2.7b"),
-                                          (1, "persistent", "small"), (2, "persistent", "small")])
+                                          (1, "persistent", "small"), (2, "persistent", "small"),
+                                          # batches of 3..6 run the persistent kernel per group of two
+                                          (3, "persistent", "small"), (5, "persistent", "small")])
 def test_single_layer_matches_oracle(B, mode, shape):
     w = weights(shape, 1, seed=2)
     d = w.dims
@@ -203,11 +205,12 @@ def test_persistent_is_deterministic_and_reports_no_timeouts(B):
     m.check_finite()  # also fails if any bounded wait in the kernel timed out
 
 
-def test_persistent_matches_graph_tokens_on_1p3b_two_layers():
+@pytest.mark.parametrize("B", [2, 3, 4])
+def test_persistent_matches_graph_tokens_on_1p3b_two_layers(B):
     w = weights("1.3b", 2, seed=3)
-    p = np.random.default_rng(8).integers(0, w.dims.vocab, (2, 4))
-    a = model(w, 2, mode="persistent").generate(12, prompt=p, verbose=False)
-    b = model(w, 2, mode="graph").generate(12, prompt=p, verbose=False)
+    p = np.random.default_rng(8).integers(0, w.dims.vocab, (B, 4))
+    a = model(w, B, mode="persistent").generate(12, prompt=p, verbose=False)
+    b = model(w, B, mode="graph").generate(12, prompt=p, verbose=False)
     np.testing.assert_array_equal(a, b)
 
 
