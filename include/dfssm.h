@@ -63,7 +63,8 @@ int dfssm_get_dims(const dfssm_engine* e, dfssm_dims* out);
 /* Number of sequences decoded by dfssm_step (1..max_batch).  Drops the captured graph. */
 int dfssm_set_batch(dfssm_engine* e, int batch);
 /* Step execution mode: 0 = automatic (3 where supported, else 1), 1 = per-op kernels replayed from a CUDA graph,
- * 2 = per-op kernels launched eagerly, 3 = persistent whole-step kernel (batch <= 2, d_model and d_inner multiples of 512). */
+ * 2 = per-op kernels launched eagerly, 3 = persistent whole-step kernel (batch <= 6, one launch per group of two
+ * sequences; d_model and d_inner multiples of 512). */
 int dfssm_set_mode(dfssm_engine* e, int mode);
 int dfssm_get_mode(const dfssm_engine* e, int* mode);
 
