@@ -76,3 +76,16 @@ def test_reference_arm_without_a_counterpart_prints_unavailable(config):
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [json.loads(l) for l in r.stdout.splitlines() if l.startswith("{")]
     assert len(lines) == 1 and lines[0]["impl"] == "reference" and lines[0]["unavailable"]
+
+
+def test_roofline_bytes_per_step():
+    """Algorithmic HBM bytes of one decode step, the numerator of bench.py's roofline: packed
+    scaffold, fp16 scales, int8 LoRA, conv/SSM parameters and norms (173.1 MB at 48 layers of the
+    1.3B shape), the int8 embedding with its scales (103.2 MB) and per sequence the fp32 SSM and
+    conv state read and written (206.3 MB)."""
+    from dfssm_b200 import synthetic
+    d = synthetic.make_dims("1.3b", 48)
+    one, many = bench.step_bytes(d, 1), bench.step_bytes(d, 32)
+    assert (one["weights"], one["embedding"], one["state"]) == (173100032, 103174560, 206340096)
+    assert one["total"] == 482614688
+    assert many["state"] == 32 * one["state"] and many["total"] == one["total"] + 31 * one["state"]
