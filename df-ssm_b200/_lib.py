@@ -42,12 +42,15 @@ SIGNATURES = {
     "dfssm_layer_step": (c_int, [c_void_p, c_int, c_void_p]),
     "dfssm_trace_entries": (c_size_t, [c_void_p]),
     "dfssm_trace_step": (c_int, [c_void_p, c_void_p, c_void_p]),
+    "dfssm_debug_set_wait_limit": (c_int, [c_void_p, c_uint32]),
+    "dfssm_debug_skew_next_step": (c_int, [c_void_p]),
     "dfssm_scaffold_gemm_workspace": (c_size_t, [c_int, c_int]),
     "dfssm_scaffold_gemm": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "dfssm_scaffold_gemm_noalloc": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "dfssm_conv_step": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "dfssm_ssm_step": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
                                c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p]),
+    "dfssm_rmsnorm_quantize": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     "dfssm_lm_head_workspace": (c_size_t, [c_int]),
     "dfssm_lm_head_argmax": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p,
                                      c_void_p, c_void_p]),

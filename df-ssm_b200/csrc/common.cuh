@@ -173,10 +173,12 @@ __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
 }
 
 // Wait until the mbarrier phase with `parity` completes; bounded (a copy from valid memory always
-// completes, the bound only keeps a fault elsewhere from turning into an endless spin).
-__device__ __forceinline__ void mbar_wait_bounded(uint64_t* bar, unsigned parity) {
-  for (unsigned it = 0; it < (1u << 24) && !mbar_try_wait(bar, parity); ++it) {
-  }
+// completes, the bound only keeps a fault elsewhere from turning into an endless spin).  Returns
+// false if the wait ran out; the caller records that in an error word the host checks.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity) {
+  for (unsigned it = 0; it < (1u << 24); ++it)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
 }
 
 // fp16 tensor-core MMA m16n8k16 with fp32 accumulation (the LM head kernels)

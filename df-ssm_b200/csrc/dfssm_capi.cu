@@ -149,8 +149,6 @@ inline int mma_rg(int N, int K) {
   return mma_ok(K, pref) ? pref : (mma_ok(K, other) ? other : 0);
 }
 
-// error word of the tcgen05 projection (a wait that ran out); read by dfssm_check_finite
-__device__ unsigned g_umma_err;
 
 // Split-K scratch of the tcgen05 projection: int32 partial sums [rows][N] and one counter per
 // output tile, all zero between uses (the kernel clears what it used).
@@ -907,7 +905,9 @@ int dfssm_check_finite(dfssm_engine* e, void* stream) {
   unsigned sync_err = 0, umma_err = 0;
   CU(cudaMemcpy(&sync_err, e->sync + 3, 4, cudaMemcpyDeviceToHost));
   CU(cudaMemcpyFromSymbol(&umma_err, g_umma_err, 4));
-  if (umma_err) return dfssm_fail(DFSSM_ERR_STATE, "tcgen05 projection kernel recorded a timed-out wait");
+  if (umma_err)
+    return dfssm_fail(DFSSM_ERR_STATE, "a per-op projection or LM-head kernel recorded a timed-out wait (code %u)",
+                      umma_err);
   if (sync_err)
     return dfssm_fail(DFSSM_ERR_STATE, "persistent step kernel recorded a timed-out wait (code %u)", sync_err);
   for (size_t i = 0; i < h.size(); ++i)
@@ -932,6 +932,8 @@ int dfssm_get_buffer(dfssm_engine* e, const char* name, void** ptr, size_t* byte
   else if (!strcmp(name, "gated")) { *ptr = e->gated; *bytes = B * d.d_inner * 2; }
   else if (!strcmp(name, "logits")) { *ptr = e->logits; *bytes = B * d.vocab * 4; }
   else if (!strcmp(name, "tokens")) { *ptr = e->tokens; *bytes = B * 4; }
+  else if (!strcmp(name, "q")) { *ptr = e->q; *bytes = B * (d.d_model > d.d_inner ? d.d_model : d.d_inner); }
+  else if (!strcmp(name, "xs")) { *ptr = e->xs; *bytes = B * 2; }
   else return dfssm_fail(DFSSM_ERR_ARG, "unknown buffer '%s'", name);
   return DFSSM_OK;
 }
@@ -943,6 +945,16 @@ int dfssm_layer_step(dfssm_engine* e, int layer, void* stream) {
   if (effective_mode(e) == 3)
     return launch_persistent_layers(e, layer, layer + 1, 1, 0, static_cast<cudaStream_t>(stream));
   return enqueue_layer(e, layer, static_cast<cudaStream_t>(stream), Group{0, e->batch});
+}
+
+int dfssm_debug_set_wait_limit(dfssm_engine* e, unsigned polls) {
+  if (!e) return dfssm_fail(DFSSM_ERR_ARG, "NULL engine");
+  return persistent_debug_wait_limit(e, polls);
+}
+
+int dfssm_debug_skew_next_step(dfssm_engine* e) {
+  if (!e) return dfssm_fail(DFSSM_ERR_ARG, "NULL engine");
+  return persistent_debug_skew(e);
 }
 
 size_t dfssm_trace_entries(const dfssm_engine* e) { return e ? persistent_trace_entries(e) : 0; }
@@ -1011,6 +1023,30 @@ int dfssm_ssm_step(const void* xbc_f16, int ld_xbc, const void* dt_f16, int ld_d
       d_state, nheads, dt_bias, A_log, D, h_state, static_cast<__half*>(y_f16), ld_y);
   CHECK_LAUNCH();
   return DFSSM_OK;
+}
+
+int dfssm_rmsnorm_quantize(const void* x_f16, const float* norm_w, int batch, int K, void* xn_f16, void* scale_f16,
+                           int8_t* q, void* stream) {
+  if (!x_f16 || !norm_w || !xn_f16 || !scale_f16 || !q) return dfssm_fail(DFSSM_ERR_ARG, "NULL argument");
+  if (batch < 1) return dfssm_fail(DFSSM_ERR_ARG, "batch %d < 1", batch);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const __half* x = static_cast<const __half*>(x_f16);
+  __half* xn = static_cast<__half*>(xn_f16);
+  __half* xs = static_cast<__half*>(scale_f16);
+#define DFSSM_RQ(n)                                                                                   \
+  if (K == 512 * n) {                                                                                 \
+    rmsnorm_quant_kernel<n><<<batch, kPrepFastThreads, 0, s>>>(x, K, norm_w, xn, xs, q);              \
+    CHECK_LAUNCH();                                                                                   \
+    return DFSSM_OK;                                                                                  \
+  }
+  DFSSM_RQ(1)
+  DFSSM_RQ(2)
+  DFSSM_RQ(4)
+  DFSSM_RQ(5)
+  DFSSM_RQ(8)
+  DFSSM_RQ(10)
+#undef DFSSM_RQ
+  return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "K=%d (built for 512 x {1, 2, 4, 5, 8, 10})", K);
 }
 
 size_t dfssm_lm_head_workspace(int batch) { return batch > 0 ? align256((size_t)batch * 8) : 0; }
@@ -1112,6 +1148,10 @@ extern "C" int dfssm_scaffold_gemm_noalloc(const uint32_t* packed, const int8_t*
   p.bits = packed;
   p.N = N;
   p.K = K;
+  // the same kernel choice as dfssm_scaffold_gemm: the tensor-core kernels need no scratch beyond
+  // the permuted activations and their sums (a split-K tcgen05 launch zeroes `acc` and adds into it)
+  if (M >= kMmaMinBatch && mma_rg(N, K))
+    return launch_mma<2>(p, M, qp, qsum, nullptr, nullptr, acc, N, nullptr, nullptr, nullptr, 0, 0, s);
   const size_t sm = (size_t)kGemvBT * K;
   if (sm > 48 * 1024) CU(ensure_smem(reinterpret_cast<const void*>(proj_gemv_kernel<2>), sm));
   const int rows_per_cta = 2 * (kGemvThreads / 32);

@@ -72,3 +72,5 @@ int launch_persistent_step(dfssm_engine* e, cudaStream_t s);
 size_t persistent_trace_entries(const dfssm_engine* e);
 int launch_persistent_traced(dfssm_engine* e, unsigned long long* trace_dev, cudaStream_t s);
 int launch_persistent_layers(dfssm_engine* e, int l0, int l1, int from_x, int do_head, cudaStream_t s);
+int persistent_debug_skew(dfssm_engine* e);
+int persistent_debug_wait_limit(dfssm_engine* e, unsigned polls);

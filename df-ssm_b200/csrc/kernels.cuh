@@ -16,6 +16,10 @@
 
 namespace dfssm {
 
+// Error word of the per-op kernels' bounded waits (1: tcgen05 projection, 2: mma.sync projection
+// activations, 4: tensor-core LM head activations); read and reported by dfssm_check_finite.
+__device__ unsigned g_umma_err;
+
 constexpr int kPrepThreads = 256;
 constexpr int kGemvThreads = 256;
 constexpr int kGemvBT = 16;      // batch rows per GEMV pass (one per lane of a half-warp)
@@ -145,6 +149,33 @@ act_prep_fast_kernel(const __half* __restrict__ in, int K, const float* __restri
   }
 }
 
+// Stand-alone RMSNorm + int8 quantisation of fp16 rows with the prologue functions of the
+// persistent step kernel (prep_norm, prep_quantize): one 512-thread CTA per row, K = 512 KPT.
+// Writes the normalised fp16 row, its fp16 scale and q in natural column order.
+template <int KPT>
+__global__ void __launch_bounds__(kPrepFastThreads)
+rmsnorm_quant_kernel(const __half* __restrict__ in, int K, const float* __restrict__ w, __half* __restrict__ xn_out,
+                     __half* __restrict__ xs_out, int8_t* __restrict__ q_out) {
+  __shared__ float red[256];  // prep_norm uses red[0, 16), prep_quantize red[128, 144)
+  __shared__ float s_xs[1];
+  __shared__ int s_qpart[kPrepFastWarps];
+  __shared__ __align__(16) int8_t s_q[KPT * kPrepFastThreads];
+  const int b = blockIdx.x, k0 = threadIdx.x * KPT;
+  float wv[KPT];
+  float vals[1][KPT];
+#pragma unroll
+  for (int j = 0; j < KPT; ++j) {
+    wv[j] = __ldg(w + k0 + j);
+    vals[0][j] = h2f(in[(size_t)b * K + k0 + j]);
+  }
+  prep_norm<1, KPT>(vals, wv, K, red);
+#pragma unroll
+  for (int j = 0; j < KPT; ++j) xn_out[(size_t)b * K + k0 + j] = f2h(vals[0][j]);
+  prep_quantize<1, KPT, false>(vals, s_q, K, s_xs, s_qpart, red + 128);
+  for (int k = threadIdx.x; k < K; k += kPrepFastThreads) q_out[(size_t)b * K + k] = s_q[qperm_index(k)];
+  if (threadIdx.x == 0) xs_out[b] = f2h(s_xs[0]);
+}
+
 // ---------------------------------------------------------------------------------------
 // proj_gemv: packed 1-bit scaffold projection.
 // Each half-warp owns one output row at a time; lane l16 streams 128-bit chunks
@@ -262,7 +293,7 @@ proj_gemv_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ 
       float la = 0.f;
 #pragma unroll
       for (int r = 0; r < DFSSM_RANK; ++r) la = fmaf(h2f(tb[r]), h2f(arow[r]), la);
-      const float v = round_h(base + la);
+      const float v = round_h(base + round_h(la));
       if (MODE == 0) {
         float res = v;
         const int ch = row - d_inner;
@@ -465,7 +496,7 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
       for (int u = 0; u < U; ++u) e_cs[threadIdx.x + u * kMmaThreads] = v[u];
     }
     if (bt0 > 0) load_w();
-    mbar_wait_bounded(&qbar, phase);
+    if (!mbar_wait_bounded(&qbar, phase)) atomicOr(&g_umma_err, 2u);
     int acc[kMmaNT][4];
 #pragma unroll
     for (int tt = 0; tt < kMmaNT; ++tt)
@@ -518,7 +549,7 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
       float la = 0.f;
 #pragma unroll
       for (int r = 0; r < DFSSM_RANK; ++r) la = fmaf(e_t[bb * DFSSM_RANK + r], e_a[lr * (DFSSM_RANK + 1) + r], la);
-      const float v = round_h(base + la);
+      const float v = round_h(base + round_h(la));
       if (MODE == 0) {
         float res = v;
         const int ch = row - d_inner;
@@ -765,7 +796,7 @@ lm_head_mma_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, 
       for (int b = lane; b < nb; b += 32)
         bulk_g2s(sx + b * SX, xn + (size_t)(bt0 + b) * d, (unsigned)(d * 2), &xbar);
     }
-    mbar_wait_bounded(&xbar, phase);
+    if (!mbar_wait_bounded(&xbar, phase)) atomicOr(&g_umma_err, 4u);
     unsigned long long wbest[kHeadMmaNT][2];
 #pragma unroll
     for (int tt = 0; tt < kHeadMmaNT; ++tt) wbest[tt][0] = wbest[tt][1] = 0ull;

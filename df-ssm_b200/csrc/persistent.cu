@@ -49,6 +49,10 @@ constexpr int kThreads = 512;              // compute threads (named barrier 1)
 constexpr int kWarps = kThreads / 32;
 constexpr int kBlockThreads = kThreads + 32;  // + one warp that issues the weight/state copies
 constexpr unsigned kSpinLimit = 1u << 22;
+// Polls after which a bounded wait gives up (kSpinLimit unless dfssm_debug_set_wait_limit lowered
+// it for a test of the timeout path); read only every 256 polls.
+__constant__ unsigned c_spin_limit = kSpinLimit;
+__device__ __forceinline__ unsigned spin_limit() { return c_spin_limit; }
 #ifndef DFSSM_GFIRST
 #define DFSSM_GFIRST 1  // gated vector: poll one word per thread before loading the rest
 #endif
@@ -97,6 +101,7 @@ struct PParams {
   int l0, l1;      // layers run by this launch
   int from_x;      // 1: layer l0 starts from x_g instead of the token embedding
   int do_head;     // 1: final norm + LM head + argmax after layer l1-1
+  int skew;        // test of the timeout path: CTA 0 runs with the next step's tags (never match)
   int n_bc;        // number of B/C CTAs
   int n_t;         // number of LoRA-t producer CTAs (the first n_t B/C CTAs; rank r -> producer r % n_t)
   int ns;          // ring stages
@@ -150,7 +155,7 @@ __device__ __forceinline__ void take_words(const unsigned long long* p, size_t g
       unsigned long long w0;
       asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w0) : "l"(p) : "memory");
       if ((unsigned)(w0 >> 32) == tag) break;
-      if ((it & 255u) == 255u && (ld_acquire(err) != 0 || it > kSpinLimit)) break;
+      if ((it & 255u) == 255u && (ld_acquire(err) != 0 || it > spin_limit())) break;
     }
   }
   for (unsigned it = 0;; ++it) {
@@ -176,7 +181,7 @@ __device__ __forceinline__ void take_words(const unsigned long long* p, size_t g
     if (ok) break;
     if ((it & 255u) == 255u) {
       if (ld_acquire(err) != 0) break;
-      if (it > kSpinLimit) {
+      if (it > spin_limit()) {
         atomicOr(err, code);
         break;
       }
@@ -210,7 +215,7 @@ __device__ __forceinline__ void wait_stage(const PParams& P, uint64_t* bars, int
     unsigned it = 0;
     while (!mbar_try_wait(bars + slot, parity)) {
       if ((++it & 1023u) == 0 && ld_acquire(P.sync + 3) != 0) break;
-      if (it > kSpinLimit) {
+      if (it > spin_limit()) {
         atomicOr(P.sync + 3, 2u);
         break;
       }
@@ -363,7 +368,7 @@ __device__ __forceinline__ float proj_out(int dot, float xs, float wscale, const
     p[i & 3] = fmaf(t[2 * i], f.x, p[i & 3]);
     p[i & 3] = fmaf(t[2 * i + 1], f.y, p[i & 3]);
   }
-  return round_hc(base + ((p[0] + p[1]) + (p[2] + p[3])));
+  return round_hc(base + round_hc((p[0] + p[1]) + (p[2] + p[3])));
 }
 
 __device__ __forceinline__ float conv_silu(float s0, float s1, float s2, float v, const __half* cw, float cb) {
@@ -451,7 +456,7 @@ __device__ void copy_issuer(const PParams& P, const CtaPlan& pl, unsigned char* 
                 ok = 0;
                 break;
               }
-              if (it > kSpinLimit) {
+              if (it > spin_limit()) {
                 atomicOr(P.sync + 3, 32u);
                 ok = 0;
                 break;
@@ -493,7 +498,7 @@ __device__ void copy_issuer(const PParams& P, const CtaPlan& pl, unsigned char* 
               ok = 0;
               break;
             }
-            if (it > kSpinLimit) {
+            if (it > spin_limit()) {
               atomicOr(P.sync + 3, 32u);
               ok = 0;
               break;
@@ -559,7 +564,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
 
   const CtaPlan pl = P.plans[blockIdx.x];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, l16 = lane & 15, hw = tid >> 4;
-  const unsigned ebase = __ldcg(P.sync + 16);  // tag epoch of this launch
+  const unsigned ebase0 = __ldcg(P.sync + 16);  // tag epoch of this launch
+  const unsigned step_tags = (unsigned)(P.n_layer + 1) * kTagsPerLayer;
+  const unsigned ebase = ebase0 + (P.skew && blockIdx.x == 0 ? step_tags : 0u);
   const int XW = d_model / 2, GW = d_inner / 2;
   const size_t rep_off = (size_t)(blockIdx.x % kReplicas) * P.rs;  // this CTA's copy of the exchange words
 
@@ -1021,7 +1028,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
     for (int s = 0; s < P.ns && s < ni; ++s) {
       const int last = s + ((ni - 1 - s) / P.ns) * P.ns;
       unsigned it = 0;
-      while (!mbar_try_wait(bars + s, (unsigned)((last / P.ns) & 1)) && ++it < kSpinLimit) {
+      // a lowered test limit still leaves copies from valid memory ample time to land
+      const unsigned lim = spin_limit() > (1u << 16) ? spin_limit() : (1u << 16);
+      while (!mbar_try_wait(bars + s, (unsigned)((last / P.ns) & 1)) && ++it < lim) {
       }
     }
   }
@@ -1035,7 +1044,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
         const unsigned long long k = atomicExch(P.best + b, 0ull);
         P.tokens[b] = (int)argmax_key_index(k);
       }
-      P.sync[16] = ebase + (unsigned)(P.n_layer + 1) * kTagsPerLayer;  // next launch's tags
+      // next launch's tags (past a skewed CTA's, so none of its words can match them)
+      P.sync[16] = ebase0 + (P.skew ? 2u : 1u) * step_tags;
       __threadfence();
       P.sync[1] = 0;
     }
@@ -1055,6 +1065,7 @@ struct PersistentState {
 
 struct PersistentSet {
   PersistentState st[3];  // indexed by batch size 1, 2
+  int skew_next = 0;      // dfssm_debug_skew_next_step: the next launch runs skewed
 };
 
 template <int B, int KI, int KO>
@@ -1301,10 +1312,25 @@ int launch_persistent_layers(dfssm_engine* e, int l0, int l1, int from_x, int do
     P.l1 = l1;
     P.from_x = from_x;
     P.do_head = do_head;
+    P.skew = set_of(e)->skew_next;
     void* args[] = {&P};
     cudaError_t ce = cudaLaunchCooperativeKernel(ps.fn, dim3(ps.grid), dim3(kBlockThreads), args, (size_t)ps.smem, s);
     if (ce != cudaSuccess) return dfssm_fail(DFSSM_ERR_CUDA, "cooperative launch failed: %s", cudaGetErrorString(ce));
   }
+  set_of(e)->skew_next = 0;
+  return DFSSM_OK;
+}
+
+int persistent_debug_skew(dfssm_engine* e) {
+  if (!e->persist) return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "persistent kernel unavailable");
+  set_of(e)->skew_next = 1;
+  return DFSSM_OK;
+}
+
+int persistent_debug_wait_limit(dfssm_engine* e, unsigned polls) {
+  const unsigned v = polls ? polls : kSpinLimit;
+  if (cudaSetDevice(e->device) != cudaSuccess || cudaMemcpyToSymbol(c_spin_limit, &v, sizeof(v)) != cudaSuccess)
+    return dfssm_fail(DFSSM_ERR_CUDA, "setting the wait limit failed");
   return DFSSM_OK;
 }
 

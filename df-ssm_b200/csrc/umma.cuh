@@ -282,7 +282,7 @@ proj_umma_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
         float la = 0.f;
 #pragma unroll
         for (int r = 0; r < DFSSM_RANK; ++r) la = fmaf(e_t[j * DFSSM_RANK + r], a[r], la);
-        const float vv = round_h(base + la);
+        const float vv = round_h(base + round_h(la));
         if (MODE == 0) {
           float res = vv;
           if (ch >= 0) {

@@ -208,7 +208,7 @@ class DFSSMModel:
     def buffer(self, name: str, dtype, shape):
         p, n = ctypes.c_void_p(), ctypes.c_size_t()
         _lib.check(self.lib.dfssm_get_buffer(self._h, name.encode(), ctypes.byref(p), ctypes.byref(n)))
-        ts = {self.torch.float16: "<f2", self.torch.float32: "<f4", self.torch.int32: "<i4"}[dtype]
+        ts = {self.torch.float16: "<f2", self.torch.float32: "<f4", self.torch.int32: "<i4", self.torch.int8: "|i1"}[dtype]
         return self.torch.as_tensor(_DevArray(p.value, shape, ts), device=self.device)
 
     def layer_step(self, layer: int):

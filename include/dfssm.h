@@ -99,14 +99,17 @@ int dfssm_state_ptrs(dfssm_engine* e, int layer, float** ssm, float** conv);
 
 /* Named internal device buffers for tests and tools: "x" (fp16 [B][d_model] residual),
  * "proj" (fp16 [B][n_in]: z | conv'd xBC | raw dt), "gated" (fp16 [B][d_inner]),
- * "logits" (fp32 [B][vocab]), "tokens" (int32 [B]). */
+ * "logits" (fp32 [B][vocab]), "tokens" (int32 [B]); "q" (int8 [B][K] quantised activations of the
+ * last per-op projection prologue, columns in the GEMV's permuted order) and "xs" (fp16 [B], their
+ * scales). */
 int dfssm_get_buffer(dfssm_engine* e, const char* name, void** ptr, size_t* bytes);
 /* Run layer `layer` alone on the engine's "x" buffer with the kernels of the current mode
  * (per-op kernels, or the persistent kernel over the single layer when mode 3 is selected). */
 int dfssm_layer_step(dfssm_engine* e, int layer, void* stream);
 
 /* Diagnostics (no counterpart in the reference, which has no profiler hooks): number of
- * uint64 entries of a persistent-step trace, and one persistent decode step (mode 3 batch)
+ * uint64 entries of a persistent-step trace, and one persistent decode step (mode 3, batch 1 or 2
+ * only: DFSSM_ERR_UNSUPPORTED for larger batches)
  * that records %globaltimer stamps at its phase boundaries into trace_dev
  * [sm_count][4 + 16 * n_layer]: [0] start, [1] end, [2 + 16l + k] layer l point k
  * (0 alpha entry, 1 after receiving x, 3 after norm/quant/LoRA, 4 after the weight ring wait,
@@ -118,6 +121,16 @@ int dfssm_layer_step(dfssm_engine* e, int layer, void* stream);
  * [2 + 16 n_layer] head entry, [3 + 16 n_layer] after receiving the final x. */
 size_t dfssm_trace_entries(const dfssm_engine* e);
 int dfssm_trace_step(dfssm_engine* e, unsigned long long* trace_dev, void* stream);
+
+/* Test hooks of the persistent kernel's bounded waits (no counterpart in the reference).
+ * dfssm_debug_set_wait_limit: polls after which every bounded wait of the persistent kernel gives up
+ * and sets the error word (0 restores the default, 2^22); it applies to every engine on e's device.
+ * dfssm_debug_skew_next_step: the next persistent launch runs its first CTA with the following
+ * step's exchange tags, so the exchanges with it never complete: every wait runs out, the launch
+ * returns, dfssm_check_finite reports DFSSM_ERR_STATE, and dfssm_reset clears the error word so
+ * that later steps run normally. */
+int dfssm_debug_set_wait_limit(dfssm_engine* e, unsigned polls);
+int dfssm_debug_skew_next_step(dfssm_engine* e);
 
 /* ---- stand-alone ops (reference operator replacements) ---- */
 
@@ -139,7 +152,8 @@ int dfssm_scaffold_gemm(const uint32_t* packed, const int8_t* q, int M, int N, i
  * up the array's device address (cudaGetSymbolAddress), so make that first call before any
  * stream capture.  All calls on a device share the one array: calls that overlap on the GPU
  * (different streams, or threads racing on one device) corrupt each other's results.  Nothing
- * from a previous call is relied on; the scratch is fully rewritten every call. */
+ * from a previous call is relied on; the scratch is fully rewritten every call.  Kernel choice is
+ * that of dfssm_scaffold_gemm (1-bit GEMV below 8 rows, tensor-core kernels from 8 rows). */
 int dfssm_scaffold_gemm_noalloc(const uint32_t* packed, const int8_t* q, int M, int N, int K,
                                 int32_t* acc, void* stream);
 
@@ -158,6 +172,14 @@ int dfssm_ssm_step(const void* xbc_f16, int ld_xbc, const void* dt_f16, int ld_d
                    const float* dt_bias, const float* A_log, const float* D, float* h_state,
                    void* y_f16, int ld_y, int batch, int nheads, int headdim, int d_state,
                    void* stream);
+
+/* RMSNorm + per-row int8 quantisation (df_ssm_inference.py:141-152, _rms_norm then
+ * _quantize_to_int8) of x fp16 [batch][K] with norm weights norm_w fp32 [K]: xn fp16 [batch][K]
+ * = fp16(x * rsqrt(mean(x^2) + 1e-5) * w), scale fp16 [batch] = fp16(max(amax|xn|, fp16(1e-4)) / 127)
+ * and q int8 [batch][K] = clamp(rne(fp16(xn / scale))), in natural column order.  Runs the device
+ * functions of the persistent step kernel's prologues.  K = 512 x {1, 2, 4, 5, 8, 10}. */
+int dfssm_rmsnorm_quantize(const void* x_f16, const float* norm_w, int batch, int K, void* xn_f16, void* scale_f16,
+                           int8_t* q, void* stream);
 
 /* Scratch bytes dfssm_lm_head_argmax needs for `batch` rows. */
 size_t dfssm_lm_head_workspace(int batch);

@@ -18,7 +18,9 @@ following the same points can be compared tightly:
   scaffold      df_ssm_inference.py:154-158   int32 = q . W(+-1)^T; fp16(fp16(fp16(acc)*xs)*ws)
   LoRA          df_ssm_inference.py:78-83,92-97,173,204
                                                A,B dequantised to fp16; t = fp16(x_norm.B^T);
-                                               proj = fp16(proj + t.A^T)
+                                               proj = fp16(proj + fp16(t.A^T)) on CUDA (the fp16
+                                               addmm_ rounds the product first), fp16(proj + t.A^T)
+                                               on the CPU
   split         df_ssm_inference.py:176-178
   conv_step     df_ssm_kernels.cu:27-47        shift register, 4-tap conv + bias, SiLU -> fp16
   ssm_step      df_ssm_kernels.cu:53-103       dt=softplus(dt_raw+dt_bias), Abar=exp(-dt*exp(A_log)),
@@ -33,8 +35,10 @@ Options select the documented deviations of the B200 engine from the literal
 reference: ``state_dtype`` ("f16" is the reference, "f32" the engine contract) and
 ``emb`` ("f16": logits from the fp16 embedding as the reference computes them;
 "int8": logits = fp16(scale_v * sum_k q_vk*x_k), as the engine's int8 LM head).
-``div_mode="cpu"`` switches the quantisation scale to true division, which is what
-torch does on the CPU (used only when checking against goldens made on the CPU).
+``div_mode`` selects where the reference ran: "cuda" (its GPU path: the quantisation scale is a
+multiply by the fp32 reciprocal of 127 and the LoRA product is rounded to fp16 before the add) or
+"cpu" (true division, one rounding of the LoRA add; used only when checking against goldens made
+on the CPU).
 """
 from __future__ import annotations
 
@@ -85,10 +89,16 @@ def lora_dequant(p: fmt.Proj):
     return A16, B16
 
 
-def lora_add(base16: np.ndarray, x16: np.ndarray, A16: np.ndarray, B16: np.ndarray) -> np.ndarray:
-    """df_ssm_inference.py:173: base.addmm_(x @ B^T, A^T), fp32-or-better accumulate."""
+def lora_add(base16: np.ndarray, x16: np.ndarray, A16: np.ndarray, B16: np.ndarray, div_mode: str = "cuda") -> np.ndarray:
+    """df_ssm_inference.py:173,204: base.addmm_(x @ B^T, A^T), fp32-or-better accumulate.
+    t = fp16(x . B^T).  On CUDA (torch 2.11 / cuBLAS, measured on the B200) the fp16 addmm_ rounds
+    the rank-16 product t . A^T to fp16 before adding it to base: fp16(base + fp16(t . A^T)); on
+    the CPU it rounds once: fp16(base + t . A^T)."""
     t = (x16.astype(np.float64) @ B16.astype(np.float64).T).astype(F16)
-    return (base16.astype(np.float64) + t.astype(np.float64) @ A16.astype(np.float64).T).astype(F16)
+    prod = t.astype(np.float64) @ A16.astype(np.float64).T
+    if div_mode == "cuda":
+        prod = prod.astype(F16).astype(np.float64)
+    return (base16.astype(np.float64) + prod).astype(F16)
 
 
 def silu_f32(v: np.ndarray) -> np.ndarray:
@@ -201,7 +211,7 @@ class OracleModel:
         acc = scaffold_int32(q, self.signs(l, which))
         base = dequant(acc, xs, p.scale)
         A16, B16 = self._lora[l][0 if which == "in_proj" else 1]
-        return lora_add(base, x16, A16, B16)
+        return lora_add(base, x16, A16, B16, self.div_mode)
 
     def layer(self, x16: np.ndarray, l: int) -> np.ndarray:
         d, L = self.d, self.w.layers[l]

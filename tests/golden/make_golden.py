@@ -12,10 +12,10 @@ CPU of the build container, imported from the reference checkout given by
     same tensor dtypes `_load` produces (LoRA dequantised to fp16, int8 +-1 weights
     transposed, fp16 norms);
   * `_graph` is replaced by a direct call of `_run_layers` (no CUDA graph on a CPU);
-  * `df_ssm_kernels` (a CUDA extension) is replaced by a torch restatement of
-    conv_step_kernel / ssm_step_kernel (df_ssm_kernels.cu:27-47, 53-103).  That
-    restatement is pinned separately against the real CUDA kernels on a GPU
-    (tests/test_ref_kernels_gpu.py);
+  * `df_ssm_kernels` (a CUDA extension) is replaced by the torch restatement of
+    conv_step_kernel / ssm_step_kernel (df_ssm_kernels.cu:27-47, 53-103) in
+    oracle/ref_torch.py.  That restatement is pinned separately against the real
+    CUDA kernels on a GPU (tests/test_parity_ref_gpu.py);
   * variant "f32state" allocates h/conv state in fp32 instead of fp16
     (df_ssm_inference.py:114-121), the contract the B200 engine implements.
 
@@ -37,39 +37,14 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 
 from dfssm_b200 import synthetic  # noqa: E402
 
-
-def _conv_step(conv_state, xBC, conv_weight, conv_bias, d_xBC):
-    s = conv_state.float()
-    xv = xBC.float()
-    w = conv_weight.float()
-    out = s[..., 0] * w[:, 0] + s[..., 1] * w[:, 1] + s[..., 2] * w[:, 2] + xv * w[:, 3] + conv_bias.float()
-    conv_state[..., 0] = s[..., 1].to(conv_state.dtype)
-    conv_state[..., 1] = s[..., 2].to(conv_state.dtype)
-    conv_state[..., 2] = xv.to(conv_state.dtype)
-    xBC.copy_((out * (1.0 / (1.0 + torch.exp(-out)))).to(xBC.dtype))
-
-
-def _make_ssm_step(d):
-    def _ssm_step(h_state, xBC, dt, dt_bias, A_log, D_param, y_out):
-        B = h_state.shape[0]
-        H, P = d.nheads, d.headdim
-        dtv = torch.log1p(torch.exp(dt.float() + dt_bias.float()))                  # [B,H]
-        Abar = torch.exp(dtv * (-torch.exp(A_log.float())))
-        x = xBC[:, :d.d_inner].float().reshape(B, H, P)
-        Bp = xBC[:, d.d_inner:d.d_inner + d.d_state].float()
-        Cp = xBC[:, d.d_inner + d.d_state:d.d_inner + 2 * d.d_state].float()
-        X = x * dtv[:, :, None]
-        h = Abar[:, :, None, None] * h_state.float() + X[..., None] * Bp[:, None, None, :]
-        h_state.copy_(h.to(h_state.dtype))
-        y = (h * Cp[:, None, None, :]).sum(-1) + x * D_param.float()[None, :, None]
-        y_out.copy_(y.reshape(B, H * P).to(y_out.dtype))
-    return _ssm_step
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(HERE)), "oracle"))
+from ref_torch import conv_step_torch, make_ssm_step_torch  # noqa: E402
 
 
 def load_reference(ref_root: str, d):
     stub = types.ModuleType("df_ssm_kernels")
-    stub.conv_step = _conv_step
-    stub.ssm_step = _make_ssm_step(d)
+    stub.conv_step = conv_step_torch
+    stub.ssm_step = make_ssm_step_torch(d.d_inner, d.d_state, d.nheads, d.headdim)
     sys.modules["df_ssm_kernels"] = stub
     path = os.path.join(ref_root, "inference", "gpu", "df_ssm_inference.py")
     spec = importlib.util.spec_from_file_location("df_ssm_inference_ref", path)

@@ -58,7 +58,11 @@ def test_single_layer_matches_oracle(B, mode, shape):
     # is in ulps of the residual stream rather than a fraction of bit-identical entries
     got_x, want_x = xb[:B].cpu().numpy().astype(np.float32), ref["x"].astype(np.float32)
     assert np.abs(got_x - want_x).max() <= 8 * f16_ulp(np.abs(want_x).max())
-    np.testing.assert_allclose(m.h_states[0][:B].cpu().numpy(), hs, rtol=2e-3, atol=2e-4)
+    # one flipped fp16 input (an x channel or a head's dt) moves that row's update by ~1e-3 of
+    # itself, so the state is bounded in norm and by a small fraction of its scale elementwise
+    h = m.h_states[0][:B].cpu().numpy()
+    assert np.linalg.norm(h - hs) <= 1e-3 * np.linalg.norm(hs)
+    assert np.abs(h - hs).max() <= 5e-3 * np.abs(hs).max()
     np.testing.assert_allclose(m.conv_states[0][:B].cpu().numpy(), cs, rtol=1e-2, atol=1e-2)
 
 
@@ -105,7 +109,8 @@ def test_tiny_model_matches_oracle(B, mode, shape):
 @pytest.mark.parametrize("mode", ["graph", "persistent"])
 @pytest.mark.parametrize("variant", ["f32state", "f16state"])
 def test_cfg0_matches_reference_golden(variant, mode):
-    """Config 0 (2-layer 1.3B width, batch 1) against the reference driver's own outputs."""
+    """Config 0 (2-layer 1.3B width, batch 1) against the reference driver's own outputs, as run
+    on the CPU (tokens and logits, teacher-forced)."""
     g = np.load(os.path.join(GOLDEN, "golden_cfg0.npz"))
     w = weights("1.3b", 2, seed=0)
     m = model(w, 1, mode=mode)
@@ -116,11 +121,9 @@ def test_cfg0_matches_reference_golden(variant, mode):
     mine = np.take_along_axis(logs, idx, -1)
     _check_logits(mine, ref)
     np.testing.assert_array_equal(toks, gt)
-    if variant == "f32state":
-        for l in range(2):
-            h = m.h_states[l][:1, :2].cpu().numpy()
-            rh = g[f"f32state_h{l}"]
-            assert np.abs(h - rh).max() / np.abs(rh).max() <= 5e-3
+    # The goldens ran on the CPU, whose fp16 LoRA add rounds once; the engine follows the
+    # reference's GPU path (the LoRA product rounded to fp16 first), so the state is compared with
+    # that path on the GPU instead (tests/test_parity_ref_gpu.py, rel 1e-3 after 128 steps).
 
 
 def test_graph_and_eager_are_bitwise_equal():
@@ -205,13 +208,43 @@ def test_persistent_is_deterministic_and_reports_no_timeouts(B):
     m.check_finite()  # also fails if any bounded wait in the kernel timed out
 
 
-@pytest.mark.parametrize("B", [2, 3, 4])
+@pytest.mark.parametrize("B", [2, 3, 4, 6])
 def test_persistent_matches_graph_tokens_on_1p3b_two_layers(B):
     w = weights("1.3b", 2, seed=3)
     p = np.random.default_rng(8).integers(0, w.dims.vocab, (B, 4))
     a = model(w, B, mode="persistent").generate(12, prompt=p, verbose=False)
     b = model(w, B, mode="graph").generate(12, prompt=p, verbose=False)
     np.testing.assert_array_equal(a, b)
+
+
+def test_persistent_wait_timeout_returns_error_and_recovers():
+    """The persistent kernel's bounded waits run out without a fault: with a lowered poll limit and
+    one CTA on the next step's exchange tags (dfssm_debug_skew_next_step), no exchange completes,
+    the launch still returns, dfssm_check_finite reports DFSSM_ERR_STATE, and after dfssm_reset the
+    engine decodes exactly as a fresh one."""
+    import time
+    from dfssm_b200 import _lib
+    w = weights("small", 2, seed=5)
+    p = np.random.default_rng(3).integers(0, w.dims.vocab, (1, 4))
+    want = model(w, 1, mode="persistent").generate(6, prompt=p, verbose=False)
+    m = model(w, 1, mode="persistent")
+    lib = m.lib
+    m.generate(2, prompt=p, verbose=False)
+    try:
+        _lib.check(lib.dfssm_debug_set_wait_limit(m._h, 4096))
+        _lib.check(lib.dfssm_debug_skew_next_step(m._h))
+        t0 = time.perf_counter()
+        m.step(None, logits=True)
+        torch.cuda.synchronize()
+        assert time.perf_counter() - t0 < 10.0  # ended by the limit, not by a hang
+        with pytest.raises(_lib.DFSSMError) as ei:
+            m.check_finite()
+        assert ei.value.code == 6  # DFSSM_ERR_STATE
+        assert b"timed-out wait" in lib.dfssm_last_error()
+    finally:
+        _lib.check(lib.dfssm_debug_set_wait_limit(m._h, 0))
+    np.testing.assert_array_equal(m.generate(6, prompt=p, verbose=False), want)
+    m.check_finite()
 
 
 @pytest.mark.parametrize("groups", ["2", "4"])
