@@ -196,13 +196,17 @@ def run_reference_arm(args, cfg, rank, world):
         print(json.dumps({"impl": "reference", "unavailable": res["unavailable"]}))
         return
     value = res["tok_per_s"]
+    from dfssm_b200 import synthetic
+    dims = synthetic.make_dims(cfg["shape"], cfg["layers"])
     sample = f"{args.steps} greedy steps x batch {batch} after a {PROMPT_LEN}-token prompt, {cfg['layers']}-layer {cfg['shape']}"
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": res["seconds"] / args.steps * 1e3, "higher_is_better": True,
             "scaling": cfg["scaling"], "vs_baseline": None, "dtype": "int8/fp32 (AVX-512 VNNI)",
             "data": "synthetic (seeded random weights and prompts)", "impl": "reference",
-            "config": {"workload": args.config, "shape": cfg["shape"], "layers": cfg["layers"], "batch": batch,
-                       "engine": "reference inference/cpu/cpu_inference.c (HEADDIM 64), cpu_inference_driver loop"},
+            "config": workload_config(args.config, cfg, rank_batch(cfg, world)[0], batch,
+                                      step_bytes(dims, rank_batch(cfg, world)[0])["total"]),
+            "engine": {"impl": "reference inference/cpu/cpu_inference.c (HEADDIM 64), cpu_inference_driver loop",
+                       "parallelism": "rank 0 decodes every sequence of the job on the host cores"},
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "reference",
                              "sample": sample, "cpu": cpu_model_name()},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -333,6 +337,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--mode", default="auto", choices=["auto", "graph", "eager", "persistent"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub", action="store_true", help="skip the sub-records (batch-32 and cfg4 lines)")
+    ap.add_argument("--cfg4", action="store_true", help="add the cfg4 batch-256 strong-split sub-record at N = 1 too")
     ap.add_argument("--prefill", type=int, default=0, metavar="T",
                     help="time K prompt prefills of T tokens per sequence instead of decode steps")
     args = ap.parse_args()
@@ -377,45 +383,23 @@ def main():
     batch, job_batch = rank_batch(cfg, world)
     dims = synthetic.make_dims(cfg["shape"], cfg["layers"])
     w = synthetic.make_weights(dims, seed=0)
-    prompts = synthetic.make_prompts(dims.vocab, job_batch, PROMPT_LEN, seed=0)
-    my_prompts = prompts[rank_rows(rank, batch)]
-    m = DFSSMModel(w, device=f"cuda:{local}", batch_size=batch, mode=args.mode)
-    del w
-    stream = torch.cuda.current_stream()
     if args.prefill:
+        m = DFSSMModel(w, device=f"cuda:{local}", batch_size=batch, mode=args.mode)
         run_prefill_bench(args, cfg, m, batch, world, rank, local, dims)
         return
 
-    # prompt + warm-up (untimed)
-    m.reset_state()
-    m.prefill(torch.from_numpy(my_prompts))
-    for _ in range(args.warmup):
-        m.step(None, logits=False)
-    torch.cuda.synchronize()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    ids = [v for v in vis.split(",") if v.strip()]
+    phys = int(ids[local]) if ids and local < len(ids) and ids[local].strip().isdigit() else local
+    rec, m = decode_record(args, args.config, cfg, w, dims, world, rank, local, phys, keep=True)
+    batch = rec["batch"]
 
+    # ---------------- end-to-end through the public host-buffer API (tokens in/out via pinned host memory)
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
-    # ---------------- device-timed region: K greedy steps, inputs resident in HBM
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
-    ids = [v for v in vis.split(",") if v.strip()]
-    phys = int(ids[local]) if ids and local < len(ids) and ids[local].strip().isdigit() else local
-    clocks = ClockSampler(phys)
-    clocks.start()
-    time.sleep(0.3)
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        m.step(None, logits=False)
-    e1.record(stream)
-    barrier()
-    clk = clocks.stop()
-    ms_max = max_over_ranks(e0.elapsed_time(e1), world, torch.device("cuda", local))
-
-    # ---------------- end-to-end through the public host-buffer API (tokens in/out via pinned host memory)
     tok_h = torch.empty(batch, dtype=torch.int32).pin_memory().numpy()
     nxt_h = torch.empty(batch, dtype=torch.int32).pin_memory().numpy()
     tok_h[:] = m._tok_out[:batch].cpu().numpy()
@@ -428,23 +412,12 @@ def main():
     e2e_s = time.perf_counter() - t0
     e2e_s = max_over_ranks(e2e_s, world, torch.device("cuda", local))
     m.check_finite()
+    mode = m.mode
+    m.close()
+    del m
 
     tokens_total = batch * world * args.steps
-    value = tokens_total / (ms_max / 1e3)
     e2e_value = tokens_total / e2e_s
-    sb = step_bytes(dims, batch)
-    peak, peak_kind = load_peaks()
-    step_ms = ms_max / args.steps
-    achieved = sb["total"] / (step_ms / 1e3) / 1e9
-    n_launch = {"graph": 5 * dims.n_layer + 4, "eager": 5 * dims.n_layer + 4, "persistent": 1}[m.mode]
-    traffic = None
-    tf = os.path.join(ROOT, "profiles", "dram_traffic.json")
-    if os.path.exists(tf):
-        with open(tf) as f:
-            tj = json.load(f)
-        ent = tj.get(f"{args.config}:{m.mode}:b{batch}")
-        if ent:
-            traffic = ent["bytes_per_launch"]
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -459,31 +432,127 @@ def main():
         else:
             cpu = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference", "sample": res["unavailable"]}
 
+    # ---------------- sub-records timed in the same process: the other half of the metric (batch 32 per
+    # GPU) and, on multi-GPU runs, the batch-256 2.7B decode split over the ranks (strong scaling)
+    subs = {}
+    if args.config == "cfg1" and not args.no_sub:
+        del w
+        subs["cfg2_batch32"] = decode_record(args, "cfg2", dict(CONFIGS["cfg2"]), None, None, world, rank, local, phys)[0]
+    if (args.gpus > 1 or world > 1 or args.cfg4) and args.config != "cfg4" and not args.no_sub:
+        subs["cfg4_batch256_strong"] = decode_record(args, "cfg4", dict(CONFIGS["cfg4"]), None, None, world, rank,
+                                                     local, phys, steps=min(args.steps, 32))[0]
+
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": cfg["scaling"],
-            "vs_baseline": None, "dtype": "int8 x 1-bit -> int32 scaffold, fp16 activations, fp32 state",
+            "metric": METRIC, "value": rec["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": rec["ms_per_step"], "higher_is_better": True,
+            "scaling": cfg["scaling"], "vs_baseline": None,
+            "dtype": "int8 x 1-bit -> int32 scaffold, fp16 activations, fp32 state",
             "data": "synthetic (seeded random weights of the named shape and random prompts)",
-            "config": {"workload": args.config, "shape": cfg["shape"], "layers": cfg["layers"],
-                       "batch_per_gpu": batch, "global_batch": batch * world, "prompt": PROMPT_LEN,
-                       "parallelism": f"sequence-sharded dp{world} (no collective)", "mode": m.mode,
-                       "l2": "no flush: each step streams >= %.0f MB from HBM (> 126 MB L2)" % (sb["total"] / 1e6)},
-            "roofline": {"bound": "hbm", "kernel": "whole decode step" if m.mode != "persistent" else "persistent step kernel",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "bytes_per_step": sb["total"], "traffic": traffic},
+            "config": rec["config"],
+            "engine": {"mode": mode, "parallelism": f"sequence-sharded dp{world} (no collective)"},
+            "roofline": rec["roofline"],
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4 * batch,
                     "d2h_bytes_per_step": 4 * batch},
-            "gpu_launches": n_launch * args.steps,
-            "clocks": clk,
+            "gpu_launches": rec["gpu_launches"] + sum(r["gpu_launches"] for r in subs.values()),
+            "clocks": rec["clocks"],
             "cpu_baseline": cpu,
         }
+        for k, r in subs.items():
+            line[k] = {kk: r[kk] for kk in ("value", "unit", "ms_per_step", "steps", "scaling", "config", "engine",
+                                            "roofline", "gpu_launches", "clocks")}
         print(json.dumps(line))
-    m.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
 
+
+def persistent_launches(batch: int) -> int:
+    """Launches of the persistent step kernel per step: one per group of 4, 2 and 1 sequences."""
+    n = 0
+    while batch > 0:
+        batch -= 4 if batch >= 4 else (2 if batch >= 2 else 1)
+        n += 1
+    return n
+
+
+def workload_config(name: str, cfg: dict, batch: int, job_batch: int, total_bytes: float) -> dict:
+    """The workload keys, identical in both arms (the reference arm runs the same workload)."""
+    return {"workload": name, "shape": cfg["shape"], "layers": cfg["layers"], "batch_per_gpu": batch,
+            "global_batch": job_batch, "prompt": PROMPT_LEN,
+            "l2": "no flush: each step streams >= %.0f MB from HBM (> 126 MB L2)" % (total_bytes / 1e6)}
+
+
+def decode_record(args, name, cfg, w, dims, world, rank, local, phys, keep=False, steps=None):
+    """Builds the engine for one decode workload, consumes the prompts and W warm-up steps, then
+    times K greedy steps with CUDA events between a barrier + synchronize on each side (max over
+    ranks).  Returns (record, engine if keep else None)."""
+    import torch
+    import torch.distributed as dist
+    from dfssm_b200 import synthetic
+    from dfssm_b200.model import DFSSMModel
+    steps = steps or args.steps
+    batch, job_batch = rank_batch(cfg, world)
+    if w is None:
+        dims = synthetic.make_dims(cfg["shape"], cfg["layers"])
+        w = synthetic.make_weights(dims, seed=0)
+    prompts = synthetic.make_prompts(dims.vocab, job_batch, PROMPT_LEN, seed=0)
+    my_prompts = prompts[rank_rows(rank, batch)]
+    m = DFSSMModel(w, device=f"cuda:{local}", batch_size=batch, mode=args.mode)
+    del w
+    stream = torch.cuda.current_stream()
+    m.reset_state()
+    m.prefill(torch.from_numpy(my_prompts))
+    for _ in range(args.warmup):
+        m.step(None, logits=False)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    clocks = ClockSampler(phys)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        m.step(None, logits=False)
+    e1.record(stream)
+    barrier()
+    clk = clocks.stop()
+    ms_max = max_over_ranks(e0.elapsed_time(e1), world, torch.device("cuda", local))
+    m.check_finite()
+    sb = step_bytes(dims, batch)
+    peak, peak_kind = load_peaks()
+    step_ms = ms_max / steps
+    achieved = sb["total"] / (step_ms / 1e3) / 1e9
+    n_launch = {"graph": 5 * dims.n_layer + 4, "eager": 5 * dims.n_layer + 4,
+                "persistent": persistent_launches(batch)}[m.mode]
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    if os.path.exists(tf):
+        with open(tf) as f:
+            tj = json.load(f)
+        ent = tj.get(f"{name}:{m.mode}:b{batch}")
+        if ent:
+            traffic = ent["bytes_per_launch"]
+    rec = {"value": batch * world * steps / (ms_max / 1e3), "unit": "tok/s", "ms_per_step": step_ms, "steps": steps,
+           "scaling": cfg["scaling"], "batch": batch,
+           "config": workload_config(name, cfg, batch, job_batch, sb["total"]),
+           "engine": {"mode": m.mode, "parallelism": f"sequence-sharded dp{world} (no collective)"},
+           "roofline": {"bound": "hbm", "kernel": "whole decode step" if m.mode != "persistent" else "persistent step kernel",
+                        "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                        "peak_kind": peak_kind, "bytes_per_step": sb["total"], "traffic": traffic},
+           "gpu_launches": n_launch * steps, "clocks": clk}
+    if keep:
+        return rec, m
+    m.close()
+    del m
+    torch.cuda.empty_cache()
+    return rec, None
 
 if __name__ == "__main__":
     main()

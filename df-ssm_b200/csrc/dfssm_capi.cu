@@ -82,7 +82,14 @@ namespace {
 // (batch <= 2), else the per-op kernels replayed from a CUDA graph.
 int effective_mode(const dfssm_engine* e) {
   if (e->mode != 0) return e->mode;
-  return persistent_supported(e) ? 3 : 1;
+  // measured at the 1.3B shape: batches 1, 2 and 4 run one persistent launch (0.55, 0.72 and
+  // 1.23 ms per step), batch 3 two (1.26 ms); from batch 5 the per-op graph on the mma.sync
+  // projections is faster (1.76 ms at 5, 1.83 at 6 against 1.77 and 1.96 for two launches)
+  static const int persist_max = [] {
+    const char* v = getenv("DFSSM_PERSIST_MAX");
+    return v ? atoi(v) : 4;
+  }();
+  return e->batch <= persist_max && persistent_supported(e) ? 3 : 1;
 }
 
 // ------------------------------------------------------------------ kernel launches
@@ -142,6 +149,16 @@ constexpr int kMmaMinBatch = 8;
 inline bool mma_ok(int K, int RG) {
   const int KS = (kMmaThreads / 32) / RG;
   return K % 128 == 0 && ((K / 32) % KS) == 0 && ((K / 32 / KS) % 4) == 0 && (K / 32 / KS) <= 4 * kMmaMaxBlk;
+}
+// Batch from which the engine's per-op projections use the mma.sync kernel instead of the 1-bit
+// GEMV (DFSSM_MMA_MIN overrides it): at the 1.3B shape the per-op step took 1.60 ms at batch 3 on
+// mma.sync against ~2.8 ms on the GEMV.
+int mma_min_batch() {
+  static const int v = [] {
+    const char* e = getenv("DFSSM_MMA_MIN");
+    return e ? atoi(e) : 3;
+  }();
+  return v;
 }
 // Row groups per CTA for an N x K projection (0 = no tensor-core configuration fits).
 inline int mma_rg(int N, int K) {
@@ -302,7 +319,7 @@ template <int MODE>
 int launch_gemv(dfssm_engine* e, const ProjW& p, int B, const int8_t* q, const int* qsum, const __half* xs,
                 const __half* t, void* out, int ld_out, float* conv_state, const LayerW* L, cudaStream_t s,
                 UmmaScratch us) {
-  if (B >= kMmaMinBatch && mma_rg(p.N, p.K))
+  if (B >= mma_min_batch() && mma_rg(p.N, p.K))
     return launch_mma<MODE>(p, B, q, qsum, xs, t, out, ld_out, conv_state, L ? L->conv_w : nullptr,
                             L ? L->conv_b : nullptr, e->d.d_inner, e->d.d_xbc, s, us);
   const size_t sm = (size_t)kGemvBT * p.K;
@@ -655,6 +672,12 @@ int build_engine(const unsigned char* img, size_t n, int device, int max_batch, 
     off = align256(off + bytes);
     return o;
   };
+  // The persistent kernel's sync words and tagged exchange words (x, B/C, gated and LoRA t for 2
+  // layer parities x its largest launch group, in replicas) come first, at the allocation's
+  // aligned base: their L2 placement affects every exchange, so it must not move with the batch
+  // capacity or the model's state size.
+  const size_t o_sync = take(4096);
+  const size_t o_xch = take(persistent_xch_bytes(d));
   const size_t o_ssm = take(e->ssm_layer * d.n_layer * 4);
   const size_t o_conv = take(e->conv_layer * d.n_layer * 4);
   const size_t o_x = take((size_t)B * d.d_model * 2);
@@ -668,10 +691,6 @@ int build_engine(const unsigned char* img, size_t n, int device, int max_batch, 
   const size_t o_logits = take((size_t)B * d.vocab * 4);
   const size_t o_best = take((size_t)B * 8);
   const size_t o_tok = take((size_t)B * 4);
-  const size_t o_sync = take(4096);
-  // tagged exchange words of the persistent kernel: x, B/C, gated and LoRA t for 2 layer
-  // parities x 2 sequences
-  const size_t o_xch = take(persistent_xch_bytes(d));
   const size_t umma_rows = B >= kMmaMinBatch ? (size_t)B : 0;  // any batch that may take the tcgen05 path
   const size_t o_uacc = take(umma_rows * (d.n_in > d.d_model ? d.n_in : d.d_model) * 4);
   const size_t o_ucnt = take(umma_rows ? (size_t)kUmmaMaxTiles * 4 : 0);

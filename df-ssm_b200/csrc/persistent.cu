@@ -34,6 +34,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <type_traits>
 #include <vector>
 
 #include "engine.h"
@@ -57,6 +58,11 @@ __device__ __forceinline__ unsigned spin_limit() { return c_spin_limit; }
 #define DFSSM_GFIRST 1  // gated vector: poll one word per thread before loading the rest
 #endif
 constexpr int kMaxRPW = 2;  // SSM rows per warp (np = 32 channels over 16 warps)
+constexpr int kDotRows = 64;  // in_proj / out_proj rows a CTA may own (GEMV results in shared memory)
+// Reduction scratch: three rotating single-barrier buffers of 16 x B floats at red, red + 64 and
+// red + 128 (B <= 4), the (16 + 1) x B floats of the final norm's reduction and the 16 x B argmax
+// keys of the LM head.
+constexpr int kRedFloats = 192;
 
 struct CtaPlan {
   int role;       // 0 = head item, 1 = B/C rows, 2 = no in_proj rows
@@ -74,7 +80,8 @@ struct Layout {  // byte offsets inside one ring stage (identical for every CTA)
 };
 
 struct PParams {
-  const LayerW* layers;
+  LayerW lw0;          // layer 0's weights; layer l's arrays lie lstride bytes further per layer
+  long long lstride;
   const CtaPlan* plans;
   Layout lay;
   int n_layer, d_model, d_inner, d_state, d_xbc, n_in, nheads, vocab;
@@ -117,6 +124,18 @@ __device__ __forceinline__ void stamp(const PParams& P, int idx) {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     P.trace[(size_t)blockIdx.x * (4 + kTracePerLayer * P.n_layer) + idx] = t;
   }
+}
+
+// Weight pointers of layer l: every layer's arrays sit at the same offsets within equal-sized
+// slices of the weight arena (checked on the host when the plan is built).
+__device__ __forceinline__ LayerW layer_w(const PParams& P, int l) {
+  const long long o = (long long)l * P.lstride;
+  LayerW L = P.lw0;
+  auto mv = [o](auto*& p) { p = reinterpret_cast<std::remove_reference_t<decltype(p)>>(reinterpret_cast<const char*>(p) + o); };
+  mv(L.in.bits), mv(L.in.scale), mv(L.in.A16), mv(L.in.B16);
+  mv(L.out.bits), mv(L.out.scale), mv(L.out.A16), mv(L.out.B16);
+  mv(L.conv_w), mv(L.conv_b), mv(L.A_log), mv(L.Dp), mv(L.dt_bias), mv(L.norm_w), mv(L.ln_w);
+  return L;
 }
 
 // ---- tagged exchange words
@@ -229,9 +248,9 @@ __device__ __forceinline__ void wait_stage(const PParams& P, uint64_t* bars, int
 // size (0 = none); all 16-byte aligned, sizes multiples of 16.  The byte total of a stage is
 // precomputed on the host (CtaPlan::tx).
 template <int B>
-__device__ __forceinline__ void copy_desc(const PParams& P, const CtaPlan& pl, int layer, const LayerW* layers, int i,
+__device__ __forceinline__ void copy_desc(const PParams& P, const CtaPlan& pl, int layer, int i,
                                           const void*& src, int& dst, unsigned& bytes) {
-  const LayerW& L = layers[layer];
+  const LayerW L = layer_w(P, layer);
   const Layout& Y = P.lay;
   const int RB = P.d_model / 8, RBO = P.d_inner / 8;
   const void* s_ = nullptr;
@@ -434,7 +453,7 @@ __device__ __forceinline__ void fetch_t(const PParams& P, const unsigned long lo
 // Bounded: gives up when a wait times out or the error word is set.
 template <int B>
 __device__ void copy_issuer(const PParams& P, const CtaPlan& pl, unsigned char* ring, uint64_t* full,
-                            uint64_t* empty, const LayerW* layers) {
+                            uint64_t* empty) {
   const int lane = threadIdx.x & 31;
   const int nl = P.l1 - P.l0;
   const unsigned tx = (unsigned)pl.tx;
@@ -479,7 +498,7 @@ __device__ void copy_issuer(const PParams& P, const CtaPlan& pl, unsigned char* 
     const void* src;
     int dst;
     unsigned n;
-    copy_desc<B>(P, pl, layer, layers, lane, src, dst, n);
+    copy_desc<B>(P, pl, layer, lane, src, dst, n);
     unsigned pre = n;  // inclusive prefix sum of the copy sizes over lanes -> first byte of mine
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -544,8 +563,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
   float* s_misc = reinterpret_cast<float*>(smem + B * d_model * 2 + B * d_inner);
   // reduction buffers: red (norm, odd LoRA ranks), red + 64 (even LoRA ranks), red + 128
   // (quantisation amax) -- consecutive single-barrier reductions never share one
-  float* red = s_misc;                              // [(kWarps + 1) * (B*16+B)] >= 192
-  float* s_t = red + (kWarps + 1) * (B * 16 + B);   // [B*16]
+  float* red = s_misc;                              // [kRedFloats]
+  float* s_t = red + kRedFloats;                    // [B*16]
   float* s_xs = s_t + B * 16;                       // [B]
   int* s_qpart = reinterpret_cast<int*>(s_xs + B);  // [B][kWarps] per-warp q sums
   float* s_lbs = reinterpret_cast<float*>(s_qpart + B * kWarps);  // [16]
@@ -553,11 +572,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
   float* s_xc = s_z + B * 64;                       // [B][64]
   float* s_dt = s_xc + B * 64;                      // [B]
   float* s_bc = s_dt + B;                           // [B][2*d_state] (fp32)
-  int* s_dot = reinterpret_cast<int*>(s_bc + B * 2 * DFSSM_DSTATE);  // [128][B] GEMV results
-  // per-layer tables copied once at kernel start (no dependent global loads inside the loop):
+  int* s_dot = reinterpret_cast<int*>(s_bc + B * 2 * DFSSM_DSTATE);  // [kDotRows][B] GEMV results
+  // per-layer table copied once at kernel start (no dependent global loads inside the loop):
   // the layer pointer table, and this CTA's head scalars (dt_bias, A_log, D) for every layer
-  LayerW* s_layers = reinterpret_cast<LayerW*>(smem + P.tab_off);
-  float* s_hptab = reinterpret_cast<float*>(smem + P.tab_off + ((P.n_layer * (int)sizeof(LayerW) + 15) & ~15));  // [n_layer][4], 16-byte aligned
+  float* s_hptab = reinterpret_cast<float*>(smem + P.tab_off);  // [n_layer][4], 16-byte aligned
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.ring_off - 8 * 8);      // ring slot full
   uint64_t* empties = reinterpret_cast<uint64_t*>(smem + P.ring_off - 8 * 8 - 8 * 4 * 8);  // [slot][part] released
   unsigned char* ring = smem + P.ring_off;
@@ -580,12 +598,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
   __syncthreads();
   stamp(P, 0);
   {
-    const int nw = P.n_layer * (int)sizeof(LayerW) / 8;
-    for (int i = tid; i < nw; i += kBlockThreads)
-      reinterpret_cast<unsigned long long*>(s_layers)[i] = reinterpret_cast<const unsigned long long*>(P.layers)[i];
     if (pl.role == 0) {
       for (int l = tid; l < P.n_layer; l += kBlockThreads) {
-        const LayerW& G = P.layers[l];
+        const LayerW G = layer_w(P, l);
         float* e = s_hptab + l * 4;
         e[0] = G.dt_bias[pl.h];
         e[1] = G.A_log[pl.h];
@@ -595,7 +610,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
   }
   __syncthreads();
   if (wid == kWarps) {
-    copy_issuer<B>(P, pl, ring, bars, empties, s_layers);
+    copy_issuer<B>(P, pl, ring, bars, empties);
     return;
   }
 
@@ -609,7 +624,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
   cta_sync();
 
   for (int layer = P.l0; layer < P.l1; ++layer) {
-    const LayerW& L = s_layers[layer];
+    const LayerW L = layer_w(P, layer);
     unsigned char* st = ring + (size_t)((layer - P.l0) % P.ns) * P.lay.stage_bytes;
     // ---------------- alpha: per-thread weights are loaded before waiting for x
     float w_in[KI];
@@ -672,12 +687,17 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       release_part(P, empties, layer, 1);
       fetch_t<B>(P, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTin), s_t, t_early);
       stamp(P, tb + 2);
-      // threads < B * d_state take the B/C words, the next B threads the word holding dt of head h
-      const int bc_b = tid < B * DFSSM_DSTATE ? tid / DFSSM_DSTATE : tid - B * DFSSM_DSTATE;
-      const int bc_j = tid < B * DFSSM_DSTATE ? tid - bc_b * DFSSM_DSTATE : DFSSM_DSTATE + pl.h / 2;
-      const bool bc_taker = tid < B * (DFSSM_DSTATE + 1);
-      const unsigned long long* bcw_mine =
-          P.bcw + ((size_t)par * B + (bc_taker ? bc_b : 0)) * P.bcw_per_seq + rep_off + (bc_taker ? bc_j : 0);
+      // word i < B * d_state is B/C word i % d_state of sequence i / d_state, word B * d_state + b
+      // the one holding dt of head h for sequence b; thread tid takes word tid (read ahead once
+      // here) and, where B * (d_state + 1) > kThreads, word tid + kThreads as well
+      constexpr int kBcWords = B * (DFSSM_DSTATE + 1);
+      auto bc_word = [&](int i) {
+        const int b = i < B * DFSSM_DSTATE ? i / DFSSM_DSTATE : i - B * DFSSM_DSTATE;
+        const int j = i < B * DFSSM_DSTATE ? i - b * DFSSM_DSTATE : DFSSM_DSTATE + pl.h / 2;
+        return P.bcw + ((size_t)par * B + b) * P.bcw_per_seq + rep_off + j;
+      };
+      const bool bc_taker = tid < kBcWords;
+      const unsigned long long* bcw_mine = bc_word(bc_taker ? tid : 0);
       const unsigned long long bc_early = bc_taker ? peek_word(bcw_mine) : 0ull;
       for (int e2 = tid; e2 < nrows * B; e2 += kThreads) {
         const int row = e2 / B, b = e2 - row * B;
@@ -697,15 +717,19 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       }
       cta_sync();
       stamp(P, tb + 5);
-      // wait for every B/C CTA of this layer, then fetch conv'd B and C and dt (B * (d_state + 1)
-      // <= 512 words)
+      // wait for every B/C CTA of this layer, then fetch conv'd B and C and dt
       if (bc_taker) {
-        const unsigned v = take_word(bcw_mine, bc_early, tag_of(ebase, layer, kTagBC), P.sync + 3, 4u);
-        if (tid < B * DFSSM_DSTATE) {
-          s_bc[2 * tid] = lo_h(v);
-          s_bc[2 * tid + 1] = hi_h(v);
-        } else {
-          s_dt[bc_b] = (pl.h & 1) ? hi_h(v) : lo_h(v);
+#pragma unroll
+        for (int i = tid, k = 0; k < (kBcWords + kThreads - 1) / kThreads; ++k, i += kThreads) {
+          if (i >= kBcWords) break;
+          const unsigned v = k == 0 ? take_word(bcw_mine, bc_early, tag_of(ebase, layer, kTagBC), P.sync + 3, 4u)
+                                    : take_word(bc_word(i), 0ull, tag_of(ebase, layer, kTagBC), P.sync + 3, 4u);
+          if (i < B * DFSSM_DSTATE) {
+            s_bc[2 * i] = lo_h(v);
+            s_bc[2 * i + 1] = hi_h(v);
+          } else {
+            s_dt[i - B * DFSSM_DSTATE] = (pl.h & 1) ? hi_h(v) : lo_h(v);
+          }
         }
       }
       cta_sync();
@@ -964,14 +988,16 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
               mma_f16(acc, a0, a1, a2, a3, bv.x, bv.y);
             }
           }
-          // D: acc[0..1] -> row g, columns 2c, 2c + 1; acc[2..3] -> row g + 8; only c = 0 holds
-          // batch columns 0 and 1
-          if (c == 0) {
+          // D: acc[0..1] -> row g, columns 2c, 2c + 1; acc[2..3] -> row g + 8
+          if (2 * c < B) {  // lane (g, c) holds batch columns 2c and 2c + 1
             float* pp = part + ((size_t)(wtile * 8 + slice) * 16) * B;
 #pragma unroll
-            for (int b = 0; b < B; ++b) {
-              pp[g * B + b] = acc[b];
-              pp[(g + 8) * B + b] = acc[2 + b];
+            for (int k = 0; k < 2; ++k) {
+              const int b = 2 * c + k;
+              if (b < B) {
+                pp[g * B + b] = acc[k];
+                pp[(g + 8) * B + b] = acc[2 + k];
+              }
             }
           }
         }
@@ -1054,6 +1080,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
 
 // ------------------------------------------------------------------ host side
 
+// Tagged exchange words of one replica for launch groups of up to G sequences.
+size_t xch_words(const dfssm_dims& d, size_t G) {
+  return 2 * G * (d.d_model / 2) + 2 * G * (d.d_state + d.nheads / 2) + 2 * G * (d.d_inner / 2) +
+         2 * 2 * G * DFSSM_RANK;
+}
+constexpr size_t kXchSlack = 4096;  // spare words per replica (room for a layout pad)
+
 struct PersistentState {
   int ready = 0;
   void* fn = nullptr;
@@ -1063,8 +1096,10 @@ struct PersistentState {
   int grid = 0;
 };
 
+constexpr int kPersistGroupMax = 4;  // largest batch one launch of the kernel takes
+
 struct PersistentSet {
-  PersistentState st[3];  // indexed by batch size 1, 2
+  PersistentState st[kPersistGroupMax + 1];  // indexed by the group size: 1, 2 and 4
   int skew_next = 0;      // dfssm_debug_skew_next_step: the next launch runs skewed
 };
 
@@ -1078,6 +1113,7 @@ void* pick_kernel(int B, int KI, int KO) {
   if (B == b && KI == ki && KO == ko) return kernel_ptr<b, ki, ko>();
   DFSSM_PK(1, 4, 8)
   DFSSM_PK(2, 4, 8)
+  DFSSM_PK(4, 4, 8)
   DFSSM_PK(1, 1, 2)
   DFSSM_PK(2, 1, 2)
 #undef DFSSM_PK
@@ -1172,11 +1208,12 @@ int build_plan(const dfssm_engine* e, int B, int grid, std::vector<CtaPlan>& pla
   lay.state = off; off += a16(B * np * DFSSM_DSTATE * 4);
   lay.cstate = off; off += a16(B * 3 * ch * 4);
   lay.stage_bytes = (off + 127) & ~127;
-  const int misc_floats = (kWarps + 1) * (B * 16 + B) + B * 16 + B + B * kWarps + 16 + B * 64 * 2 + B + B * 256 + 128 * B + 8;
+  if (2 * np > kDotRows || max_nbc > kDotRows || max_no > kDotRows) return 0;
+  const int misc_floats = kRedFloats + B * 16 + B + B * kWarps + 16 + B * 64 * 2 + B + B * 256 + kDotRows * B + 8;
   int work = B * d.d_model * 2 + B * d.d_inner + misc_floats * 4;
   work = (work + 127) & ~127;
   tab_off = work;
-  work += ((d.n_layer * (int)sizeof(LayerW) + 15) & ~15) + d.n_layer * 4 * 4;
+  work += d.n_layer * 4 * 4;  // head scalars (dt_bias, A_log, D) of every layer
   work = (work + 127) & ~127;
   const int ring_off = work + 384;  // 8 full + 8 x 4 released mbarriers live just below the ring
   int max_smem = 0;
@@ -1200,9 +1237,33 @@ void persistent_destroy(dfssm_engine* e) {
   e->persist = nullptr;
 }
 
+// Byte stride between consecutive layers' weights if every array of every layer sits at the
+// same offset from its layer's first array (the arena's plan), else 0.
+long long uniform_layer_stride(const dfssm_engine* e) {
+  const auto& Ls = e->layers;
+  if (Ls.size() < 2) return 0;
+  auto fields = [](const LayerW& L) {
+    return std::vector<const char*>{
+        (const char*)L.in.bits, (const char*)L.in.scale, (const char*)L.in.A16, (const char*)L.in.B16,
+        (const char*)L.out.bits, (const char*)L.out.scale, (const char*)L.out.A16, (const char*)L.out.B16,
+        (const char*)L.conv_w, (const char*)L.conv_b, (const char*)L.A_log, (const char*)L.Dp,
+        (const char*)L.dt_bias, (const char*)L.norm_w, (const char*)L.ln_w};
+  };
+  const auto f0 = fields(Ls[0]);
+  const long long st = (long long)(fields(Ls[1])[0] - f0[0]);
+  for (size_t l = 0; l < Ls.size(); ++l) {
+    const auto fl = fields(Ls[l]);
+    for (size_t i = 0; i < f0.size(); ++i)
+      if ((long long)(fl[i] - f0[i]) != (long long)l * st) return 0;
+  }
+  return st;
+}
+
 int persistent_init(dfssm_engine* e) {
   if (!e->persist) e->persist = new PersistentSet();
-  for (int B = 1; B <= 2; ++B) {
+  const long long lstride = e->d.n_layer > 1 ? uniform_layer_stride(e) : 0;
+  if (e->d.n_layer > 1 && lstride == 0) return DFSSM_OK;  // no persistent kernel: it derives layer pointers
+  for (int B = 1; B <= kPersistGroupMax; ++B) {
     PersistentState& ps = set_of(e)->st[B];
     ps.ready = 0;
     if (B > e->max_batch) continue;
@@ -1226,7 +1287,8 @@ int persistent_init(dfssm_engine* e) {
     if (cudaMemcpy(ps.d_plans, plans.data(), sizeof(CtaPlan) * grid, cudaMemcpyHostToDevice) != cudaSuccess)
       return dfssm_fail(DFSSM_ERR_CUDA, "plan upload");
     PParams& P = ps.params;
-    P.layers = e->d_layers;
+    P.lw0 = e->layers[0];
+    P.lstride = lstride;
     P.plans = ps.d_plans;
     P.lay = lay;
     P.n_layer = d.n_layer;
@@ -1246,11 +1308,23 @@ int persistent_init(dfssm_engine* e) {
     P.conv_layer = (long long)e->conv_layer;
     P.x_g = e->x;
     P.xw = e->xch;
-    P.rs = persistent_xch_words(d);
-    P.bcw = P.xw + 2 * 2 * d.d_model / 2;
+    // Every exchange region holds [2 parities][G sequences][...] with G = 2 for launches of one or
+    // two sequences and 4 for four, then the next replica follows after `pad` more words
+    // (DFSSM_XPAD; default 0).  Where the words fall among the L2 slices moves the batch-1 step by
+    // up to +-3% (pads of 0..384 words on one box: 1768..1870 tok/s), but which pad is best changed
+    // from box to box, so no pad is tuned in.
+    const int G = B <= 2 ? 2 : kPersistGroupMax;
+    static const size_t pad = [] {
+      const char* v = getenv("DFSSM_XPAD");
+      const long long p = v ? atoll(v) : 0;
+      // whole 64-byte lines: the exchange words are also read as 16-byte pairs
+      return (size_t)(p < 0 ? 0 : (p > (long long)kXchSlack ? (long long)kXchSlack : p)) & ~(size_t)7;
+    }();
+    P.rs = xch_words(d, G) + pad;
+    P.bcw = P.xw + 2 * G * d.d_model / 2;
     P.bcw_per_seq = d.d_state + d.nheads / 2;
-    P.gw = P.bcw + 2 * 2 * P.bcw_per_seq;
-    P.tw = P.gw + 2 * 2 * d.d_inner / 2;
+    P.gw = P.bcw + 2 * G * P.bcw_per_seq;
+    P.tw = P.gw + 2 * G * d.d_inner / 2;
     P.gated_g = e->gated;
     P.logits = e->logits;
     P.best = e->best;
@@ -1274,30 +1348,38 @@ int persistent_init(dfssm_engine* e) {
   return DFSSM_OK;
 }
 
-size_t persistent_xch_words(const dfssm_dims& d) {
-  return (size_t)2 * 2 * (d.d_model / 2) + 2 * 2 * (d.d_state + d.nheads / 2) + 2 * 2 * (d.d_inner / 2) +
-         2 * 2 * 2 * DFSSM_RANK;
-}
+size_t persistent_xch_words(const dfssm_dims& d) { return xch_words(d, kPersistGroupMax) + kXchSlack; }
 size_t persistent_xch_bytes(const dfssm_dims& d) { return 8 * persistent_xch_words(d) * kReplicas; }
 
-// Batches of 3 to kPersistMaxBatch sequences run as consecutive launches over groups of two (the
-// last may hold one): at the 1.3B shape two launches of the batch-2 kernel (2 x 0.73 ms) beat the
-// per-op graph at batch 4 (2.8 ms, bound by its per-kernel latency chain).
-constexpr int kPersistMaxBatch = 6;
+// Batches of up to kPersistMaxBatch sequences run as consecutive launches over groups of the
+// largest sizes the kernel has (4, 2, 1), each group on its rows of the state and activation
+// buffers.
+constexpr int kPersistMaxBatch = 8;
+
+// Size of the group that starts a batch of n remaining sequences (0 if no instance fits).
+int group_size(const PersistentSet* ps, int n) {
+  for (int g = n < kPersistGroupMax ? n : kPersistGroupMax; g >= 1; --g)
+    if (ps->st[g].ready) return g;
+  return 0;
+}
 
 bool persistent_supported(const dfssm_engine* e) {
   if (!e->persist || e->batch < 1 || e->batch > kPersistMaxBatch) return false;
   const PersistentSet* ps = set_of(e);
-  if (e->batch <= 2) return ps->st[e->batch].ready;
-  return ps->st[2].ready && (e->batch % 2 == 0 || ps->st[1].ready);
+  for (int n = e->batch; n > 0;) {
+    const int g = group_size(ps, n);
+    if (!g) return false;
+    n -= g;
+  }
+  return true;
 }
 
 int launch_persistent_layers(dfssm_engine* e, int l0, int l1, int from_x, int do_head, cudaStream_t s) {
   if (!persistent_supported(e)) return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "persistent kernel unavailable");
   if (l0 < 0 || l1 > e->d.n_layer || l0 >= l1) return dfssm_fail(DFSSM_ERR_ARG, "bad layer range [%d, %d)", l0, l1);
   const dfssm_dims& d = e->d;
-  for (int b0 = 0; b0 < e->batch; b0 += 2) {
-    const int nb = e->batch - b0 < 2 ? e->batch - b0 : 2;
+  for (int b0 = 0, nb = 0; b0 < e->batch; b0 += nb) {
+    nb = group_size(set_of(e), e->batch - b0);
     PersistentState& ps = set_of(e)->st[nb];
     PParams P = ps.params;
     // this group's rows of every per-sequence buffer (the layer strides stay those of max_batch)
@@ -1343,8 +1425,8 @@ size_t persistent_trace_entries(const dfssm_engine* e) {
 }
 
 int launch_persistent_traced(dfssm_engine* e, unsigned long long* trace_dev, cudaStream_t s) {
-  if (!persistent_supported(e) || e->batch > 2)
-    return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "the phase trace runs the persistent kernel at batch 1 or 2");
+  if (!persistent_supported(e) || group_size(set_of(e), e->batch) != e->batch)
+    return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "the phase trace runs one persistent launch: batch 1, 2 or 4");
   PersistentState& ps = set_of(e)->st[e->batch];
   PParams P = ps.params;
   P.trace = trace_dev;

@@ -63,8 +63,8 @@ int dfssm_get_dims(const dfssm_engine* e, dfssm_dims* out);
 /* Number of sequences decoded by dfssm_step (1..max_batch).  Drops the captured graph. */
 int dfssm_set_batch(dfssm_engine* e, int batch);
 /* Step execution mode: 0 = automatic (3 where supported, else 1), 1 = per-op kernels replayed from a CUDA graph,
- * 2 = per-op kernels launched eagerly, 3 = persistent whole-step kernel (batch <= 6, one launch per group of two
- * sequences; d_model and d_inner multiples of 512). */
+ * 2 = per-op kernels launched eagerly, 3 = persistent whole-step kernel (batch <= 8, one launch per group of up to
+ * four sequences, groups of 4, 2 and 1; d_model and d_inner multiples of 512). */
 int dfssm_set_mode(dfssm_engine* e, int mode);
 int dfssm_get_mode(const dfssm_engine* e, int* mode);
 
@@ -108,8 +108,8 @@ int dfssm_get_buffer(dfssm_engine* e, const char* name, void** ptr, size_t* byte
 int dfssm_layer_step(dfssm_engine* e, int layer, void* stream);
 
 /* Diagnostics (no counterpart in the reference, which has no profiler hooks): number of
- * uint64 entries of a persistent-step trace, and one persistent decode step (mode 3, batch 1 or 2
- * only: DFSSM_ERR_UNSUPPORTED for larger batches)
+ * uint64 entries of a persistent-step trace, and one persistent decode step (mode 3, batch 1, 2 or 4:
+ * one launch; DFSSM_ERR_UNSUPPORTED for other batches)
  * that records %globaltimer stamps at its phase boundaries into trace_dev
  * [sm_count][4 + 16 * n_layer]: [0] start, [1] end, [2 + 16l + k] layer l point k
  * (0 alpha entry, 1 after receiving x, 3 after norm/quant/LoRA, 4 after the weight ring wait,

@@ -28,8 +28,9 @@ def _close(got, ref, frac_exact=0.9, rel=1e-2):
                                           # 2.7B widths: prologues with 5 and 10 columns per thread
                                           (3, "graph", "2.7b"), (100, "graph", "2.7b"),
                                           (1, "persistent", "small"), (2, "persistent", "small"),
-                                          # batches of 3..6 run the persistent kernel per group of two
-                                          (3, "persistent", "small"), (5, "persistent", "small")])
+                                          # batches of 3..8 run the persistent kernel per group of 4, 2, 1
+                                          (3, "persistent", "small"), (4, "persistent", "small"),
+                                          (7, "persistent", "small")])
 def test_single_layer_matches_oracle(B, mode, shape):
     w = weights(shape, 1, seed=2)
     d = w.dims
@@ -194,7 +195,7 @@ def test_cfg1_48_layers_layerwise_match_oracle(mode):
     assert np.mean(exact) >= 0.8, np.mean(exact)
 
 
-@pytest.mark.parametrize("B", [1, 2])
+@pytest.mark.parametrize("B", [1, 2, 4])
 def test_persistent_is_deterministic_and_reports_no_timeouts(B):
     w = weights("1.3b", 4, seed=7)
     p = np.random.default_rng(5).integers(0, w.dims.vocab, (B, 4))
@@ -208,7 +209,7 @@ def test_persistent_is_deterministic_and_reports_no_timeouts(B):
     m.check_finite()  # also fails if any bounded wait in the kernel timed out
 
 
-@pytest.mark.parametrize("B", [2, 3, 4, 6])
+@pytest.mark.parametrize("B", [2, 3, 4, 6, 8])
 def test_persistent_matches_graph_tokens_on_1p3b_two_layers(B):
     w = weights("1.3b", 2, seed=3)
     p = np.random.default_rng(8).integers(0, w.dims.vocab, (B, 4))

@@ -64,7 +64,12 @@ def test_reference_arm_under_torchrun_prints_one_job_line():
     line = lines[0]
     assert line["impl"] == "reference"
     if "unavailable" not in line:
-        assert line["config"]["batch"] == 2 and line["n_gpus"] == 2 and line["value"] > 0
+        assert line["config"]["global_batch"] == 2 and line["n_gpus"] == 2 and line["value"] > 0
+        # the same workload keys and values as the engine's arm prints for cfg0 at two ranks
+        from dfssm_b200 import synthetic
+        cfg = bench.CONFIGS["cfg0"]
+        d = synthetic.make_dims(cfg["shape"], cfg["layers"])
+        assert line["config"] == bench.workload_config("cfg0", cfg, 1, 2, bench.step_bytes(d, 1)["total"])
 
 
 @pytest.mark.parametrize("config", ["cfg3", "cfg1 --prefill 16"])
