@@ -468,12 +468,8 @@ def main():
 
 
 def persistent_launches(batch: int) -> int:
-    """Launches of the persistent step kernel per step: one per group of 4, 2 and 1 sequences."""
-    n = 0
-    while batch > 0:
-        batch -= 4 if batch >= 4 else (2 if batch >= 2 else 1)
-        n += 1
-    return n
+    """Launches of the persistent step kernel per step: one per group of up to 4 sequences."""
+    return -(-batch // 4)
 
 
 def workload_config(name: str, cfg: dict, batch: int, job_batch: int, total_bytes: float) -> dict:

@@ -20,6 +20,7 @@ STATUS = {1: "ERR_ARG", 2: "ERR_FORMAT", 3: "ERR_UNSUPPORTED", 4: "ERR_CUDA", 5:
 SIGNATURES = {
     "dfssm_version": (c_char_p, []),
     "dfssm_last_error": (c_char_p, []),
+    "dfssm_kernel_binary_version": (c_int, [c_int, POINTER(c_int)]),
     "dfssm_create_from_memory": (c_int, [c_void_p, c_size_t, c_int, c_int, POINTER(c_void_p)]),
     "dfssm_create_from_file": (c_int, [c_char_p, c_int, c_int, POINTER(c_void_p)]),
     "dfssm_destroy": (None, [c_void_p]),
@@ -37,8 +38,10 @@ SIGNATURES = {
                              ctypes.c_uint64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "dfssm_set_sampling": (c_int, [c_void_p, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_uint64]),
     "dfssm_prefill": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
+    "dfssm_prefill_slots": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "dfssm_state_ptrs": (c_int, [c_void_p, c_int, POINTER(c_void_p), POINTER(c_void_p)]),
     "dfssm_get_buffer": (c_int, [c_void_p, c_char_p, POINTER(c_void_p), POINTER(c_size_t)]),
+    "dfssm_weight_ptr": (c_int, [c_void_p, c_int, c_char_p, POINTER(c_void_p), POINTER(c_size_t)]),
     "dfssm_layer_step": (c_int, [c_void_p, c_int, c_void_p]),
     "dfssm_trace_entries": (c_size_t, [c_void_p]),
     "dfssm_trace_step": (c_int, [c_void_p, c_void_p, c_void_p]),

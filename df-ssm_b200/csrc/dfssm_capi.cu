@@ -373,7 +373,13 @@ int enqueue_head(dfssm_engine* e, cudaStream_t s) {
   const dfssm_dims& d = e->d;
   int rc;
   if ((rc = launch_prep(e, e->x, d.d_model, e->norm_f, 0, nullptr, s, Group{0, e->batch}, engine_rows(e)))) return rc;
-  if (e->batch >= kMmaMinBatch && d.d_model % 64 == 0) {
+  // the tensor-core head from batch 3 (DFSSM_HEAD_MMA_MIN overrides): at the 1.3B shape the
+  // per-row GEMV head cost batches 5-7 about 0.25 ms more per step than batch 8 on the MMA head
+  static const int head_mma_min = [] {
+    const char* v = getenv("DFSSM_HEAD_MMA_MIN");
+    return v ? atoi(v) : 3;
+  }();
+  if (e->batch >= head_mma_min && d.d_model % 64 == 0) {
     const size_t sm = lm_head_mma_smem(d.d_model);
     CU(ensure_smem(reinterpret_cast<const void*>(lm_head_mma_kernel), sm));
     lm_head_mma_kernel<<<e->sm_count, kHeadMmaThreads, sm, s>>>(e->Eq, e->Es, d.vocab, d.d_model, e->xn, e->batch,
@@ -757,6 +763,15 @@ int build_engine(const unsigned char* img, size_t n, int device, int max_batch, 
 extern "C" {
 
 const char* dfssm_version(void) { return "dfssm-b200 0.1 (sm_100a)"; }
+
+int dfssm_kernel_binary_version(int device, int* version) {
+  if (!version) return dfssm_fail(DFSSM_ERR_ARG, "NULL argument");
+  CU(cudaSetDevice(device));
+  cudaFuncAttributes a;
+  CU(cudaFuncGetAttributes(&a, reinterpret_cast<const void*>(embed_kernel)));
+  *version = a.binaryVersion;
+  return DFSSM_OK;
+}
 const char* dfssm_last_error(void) { return g_err.c_str(); }
 
 int dfssm_create_from_memory(const void* image, size_t image_bytes, int device, int max_batch, dfssm_engine** out) {
@@ -954,6 +969,39 @@ int dfssm_get_buffer(dfssm_engine* e, const char* name, void** ptr, size_t* byte
   else if (!strcmp(name, "q")) { *ptr = e->q; *bytes = B * (d.d_model > d.d_inner ? d.d_model : d.d_inner); }
   else if (!strcmp(name, "xs")) { *ptr = e->xs; *bytes = B * 2; }
   else return dfssm_fail(DFSSM_ERR_ARG, "unknown buffer '%s'", name);
+  return DFSSM_OK;
+}
+
+int dfssm_weight_ptr(dfssm_engine* e, int layer, const char* name, void** ptr, size_t* bytes) {
+  if (!e || !name || !ptr || !bytes) return dfssm_fail(DFSSM_ERR_ARG, "NULL argument");
+  const dfssm_dims& d = e->d;
+  if (layer < 0) {
+    if (!strcmp(name, "emb_q")) { *ptr = const_cast<int8_t*>(e->Eq); *bytes = (size_t)d.vocab * d.d_model; }
+    else if (!strcmp(name, "emb_s")) { *ptr = const_cast<float*>(e->Es); *bytes = (size_t)d.vocab * 4; }
+    else if (!strcmp(name, "norm_f")) { *ptr = const_cast<float*>(e->norm_f); *bytes = (size_t)d.d_model * 4; }
+    else return dfssm_fail(DFSSM_ERR_ARG, "unknown model weight '%s'", name);
+    return DFSSM_OK;
+  }
+  if (layer >= d.n_layer) return dfssm_fail(DFSSM_ERR_ARG, "layer %d out of range", layer);
+  const LayerW& L = e->layers[layer];
+  auto proj = [&](const ProjW& p, const char* f) -> int {
+    if (!strcmp(f, "bits")) { *ptr = const_cast<uint32_t*>(p.bits); *bytes = (size_t)p.N * (p.K / 32) * 4; }
+    else if (!strcmp(f, "scale")) { *ptr = const_cast<__half*>(p.scale); *bytes = (size_t)p.N * 2; }
+    else if (!strcmp(f, "lora_A")) { *ptr = const_cast<__half*>(p.A16); *bytes = (size_t)p.N * kRank * 2; }
+    else if (!strcmp(f, "lora_B")) { *ptr = const_cast<__half*>(p.B16); *bytes = (size_t)kRank * p.K * 2; }
+    else return 0;
+    return 1;
+  };
+  if (!strncmp(name, "in_", 3) && proj(L.in, name + 3)) return DFSSM_OK;
+  if (!strncmp(name, "out_", 4) && proj(L.out, name + 4)) return DFSSM_OK;
+  if (!strcmp(name, "conv_w")) { *ptr = const_cast<__half*>(L.conv_w); *bytes = (size_t)d.d_xbc * 4 * 2; }
+  else if (!strcmp(name, "conv_b")) { *ptr = const_cast<__half*>(L.conv_b); *bytes = (size_t)d.d_xbc * 2; }
+  else if (!strcmp(name, "A_log")) { *ptr = const_cast<float*>(L.A_log); *bytes = (size_t)d.nheads * 4; }
+  else if (!strcmp(name, "D")) { *ptr = const_cast<float*>(L.Dp); *bytes = (size_t)d.nheads * 4; }
+  else if (!strcmp(name, "dt_bias")) { *ptr = const_cast<float*>(L.dt_bias); *bytes = (size_t)d.nheads * 4; }
+  else if (!strcmp(name, "norm_w")) { *ptr = const_cast<float*>(L.norm_w); *bytes = (size_t)d.d_inner * 4; }
+  else if (!strcmp(name, "ln_w")) { *ptr = const_cast<float*>(L.ln_w); *bytes = (size_t)d.d_model * 4; }
+  else return dfssm_fail(DFSSM_ERR_ARG, "unknown layer weight '%s'", name);
   return DFSSM_OK;
 }
 
@@ -1337,8 +1385,12 @@ int prefill_chunk(dfssm_engine* e, const PrefillBufs& P, int T, cudaStream_t s) 
 
 }  // namespace
 
-int dfssm_prefill(dfssm_engine* e, const int32_t* tokens_dev, int T, float* logits_dev, int32_t* next_tokens_dev,
-                  void* stream) {
+namespace {
+
+// The prefill of dfssm_prefill for engine `e`, which may be a slot view of `owner` (the engine
+// that owns the prompt-row buffers).
+int prefill_impl(dfssm_engine* e, dfssm_engine* owner, const int32_t* tokens_dev, int T, float* logits_dev,
+                 int32_t* next_tokens_dev, void* stream) {
   if (!e || !tokens_dev) return dfssm_fail(DFSSM_ERR_ARG, "NULL argument");
   if (T < 1) return dfssm_fail(DFSSM_ERR_ARG, "prompt length %d", T);
   CU(cudaSetDevice(e->device));
@@ -1358,7 +1410,7 @@ int dfssm_prefill(dfssm_engine* e, const int32_t* tokens_dev, int T, float* logi
   }
   PrefillBufs P;
   int rc;
-  if ((rc = prefill_bufs(e, B * Tc, P))) return rc;
+  if ((rc = prefill_bufs(owner, B * Tc, P))) return rc;
   CU(cudaEventRecord(e->ev_in, us));
   CU(cudaStreamWaitEvent(e->s, e->ev_in, 0));
   for (int t0 = 0; t0 < T; t0 += Tc) {
@@ -1401,4 +1453,51 @@ int dfssm_prefill(dfssm_engine* e, const int32_t* tokens_dev, int T, float* logi
   CU(cudaEventRecord(e->ev_out, e->s));
   CU(cudaStreamWaitEvent(us, e->ev_out, 0));
   return DFSSM_OK;
+}
+
+// A shallow copy of the engine whose per-sequence buffers start at slot `first` and whose batch is
+// `count` (per-layer strides stay those of max_batch).  It runs the per-op kernels eagerly (mode 2:
+// no captured graph, no persistent kernel, whose pointers are fixed to slot 0) and owns nothing:
+// it is never destroyed, and prompt-row buffers come from the owning engine.
+dfssm_engine slot_view(const dfssm_engine* e, int first, int count) {
+  const dfssm_dims& d = e->d;
+  const size_t kmax = d.d_inner > d.d_model ? d.d_inner : d.d_model, f = (size_t)first;
+  dfssm_engine v = *e;
+  v.ssm += f * d.nheads * DFSSM_HEADDIM * DFSSM_DSTATE;
+  v.conv += f * 3 * d.d_xbc;
+  v.x += f * d.d_model;
+  v.xn += f * kmax;
+  v.q += f * kmax;
+  v.xs += f;
+  v.qsum += f;
+  v.t += f * kRank;
+  v.proj += f * d.n_in;
+  v.gated += f * d.d_inner;
+  v.logits += f * d.vocab;
+  v.best += f;
+  v.tokens += f;
+  v.seen += f * v.seen_words;
+  v.counters += f;
+  v.batch = count;
+  v.mode = 2;
+  v.gexec = nullptr;
+  v.graph_batch = v.graph_mode = -1;
+  v.persist = nullptr;
+  return v;
+}
+
+}  // namespace
+
+int dfssm_prefill(dfssm_engine* e, const int32_t* tokens_dev, int T, float* logits_dev, int32_t* next_tokens_dev,
+                  void* stream) {
+  return prefill_impl(e, e, tokens_dev, T, logits_dev, next_tokens_dev, stream);
+}
+
+int dfssm_prefill_slots(dfssm_engine* e, int first, int count, const int32_t* tokens_dev, int T, float* logits_dev,
+                        int32_t* next_tokens_dev, void* stream) {
+  if (!e) return dfssm_fail(DFSSM_ERR_ARG, "NULL engine");
+  if (first < 0 || count < 1 || first + count > e->batch)
+    return dfssm_fail(DFSSM_ERR_ARG, "slots [%d, %d) outside the batch of %d", first, first + count, e->batch);
+  dfssm_engine v = slot_view(e, first, count);
+  return prefill_impl(&v, e, tokens_dev, T, logits_dev, next_tokens_dev, stream);
 }

@@ -555,6 +555,8 @@ __device__ __forceinline__ void release_part(const PParams& P, uint64_t* empties
 
 template <int B, int KI, int KO>
 __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PParams P) {
+  static_assert(B >= 1 && B <= 4, "the reduction scratch and the copy table hold up to four sequences");
+  constexpr int kEpiLanes = (32 / (2 * B)) * (2 * B);  // epilogue entries per warp: whole row pairs
   extern __shared__ __align__(128) unsigned char smem[];
   const int d_model = P.d_model, d_inner = P.d_inner;
   // working smem (carve-up mirrored by build_plan)
@@ -797,12 +799,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       stamp(P, tb + 2);
       unsigned long long* bcw = P.bcw + (size_t)par * B * P.bcw_per_seq;
       const unsigned tg_bc = tag_of(ebase, layer, kTagBC);
-      // one thread per (row, b), e = row * B + b; the partner row of a pair sits B lanes up in
-      // the same warp (32 is a multiple of 2B), and the even row's lane publishes the pair
-      for (int e0 = wid * 32; e0 < nb * B; e0 += kThreads) {
+      // one thread per (row, b), e = row * B + b; a warp takes kEpiLanes consecutive entries (whole
+      // row pairs), so the partner row of a pair sits B lanes up in the same warp, and the even
+      // row's lane publishes the pair
+      for (int e0 = wid * kEpiLanes; e0 < nb * B; e0 += kWarps * kEpiLanes) {
         const int e2 = e0 + lane, row = e2 / B, b = e2 - row * B;
+        const bool mine = lane < kEpiLanes && e2 < nb * B;
         float o = 0.f;
-        if (e2 < nb * B) {
+        if (mine) {
           const float v = proj_out(s_dot[e2], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
           if (pl.bc0 + row < 2 * DFSSM_DSTATE) {  // B/C channel: conv1d + SiLU
             const int ch = d_inner + pl.bc0 + row;
@@ -817,7 +821,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
           }
         }
         const float o_next = __shfl_down_sync(0xffffffffu, o, B);
-        if (e2 < nb * B && (row & 1) == 0)
+        if (mine && (row & 1) == 0)
           put_word(bcw + (size_t)b * P.bcw_per_seq + (pl.bc0 + row) / 2, P.rs, pack_h2(o, o_next), tg_bc);
       }
       cta_sync();
@@ -893,16 +897,17 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       unsigned long long* xw = P.xw + (size_t)(par ^ 1) * B * XW;
       const unsigned tg_x = tag_of(ebase, layer + 1, kTagX);
       // one thread per (row, b) as in the B/C epilogue; the even row's lane publishes the pair
-      for (int e0 = wid * 32; e0 < pl.no * B; e0 += kThreads) {
+      for (int e0 = wid * kEpiLanes; e0 < pl.no * B; e0 += kWarps * kEpiLanes) {
         const int e2 = e0 + lane, row = e2 / B, b = e2 - row * B;
         const int o = pl.o0 + row;
+        const bool mine = lane < kEpiLanes && e2 < pl.no * B;
         float xo = 0.f;
-        if (e2 < pl.no * B) {
+        if (mine) {
           const float v = proj_out(s_dot[e2], s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
           xo = h2f(s_x[b * d_model + o]) + v;
         }
         const float xo_next = __shfl_down_sync(0xffffffffu, xo, B);
-        if (e2 < pl.no * B && (row & 1) == 0) {
+        if (mine && (row & 1) == 0) {
           const unsigned w = pack_h2(xo, xo_next);
           put_word(xw + (size_t)b * XW + o / 2, P.rs, w, tg_x);
           *reinterpret_cast<unsigned*>(P.x_g + (size_t)b * d_model + o) = w;  // plain copy for the host API
@@ -1096,10 +1101,10 @@ struct PersistentState {
   int grid = 0;
 };
 
-constexpr int kPersistGroupMax = 4;  // largest batch one launch of the kernel takes
+constexpr int kPersistGroupMax = 4;  // largest batch one launch of the kernel takes (instances 1 to 4)
 
 struct PersistentSet {
-  PersistentState st[kPersistGroupMax + 1];  // indexed by the group size: 1, 2 and 4
+  PersistentState st[kPersistGroupMax + 1];  // indexed by the group size: 1 to 4
   int skew_next = 0;      // dfssm_debug_skew_next_step: the next launch runs skewed
 };
 
@@ -1113,6 +1118,7 @@ void* pick_kernel(int B, int KI, int KO) {
   if (B == b && KI == ki && KO == ko) return kernel_ptr<b, ki, ko>();
   DFSSM_PK(1, 4, 8)
   DFSSM_PK(2, 4, 8)
+  DFSSM_PK(3, 4, 8)
   DFSSM_PK(4, 4, 8)
   DFSSM_PK(1, 1, 2)
   DFSSM_PK(2, 1, 2)
@@ -1313,7 +1319,7 @@ int persistent_init(dfssm_engine* e) {
     // (DFSSM_XPAD; default 0).  Where the words fall among the L2 slices moves the batch-1 step by
     // up to +-3% (pads of 0..384 words on one box: 1768..1870 tok/s), but which pad is best changed
     // from box to box, so no pad is tuned in.
-    const int G = B <= 2 ? 2 : kPersistGroupMax;
+    const int G = B <= 2 ? 2 : kPersistGroupMax;  // (B = 3 and 4 share the four-sequence layout)
     static const size_t pad = [] {
       const char* v = getenv("DFSSM_XPAD");
       const long long p = v ? atoll(v) : 0;
@@ -1352,7 +1358,7 @@ size_t persistent_xch_words(const dfssm_dims& d) { return xch_words(d, kPersistG
 size_t persistent_xch_bytes(const dfssm_dims& d) { return 8 * persistent_xch_words(d) * kReplicas; }
 
 // Batches of up to kPersistMaxBatch sequences run as consecutive launches over groups of the
-// largest sizes the kernel has (4, 2, 1), each group on its rows of the state and activation
+// largest sizes the kernel has (4, then the remaining 1 to 4), each group on its rows of the state and activation
 // buffers.
 constexpr int kPersistMaxBatch = 8;
 

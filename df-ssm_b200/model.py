@@ -2,7 +2,8 @@
 
 Mirrors class DFSSMModel of inference/gpu/df_ssm_inference.py:47-243 (constructor
 `DFSSMModel(path, device="cuda", batch_size=1)`, `forward(token_ids) -> logits`,
-`generate(n_tokens=128)`, `reset_state()`, attributes `h_states`, `conv_states`) and
+`generate(n_tokens=128)`, `reset_state()`, attributes `h_states`, `conv_states`, `layers`,
+`embedding`) and
 its CLI (`model --batch_size B --n_tokens N`, :246-252).  All compute runs in
 libdfssm.so (sm_100a kernels behind a C ABI); PyTorch only supplies device memory,
 the current stream and tensor views.
@@ -35,6 +36,52 @@ class _DevArray:
     def __init__(self, ptr: int, shape, typestr: str, strides=None):
         self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
                                          "version": 2, "strides": strides}
+
+
+class LayerWeights:
+    """Read-only device views of one layer's resident weights, named after the reference's
+    LayerWeights (df_ssm_inference.py:32-44,68-106).  The scaffold stays bit-packed as in the file
+    (`in_packed` / `out_packed`, int32 [N, K/32]); `in_w_T` / `out_w_T` unpack it on demand to the
+    reference's int8 +-1 transpose [K, N] (a new tensor: the engine never holds it).  Norm weights
+    are fp32 (the exporter's dtype)."""
+
+    _FIELDS = {  # attribute: (engine name, dtype, shape from dims)
+        "in_packed": ("in_bits", "<i4", lambda d: (d.n_in, d.d_model // 32)),
+        "in_scale": ("in_scale", "<f2", lambda d: (d.n_in,)),
+        "in_lora_A": ("in_lora_A", "<f2", lambda d: (d.n_in, 16)),
+        "in_lora_B": ("in_lora_B", "<f2", lambda d: (16, d.d_model)),
+        "out_packed": ("out_bits", "<i4", lambda d: (d.d_model, d.d_inner // 32)),
+        "out_scale": ("out_scale", "<f2", lambda d: (d.d_model,)),
+        "out_lora_A": ("out_lora_A", "<f2", lambda d: (d.d_model, 16)),
+        "out_lora_B": ("out_lora_B", "<f2", lambda d: (16, d.d_inner)),
+        "conv_weight": ("conv_w", "<f2", lambda d: (d.d_xbc, 4)),
+        "conv_bias": ("conv_b", "<f2", lambda d: (d.d_xbc,)),
+        "A_log": ("A_log", "<f4", lambda d: (d.nheads,)),
+        "D": ("D", "<f4", lambda d: (d.nheads,)),
+        "dt_bias": ("dt_bias", "<f4", lambda d: (d.nheads,)),
+        "norm_weight": ("norm_w", "<f4", lambda d: (d.d_inner,)),
+        "layer_norm_weight": ("ln_w", "<f4", lambda d: (d.d_model,)),
+    }
+
+    def __init__(self, model: "DFSSMModel", layer: int):
+        for attr, (name, ts, shape) in self._FIELDS.items():
+            setattr(self, attr, model._weight(layer, name, ts, shape(model.dims)))
+
+    @staticmethod
+    def _unpack_T(packed):
+        """Packed signs [N, K/32] -> int8 +-1 [K, N] (bit b of word j is column 32j + b)."""
+        import torch
+        n, w = packed.shape
+        bits = (packed.unsqueeze(-1) >> torch.arange(32, device=packed.device, dtype=torch.int32)) & 1
+        return (2 * bits - 1).to(torch.int8).reshape(n, w * 32).T.contiguous()
+
+    @property
+    def in_w_T(self):
+        return self._unpack_T(self.in_packed)
+
+    @property
+    def out_w_T(self):
+        return self._unpack_T(self.out_packed)
 
 
 class DFSSMModel:
@@ -80,6 +127,23 @@ class DFSSMModel:
                 _DevArray(sp.value, (B, dims.nheads, dims.headdim, dims.d_state), "<f4"), device=self.device))
             conv = torch.as_tensor(_DevArray(cp.value, (B, 3, dims.d_xbc), "<f4"), device=self.device)
             self.conv_states.append(conv.permute(0, 2, 1))  # [B, D_XBC, 3] view
+        # resident weights as read-only device views (the reference's DFSSMModel.layers /
+        # .embedding, df_ssm_inference.py:51,62-110)
+        self.layers = [LayerWeights(self, l) for l in range(dims.n_layer)]
+        self.embedding_q = self._weight(-1, "emb_q", "|i1", (dims.vocab, dims.d_model))
+        self.embedding_scale = self._weight(-1, "emb_s", "<f4", (dims.vocab,))
+        self.norm_f_weight = self._weight(-1, "norm_f", "<f4", (dims.d_model,))
+
+    def _weight(self, layer: int, name: str, typestr: str, shape):
+        p, n = ctypes.c_void_p(), ctypes.c_size_t()
+        _lib.check(self.lib.dfssm_weight_ptr(self._h, layer, name.encode(), ctypes.byref(p), ctypes.byref(n)))
+        return self.torch.as_tensor(_DevArray(p.value, shape, typestr), device=self.device)
+
+    @property
+    def embedding(self):
+        """The tied embedding as fp16 [vocab, d_model] (df_ssm_inference.py:65), dequantised on demand
+        from the resident int8 rows and their scales (fp16(q * s)); a new tensor each access."""
+        return (self.embedding_q.float() * self.embedding_scale[:, None]).half()
 
     # ------------------------------------------------------------------ lifecycle
     def close(self):
@@ -165,6 +229,23 @@ class DFSSMModel:
         _lib.check(self.lib.dfssm_prefill(self._h, ctypes.c_void_p(tok.data_ptr()), int(tok.shape[1]), lg,
                                           ctypes.c_void_p(self._tok_out.data_ptr()), self._stream()))
         return self._tok_out[: self.batch_size]
+
+    def prefill_slots(self, first: int, prompt, logits: bool = False):
+        """Consume prompt tokens [count, T] into sequence slots [first, first + count) only
+        (dfssm_prefill_slots; continuous batching: reset_sequences() the slots first for new
+        sequences).  Returns the next tokens of those slots (device int32 [count]); with `logits`
+        their rows of self.logits are filled.  The other slots are untouched."""
+        torch = self.torch
+        prompt = torch.as_tensor(prompt)
+        if prompt.dim() == 1:
+            prompt = prompt.reshape(1, -1)
+        count = int(prompt.shape[0])
+        tok = prompt.to(device=self.device, dtype=torch.int32).contiguous()
+        lg = ctypes.c_void_p(self.logits[first:].data_ptr()) if logits else None
+        _lib.check(self.lib.dfssm_prefill_slots(self._h, int(first), count, ctypes.c_void_p(tok.data_ptr()),
+                                                int(tok.shape[1]), lg, ctypes.c_void_p(self._tok_out[first:].data_ptr()),
+                                                self._stream()))
+        return self._tok_out[first:first + count]
 
     def set_sampling(self, temperature: float = 0.0, top_p: float = 1.0, rep_penalty: float = 1.0, seed: int = 0):
         """Token choice of later steps: greedy argmax for temperature <= 0 (the default, as the

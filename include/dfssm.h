@@ -46,6 +46,9 @@ typedef struct dfssm_engine dfssm_engine;
 
 /* Library version string. */
 const char* dfssm_version(void);
+/* Diagnostics (no counterpart in the reference): the binary architecture version of the library's
+ * kernels as the CUDA runtime loaded them on `device` (major * 10 + minor: 100 for sm_100a). */
+int dfssm_kernel_binary_version(int device, int* version);
 /* Message of the last failed call on this thread ("" if none). */
 const char* dfssm_last_error(void);
 
@@ -64,7 +67,7 @@ int dfssm_get_dims(const dfssm_engine* e, dfssm_dims* out);
 int dfssm_set_batch(dfssm_engine* e, int batch);
 /* Step execution mode: 0 = automatic (3 where supported, else 1), 1 = per-op kernels replayed from a CUDA graph,
  * 2 = per-op kernels launched eagerly, 3 = persistent whole-step kernel (batch <= 8, one launch per group of up to
- * four sequences, groups of 4, 2 and 1; d_model and d_inner multiples of 512). */
+ * four sequences: groups of 4, then the rest; d_model and d_inner multiples of 512). */
 int dfssm_set_mode(dfssm_engine* e, int mode);
 int dfssm_get_mode(const dfssm_engine* e, int* mode);
 
@@ -103,6 +106,15 @@ int dfssm_state_ptrs(dfssm_engine* e, int layer, float** ssm, float** conv);
  * last per-op projection prologue, columns in the GEMV's permuted order) and "xs" (fp16 [B], their
  * scales). */
 int dfssm_get_buffer(dfssm_engine* e, const char* name, void** ptr, size_t* bytes);
+/* Device pointer and size of one resident weight array (read-only views; the reference exposes its
+ * weights as DFSSMModel.embedding and DFSSMModel.layers, df_ssm_inference.py:51,62-110).  layer >= 0:
+ * "in_bits" / "out_bits" (packed signs uint32 [N][K/32], the file's layout, where the reference keeps
+ * the unpacked int8 transpose in_w_T / out_w_T), "in_scale" / "out_scale" (fp16 [N]), "in_lora_A" /
+ * "out_lora_A" (fp16 [N][16]) and "in_lora_B" / "out_lora_B" (fp16 [16][K]) dequantised as the
+ * reference loader does, "conv_w" (fp16 [d_xbc][4]), "conv_b" (fp16 [d_xbc]), "A_log", "D", "dt_bias"
+ * (fp32 [nheads]), "norm_w" (fp32 [d_inner]), "ln_w" (fp32 [d_model]).  layer = -1: "emb_q" (int8
+ * [vocab][d_model]) and "emb_s" (fp32 [vocab]) of the tied embedding, "norm_f" (fp32 [d_model]). */
+int dfssm_weight_ptr(dfssm_engine* e, int layer, const char* name, void** ptr, size_t* bytes);
 /* Run layer `layer` alone on the engine's "x" buffer with the kernels of the current mode
  * (per-op kernels, or the persistent kernel over the single layer when mode 3 is selected). */
 int dfssm_layer_step(dfssm_engine* e, int layer, void* stream);
@@ -202,6 +214,17 @@ int dfssm_lm_head_argmax(const int8_t* E_q, const float* E_s, int vocab, int d, 
  * dfssm_step. */
 int dfssm_prefill(dfssm_engine* e, const int32_t* tokens_dev, int T, float* logits_dev, int32_t* next_tokens_dev,
                   void* stream);
+
+/* Prompt prefill of sequence slots [first, first + count) of the current batch only (continuous
+ * batching: a finished sequence's slot takes a new prompt while the other slots keep their state).
+ * tokens_dev int32 [count][T]; logits_dev fp32 [count][vocab] and next_tokens_dev int32 [count] (either
+ * may be NULL) receive the slots' results.  The slots continue from their current state (call
+ * dfssm_reset_slots first for a new sequence); the other slots' state, tokens and logits are not
+ * touched.  Runs the per-op kernels of dfssm_prefill on the slots' rows (a short prompt steps token by
+ * token through eagerly launched per-op kernels).  The reference has no per-slot prefill: its drivers
+ * feed one prompt token per forward() for the whole batch (df_ssm_inference.py:219-231). */
+int dfssm_prefill_slots(dfssm_engine* e, int first, int count, const int32_t* tokens_dev, int T, float* logits_dev,
+                        int32_t* next_tokens_dev, void* stream);
 
 /* Sampling epilogue (eval/gen_test.py:54-95, the reference's generate(): temperature,
  * repetition penalty, top-p nucleus, multinomial draw), one draw per row:

@@ -23,7 +23,8 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
-DEFAULT_REF = "/root/reference"
+# the reference checkout: $DFSSM_REFERENCE, else a `reference` directory beside this repository
+DEFAULT_REF = os.environ.get("DFSSM_REFERENCE") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 
 SHAPES = {
     "1p3b": dict(D_MODEL=2048, D_INNER=4096, D_XBC=4352, D_STATE=128, NHEADS=64, HEADDIM=64, IN_PROJ_OUT=8512),

@@ -35,9 +35,19 @@ def test_header_declarations_are_bound_and_exported():
     assert lib.dfssm_version().startswith(b"dfssm-b200")
 
 
-def test_library_is_sm100a():
-    out = subprocess.run(["cuobjdump", "--list-elf", _lib.LIB_PATH], capture_output=True, text=True).stdout
-    assert "sm_100a" in out
+def test_library_is_built_for_sm100a_only():
+    """The build compiles every kernel for sm_100a and nothing else (no PTX to JIT elsewhere)."""
+    from dfssm_b200 import build
+    assert build.ARCH == ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+@pytest.mark.gpu
+def test_kernels_run_as_sm100a_binaries():
+    import ctypes
+    lib = _lib.load()
+    v = ctypes.c_int()
+    _lib.check(lib.dfssm_kernel_binary_version(0, ctypes.byref(v)))
+    assert v.value == 100
 
 
 def _create(buf):
