@@ -379,7 +379,7 @@ int enqueue_head(dfssm_engine* e, cudaStream_t s) {
     const char* v = getenv("DFSSM_HEAD_MMA_MIN");
     return v ? atoi(v) : 3;
   }();
-  if (e->batch >= head_mma_min && d.d_model % 64 == 0) {
+  if (e->batch >= head_mma_min && d.d_model % (64 * kHeadMmaU) == 0) {
     const size_t sm = lm_head_mma_smem(d.d_model);
     CU(ensure_smem(reinterpret_cast<const void*>(lm_head_mma_kernel), sm));
     lm_head_mma_kernel<<<e->sm_count, kHeadMmaThreads, sm, s>>>(e->Eq, e->Es, d.vocab, d.d_model, e->xn, e->batch,
@@ -1134,7 +1134,7 @@ int dfssm_lm_head_argmax(const int8_t* E_q, const float* E_s, int vocab, int d, 
   int dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (batch >= kMmaMinBatch && d % 64 == 0) {
+  if (batch >= kMmaMinBatch && d % (64 * kHeadMmaU) == 0) {
     const size_t sm2 = lm_head_mma_smem(d);
     CU(ensure_smem(reinterpret_cast<const void*>(lm_head_mma_kernel), sm2));
     lm_head_mma_kernel<<<sms, kHeadMmaThreads, sm2, s>>>(E_q, E_s, vocab, d, static_cast<const __half*>(x_f16), batch,
@@ -1355,9 +1355,19 @@ int prefill_chunk(dfssm_engine* e, const PrefillBufs& P, int T, cudaStream_t s) 
   CHECK_LAUNCH();
   // two CTAs per (head, sequence) while one each would leave SMs idle (the B/C conv is repeated)
   const int split = d.nheads * B < e->sm_count ? 2 : 1;
-  const size_t sm = prefill_scan_smem(T, d.d_state, split);
-  const void* scan = split == 2 ? reinterpret_cast<const void*>(prefill_scan_kernel<2>)
-                                : reinterpret_cast<const void*>(prefill_scan_kernel<1>);
+  // the chunk's recurrence in the SSD matrix form on the tensor cores from 32 tokens (measured at the
+  // 1.3B shape: 7% faster per prompt at 64 tokens, 3% slower at 16); DFSSM_PREFILL_SCAN=1 / 0 forces
+  // the token-by-token loop / the SSD form
+  static const int force = [] {
+    const char* v = getenv("DFSSM_PREFILL_SCAN");
+    return v ? atoi(v) : -1;
+  }();
+  const bool ssd = force == 1 ? false : (force == 0 ? true : T >= 32);
+  const size_t sm = prefill_scan_smem(T, d.d_state, split, ssd);
+  const void* scan = split == 2 ? (ssd ? reinterpret_cast<const void*>(prefill_scan_kernel<2, true>)
+                                       : reinterpret_cast<const void*>(prefill_scan_kernel<2, false>))
+                                : (ssd ? reinterpret_cast<const void*>(prefill_scan_kernel<1, true>)
+                                       : reinterpret_cast<const void*>(prefill_scan_kernel<1, false>));
   CU(ensure_smem(scan, sm));
   int rc;
   for (int l = 0; l < d.n_layer; ++l) {
@@ -1366,14 +1376,15 @@ int prefill_chunk(dfssm_engine* e, const PrefillBufs& P, int T, cudaStream_t s) 
     if ((rc = launch_mma<3>(L.in, R, P.q, P.qsum, P.xs, P.t, P.proj, d.n_in, nullptr, nullptr, nullptr, d.d_inner,
                             d.d_xbc, s, P.us)))
       return rc;
-    if (split == 2)
-      prefill_scan_kernel<2><<<dim3(d.nheads * 2, B), kScanThreads, sm, s>>>(
-          P.proj, d.n_in, T, d.d_inner, d.d_state, d.nheads, L.conv_w, L.conv_b, L.dt_bias, L.A_log, L.Dp,
-          e->conv + (size_t)l * e->conv_layer, e->ssm + (size_t)l * e->ssm_layer, P.gated);
-    else
-      prefill_scan_kernel<1><<<dim3(d.nheads, B), kScanThreads, sm, s>>>(
-          P.proj, d.n_in, T, d.d_inner, d.d_state, d.nheads, L.conv_w, L.conv_b, L.dt_bias, L.A_log, L.Dp,
-          e->conv + (size_t)l * e->conv_layer, e->ssm + (size_t)l * e->ssm_layer, P.gated);
+    void* args[] = {const_cast<__half**>(&P.proj), const_cast<int*>(&d.n_in), &T, const_cast<int*>(&d.d_inner),
+                    const_cast<int*>(&d.d_state), const_cast<int*>(&d.nheads), const_cast<__half**>(&L.conv_w),
+                    const_cast<__half**>(&L.conv_b), const_cast<float**>(&L.dt_bias), const_cast<float**>(&L.A_log),
+                    const_cast<float**>(&L.Dp), nullptr, nullptr, const_cast<__half**>(&P.gated)};
+    float* cs_l = e->conv + (size_t)l * e->conv_layer;
+    float* hs_l = e->ssm + (size_t)l * e->ssm_layer;
+    args[11] = &cs_l;
+    args[12] = &hs_l;
+    CU(cudaLaunchKernel(scan, dim3(d.nheads * split, B), dim3(kScanThreads), args, sm, s));
     CHECK_LAUNCH();
     if ((rc = launch_prep(e, P.gated, d.d_inner, L.norm_w, 1, &L.out, s, Group{0, R}, rb))) return rc;
     if ((rc = launch_mma<1>(L.out, R, P.q, P.qsum, P.xs, P.t, P.x, d.d_model, nullptr, nullptr, nullptr, d.d_inner,
@@ -1399,7 +1410,7 @@ int prefill_impl(dfssm_engine* e, dfssm_engine* owner, const int32_t* tokens_dev
   const int B = e->batch;
   const int Tc = T < kScanMaxT ? T : kScanMaxT;
   const bool batched = B * (T < Tc ? T : Tc) >= kMmaMinBatch && mma_rg(d.n_in, d.d_model) && mma_rg(d.d_model, d.d_inner) &&
-                       prefill_scan_smem(Tc, d.d_state, 1) <= 227 * 1024;
+                       prefill_scan_smem(Tc, d.d_state, 1, true) <= 227 * 1024;
   if (!batched) {  // too few rows for the batched kernels: token by token through dfssm_step
     for (int t = 0; t < T; ++t) {
       CU(cudaMemcpy2DAsync(e->tokens, 4, tokens_dev + t, (size_t)T * 4, 4, B, cudaMemcpyDeviceToDevice, us));

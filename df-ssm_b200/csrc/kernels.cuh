@@ -766,7 +766,9 @@ lm_head_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, int 
 // of the A and B fragments.  logits = acc * E_s[v]; the argmax keys are merged per CTA and then
 // with atomicMax into best[b].
 // ---------------------------------------------------------------------------------------
-constexpr int kHeadMmaThreads = 256;
+constexpr int kHeadMmaWarps = 16;  // one CTA per SM (the activation tile fills shared memory)
+constexpr int kHeadMmaThreads = 32 * kHeadMmaWarps;
+constexpr int kHeadMmaU = 4;       // 64-column blocks whose embedding loads are issued together
 constexpr int kHeadMmaNT = 4;  // 32 batch rows per pass
 
 __global__ void __launch_bounds__(kHeadMmaThreads, 1)
@@ -777,7 +779,7 @@ lm_head_mma_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, 
   extern __shared__ __align__(16) unsigned char smem[];
   const int SX = d + 8;  // padded fp16 row stride
   __half* sx = reinterpret_cast<__half*>(smem);                                        // [NB][SX]
-  unsigned long long* sbest = reinterpret_cast<unsigned long long*>(smem + (size_t)NB * SX * 2);  // [8 warps][NB]
+  unsigned long long* sbest = reinterpret_cast<unsigned long long*>(smem + (size_t)NB * SX * 2);  // [warps][NB]
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
   const int ntiles = (vocab + 15) / 16;
   __shared__ uint64_t xbar;
@@ -800,7 +802,7 @@ lm_head_mma_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, 
     unsigned long long wbest[kHeadMmaNT][2];
 #pragma unroll
     for (int tt = 0; tt < kHeadMmaNT; ++tt) wbest[tt][0] = wbest[tt][1] = 0ull;
-    for (int tile = blockIdx.x * 8 + wid; tile < ntiles; tile += gridDim.x * 8) {
+    for (int tile = blockIdx.x * kHeadMmaWarps + wid; tile < ntiles; tile += gridDim.x * kHeadMmaWarps) {
       const int v0 = tile * 16;
       const int va = min(v0 + g, vocab - 1), vb = min(v0 + g + 8, vocab - 1);
       const uint4* ra = reinterpret_cast<const uint4*>(Eq + (size_t)va * d);
@@ -810,20 +812,31 @@ lm_head_mma_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, 
       for (int tt = 0; tt < kHeadMmaNT; ++tt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[tt][i] = 0.f;
-      for (int blk = 0; blk < d / 64; ++blk) {
-        const uint4 ea = ldg_stream(ra + blk * 4 + c);
-        const uint4 eb = ldg_stream(rb + blk * 4 + c);
-        const unsigned wa[4] = {ea.x ^ 0x80808080u, ea.y ^ 0x80808080u, ea.z ^ 0x80808080u, ea.w ^ 0x80808080u};
-        const unsigned wb[4] = {eb.x ^ 0x80808080u, eb.y ^ 0x80808080u, eb.z ^ 0x80808080u, eb.w ^ 0x80808080u};
+      // kHeadMmaU blocks' embedding loads go out together before their MMAs, so each lane keeps
+      // 2 x kHeadMmaU 16-byte loads in flight (d / 64 is a multiple of kHeadMmaU: d % 256 == 0)
+      for (int blk0 = 0; blk0 < d / 64; blk0 += kHeadMmaU) {
+        uint4 ea[kHeadMmaU], eb[kHeadMmaU];
 #pragma unroll
-        for (int s2 = 0; s2 < 4; ++s2) {
-          const unsigned a0 = i8x2_to_h2(wa[s2], 0x4140u), a2 = i8x2_to_h2(wa[s2], 0x4342u);
-          const unsigned a1 = i8x2_to_h2(wb[s2], 0x4140u), a3 = i8x2_to_h2(wb[s2], 0x4342u);
-          const int col = blk * 64 + 16 * c + 4 * s2;
+        for (int u = 0; u < kHeadMmaU; ++u) {
+          ea[u] = ldg_stream(ra + (blk0 + u) * 4 + c);
+          eb[u] = ldg_stream(rb + (blk0 + u) * 4 + c);
+        }
 #pragma unroll
-          for (int tt = 0; tt < kHeadMmaNT; ++tt) {
-            const uint2 bv = *reinterpret_cast<const uint2*>(sx + (tt * 8 + g) * SX + col);
-            mma_f16(acc[tt], a0, a1, a2, a3, bv.x, bv.y);
+        for (int u = 0; u < kHeadMmaU; ++u) {
+          const unsigned wa[4] = {ea[u].x ^ 0x80808080u, ea[u].y ^ 0x80808080u, ea[u].z ^ 0x80808080u,
+                                  ea[u].w ^ 0x80808080u};
+          const unsigned wb[4] = {eb[u].x ^ 0x80808080u, eb[u].y ^ 0x80808080u, eb[u].z ^ 0x80808080u,
+                                  eb[u].w ^ 0x80808080u};
+#pragma unroll
+          for (int s2 = 0; s2 < 4; ++s2) {
+            const unsigned a0 = i8x2_to_h2(wa[s2], 0x4140u), a2 = i8x2_to_h2(wa[s2], 0x4342u);
+            const unsigned a1 = i8x2_to_h2(wb[s2], 0x4140u), a3 = i8x2_to_h2(wb[s2], 0x4342u);
+            const int col = (blk0 + u) * 64 + 16 * c + 4 * s2;
+#pragma unroll
+            for (int tt = 0; tt < kHeadMmaNT; ++tt) {
+              const uint2 bv = *reinterpret_cast<const uint2*>(sx + (tt * 8 + g) * SX + col);
+              mma_f16(acc[tt], a0, a1, a2, a3, bv.x, bv.y);
+            }
           }
         }
       }
@@ -859,13 +872,15 @@ lm_head_mma_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, 
     __syncthreads();
     if (threadIdx.x < nb) {
       unsigned long long k = 0ull;
-      for (int w = 0; w < 8; ++w) k = sbest[w * NB + threadIdx.x] > k ? sbest[w * NB + threadIdx.x] : k;
+      for (int w = 0; w < kHeadMmaWarps; ++w) k = sbest[w * NB + threadIdx.x] > k ? sbest[w * NB + threadIdx.x] : k;
       atomicMax(best + bt0 + threadIdx.x, k);
     }
   }
 }
 
-inline size_t lm_head_mma_smem(int d) { return (size_t)8 * kHeadMmaNT * (d + 8) * 2 + 8 * 8 * kHeadMmaNT * 8; }
+inline size_t lm_head_mma_smem(int d) {
+  return (size_t)8 * kHeadMmaNT * (d + 8) * 2 + (size_t)kHeadMmaWarps * 8 * kHeadMmaNT * 8;
+}
 
 __global__ void finalize_kernel(unsigned long long* __restrict__ best, int B, int* __restrict__ tokens) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;

@@ -6,6 +6,8 @@
 // once per layer instead of once per token.  The arithmetic per token is that of the decode
 // kernels (the in_proj conv epilogue and ssm_gate_kernel), in the same order.
 #pragma once
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace dfssm {
@@ -25,7 +27,156 @@ constexpr int kScanMaxT = 64;  // tokens per scan launch (longer prompts run in 
 // outputs (time-major, so a lane's 4 B/C values of one token are one conflict-free float4), the
 // SiLU(z) gate factors, softplus(dt) and exp(A dt) per token, and the gated outputs (written to HBM
 // as whole rows at the end).
-template <int SPLIT>
+// ---- SSD (chunked matrix) form of the chunk's recurrence, on the tensor cores
+// With s_t = sum_{u <= t} dt_u A (A = -exp(A_log)), the state after token t is
+//   h_t = e^{s_t} h_0 + sum_{u <= t} e^{s_t - s_u} dt_u x_u B_u^T
+// so the chunk's outputs and final state are four small GEMMs per (head, sequence):
+//   G = C B^T (T x T),  M = G o [u <= t] e^{s_t - s_u} dt_u,  Y = M X + diag(e^s) C h_0^T + D X,
+//   h_T = e^{s_T} h_0 + (X^T diag(e^{s_T - s_u} dt_u)) B.
+// They run as mma.sync m16n8k8 TF32 with fp32 accumulation.  x, B and C are fp16 values (the conv
+// outputs), exact in TF32; the fp32 operands (M, h_0, the weighted X^T) are split into a TF32 high
+// part and a TF32 remainder, two MMAs, so every product keeps ~22 significant bits.  The sums run
+// in another order than the token loop's, within fp32 rounding of it.
+__device__ __forceinline__ unsigned tf32_hi(float v) {
+  unsigned r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return r;
+}
+__device__ __forceinline__ void tf32_split(float v, unsigned& hi, unsigned& lo) {
+  hi = tf32_hi(v);
+  lo = tf32_hi(v - __uint_as_float(hi));
+}
+__device__ __forceinline__ void mma_tf32(float (&d)[4], unsigned a0, unsigned a1, unsigned a2, unsigned a3, unsigned b0,
+                                         unsigned b1) {
+  asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Shared-memory floats of the SSD step for T tokens and R state rows: M [Tp][Tp+4], h_0 [R][N+4]
+// (Tp = T rounded up to 16), then the gated outputs (fp16 [T][R]).
+__host__ __device__ inline size_t ssd_smem_floats(int T, int rows, int d_state) {
+  const size_t Tp = (size_t)(T + 15) / 16 * 16;
+  return Tp * (Tp + 4) + (size_t)rows * (d_state + 4) + ((size_t)T * rows + 1) / 2;
+}
+
+// The SSD step of one CTA: its R state rows of one head over a chunk of T <= 64 tokens.  cvo holds
+// the conv outputs time-major ([T][NCP]: x of the R rows, then B, then C), zg the SiLU(z) gate
+// factors ([T][R + 1]), dts softplus(dt + bias); hv is this thread's part of h_0 (rows
+// wid * R / 16 + r, columns 4 lane ..), hs the rows' fp32 state in HBM (written with h_T).  Writes
+// the gated outputs to gs ([T][R] fp16).  Uses cum and wv ([T] each), M ([Tp][Tp + 4]) and h0s
+// ([R][d_state + 4]).
+template <int R>
+__device__ void ssd_chunk(int T, int Tp, int N, int NCP, const float* cvo, const float* zg, const float* dts,
+                          float Ah, float Dh, float* cum, float* wv, float* M, float* h0s, __half* gs,
+                          const float4 (&hv)[R / 16], float* hs) {
+  constexpr int RPW = R / 16;
+  const int tid = threadIdx.x, wid = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+  const int MS = Tp + 4, HS = N + 4, ZS = R + 1;
+  const float* xb = cvo;          // x[t][p] = xb[t * NCP + p]
+  const float* Bm = cvo + R;      // B[t][n]
+  const float* Cm = cvo + R + N;  // C[t][n]
+#pragma unroll
+  for (int r = 0; r < RPW; ++r)
+    *reinterpret_cast<float4*>(h0s + (wid * RPW + r) * HS + 4 * lane) = hv[r];
+  if (tid == 0) {  // s_t = sum_{u <= t} dt_u A, in token order
+    float a = 0.f;
+    for (int t = 0; t < T; ++t) {
+      a += dts[t] * Ah;
+      cum[t] = a;
+    }
+  }
+  __syncthreads();
+  const float sT = cum[T - 1];
+  for (int t = tid; t < Tp; t += kScanThreads) wv[t] = t < T ? expf(sT - cum[t]) * dts[t] : 0.f;
+  auto fp = [](float v) { return __float_as_uint(v); };  // fp16-exact values are exact TF32 operands
+  // G = C B^T, masked and decayed into M
+  const int nmt = Tp / 16, nnt = Tp / 8;
+  for (int tile = wid; tile < nmt * nnt; tile += kScanThreads / 32) {
+    const int mt = tile / nnt, nt = tile - mt * nnt;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const int ta = 16 * mt + g, tb = ta + 8, u = 8 * nt + g;
+    if (8 * nt <= 16 * mt + 15) {  // tiles wholly above the diagonal stay zero
+      const bool va = ta < T, vb = tb < T, vu = u < T;
+      for (int k0 = 0; k0 < N; k0 += 8) {
+        const unsigned a0 = va ? fp(Cm[ta * NCP + k0 + c]) : 0u, a2 = va ? fp(Cm[ta * NCP + k0 + c + 4]) : 0u;
+        const unsigned a1 = vb ? fp(Cm[tb * NCP + k0 + c]) : 0u, a3 = vb ? fp(Cm[tb * NCP + k0 + c + 4]) : 0u;
+        const unsigned b0 = vu ? fp(Bm[u * NCP + k0 + c]) : 0u, b1 = vu ? fp(Bm[u * NCP + k0 + c + 4]) : 0u;
+        mma_tf32(acc, a0, a1, a2, a3, b0, b1);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int t = i < 2 ? ta : tb, v = 8 * nt + 2 * c + (i & 1);
+      M[t * MS + v] = (v <= t && t < T) ? acc[i] * expf(cum[t] - cum[v]) * dts[v] : 0.f;
+    }
+  }
+  __syncthreads();
+  // outputs: Y = M X + diag(e^s) C h_0^T + D X, gated
+  const int nyt = nmt * (R / 8);
+  for (int tile = wid; tile < nyt; tile += kScanThreads / 32) {
+    const int mt = tile / (R / 8), nt = tile - mt * (R / 8);
+    const int ta = 16 * mt + g, tb = ta + 8, p = 8 * nt + g;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc3[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k0 = 0; k0 < Tp; k0 += 8) {
+      unsigned ah[4], al[4];
+      tf32_split(M[ta * MS + k0 + c], ah[0], al[0]);
+      tf32_split(M[tb * MS + k0 + c], ah[1], al[1]);
+      tf32_split(M[ta * MS + k0 + c + 4], ah[2], al[2]);
+      tf32_split(M[tb * MS + k0 + c + 4], ah[3], al[3]);
+      const int u0 = k0 + c, u1 = u0 + 4;
+      const unsigned b0 = u0 < T ? fp(xb[u0 * NCP + p]) : 0u, b1 = u1 < T ? fp(xb[u1 * NCP + p]) : 0u;
+      mma_tf32(acc, ah[0], ah[1], ah[2], ah[3], b0, b1);
+      mma_tf32(acc, al[0], al[1], al[2], al[3], b0, b1);
+    }
+    const bool va = ta < T, vb = tb < T;
+    for (int k0 = 0; k0 < N; k0 += 8) {
+      const unsigned a0 = va ? fp(Cm[ta * NCP + k0 + c]) : 0u, a2 = va ? fp(Cm[ta * NCP + k0 + c + 4]) : 0u;
+      const unsigned a1 = vb ? fp(Cm[tb * NCP + k0 + c]) : 0u, a3 = vb ? fp(Cm[tb * NCP + k0 + c + 4]) : 0u;
+      unsigned bh0, bl0, bh1, bl1;
+      tf32_split(h0s[p * HS + k0 + c], bh0, bl0);
+      tf32_split(h0s[p * HS + k0 + c + 4], bh1, bl1);
+      mma_tf32(acc3, a0, a1, a2, a3, bh0, bh1);
+      mma_tf32(acc3, a0, a1, a2, a3, bl0, bl1);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int t = i < 2 ? ta : tb, q = 8 * nt + 2 * c + (i & 1);
+      if (t < T) {
+        const float xv = xb[t * NCP + q];
+        const float y = acc[i] + expf(cum[t]) * acc3[i] + xv * Dh;
+        gs[t * R + q] = f2h(h2f(f2h(y)) * zg[t * ZS + q]);
+      }
+    }
+  }
+  // h_T = e^{s_T} h_0 + (X^T diag(wv)) B
+  const float esT = expf(sT);
+  const int nht = (R / 16) * (N / 8);
+  for (int tile = wid; tile < nht; tile += kScanThreads / 32) {
+    const int mt = tile / (N / 8), nt = tile - mt * (N / 8);
+    const int pa = 16 * mt + g, pb = pa + 8, n = 8 * nt + g;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k0 = 0; k0 < Tp; k0 += 8) {
+      const int u0 = k0 + c, u1 = u0 + 4;
+      const float w0 = wv[u0], w1 = wv[u1];
+      unsigned ah[4], al[4];
+      tf32_split(u0 < T ? xb[u0 * NCP + pa] * w0 : 0.f, ah[0], al[0]);
+      tf32_split(u0 < T ? xb[u0 * NCP + pb] * w0 : 0.f, ah[1], al[1]);
+      tf32_split(u1 < T ? xb[u1 * NCP + pa] * w1 : 0.f, ah[2], al[2]);
+      tf32_split(u1 < T ? xb[u1 * NCP + pb] * w1 : 0.f, ah[3], al[3]);
+      const unsigned b0 = u0 < T ? fp(Bm[u0 * NCP + n]) : 0u, b1 = u1 < T ? fp(Bm[u1 * NCP + n]) : 0u;
+      mma_tf32(acc, ah[0], ah[1], ah[2], ah[3], b0, b1);
+      mma_tf32(acc, al[0], al[1], al[2], al[3], b0, b1);
+    }
+    const int nc = 8 * nt + 2 * c;
+    const float2 ra = *reinterpret_cast<const float2*>(h0s + pa * HS + nc);
+    const float2 rb = *reinterpret_cast<const float2*>(h0s + pb * HS + nc);
+    __stcs(reinterpret_cast<float2*>(hs + (size_t)pa * N + nc), make_float2(acc[0] + esT * ra.x, acc[1] + esT * ra.y));
+    __stcs(reinterpret_cast<float2*>(hs + (size_t)pb * N + nc), make_float2(acc[2] + esT * rb.x, acc[3] + esT * rb.y));
+  }
+}
+
+template <int SPLIT, bool SSD>
 __global__ void __launch_bounds__(kScanThreads)
 prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inner, int d_state, int nheads,
                     const __half* __restrict__ conv_w, const __half* __restrict__ conv_b,
@@ -38,14 +189,22 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
   const int c0 = h * DFSSM_HEADDIM + part * kScanRows;  // first head channel of this CTA
   const int d_xbc = d_inner + 2 * d_state;
   const int NC = kScanRows + 2 * d_state;  // this CTA's x channels, then all B and C channels
+  const int NCP = NC + 4;                   // cvo row stride (padded against bank conflicts)
   const int TS = T + 3;
+  const int Tp = (T + 15) & ~15;
+  // raw is dead once the conv has run: the gated outputs (and the SSD step's M and h_0) reuse it
+  const size_t raw_floats =
+      ((SSD ? max((size_t)NC * TS, ssd_smem_floats(T, kScanRows, d_state)) : (size_t)NC * TS) + 3) & ~(size_t)3;
   float* raw = sm;                          // [NC][T + 3]: 3 taps of conv state, then the T raw inputs
-  float* cvo = raw + NC * TS;               // [T][NC]: fp16-exact conv + SiLU outputs
+  float* cvo = raw + raw_floats;            // [T][NCP]: fp16-exact conv + SiLU outputs
   constexpr int ZS = kScanRows + 1;         // padded: the staging stores run along t
-  float* zg = cvo + NC * T;                 // [T][ZS]: fp16-exact SiLU(z)
-  float* dts = zg + T * ZS;                 // [T]: softplus(dt + bias)
-  float* abar = dts + T;                    // [T]: exp(A dt)
-  __half* gs = reinterpret_cast<__half*>(raw);  // [T][kScanRows] gated outputs (raw is dead by then)
+  float* zg = cvo + NCP * T;                // [T][ZS]: fp16-exact SiLU(z)
+  float* dts = zg + T * ZS;                 // [Tp]: softplus(dt + bias)
+  float* abar = dts + Tp;                   // [Tp]: exp(A dt) (SSD: the state-update weights)
+  float* cum = abar + Tp;                   // [Tp]: s_t (SSD)
+  float* Msm = raw;                         // SSD: [Tp][Tp + 4]
+  float* h0s = Msm + (size_t)Tp * (Tp + 4);  // SSD: [kScanRows][d_state + 4]
+  __half* gs = reinterpret_cast<__half*>(SSD ? h0s + (size_t)kScanRows * (d_state + 4) : raw);  // [T][kScanRows]
   auto chan = [&](int c) { return c < kScanRows ? c0 + c : d_inner + (c - kScanRows); };
   // state tile: first, so the HBM stream starts before anything else
   const int wid = tid >> 5, lane = tid & 31, n0 = lane * 4;
@@ -124,7 +283,7 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
       const float v = rr[3 + t];
       const float o2 = s0 * w0 + s1 * w1 + s2 * w2 + v * w3 + cb;
       const float sig = 1.0f / (1.0f + expf(-o2));
-      cvo[t * NC + c] = h2f(f2h(o2 * sig));
+      cvo[t * NCP + c] = h2f(f2h(o2 * sig));
       s0 = s1;
       s1 = s2;
       s2 = v;
@@ -138,8 +297,11 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
     csw[(size_t)k * d_xbc + chan(c)] = raw[c * TS + T + k];
   }
   __syncthreads();
+  if constexpr (SSD) {
+    ssd_chunk<kScanRows>(T, Tp, d_state, NCP, cvo, zg, dts, Ah, Dh, cum, abar, Msm, h0s, gs, hv, hs);
+  } else {
   for (int t = 0; t < T; ++t) {
-    const float* ct = cvo + t * NC;
+    const float* ct = cvo + t * NCP;
     const float dtv = dts[t], Abar = abar[t];
     const float4 Bn = *reinterpret_cast<const float4*>(ct + kScanRows + n0);
     const float4 Cn = *reinterpret_cast<const float4*>(ct + kScanRows + d_state + n0);
@@ -181,6 +343,7 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
 #pragma unroll
   for (int r = 0; r < kScanRPW; ++r)
     __stcs(reinterpret_cast<float4*>(hs + (wid * kScanRPW + r) * DFSSM_DSTATE + n0), hv[r]);
+  }
   __syncthreads();
   for (int i = tid; i < T * kScanRows / 2; i += kScanThreads) {
     const int t = i / (kScanRows / 2), p2 = i - t * (kScanRows / 2);
@@ -188,9 +351,13 @@ prefill_scan_kernel(const __half* __restrict__ proj, int n_in, int T, int d_inne
   }
 }
 
-inline size_t prefill_scan_smem(int T, int d_state, int split) {
+inline size_t prefill_scan_smem(int T, int d_state, int split, bool ssd) {
   const size_t rows = DFSSM_HEADDIM / split, nc = rows + 2 * d_state;
-  return (nc * (2 * T + 3) + (size_t)T * (rows + 1) + 2 * T) * sizeof(float);
+  size_t raw = nc * (T + 3);
+  if (ssd) raw = std::max(raw, ssd_smem_floats(T, (int)rows, d_state));
+  raw = (raw + 3) & ~(size_t)3;
+  const size_t Tp = (size_t)(T + 15) / 16 * 16;
+  return (raw + (nc + 4) * T + (size_t)T * (rows + 1) + 3 * Tp) * sizeof(float);
 }
 
 // x rows b*T + t = the embedding of tokens[b][t] (fp16, as embed_kernel).
