@@ -622,30 +622,47 @@ ssm_gate_kernel(const __half* __restrict__ xbc, int ld_xbc, const __half* __rest
       Cn[i] = h2f(ch[i]);
     }
   }
+  float part[8];
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
     const int pp = wid * 8 + r;
-    const float xv = h2f(xc[h * DFSSM_HEADDIM + pp]);
-    const float X = xv * dtv;
+    const float X = h2f(xc[h * DFSSM_HEADDIM + pp]) * dtv;
     float4 o;
     o.x = Abar * hv[r].x + X * Bn[0];
     o.y = Abar * hv[r].y + X * Bn[1];
     o.z = Abar * hv[r].z + X * Bn[2];
     o.w = Abar * hv[r].w + X * Bn[3];
     __stcs(reinterpret_cast<float4*>(hs + pp * DFSSM_DSTATE + n0), o);
-    float part = Cn[0] * o.x + Cn[1] * o.y + Cn[2] * o.z + Cn[3] * o.w;
-    part = warp_sum(part);
-    if (lane == r) {
-      const float y = part + xv * Dh;
-      __half o16 = f2h(y);
-      if (zin != nullptr) {
-        const float z = h2f(zin[(size_t)b * ld_z + h * DFSSM_HEADDIM + pp]);
-        const float sig = round_h(1.0f / (1.0f + expf(-z)));
-        const float silu = round_h(z * sig);
-        o16 = f2h(h2f(o16) * silu);
-      }
-      out[(size_t)b * ld_out + h * DFSSM_HEADDIM + pp] = o16;
+    part[r] = Cn[0] * o.x + Cn[1] * o.y + Cn[2] * o.z + Cn[3] * o.w;
+  }
+  // C.h of the warp's 8 rows summed over the 32 lanes as a transposing butterfly: each exchange halves
+  // the values a lane holds (7 shuffles), two more finish the sums, and lane 4k + 0 ends with the sum
+  // of row rw (9 shuffles for 8 rows instead of 40); the 8 rows' epilogues then run in parallel
+  int rw = 0;
+#pragma unroll
+  for (int n = 8, off = 16; n > 1; n >>= 1, off >>= 1) {
+    const bool hi = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) {
+      const float send = hi ? part[i] : part[i + n / 2];
+      const float keep = hi ? part[i + n / 2] : part[i];
+      part[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
     }
+    rw += hi ? n / 2 : 0;
+  }
+  part[0] += __shfl_xor_sync(0xffffffffu, part[0], 2);
+  part[0] += __shfl_xor_sync(0xffffffffu, part[0], 1);
+  if ((lane & 3) == 0) {
+    const int pp = wid * 8 + rw;
+    const float y = part[0] + h2f(xc[h * DFSSM_HEADDIM + pp]) * Dh;
+    __half o16 = f2h(y);
+    if (zin != nullptr) {
+      const float z = h2f(zin[(size_t)b * ld_z + h * DFSSM_HEADDIM + pp]);
+      const float sig = round_h(1.0f / (1.0f + expf(-z)));
+      const float silu = round_h(z * sig);
+      o16 = f2h(h2f(o16) * silu);
+    }
+    out[(size_t)b * ld_out + h * DFSSM_HEADDIM + pp] = o16;
   }
 }
 
