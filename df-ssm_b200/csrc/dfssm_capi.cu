@@ -114,13 +114,22 @@ int launch_prep(dfssm_engine* e, const __half* in, int K, const float* w, int qu
                 cudaStream_t s, Group G, const RowBufs& R) {
   if (quant && p && K % 512 == 0) {
     const int kpt = K / 512;
-#define DFSSM_PREP_FAST(n)                                                                                  \
-  if (kpt == n) {                                                                                          \
-    act_prep_fast_kernel<n><<<dim3(G.nb, 2), kPrepFastThreads, 0, s>>>(in + (size_t)G.b0 * K, K, w, R.q + (size_t)G.b0 * K, \
-                                                              R.xs + G.b0, R.qsum + G.b0, p->B16, R.t + G.b0 * kRank); \
+    // rank parts per row: 8 while rows x 8 CTAs still fit on the SMs (measured at the 1.3B shape: batch 8
+    // 1.59 -> 1.53 ms per step), else 2 (4 parts were 2% slower at batches 32 and 64); DFSSM_PREP_PARTS
+    // overrides
+    static const int force_parts = [] {
+      const char* v = getenv("DFSSM_PREP_PARTS");
+      return v ? atoi(v) : 0;
+    }();
+    const int parts = force_parts ? force_parts : (G.nb * 8 <= e->sm_count ? 8 : 2);
+#define DFSSM_PREP_FAST_P(n, P)                                                                             \
+  if (kpt == n && parts == P) {                                                                             \
+    act_prep_fast_kernel<n, P><<<dim3(G.nb, P), kPrepFastThreads, 0, s>>>(in + (size_t)G.b0 * K, K, w,      \
+        R.q + (size_t)G.b0 * K, R.xs + G.b0, R.qsum + G.b0, p->B16, R.t + G.b0 * kRank);                    \
     CHECK_LAUNCH();                                                                                        \
     return DFSSM_OK;                                                                                       \
   }
+#define DFSSM_PREP_FAST(n) DFSSM_PREP_FAST_P(n, 2) DFSSM_PREP_FAST_P(n, 4) DFSSM_PREP_FAST_P(n, 8)
     DFSSM_PREP_FAST(1)
     DFSSM_PREP_FAST(2)
     DFSSM_PREP_FAST(4)
@@ -128,6 +137,7 @@ int launch_prep(dfssm_engine* e, const __half* in, int K, const float* w, int qu
     DFSSM_PREP_FAST(5)
     DFSSM_PREP_FAST(10)
 #undef DFSSM_PREP_FAST
+#undef DFSSM_PREP_FAST_P
   }
   const size_t sm = (size_t)K * sizeof(__half);
   act_prep_kernel<<<G.nb, kPrepThreads, sm, s>>>(in + (size_t)G.b0 * K, K, w, quant, R.xn + (size_t)G.b0 * K,

@@ -111,15 +111,16 @@ act_prep_kernel(const __half* __restrict__ in, int K, const float* __restrict__ 
 
 // act_prep_fast: the same prologue as act_prep_kernel (quantising variant) for K = 512 * KPT,
 // with 512 threads that each keep KPT columns and their LoRA-B slices in registers and one
-// combined block reduction for the LoRA partials and the q sum.  Grid (rows, 2): CTA (b, p)
-// computes ranks 8p..8p+7 of row b's LoRA down-projection (halving each CTA's LoRA-B stream);
-// both compute the identical q, xs and qsum, which CTA p = 0 stores.
-template <int KPT>
+// combined block reduction for the LoRA partials and the q sum.  Grid (rows, PARTS): CTA (b, p)
+// computes ranks p * 16 / PARTS.. of row b's LoRA down-projection (dividing each CTA's LoRA-B
+// stream); all compute the identical q, xs and qsum, which CTA p = 0 stores.  More parts put more
+// SMs on few rows.
+template <int KPT, int PARTS = 2>
 __global__ void __launch_bounds__(kPrepFastThreads)
 act_prep_fast_kernel(const __half* __restrict__ in, int K, const float* __restrict__ w, int8_t* __restrict__ q_out,
                      __half* __restrict__ xs_out, int* __restrict__ qsum_out, const __half* __restrict__ B16,
                      __half* __restrict__ t_out) {
-  constexpr int NR = DFSSM_RANK / 2;
+  constexpr int NR = DFSSM_RANK / PARTS;
   __shared__ float red[(kPrepFastWarps + 1) * (NR + 1)];
   __shared__ float s_t[NR];
   __shared__ float s_xs[1];
