@@ -569,8 +569,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
   float* s_t = red + kRedFloats;                    // [B*16]
   float* s_xs = s_t + B * 16;                       // [B]
   int* s_qpart = reinterpret_cast<int*>(s_xs + B);  // [B][kWarps] per-warp q sums
-  float* s_lbs = reinterpret_cast<float*>(s_qpart + B * kWarps);  // [16]
-  float* s_z = s_lbs + 16;                          // [B][64]
+  float* s_abar = reinterpret_cast<float*>(s_qpart + B * kWarps);  // [16]: exp(A dt) per sequence
+  float* s_z = s_abar + 16;                         // [B][64]: the SiLU(z) gate factors
   float* s_xc = s_z + B * 64;                       // [B][64]
   float* s_dt = s_xc + B * 64;                      // [B]
   float* s_bc = s_dt + B;                           // [B][2*d_state] (fp32)
@@ -705,8 +705,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
         const int row = e2 / B, b = e2 - row * B;
         const int dot = s_dot[e2];
         const float v = proj_out(dot, s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
-        if (row < np) {
-          s_z[b * 64 + row] = v;
+        if (row < np) {  // the gate factor fp16(z fp16(sigmoid(z))) of this channel
+          const float sig = round_h(1.0f / (1.0f + expf(-v)));
+          s_z[b * 64 + row] = round_h(v * sig);
         } else {
           const int j = row - np, ch = pl.h * DFSSM_HEADDIM + pl.p0 + j;
           const float s0 = cst[(b * 3 + 0) * np + j], s1 = cst[(b * 3 + 1) * np + j], s2 = cst[(b * 3 + 2) * np + j];
@@ -729,8 +730,11 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
           if (i < B * DFSSM_DSTATE) {
             s_bc[2 * i] = lo_h(v);
             s_bc[2 * i + 1] = hi_h(v);
-          } else {
-            s_dt[i - B * DFSSM_DSTATE] = (pl.h & 1) ? hi_h(v) : lo_h(v);
+          } else {  // dt = softplus(raw + dt_bias) and exp(A dt), once per sequence
+            const float* hp = s_hptab + layer * 4;
+            const float dtv = log1pf(expf(((pl.h & 1) ? hi_h(v) : lo_h(v)) + hp[0]));
+            s_dt[i - B * DFSSM_DSTATE] = dtv;
+            s_abar[i - B * DFSSM_DSTATE] = expf(dtv * (-expf(hp[1])));
           }
         }
       }
@@ -744,37 +748,39 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       const float* hp = s_hptab + layer * 4;
 #pragma unroll
       for (int b = 0; b < B; ++b) {
-        float dtv = s_dt[b] + hp[0];
-        dtv = log1pf(expf(dtv));
-        const float Abar = expf(dtv * (-expf(hp[1])));
+        const float dtv = s_dt[b], Abar = s_abar[b];
         const float Dh = hp[2];
         const float* bb = s_bc + b * 256 + lane * 4;
         const float4 Bn = make_float4(bb[0], bb[1], bb[2], bb[3]);
         const float4 Cn = make_float4(bb[128], bb[129], bb[130], bb[131]);
-        float gv[kMaxRPW];
+        float part[kMaxRPW];
 #pragma unroll
         for (int rr = 0; rr < kMaxRPW; ++rr) {
           const int p = wid * kMaxRPW + rr;
           const float4 hv = *reinterpret_cast<const float4*>(sst + ((size_t)b * np + p) * DFSSM_DSTATE + lane * 4);
-          const float xv = s_xc[b * 64 + p];
-          const float X = xv * dtv;
+          const float X = s_xc[b * 64 + p] * dtv;
           float4 o;
           o.x = Abar * hv.x + X * Bn.x;
           o.y = Abar * hv.y + X * Bn.y;
           o.z = Abar * hv.z + X * Bn.z;
           o.w = Abar * hv.w + X * Bn.w;
           hnew[b][rr] = o;
-          float part = Cn.x * o.x + Cn.y * o.y + Cn.z * o.z + Cn.w * o.w;
-          part = warp_sum(part);
-          const float y = part + xv * Dh;
-          const float z = s_z[b * 64 + p];
-          const float sig = round_h(1.0f / (1.0f + expf(-z)));
-          const float silu = round_h(z * sig);
-          gv[rr] = round_h(y) * silu;
+          part[rr] = Cn.x * o.x + Cn.y * o.y + Cn.z * o.z + Cn.w * o.w;
         }
+        // C.h of the two rows over the 32 lanes as a transposing butterfly (5 shuffles instead of 10):
+        // lanes 0-15 end with row 0, lanes 16-31 with row 1; lanes 0 and 16 finish their row and lane 0
+        // publishes the pair
+        static_assert(kMaxRPW == 2, "the butterfly below pairs two rows per warp");
+        const bool hi = (lane & 16) != 0;
+        float sum = (hi ? part[1] : part[0]) + __shfl_xor_sync(0xffffffffu, hi ? part[0] : part[1], 16);
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        const int pr = wid * kMaxRPW + (hi ? 1 : 0);
+        const float gmine = round_h(sum + s_xc[b * 64 + pr] * Dh) * s_z[b * 64 + pr];
+        const float gnext = __shfl_sync(0xffffffffu, gmine, 16);
         if (lane == 0) {
           const int c = pl.h * DFSSM_HEADDIM + pl.p0 + wid * kMaxRPW;
-          const unsigned w = pack_h2(gv[0], gv[1]);
+          const unsigned w = pack_h2(gmine, gnext);
           put_word(gw + (size_t)b * GW + c / 2, P.rs, w, tg_g);
           *reinterpret_cast<unsigned*>(P.gated_g + (size_t)b * d_inner + c) = w;  // plain copy for the host API
         }
