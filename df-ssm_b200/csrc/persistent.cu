@@ -55,7 +55,10 @@ constexpr unsigned kSpinLimit = 1u << 22;
 __constant__ unsigned c_spin_limit = kSpinLimit;
 __device__ __forceinline__ unsigned spin_limit() { return c_spin_limit; }
 #ifndef DFSSM_GFIRST
-#define DFSSM_GFIRST 1  // gated vector: poll one word per thread before loading the rest
+#define DFSSM_GFIRST 2  // gated vector: take_words FIRST mode (a warp leader polls first: batch 1 1897 -> 1970 tok/s against 1)
+#endif
+#ifndef DFSSM_XFIRST
+#define DFSSM_XFIRST 0  // x: take_words FIRST mode
 #endif
 constexpr int kMaxRPW = 2;  // SSM rows per warp (np = 32 channels over 16 warps)
 constexpr int kDotRows = 64;  // in_proj / out_proj rows a CTA may own (GEMV results in shared memory)
@@ -138,6 +141,28 @@ __device__ __forceinline__ LayerW layer_w(const PParams& P, int l) {
   return L;
 }
 
+// N consecutive fp32 values at p (16-byte aligned when N % 4 == 0) with the fewest load
+// instructions: 512 threads issuing scalar loads at once queue them for ~0.5 us in the LSU.
+template <int N>
+__device__ __forceinline__ void ld_f32s(const float* p, float (&v)[N]) {
+  if constexpr (N % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < N / 4; ++j) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(p) + j);
+      v[4 * j] = t.x, v[4 * j + 1] = t.y, v[4 * j + 2] = t.z, v[4 * j + 3] = t.w;
+    }
+  } else if constexpr (N % 2 == 0) {
+#pragma unroll
+    for (int j = 0; j < N / 2; ++j) {
+      const float2 t = __ldg(reinterpret_cast<const float2*>(p) + j);
+      v[2 * j] = t.x, v[2 * j + 1] = t.y;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < N; ++j) v[j] = __ldg(p + j);
+  }
+}
+
 // ---- tagged exchange words
 enum : unsigned { kTagX = 1, kTagTin = 2, kTagBC = 3, kTagGated = 4, kTagTout = 5, kTagsPerLayer = 8 };
 __device__ __forceinline__ unsigned tag_of(unsigned base, int layer, unsigned kind) {
@@ -165,11 +190,14 @@ __device__ __forceinline__ void put_word(unsigned long long* p, size_t rstride, 
 // 8*N-byte aligned for N > 1) until every tag equals `tag`; the data go to out[][].  All loads
 // of one poll are issued together.  Bounded: after kSpinLimit polls the error word gets
 // `code`, and once the error word is set every poll gives up at its next check.
-template <int G, int N, bool FIRST = false>
+// FIRST = 1: every thread first waits on its first word alone, then takes all; FIRST = 2: lane 0 of
+// each warp waits on its first word while the other lanes wait at the warp's barrier (the whole warp
+// must call), then the warp takes all (1/32 of the poll traffic while the words are not ready).
+template <int G, int N, int FIRST = 0>
 __device__ __forceinline__ void take_words(const unsigned long long* p, size_t gstride, unsigned tag,
                                            unsigned (&out)[G][N], unsigned* err, unsigned code) {
   unsigned long long w[G][N];
-  if (FIRST) {  // wait on the first word alone (an eighth of the poll traffic), then take all
+  if (FIRST == 1 || (FIRST == 2 && (threadIdx.x & 31) == 0)) {
     for (unsigned it = 0;; ++it) {
       unsigned long long w0;
       asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w0) : "l"(p) : "memory");
@@ -177,6 +205,7 @@ __device__ __forceinline__ void take_words(const unsigned long long* p, size_t g
       if ((it & 255u) == 255u && (ld_acquire(err) != 0 || it > spin_limit())) break;
     }
   }
+  if (FIRST == 2) __syncwarp();
   for (unsigned it = 0;; ++it) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -219,7 +248,7 @@ __device__ __forceinline__ void take_x(const unsigned long long* xw, int n_words
   constexpr int XPT = (B * KI) / 2 >= 4 ? 4 : ((B * KI) / 2 >= 2 ? 2 : 1);  // words per thread
   for (int i = threadIdx.x * XPT; i < n_words; i += kThreads * XPT) {
     unsigned v[1][XPT];
-    take_words<1, XPT>(xw + i, 0, tag, v, err, 1u);
+    take_words<1, XPT, DFSSM_XFIRST>(xw + i, 0, tag, v, err, 1u);
 #pragma unroll
     for (int k = 0; k < XPT; ++k) reinterpret_cast<unsigned*>(s_x)[i + k] = v[0][k];
   }
@@ -631,9 +660,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
     // ---------------- alpha: per-thread weights are loaded before waiting for x
     float w_in[KI];
     {
-      const int k0 = tid * KI;
-#pragma unroll
-      for (int j = 0; j < KI; ++j) w_in[j] = __ldg(L.ln_w + k0 + j);
+      ld_f32s<KI>(L.ln_w + tid * KI, w_in);
     }
     const bool t_producer = pl.role == 1 && pl.tj < P.n_t;
     typename RankHalves<KI>::T tb_in{};
@@ -838,9 +865,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
     // ---------------- beta: out_proj rows
     float w_out[KO];
     {
-      const int k0 = tid * KO;
-#pragma unroll
-      for (int j = 0; j < KO; ++j) w_out[j] = __ldg(L.norm_w + k0 + j);
+      ld_f32s<KO>(L.norm_w + tid * KO, w_out);
     }
     typename RankHalves<KO>::T tb_out{};
     if (t_producer) tb_out = load_rank_b<KO>(L.out.B16, d_inner, pl.tj);
@@ -866,7 +891,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       unsigned v[B][KO / 2];
       // the gated vector is the largest exchange (every CTA takes all of it while most wait for
       // the slowest head): poll one word per thread, then load the rest
-      take_words<B, KO / 2, DFSSM_GFIRST != 0>(gw + rep_off + tid * (KO / 2), GW, tg_g, v, P.sync + 3, 16u);
+      take_words<B, KO / 2, DFSSM_GFIRST>(gw + rep_off + tid * (KO / 2), GW, tg_g, v, P.sync + 3, 16u);
 #pragma unroll
       for (int b = 0; b < B; ++b)
 #pragma unroll
