@@ -472,6 +472,24 @@ __device__ __forceinline__ void fetch_t(const PParams& P, const unsigned long lo
   cta_sync();
 }
 
+// The LoRA t words can be taken by the last warps of the CTA while the others run the dot products
+// of `rows` rows (one per half-warp) when those warps have no row: kTWarps warps from thread kT0.
+template <int B>
+struct IdleT {
+  static constexpr int kTWarps = (B * DFSSM_RANK + 31) / 32;
+  static constexpr int kT0 = (kWarps - kTWarps) * 32;
+  // (batches 3 and 4 measured 1-2% slower with it: their words are better read ahead of the dots)
+  static __device__ __forceinline__ bool fits(int rows) { return B <= 2 && ((rows + 1) & ~1) <= kT0 / 16; }
+  // the calling thread's t word, taken into s_t (threads outside [kT0, kT0 + B * 16) do nothing)
+  static __device__ __forceinline__ void take(const PParams& P, const unsigned long long* tw, unsigned tag,
+                                              float* s_t) {
+    const int i = (int)threadIdx.x - kT0;
+    if (i >= 0 && i < B * DFSSM_RANK)
+      s_t[i] = __uint_as_float(
+          take_word(tw + (blockIdx.x % kReplicas) * P.rs + i, 0ull, tag, P.sync + 3, 8u));
+  }
+};
+
 // The copy-issuing warp: fills ring slot (k % ns) with layer l0 + k.  The first ns layers go
 // out at once; later ones part by part, each as soon as the compute threads have released that
 // part of the slot (empty barrier slot * kParts + part) while running the layer after the one
@@ -725,10 +743,28 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
         const int j = i < B * DFSSM_DSTATE ? i - b * DFSSM_DSTATE : DFSSM_DSTATE + pl.h / 2;
         return P.bcw + ((size_t)par * B + b) * P.bcw_per_seq + rep_off + j;
       };
-      const bool bc_taker = tid < kBcWords;
-      const unsigned long long* bcw_mine = bc_word(bc_taker ? tid : 0);
-      const unsigned long long bc_early = bc_taker ? peek_word(bcw_mine) : 0ull;
-      for (int e2 = tid; e2 < nrows * B; e2 += kThreads) {
+      // The B/C and dt words: where there are enough threads without an epilogue entry (tid >= E) for
+      // one word each, they wait for and take them while the others run the epilogue, so the wait
+      // overlaps the epilogue instead of following it; else every thread takes them after the epilogue,
+      // each thread's first word read once ahead of it (measured: batch 1 +2.6%; two words per idle
+      // thread made batches 3 and 4 slower).
+      const int E = nrows * B;  // epilogue entries, one per thread
+      const bool bc_idle = E + kBcWords <= kThreads;
+      auto take_bc = [&](int i, unsigned long long early) {
+        const unsigned v = take_word(bc_word(i), early, tag_of(ebase, layer, kTagBC), P.sync + 3, 4u);
+        if (i < B * DFSSM_DSTATE) {
+          s_bc[2 * i] = lo_h(v);
+          s_bc[2 * i + 1] = hi_h(v);
+        } else {  // dt = softplus(raw + dt_bias) and exp(A dt), once per sequence
+          const float* hp = s_hptab + layer * 4;
+          const float dtv = log1pf(expf(((pl.h & 1) ? hi_h(v) : lo_h(v)) + hp[0]));
+          s_dt[i - B * DFSSM_DSTATE] = dtv;
+          s_abar[i - B * DFSSM_DSTATE] = expf(dtv * (-expf(hp[1])));
+        }
+      };
+      if (bc_idle && tid >= E && tid - E < kBcWords) take_bc(tid - E, 0ull);
+      const unsigned long long bc_early = !bc_idle && tid < kBcWords ? peek_word(bc_word(tid)) : 0ull;
+      for (int e2 = tid; e2 < E; e2 += kThreads) {
         const int row = e2 / B, b = e2 - row * B;
         const int dot = s_dot[e2];
         const float v = proj_out(dot, s_xs[b], h2f(sc[row]), la + row * 16, s_t + b * 16);
@@ -745,27 +781,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
           s_xc[b * 64 + j] = round_hc(conv_silu(s0, s1, s2, v, cw + j * 4, h2f(cb[j])));
         }
       }
+      if (!bc_idle)
+        for (int i = tid; i < kBcWords; i += kThreads) take_bc(i, i == tid ? bc_early : 0ull);
       cta_sync();
       stamp(P, tb + 5);
-      // wait for every B/C CTA of this layer, then fetch conv'd B and C and dt
-      if (bc_taker) {
-#pragma unroll
-        for (int i = tid, k = 0; k < (kBcWords + kThreads - 1) / kThreads; ++k, i += kThreads) {
-          if (i >= kBcWords) break;
-          const unsigned v = k == 0 ? take_word(bcw_mine, bc_early, tag_of(ebase, layer, kTagBC), P.sync + 3, 4u)
-                                    : take_word(bc_word(i), 0ull, tag_of(ebase, layer, kTagBC), P.sync + 3, 4u);
-          if (i < B * DFSSM_DSTATE) {
-            s_bc[2 * i] = lo_h(v);
-            s_bc[2 * i + 1] = hi_h(v);
-          } else {  // dt = softplus(raw + dt_bias) and exp(A dt), once per sequence
-            const float* hp = s_hptab + layer * 4;
-            const float dtv = log1pf(expf(((pl.h & 1) ? hi_h(v) : lo_h(v)) + hp[0]));
-            s_dt[i - B * DFSSM_DSTATE] = dtv;
-            s_abar[i - B * DFSSM_DSTATE] = expf(dtv * (-expf(hp[1])));
-          }
-        }
-      }
-      cta_sync();
       stamp(P, tb + 6);
       // SSM state update + gate; warp w owns rows p = 2w, 2w+1 (np = 2 * kWarps), lane owns
       // n = 4*lane..; lane 0 publishes the gated pair as one word
@@ -819,16 +838,19 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       const __half* cw = reinterpret_cast<const __half*>(st + P.lay.conv_w);
       const __half* cb = reinterpret_cast<const __half*>(st + P.lay.conv_b);
       const float* cst = reinterpret_cast<const float*>(st + P.lay.cstate);
-      const unsigned long long t_early = peek_word(t_word<B>(P, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK));
+      const unsigned long long* tw_in = P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK;
+      const bool t_idle = IdleT<B>::fits(nb);  // warps without B/C rows take t during the dot products
+      const unsigned long long t_early = t_idle ? 0ull : peek_word(t_word<B>(P, tw_in));
       for (int i = hw; i < ((nb + 1) & ~1); i += 2 * kWarps) {
         const int row = i < nb ? i : nb - 1;
         const Dots<B> dd = row_dot<B>(st + P.lay.in_bits + (size_t)row * RB, d_model, s_q, d_inner, l16, qs);
         if (i < nb && l16 < B) s_dot[row * B + l16] = dd.v[l16];
       }
+      if (t_idle) IdleT<B>::take(P, tw_in, tag_of(ebase, layer, kTagTin), s_t);
       cta_sync();
       stamp(P, tb + 12);
       release_part(P, empties, layer, 1);
-      fetch_t<B>(P, P.tw + (size_t)(par * 2 + 0) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTin), s_t, t_early);
+      if (!t_idle) fetch_t<B>(P, tw_in, tag_of(ebase, layer, kTagTin), s_t, t_early);
       stamp(P, tb + 2);
       unsigned long long* bcw = P.bcw + (size_t)par * B * P.bcw_per_seq;
       const unsigned tg_bc = tag_of(ebase, layer, kTagBC);
@@ -910,7 +932,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
     for (int b = 0; b < B; ++b) qs[b] = qsum_of(s_qpart, b);
     stamp(P, tb + 10);
     release_part(P, empties, layer, 3);
-    const unsigned long long to_early = pl.no > 0 ? peek_word(t_word<B>(P, P.tw + (size_t)(par * 2 + 1) * B * DFSSM_RANK)) : 0ull;
+    const unsigned long long* tw_out = P.tw + (size_t)(par * 2 + 1) * B * DFSSM_RANK;
+    const bool to_idle = IdleT<B>::fits(pl.no);  // warps without out_proj rows take t meanwhile
+    const unsigned long long to_early = pl.no > 0 && !to_idle ? peek_word(t_word<B>(P, tw_out)) : 0ull;
     if (pl.no > 0) {
       const int RBO = d_inner / 8;
       for (int i = hw; i < ((pl.no + 1) & ~1); i += 2 * kWarps) {
@@ -918,11 +942,12 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
         const Dots<B> dd = row_dot<B>(st + P.lay.out_bits + (size_t)row * RBO, d_inner, s_q, d_inner, l16, qs);
         if (i < pl.no && l16 < B) s_dot[row * B + l16] = dd.v[l16];
       }
+      if (to_idle) IdleT<B>::take(P, tw_out, tag_of(ebase, layer, kTagTout), s_t);
     }
     cta_sync();
     stamp(P, tb + 13);
     if (pl.no > 0) {
-      fetch_t<B>(P, P.tw + (size_t)(par * 2 + 1) * B * DFSSM_RANK, tag_of(ebase, layer, kTagTout), s_t, to_early);
+      if (!to_idle) fetch_t<B>(P, tw_out, tag_of(ebase, layer, kTagTout), s_t, to_early);
       const __half* sc = reinterpret_cast<const __half*>(st + P.lay.out_scale);
       const __half* la = reinterpret_cast<const __half*>(st + P.lay.out_lA);
       unsigned long long* xw = P.xw + (size_t)(par ^ 1) * B * XW;
