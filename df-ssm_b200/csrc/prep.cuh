@@ -38,9 +38,9 @@ __device__ __forceinline__ void block_sum_n(float (&v)[N], float* red) {
   for (int i = 0; i < N; ++i) v[i] = red[kPrepFastWarps * N + i];
 }
 template <int N>
-__device__ __forceinline__ void block_max_n(float (&v)[N], float* red) {
+__device__ __forceinline__ void block_max_n(float (&v)[N], float* red) {  // v >= 0 (absolute values)
 #pragma unroll
-  for (int i = 0; i < N; ++i) v[i] = warp_max(v[i]);
+  for (int i = 0; i < N; ++i) v[i] = warp_max_nonneg(v[i]);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   cta_sync();
   if (l == 0)
@@ -80,9 +80,9 @@ __device__ __forceinline__ void block_sum1(float (&v)[N], float* red) {
   }
 }
 template <int N>
-__device__ __forceinline__ void block_max1(float (&v)[N], float* red) {
+__device__ __forceinline__ void block_max1(float (&v)[N], float* red) {  // v >= 0 (absolute values)
 #pragma unroll
-  for (int i = 0; i < N; ++i) v[i] = warp_max(v[i]);
+  for (int i = 0; i < N; ++i) v[i] = warp_max_nonneg(v[i]);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   if (l == 0)
 #pragma unroll
@@ -296,7 +296,7 @@ __device__ void prep_quantize(const float (&vals)[B][KPT], int8_t* sq, int Kq, f
       sq[b * Kq + (SWZ ? qswz(qperm_index(k0 + j)) : qperm_index(k0 + j))] = (int8_t)q;
       qsum += q;
     }
-    qsum = warp_sum(qsum);
+    qsum = __reduce_add_sync(0xffffffffu, qsum);
     if ((threadIdx.x & 31) == 0) s_qpart[b * kPrepFastWarps + (threadIdx.x >> 5)] = qsum;
     if (threadIdx.x == 0) s_xs[b] = s;
   }
