@@ -157,7 +157,7 @@ template <int KPT>
 __global__ void __launch_bounds__(kPrepFastThreads)
 rmsnorm_quant_kernel(const __half* __restrict__ in, int K, const float* __restrict__ w, __half* __restrict__ xn_out,
                      __half* __restrict__ xs_out, int8_t* __restrict__ q_out) {
-  __shared__ float red[256];  // prep_norm uses red[0, 16), prep_quantize red[128, 144)
+  __shared__ __align__(16) float red[256];  // prep_norm uses red[0, 16), prep_quantize red[128, 144)
   __shared__ float s_xs[1];
   __shared__ int s_qpart[kPrepFastWarps];
   __shared__ __align__(16) int8_t s_q[KPT * kPrepFastThreads];

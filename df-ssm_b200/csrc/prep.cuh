@@ -62,6 +62,20 @@ __device__ __forceinline__ void block_max_n(float (&v)[N], float* red) {  // v >
 // thread combines the 16 partials of each value itself, in the same fixed order, so all
 // threads hold identical totals.  `red` must not still be read by the previous reduction that
 // used it: callers rotate buffers so that a barrier separates the two uses.
+// The 16 x N warp partials at red (16-byte aligned), read with vector loads for N <= 2.
+template <int N>
+__device__ __forceinline__ void load_partials(const float* red, float (&p)[kPrepFastWarps * N]) {
+  if constexpr (N <= 2) {
+#pragma unroll
+    for (int j = 0; j < kPrepFastWarps * N / 4; ++j) {
+      const float4 t = reinterpret_cast<const float4*>(red)[j];
+      p[4 * j] = t.x, p[4 * j + 1] = t.y, p[4 * j + 2] = t.z, p[4 * j + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kPrepFastWarps * N; ++j) p[j] = red[j];
+  }
+}
 template <int N>
 __device__ __forceinline__ void block_sum1(float (&v)[N], float* red) {
 #pragma unroll
@@ -71,11 +85,13 @@ __device__ __forceinline__ void block_sum1(float (&v)[N], float* red) {
 #pragma unroll
     for (int i = 0; i < N; ++i) red[w * N + i] = v[i];
   cta_sync();
+  float p[kPrepFastWarps * N];
+  load_partials<N>(red, p);
 #pragma unroll
   for (int i = 0; i < N; ++i) {
     float s = 0.f;
 #pragma unroll
-    for (int j = 0; j < kPrepFastWarps; ++j) s += red[j * N + i];
+    for (int j = 0; j < kPrepFastWarps; ++j) s += p[j * N + i];
     v[i] = s;
   }
 }
@@ -88,11 +104,13 @@ __device__ __forceinline__ void block_max1(float (&v)[N], float* red) {  // v >=
 #pragma unroll
     for (int i = 0; i < N; ++i) red[w * N + i] = v[i];
   cta_sync();
+  float p[kPrepFastWarps * N];
+  load_partials<N>(red, p);
 #pragma unroll
   for (int i = 0; i < N; ++i) {
-    float s = red[i];
+    float s = p[i];
 #pragma unroll
-    for (int j = 1; j < kPrepFastWarps; ++j) s = fmaxf(s, red[j * N + i]);
+    for (int j = 1; j < kPrepFastWarps; ++j) s = fmaxf(s, p[j * N + i]);
     v[i] = s;
   }
 }
