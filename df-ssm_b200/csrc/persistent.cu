@@ -1031,6 +1031,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
       const unsigned char* st = ring + (size_t)(item % P.ns) * P.lay.stage_bytes;
       const int r0 = pl.v0 + ch * RC, nr = min(RC, pl.v0 + pl.nv - r0);
       for (int t0 = 0; t0 < nr; t0 += 32) {  // a pass: tiles t0 / 16 and t0 / 16 + 1
+        // the row scale of the thread that finishes (tile, row, sequence) below, requested before the
+        // MMAs so that its memory round trip overlaps them
+        float es_pre = 0.f;
+        if (tid < 32 * B) {
+          const int tile = tid / (16 * B), row = (tid - tile * 16 * B) / B, r = t0 + 16 * tile + row;
+          if (r < nr) es_pre = __ldg(P.Es + r0 + r);
+        }
         const int tr0 = t0 + 16 * wtile;      // this warp's tile's first row
         if (tr0 < nr) {
           const uint4* ra = reinterpret_cast<const uint4*>(st + (size_t)min(tr0 + g, nr - 1) * d_model);
@@ -1072,7 +1079,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) persistent_step_kernel(PPara
 #pragma unroll
             for (int sl = 0; sl < 8; ++sl) sum += pp[(size_t)sl * 16 * B];
             const int vr = r0 + r;
-            const float lg = sum * P.Es[vr];
+            const float lg = sum * es_pre;
             P.logits[(size_t)b * P.vocab + vr] = lg;
             const unsigned long long key = argmax_key(f2h(lg), (uint32_t)vr);
 #pragma unroll
