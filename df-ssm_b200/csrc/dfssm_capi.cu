@@ -1053,24 +1053,33 @@ int dfssm_scaffold_gemm(const uint32_t* packed, const int8_t* q, int M, int N, i
   if (M < 1 || N < 1 || K < 128 || K % 128 || K > 65536) return dfssm_fail(DFSSM_ERR_ARG, "bad sizes M=%d N=%d K=%d", M, N, K);
   if (((uintptr_t)packed | (uintptr_t)workspace) & 15) return dfssm_fail(DFSSM_ERR_ARG, "packed/workspace must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ProjW p{};
+  p.bits = packed;
+  p.N = N;
+  p.K = K;
+  const int rows_per_cta = 2 * (kGemvThreads / 32);
+  // mma.sync from one row (measured at the 1.3B in_proj shape: M = 1 in ~6.8 us against 9.8 us on the
+  // GEMV, whose activation staging and weight loads form one more latency chain); DFSSM_GEMM_MMA_MIN
+  // overrides
+  static const int mma_from = [] {
+    const char* v = getenv("DFSSM_GEMM_MMA_MIN");
+    return v ? atoi(v) : 1;
+  }();
+  if (M < mma_from || !mma_rg(N, K)) {  // the GEMV permutes and sums the rows itself: one launch
+    if ((uintptr_t)q & 15) return dfssm_fail(DFSSM_ERR_ARG, "q must be 16-byte aligned");
+    const size_t sm = (size_t)kGemvBT * K;
+    if (sm > 48 * 1024) CU(ensure_smem(reinterpret_cast<const void*>(proj_gemv_kernel<4>), sm));
+    proj_gemv_kernel<4><<<(N + rows_per_cta - 1) / rows_per_cta, kGemvThreads, sm, s>>>(
+        p, q, nullptr, nullptr, nullptr, M, reinterpret_cast<__half*>(acc), N, nullptr, nullptr, nullptr, 0, 0);
+    CHECK_LAUNCH();
+    return DFSSM_OK;
+  }
   char* ws = static_cast<char*>(workspace);
   int8_t* qp = reinterpret_cast<int8_t*>(ws);
   int* qsum = reinterpret_cast<int*>(ws + align256((size_t)M * K));
   permute_q_kernel<<<M, kPrepThreads, 0, s>>>(q, K, qp, qsum);
   CHECK_LAUNCH();
-  ProjW p{};
-  p.bits = packed;
-  p.N = N;
-  p.K = K;
-  if (M >= kMmaMinBatch && mma_rg(N, K))
-    return launch_mma<2>(p, M, qp, qsum, nullptr, nullptr, acc, N, nullptr, nullptr, nullptr, 0, 0, s);
-  const size_t sm = (size_t)kGemvBT * K;
-  if (sm > 48 * 1024) CU(ensure_smem(reinterpret_cast<const void*>(proj_gemv_kernel<2>), sm));
-  const int rows_per_cta = 2 * (kGemvThreads / 32);
-  proj_gemv_kernel<2><<<(N + rows_per_cta - 1) / rows_per_cta, kGemvThreads, sm, s>>>(
-      p, qp, qsum, nullptr, nullptr, M, reinterpret_cast<__half*>(acc), N, nullptr, nullptr, nullptr, 0, 0);
-  CHECK_LAUNCH();
-  return DFSSM_OK;
+  return launch_mma<2>(p, M, qp, qsum, nullptr, nullptr, acc, N, nullptr, nullptr, nullptr, 0, 0, s);
 }
 
 int dfssm_conv_step(float* conv_state, void* xbc_f16, int ld_xbc, const void* conv_w_f16, const void* conv_b_f16,

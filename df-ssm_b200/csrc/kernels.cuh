@@ -192,6 +192,9 @@ rmsnorm_quant_kernel(const __half* __restrict__ in, int K, const float* __restri
 // register + SiLU (df_ssm_kernels.cu:27-47) with fp32 state [B][3][d_xbc].
 // MODE 1 (out_proj): x = fp16(x + v)                           df_ssm_inference.py:207
 // MODE 2: raw int32 accumulators (stand-alone scaffold GEMM), `out` is int32 [B][ld_out].
+// MODE 4: as MODE 2 from int8 activations in natural column order (q [B][K] row-major, qsum
+// unused): each CTA permutes them into shared memory and sums the rows itself, so the stand-alone
+// GEMM needs no separate permute launch.
 // ---------------------------------------------------------------------------------------
 template <int MODE>
 __global__ void __launch_bounds__(kGemvThreads)
@@ -202,6 +205,7 @@ proj_gemv_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ 
                  const __half* __restrict__ conv_b, int d_inner, int d_xbc) {
   extern __shared__ __align__(16) unsigned char smem[];
   int8_t* sq = reinterpret_cast<int8_t*>(smem);  // [kGemvBT][K]
+  __shared__ int s_qs[kGemvBT];                  // MODE 4: row sums of the staged activations
   const int K = p.K, N = p.N;
   const int C = K >> 7;  // 128-bit chunks per row
   const int lane = threadIdx.x & 31, l16 = lane & 15, half = lane >> 4;
@@ -211,7 +215,23 @@ proj_gemv_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ 
   for (int bt0 = 0; bt0 < B; bt0 += kGemvBT) {
     const int nb = min(kGemvBT, B - bt0);
     __syncthreads();
-    {
+    if (MODE == 4) {  // natural-order rows: permute into shared memory and sum them here
+      if (threadIdx.x < kGemvBT) s_qs[threadIdx.x] = 0;
+      __syncthreads();
+      const int n16 = nb * K / 16;
+      for (int i = threadIdx.x; i < n16; i += kGemvThreads) {
+        const int r = (i * 16) / K, k0 = i * 16 - r * K;
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(q + (size_t)(bt0 + r) * K + k0));
+        const int8_t* vb = reinterpret_cast<const int8_t*>(&v);
+        int rs = 0;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          sq[r * K + qperm_index(k0 + e)] = vb[e];
+          rs += vb[e];
+        }
+        atomicAdd(s_qs + r, rs);
+      }
+    } else {
       const uint4* src = reinterpret_cast<const uint4*>(q + (size_t)bt0 * K);
       uint4* dst = reinterpret_cast<uint4*>(sq);
       const int n16 = nb * K / 16;
@@ -282,8 +302,8 @@ proj_gemv_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ 
       }
       const int b = bt0 + l16;
       if (!valid || l16 >= nb) continue;
-      const int dot = 2 * acc[0] - qsum[b];
-      if (MODE == 2) {
+      const int dot = 2 * acc[0] - (MODE == 4 ? s_qs[l16] : qsum[b]);
+      if (MODE == 2 || MODE == 4) {
         reinterpret_cast<int*>(out)[(size_t)b * ld_out + row] = dot;
         continue;
       }
