@@ -51,6 +51,12 @@ struct dfssm_engine {
   // execution
   cudaStream_t s = nullptr;
   cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+  // The caller stream into which all of the engine's work so far is ordered (every call ends with its
+  // stream waiting for the engine's work).  A persistent step on that same stream launches on it
+  // directly; a call on another stream first makes the engine stream wait for it (ev_cat).
+  cudaStream_t order_s = nullptr;
+  bool order_valid = false;
+  cudaEvent_t ev_cat = nullptr;
   cudaStream_t gs[kMaxGroups] = {};           // streams of sequence groups 1.. (group 0 uses s)
   cudaEvent_t ev_fork = nullptr, ev_join[kMaxGroups] = {};
   cudaGraphExec_t gexec = nullptr;
