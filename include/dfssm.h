@@ -83,7 +83,9 @@ int dfssm_reset_slots(dfssm_engine* e, int first, int count, void* stream);
  * engine's own next-token buffer when NULL, i.e. greedy continuation), runs all layers,
  * the final norm, the LM head and the greedy argmax.  Optional outputs: logits_dev
  * (fp32 [batch][vocab]; fp32 scale*int8-dot logits) and next_tokens_dev (int32 [batch]).
- * Stream-ordered; no host synchronisation and no allocation.
+ * Stream-ordered; no host synchronisation and no allocation.  Calls on different streams are ordered
+ * after each other by the engine (the stream of the previous call must still exist when a call on
+ * another stream is made); persistent-mode steps on the previous call's stream launch on it directly.
  * Replaces DFSSMModel.forward + argmax (df_ssm_inference.py:219-224,236). */
 int dfssm_step(dfssm_engine* e, const int32_t* tokens_dev, float* logits_dev,
                int32_t* next_tokens_dev, void* stream);
