@@ -1,6 +1,6 @@
-// Persistent whole-step decode kernel for small batches (B <= 2 per launch; batches up to 6 run one
-// launch per group of two sequences): one cooperative launch per
-// greedy decode step runs the embedding gather, every layer, the final norm, the LM head and
+// Persistent whole-step decode kernel for small batches (instances for 1 to 4 sequences per launch;
+// larger batches in persistent mode run one launch per group of up to four): one cooperative launch
+// per greedy decode step runs the embedding gather, every layer, the final norm, the LM head and
 // the argmax.  One CTA per SM: 16 compute warps (512 threads, named barrier 1) and one warp
 // that only issues the bulk copies of the weight/state ring.
 //
