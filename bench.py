@@ -339,6 +339,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sub", action="store_true", help="skip the sub-records (batch-32 and cfg4 lines)")
     ap.add_argument("--cfg4", action="store_true", help="add the cfg4 batch-256 strong-split sub-record at N = 1 too")
+    ap.add_argument("--kernel-times", type=int, default=0, metavar="K",
+                    help="after the timed region, replay K more steps under the CUDA activity profiler and print "
+                         "each kernel's warm mean duration and its time per step (stderr, rank 0)")
     ap.add_argument("--prefill", type=int, default=0, metavar="T",
                     help="time K prompt prefills of T tokens per sequence instead of decode steps")
     args = ap.parse_args()
@@ -479,6 +482,34 @@ def workload_config(name: str, cfg: dict, batch: int, job_batch: int, total_byte
             "l2": "no flush: each step streams >= %.0f MB from HBM (> 126 MB L2)" % (total_bytes / 1e6)}
 
 
+def kernel_times(m, steps: int, label: str) -> None:
+    """Per-kernel warm durations of `steps` decode steps (graph replays included), from the CUDA activity
+    records of torch.profiler; printed to stderr.  Outside every timed region."""
+    import collections
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(steps):
+            m.step(None, logits=False)
+        torch.cuda.synchronize()
+    ev = sorted((e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA),
+                key=lambda e: e.time_range.start)
+    if not ev:
+        print(f"kernel times ({label}): no CUDA activity records", file=sys.stderr)
+        return
+    agg = collections.defaultdict(list)
+    for e in ev:
+        agg[e.name.split("(")[0][:64]].append(e.time_range.end - e.time_range.start)
+    span = (ev[-1].time_range.end - ev[0].time_range.start) / steps
+    busy = sum(sum(v) for v in agg.values()) / steps
+    print(f"kernel times ({label}): {span:.1f} us per step from first start to last end, kernels "
+          f"{busy:.1f} us per step (sum of durations)", file=sys.stderr)
+    for n, v in sorted(agg.items(), key=lambda kv: -sum(kv[1])):
+        print(f"  {n:64s} launches/step {len(v) / steps:6.1f}  mean {sum(v) / len(v):8.2f} us  "
+              f"per step {sum(v) / steps:8.1f} us  share {sum(v) / steps / busy:6.1%}", file=sys.stderr)
+
+
 def decode_record(args, name, cfg, w, dims, world, rank, local, phys, keep=False, steps=None):
     """Builds the engine for one decode workload, consumes the prompts and W warm-up steps, then
     times K greedy steps with CUDA events between a barrier + synchronize on each side (max over
@@ -521,6 +552,8 @@ def decode_record(args, name, cfg, w, dims, world, rank, local, phys, keep=False
     clk = clocks.stop()
     ms_max = max_over_ranks(e0.elapsed_time(e1), world, torch.device("cuda", local))
     m.check_finite()
+    if getattr(args, "kernel_times", 0) and rank == 0:
+        kernel_times(m, args.kernel_times, f"{name} batch {batch} ({m.mode})")
     sb = step_bytes(dims, batch)
     peak, peak_kind = load_peaks()
     step_ms = ms_max / steps
