@@ -1495,7 +1495,7 @@ size_t persistent_trace_entries(const dfssm_engine* e) {
 
 int launch_persistent_traced(dfssm_engine* e, unsigned long long* trace_dev, cudaStream_t s) {
   if (!persistent_supported(e) || group_size(set_of(e), e->batch) != e->batch)
-    return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "the phase trace runs one persistent launch: batch 1, 2 or 4");
+    return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "the phase trace runs one persistent launch: batch 1 to 4");
   PersistentState& ps = set_of(e)->st[e->batch];
   PParams P = ps.params;
   P.trace = trace_dev;

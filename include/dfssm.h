@@ -122,7 +122,7 @@ int dfssm_weight_ptr(dfssm_engine* e, int layer, const char* name, void** ptr, s
 int dfssm_layer_step(dfssm_engine* e, int layer, void* stream);
 
 /* Diagnostics (no counterpart in the reference, which has no profiler hooks): number of
- * uint64 entries of a persistent-step trace, and one persistent decode step (mode 3, batch 1, 2 or 4:
+ * uint64 entries of a persistent-step trace, and one persistent decode step (mode 3, batch 1 to 4:
  * one launch; DFSSM_ERR_UNSUPPORTED for other batches)
  * that records %globaltimer stamps at its phase boundaries into trace_dev
  * [sm_count][4 + 16 * n_layer]: [0] start, [1] end, [2 + 16l + k] layer l point k
