@@ -324,18 +324,21 @@ int launch_mma(const ProjW& p, int B, const int8_t* q, const int* qsum, const __
     if (rc != -1) return rc;  // -1: not taken, fall through to mma.sync
   }
   const int RG = mma_rg(p.N, p.K);
-  const size_t sm = proj_mma_smem(p.K, RG);
-  if (RG == 2) {
-    CU(ensure_smem(reinterpret_cast<const void*>(proj_mma_kernel<MODE, 2>), sm));
-    proj_mma_kernel<MODE, 2><<<(p.N + 31) / 32, kMmaThreads, sm, s>>>(p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out),
-                                                                     ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc);
-  } else {
-    CU(ensure_smem(reinterpret_cast<const void*>(proj_mma_kernel<MODE, 1>), sm));
-    proj_mma_kernel<MODE, 1><<<(p.N + 15) / 16, kMmaThreads, sm, s>>>(p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out),
-                                                                     ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc);
+  // batch tiles of 8 per pass: the fewest that hold the batch (batches above 32 run passes of 32)
+  const int NT = B <= 8 ? 1 : B <= 16 ? 2 : 4;
+  const size_t sm = proj_mma_smem(p.K, RG, NT);
+#define DFSSM_MMA_LAUNCH(rg, nt)                                                                            \
+  if (RG == rg && NT == nt) {                                                                               \
+    CU(ensure_smem(reinterpret_cast<const void*>(proj_mma_kernel<MODE, rg, nt>), sm));                      \
+    proj_mma_kernel<MODE, rg, nt><<<(p.N + 16 * rg - 1) / (16 * rg), kMmaThreads, sm, s>>>(                 \
+        p, q, qsum, xs, t, B, reinterpret_cast<__half*>(out), ld_out, conv_state, conv_w, conv_b, d_inner, d_xbc); \
+    CHECK_LAUNCH();                                                                                         \
+    return DFSSM_OK;                                                                                        \
   }
-  CHECK_LAUNCH();
-  return DFSSM_OK;
+  DFSSM_MMA_LAUNCH(2, 1) DFSSM_MMA_LAUNCH(2, 2) DFSSM_MMA_LAUNCH(2, 4)
+  DFSSM_MMA_LAUNCH(1, 1) DFSSM_MMA_LAUNCH(1, 2) DFSSM_MMA_LAUNCH(1, 4)
+#undef DFSSM_MMA_LAUNCH
+  return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "no mma.sync projection instance for RG %d", RG);
 }
 
 template <int MODE>

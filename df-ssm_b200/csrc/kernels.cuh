@@ -352,7 +352,7 @@ proj_gemv_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ 
 // accumulators; 3: dequantised projection only (prompt rows, whose conv runs in the prefill scan).
 // ---------------------------------------------------------------------------------------
 constexpr int kMmaThreads = 256;
-constexpr int kMmaNT = 4;  // batch tiles of 8 per pass (32 rows)
+constexpr int kMmaNT = 4;  // most batch tiles of 8 per pass (32 rows)
 constexpr int kMmaMaxBlk = 8;  // 16-byte weight blocks per warp slice (<= 32 words)
 
 __device__ __forceinline__ void mma_s8(int (&d)[4], unsigned a0, unsigned a1, unsigned a2, unsigned a3, unsigned b0,
@@ -364,7 +364,9 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], unsigned a0, unsigned a1, un
 
 // Two CTAs per SM (caps registers at 128): the in_proj grid has 266 CTAs, which one CTA per SM
 // would run as two waves.
-template <int MODE, int RG>
+// NT batch tiles of 8 per pass (NB = 8 NT rows): the launcher picks the smallest NT that holds the
+// batch (1, 2 or 4), so a batch of 8 does not run the MMAs, fragment loads and epilogue slots of 32.
+template <int MODE, int RG, int NT = kMmaNT>
 __global__ void __launch_bounds__(kMmaThreads, 2)
 proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ qsum,
                 const __half* __restrict__ xs, const __half* __restrict__ t, int B,
@@ -372,7 +374,7 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
                 float* __restrict__ conv_state, const __half* __restrict__ conv_w,
                 const __half* __restrict__ conv_b, int d_inner, int d_xbc) {
   constexpr int KS = (kMmaThreads / 32) / RG;  // K slices per CTA
-  constexpr int NB = 8 * kMmaNT;               // batch rows per pass
+  constexpr int NB = 8 * NT;                   // batch rows per pass
   constexpr int R = 16 * RG;                   // output rows per CTA
   extern __shared__ __align__(16) unsigned char smem[];
   const int K = p.K, N = p.N, W = K >> 5;
@@ -499,7 +501,8 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
         v[u] = (b < nb && row0 + lr < N) ? h2f(out[(size_t)(bt0 + b) * ld_out + row0 + lr]) : 0.f;
       }
 #pragma unroll
-      for (int u = 0; u < U; ++u) e_cs[threadIdx.x + u * kMmaThreads] = v[u];
+      for (int u = 0; u < U; ++u)
+        if (threadIdx.x + u * kMmaThreads < NB * R) e_cs[threadIdx.x + u * kMmaThreads] = v[u];
     }
     if (MODE == 0) {
       constexpr int U = (NB * 3 * R + kMmaThreads - 1) / kMmaThreads;
@@ -514,13 +517,14 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
                    : 0.f;
       }
 #pragma unroll
-      for (int u = 0; u < U; ++u) e_cs[threadIdx.x + u * kMmaThreads] = v[u];
+      for (int u = 0; u < U; ++u)
+        if (threadIdx.x + u * kMmaThreads < NB * 3 * R) e_cs[threadIdx.x + u * kMmaThreads] = v[u];
     }
     if (bt0 > 0) load_w();
     if (!mbar_wait_bounded(&qbar, phase)) atomicOr(&g_umma_err, 2u);
-    int acc[kMmaNT][4];
+    int acc[NT][4];
 #pragma unroll
-    for (int tt = 0; tt < kMmaNT; ++tt)
+    for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[tt][i] = 0;
 #pragma unroll
@@ -534,7 +538,7 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
         const unsigned a0 = (wa[j] >> c) & 0x01010101u, a2 = (wa[j] >> (c + 4)) & 0x01010101u;
         const unsigned a1 = (wb[j] >> c) & 0x01010101u, a3 = (wb[j] >> (c + 4)) & 0x01010101u;
 #pragma unroll
-        for (int tt = 0; tt < kMmaNT; ++tt) {
+        for (int tt = 0; tt < NT; ++tt) {
           const int8_t* qb = sq + (tt * 8 + g) * SQ + (kw + j) * 32;
           const unsigned b0 = *reinterpret_cast<const unsigned*>(qb + c * 4);
           const unsigned b1 = *reinterpret_cast<const unsigned*>(qb + (c + 4) * 4);
@@ -544,7 +548,7 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
     }
     // D fragment: acc[tt][0..1] -> row g, batch cols 2c, 2c+1 of tile tt; [2..3] -> row g+8
 #pragma unroll
-    for (int tt = 0; tt < kMmaNT; ++tt) {
+    for (int tt = 0; tt < NT; ++tt) {
       int* r = red + (ks * NB + tt * 8 + 2 * c) * R + rg * 16 + g;
       r[0] = acc[tt][0];
       r[R] = acc[tt][1];
@@ -596,8 +600,8 @@ proj_mma_kernel(ProjW p, const int8_t* __restrict__ q, const int* __restrict__ q
   }
 }
 
-inline size_t proj_mma_smem(int K, int RG) {
-  const int NB = 8 * kMmaNT, KS = (kMmaThreads / 32) / RG, R = 16 * RG;
+inline size_t proj_mma_smem(int K, int RG, int NT = kMmaNT) {
+  const int NB = 8 * NT, KS = (kMmaThreads / 32) / RG, R = 16 * RG;
   return (size_t)NB * (K + 16) + (size_t)KS * R * NB * 4 +
          4 * ((size_t)NB * 3 * R + NB * DFSSM_RANK + R * (DFSSM_RANK + 1) + R * 4 + 2 * R + 2 * NB);
 }
