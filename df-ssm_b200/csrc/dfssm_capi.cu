@@ -395,6 +395,23 @@ int step_groups(const dfssm_engine* e) {
              // concurrent kernels compete for shared memory instead of filling idle time)
 }
 
+// The tensor-core LM head over `grid` CTAs with the fewest batch tiles of 8 per pass that hold B.
+int launch_head_mma(const int8_t* Eq, const float* Es, int vocab, int d, const __half* xn, int B, float* logits,
+                    unsigned long long* best, int grid, cudaStream_t s) {
+  const int NT = B <= 8 ? 1 : B <= 16 ? 2 : 4;
+  const size_t sm = lm_head_mma_smem(d, NT);
+#define DFSSM_HEAD_LAUNCH(nt)                                                                                  \
+  if (NT == nt) {                                                                                              \
+    CU(ensure_smem(reinterpret_cast<const void*>(lm_head_mma_kernel<nt>), sm));                                \
+    lm_head_mma_kernel<nt><<<grid, kHeadMmaThreads, sm, s>>>(Eq, Es, vocab, d, xn, B, logits, best);           \
+    CHECK_LAUNCH();                                                                                            \
+    return DFSSM_OK;                                                                                           \
+  }
+  DFSSM_HEAD_LAUNCH(1) DFSSM_HEAD_LAUNCH(2) DFSSM_HEAD_LAUNCH(4)
+#undef DFSSM_HEAD_LAUNCH
+  return dfssm_fail(DFSSM_ERR_UNSUPPORTED, "no LM-head instance for %d batch tiles", NT);
+}
+
 int enqueue_head(dfssm_engine* e, cudaStream_t s) {
   const dfssm_dims& d = e->d;
   int rc;
@@ -406,10 +423,8 @@ int enqueue_head(dfssm_engine* e, cudaStream_t s) {
     return v ? atoi(v) : 3;
   }();
   if (e->batch >= head_mma_min && d.d_model % (64 * kHeadMmaU) == 0) {
-    const size_t sm = lm_head_mma_smem(d.d_model);
-    CU(ensure_smem(reinterpret_cast<const void*>(lm_head_mma_kernel), sm));
-    lm_head_mma_kernel<<<e->sm_count, kHeadMmaThreads, sm, s>>>(e->Eq, e->Es, d.vocab, d.d_model, e->xn, e->batch,
-                                                               e->logits, e->best);
+    int rc2 = launch_head_mma(e->Eq, e->Es, d.vocab, d.d_model, e->xn, e->batch, e->logits, e->best, e->sm_count, s);
+    if (rc2) return rc2;
   } else {
     const size_t sm = (size_t)kHeadBT * d.d_model * sizeof(float);
     lm_head_kernel<<<e->sm_count * 4, kHeadThreads, sm, s>>>(e->Eq, e->Es, d.vocab, d.d_model, e->xn, e->batch,
@@ -1193,10 +1208,8 @@ int dfssm_lm_head_argmax(const int8_t* E_q, const float* E_s, int vocab, int d, 
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (batch >= kMmaMinBatch && d % (64 * kHeadMmaU) == 0) {
-    const size_t sm2 = lm_head_mma_smem(d);
-    CU(ensure_smem(reinterpret_cast<const void*>(lm_head_mma_kernel), sm2));
-    lm_head_mma_kernel<<<sms, kHeadMmaThreads, sm2, s>>>(E_q, E_s, vocab, d, static_cast<const __half*>(x_f16), batch,
-                                                          lg, best);
+    int rc2 = launch_head_mma(E_q, E_s, vocab, d, static_cast<const __half*>(x_f16), batch, lg, best, sms, s);
+    if (rc2) return rc2;
   } else {
     lm_head_kernel<<<sms * 4, kHeadThreads, sm, s>>>(E_q, E_s, vocab, d, static_cast<const __half*>(x_f16), batch, lg,
                                                       best);

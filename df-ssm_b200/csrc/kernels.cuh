@@ -811,13 +811,15 @@ lm_head_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, int 
 constexpr int kHeadMmaWarps = 16;  // one CTA per SM (the activation tile fills shared memory)
 constexpr int kHeadMmaThreads = 32 * kHeadMmaWarps;
 constexpr int kHeadMmaU = 4;       // 64-column blocks whose embedding loads are issued together
-constexpr int kHeadMmaNT = 4;  // 32 batch rows per pass
+constexpr int kHeadMmaNT = 4;  // most batch tiles of 8 per pass (32 rows)
 
+// NT batch tiles of 8 per pass: the launcher takes the fewest that hold the batch (1, 2 or 4).
+template <int NT = kHeadMmaNT>
 __global__ void __launch_bounds__(kHeadMmaThreads, 1)
 lm_head_mma_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, int vocab, int d,
                    const __half* __restrict__ xn, int B, float* __restrict__ logits,
                    unsigned long long* __restrict__ best) {
-  constexpr int NB = 8 * kHeadMmaNT;
+  constexpr int NB = 8 * NT;
   extern __shared__ __align__(16) unsigned char smem[];
   const int SX = d + 8;  // padded fp16 row stride
   __half* sx = reinterpret_cast<__half*>(smem);                                        // [NB][SX]
@@ -841,17 +843,17 @@ lm_head_mma_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, 
         bulk_g2s(sx + b * SX, xn + (size_t)(bt0 + b) * d, (unsigned)(d * 2), &xbar);
     }
     if (!mbar_wait_bounded(&xbar, phase)) atomicOr(&g_umma_err, 4u);
-    unsigned long long wbest[kHeadMmaNT][2];
+    unsigned long long wbest[NT][2];
 #pragma unroll
-    for (int tt = 0; tt < kHeadMmaNT; ++tt) wbest[tt][0] = wbest[tt][1] = 0ull;
+    for (int tt = 0; tt < NT; ++tt) wbest[tt][0] = wbest[tt][1] = 0ull;
     for (int tile = blockIdx.x * kHeadMmaWarps + wid; tile < ntiles; tile += gridDim.x * kHeadMmaWarps) {
       const int v0 = tile * 16;
       const int va = min(v0 + g, vocab - 1), vb = min(v0 + g + 8, vocab - 1);
       const uint4* ra = reinterpret_cast<const uint4*>(Eq + (size_t)va * d);
       const uint4* rb = reinterpret_cast<const uint4*>(Eq + (size_t)vb * d);
-      float acc[kHeadMmaNT][4];
+      float acc[NT][4];
 #pragma unroll
-      for (int tt = 0; tt < kHeadMmaNT; ++tt)
+      for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[tt][i] = 0.f;
       // kHeadMmaU blocks' embedding loads go out together before their MMAs, so each lane keeps
@@ -875,7 +877,7 @@ lm_head_mma_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, 
             const unsigned a1 = i8x2_to_h2(wb[s2], 0x4140u), a3 = i8x2_to_h2(wb[s2], 0x4342u);
             const int col = (blk0 + u) * 64 + 16 * c + 4 * s2;
 #pragma unroll
-            for (int tt = 0; tt < kHeadMmaNT; ++tt) {
+            for (int tt = 0; tt < NT; ++tt) {
               const uint2 bv = *reinterpret_cast<const uint2*>(sx + (tt * 8 + g) * SX + col);
               mma_f16(acc[tt], a0, a1, a2, a3, bv.x, bv.y);
             }
@@ -884,7 +886,7 @@ lm_head_mma_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, 
       }
       // D fragment: acc[tt][0..1] -> row v0+g, batch 2c, 2c+1 of tile tt; [2..3] -> row v0+g+8
 #pragma unroll
-      for (int tt = 0; tt < kHeadMmaNT; ++tt) {
+      for (int tt = 0; tt < NT; ++tt) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int v = v0 + g + (i >= 2 ? 8 : 0);
@@ -900,7 +902,7 @@ lm_head_mma_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, 
     }
     // reduce the per-lane bests over the 8 lanes that share c (same batch columns)
 #pragma unroll
-    for (int tt = 0; tt < kHeadMmaNT; ++tt)
+    for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         unsigned long long k = wbest[tt][j];
@@ -920,8 +922,8 @@ lm_head_mma_kernel(const int8_t* __restrict__ Eq, const float* __restrict__ Es, 
   }
 }
 
-inline size_t lm_head_mma_smem(int d) {
-  return (size_t)8 * kHeadMmaNT * (d + 8) * 2 + (size_t)kHeadMmaWarps * 8 * kHeadMmaNT * 8;
+inline size_t lm_head_mma_smem(int d, int NT = kHeadMmaNT) {
+  return (size_t)8 * NT * (d + 8) * 2 + (size_t)kHeadMmaWarps * 8 * NT * 8;
 }
 
 __global__ void finalize_kernel(unsigned long long* __restrict__ best, int B, int* __restrict__ tokens) {
